@@ -20,6 +20,31 @@
 
 #define MIN(a, b) ((a) < (b) ? (a) : (b))
 
+/* bf16 storage emulation for the whole-step oracle: when on, every tensor the
+ * B200 path stores in bf16 (weights used by GEMMs, forward activations, the
+ * logits and backward activation gradients) is rounded to bf16 (round to
+ * nearest even) at the same point, and the attention forward follows the
+ * blockwise online-softmax order with bf16 probabilities.  Arithmetic stays
+ * fp32.  Off by default (plain fp32 reference semantics). */
+static int g_bf16 = 0;
+void orc_set_bf16_emulation(int on) { g_bf16 = on; }
+
+static inline float bf16r(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u) return x; /* inf / nan */
+    u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    float y;
+    memcpy(&y, &u, 4);
+    return y;
+}
+static void round_bf16(float *x, int64_t n) {
+    if (!g_bf16) return;
+#pragma omp parallel for
+    for (int64_t i = 0; i < n; ++i) x[i] = bf16r(x[i]);
+}
+
 /* ======================================================================= */
 /* seeded inputs                                                            */
 /* ======================================================================= */
@@ -599,6 +624,56 @@ void orc_attention_backward(const float *q, const float *k, const float *v, int 
         }
 }
 
+/* Flash-style causal attention forward with the B200 kernel's order: 64-key
+ * blocks, running max in base 2, probabilities rounded to bf16 before the
+ * P.V product, row sum of the unrounded probabilities, output / sum. */
+static void attention_forward_blockwise(const float *q, const float *k, const float *v, int ld, float *o, int ldo,
+                                        float *lse, int B, int S, int H, int Dh) {
+    const float scale_log2 = (1.0f / sqrtf((float)Dh)) * 1.4426950408889634f;
+#pragma omp parallel
+    {
+        float *acc = (float *)malloc((size_t)Dh * sizeof(float));
+        float *sv = (float *)malloc(64 * sizeof(float));
+#pragma omp for collapse(3) schedule(dynamic, 16)
+        for (int b = 0; b < B; ++b)
+            for (int h = 0; h < H; ++h)
+                for (int i = 0; i < S; ++i) {
+                    const float *qi = q + ((int64_t)b * S + i) * ld + (int64_t)h * Dh;
+                    float m = -INFINITY, l = 0.f;
+                    for (int d = 0; d < Dh; ++d) acc[d] = 0.f;
+                    for (int j0 = 0; j0 <= i; j0 += 64) {
+                        const int j1 = (j0 + 64 <= i + 1) ? j0 + 64 : i + 1;
+                        float mx = -INFINITY;
+                        for (int j = j0; j < j1; ++j) {
+                            const float *kj = k + ((int64_t)b * S + j) * ld + (int64_t)h * Dh;
+                            float sc = 0.f;
+                            for (int d = 0; d < Dh; ++d) sc += qi[d] * kj[d];
+                            sv[j - j0] = sc * scale_log2;
+                            if (sv[j - j0] > mx) mx = sv[j - j0];
+                        }
+                        const float mnew = m > mx ? m : mx;
+                        const float corr = exp2f(m - mnew);
+                        float sum = 0.f;
+                        for (int d = 0; d < Dh; ++d) acc[d] *= corr;
+                        for (int j = j0; j < j1; ++j) {
+                            const float p = exp2f(sv[j - j0] - mnew);
+                            sum += p;
+                            const float pb = bf16r(p);
+                            const float *vj = v + ((int64_t)b * S + j) * ld + (int64_t)h * Dh;
+                            for (int d = 0; d < Dh; ++d) acc[d] += pb * vj[d];
+                        }
+                        l = l * corr + sum;
+                        m = mnew;
+                    }
+                    float *oi = o + ((int64_t)b * S + i) * ldo + (int64_t)h * Dh;
+                    for (int d = 0; d < Dh; ++d) oi[d] = acc[d] / l;
+                    if (lse) lse[((int64_t)b * H + h) * S + i] = (m + log2f(l)) * 0.6931471805599453f;
+                }
+        free(acc);
+        free(sv);
+    }
+}
+
 float orc_ce_fused(const float *logits, const int32_t *targets, float *dlogits,
                    int rows, int classes, float eps) {
     const float cap = -logf(eps);
@@ -752,6 +827,16 @@ float orc_train_step(const orc_model_cfg *c, float *P, float *G, float *Mo, floa
     if (c->pos == 0) { pos_tab = falloc((int64_t)c->max_seq * d); orc_sinusoid_table(pos_tab, c->max_seq, (int)d); }
     else { rc = falloc((int64_t)S * Dh / 2); rsn = falloc((int64_t)S * Dh / 2); orc_rope_table(rc, rsn, S, Dh, c->rope_base); }
 
+    /* weights as the GEMMs see them (bf16 shadow in emulation mode) */
+    float *Pw = falloc(total);
+    memcpy(Pw, P, (size_t)total * sizeof(float));
+    if (g_bf16) {
+        int64_t offs_[1024], sizes_[1024];
+        int kinds_[1024];
+        int nt = orc_param_layout(c, offs_, sizes_, kinds_, 1024, NULL);
+        for (int i = 0; i < nt; ++i)
+            if (kinds_[i] == K_MAT || kinds_[i] == K_EMB) round_bf16(Pw + offs_[i], sizes_[i]);
+    }
     layer_acts *A = (layer_acts *)calloc((size_t)c->layers, sizeof(layer_acts));
     float *x = falloc(T * d);
     /* embedding: x = E[id] (+ PE[s]) */
@@ -762,49 +847,65 @@ float orc_train_step(const orc_model_cfg *c, float *P, float *G, float *Mo, floa
         for (int64_t k = 0; k < d; ++k)
             x[t * d + k] = P[Ly.emb + (int64_t)id * d + k] + (pos_tab ? pos_tab[(int64_t)s * d + k] : 0.f);
     }
+    round_bf16(x, T * d);
     for (int l = 0; l < c->layers; ++l) {
         int64_t *o = Ly.lay[l];
         layer_acts *a = &A[l];
         a->x = x;
         a->qkv = falloc(T * 3 * d);
-        gemm_nt(x, d, P + o[L_WQKV], d, a->qkv, 3 * d, T, 3 * d, d);
+        gemm_nt(x, d, Pw + o[L_WQKV], d, a->qkv, 3 * d, T, 3 * d, d);
         if (c->bias) bias_add(a->qkv, P + o[L_BQKV], T, 3 * d);
         if (c->pos == 1) {
             orc_rope_apply(a->qkv, T, S, H, Dh, (int)(3 * d), rc, rsn, 0);
             orc_rope_apply(a->qkv + d, T, S, H, Dh, (int)(3 * d), rc, rsn, 0);
         }
+        round_bf16(a->qkv, T * 3 * d);
         a->attn = falloc(T * d);
         a->lse = falloc((int64_t)B * H * S);
-        orc_attention_forward(a->qkv, a->qkv + d, a->qkv + 2 * d, (int)(3 * d), a->attn, (int)d, a->lse, B, S, H, Dh);
+        if (g_bf16)
+            attention_forward_blockwise(a->qkv, a->qkv + d, a->qkv + 2 * d, (int)(3 * d), a->attn, (int)d, a->lse,
+                                        B, S, H, Dh);
+        else
+            orc_attention_forward(a->qkv, a->qkv + d, a->qkv + 2 * d, (int)(3 * d), a->attn, (int)d, a->lse, B, S,
+                                  H, Dh);
+        round_bf16(a->attn, T * d);
         a->r1 = falloc(T * d);
-        gemm_nt(a->attn, d, P + o[L_WO], d, a->r1, d, T, d, d);
+        gemm_nt(a->attn, d, Pw + o[L_WO], d, a->r1, d, T, d, d);
         if (c->bias) bias_add(a->r1, P + o[L_BO], T, d);
         for (int64_t i = 0; i < T * d; ++i) a->r1[i] += x[i];
+        round_bf16(a->r1, T * d);
         a->h1 = falloc(T * d); a->mean1 = falloc(T); a->rstd1 = falloc(T);
         norm_fwd(c, a->r1, P + o[L_N1G], c->norm == 0 ? P + o[L_N1B] : NULL, a->h1, a->mean1, a->rstd1, T);
+        round_bf16(a->h1, T * d);
         a->f = falloc(T * F);
-        gemm_nt(a->h1, d, P + o[L_W1], d, a->f, F, T, F, d);
+        gemm_nt(a->h1, d, Pw + o[L_W1], d, a->f, F, T, F, d);
         if (c->bias) bias_add(a->f, P + o[L_B1], T, F);
         for (int64_t i = 0; i < T * F; ++i) a->f[i] = a->f[i] > 0.f ? a->f[i] : 0.f;
+        round_bf16(a->f, T * F);
         a->r2 = falloc(T * d);
-        gemm_nt(a->f, F, P + o[L_W2], F, a->r2, d, T, d, F);
+        gemm_nt(a->f, F, Pw + o[L_W2], F, a->r2, d, T, d, F);
         if (c->bias) bias_add(a->r2, P + o[L_B2], T, d);
         for (int64_t i = 0; i < T * d; ++i) a->r2[i] += a->h1[i];
+        round_bf16(a->r2, T * d);
         a->mean2 = falloc(T); a->rstd2 = falloc(T);
         x = falloc(T * d);
         norm_fwd(c, a->r2, P + o[L_N2G], c->norm == 0 ? P + o[L_N2B] : NULL, x, a->mean2, a->rstd2, T);
+        round_bf16(x, T * d);
     }
     float *hf = falloc(T * d), *meanf = falloc(T), *rstdf = falloc(T);
     norm_fwd(c, x, P + Ly.nog, c->norm == 0 ? P + Ly.nob : NULL, hf, meanf, rstdf, T);
-    const float *Whead = c->tied ? P + Ly.emb : P + Ly.head;
+    round_bf16(hf, T * d);
+    const float *Whead = c->tied ? Pw + Ly.emb : Pw + Ly.head;
     float *logits = falloc(T * V);
     gemm_nt(hf, d, Whead, d, logits, V, T, V, d);
+    round_bf16(logits, T * V);
     if (logits_out) memcpy(logits_out, logits, (size_t)(T * V) * sizeof(float));
     float *dlog = logits; /* overwritten in place by the fused CE */
     float *tmp = falloc(T * V);
     float loss = orc_ce_fused(logits, targets, tmp, (int)T, (int)V, 1e-8f);
     memcpy(dlog, tmp, (size_t)(T * V) * sizeof(float));
     free(tmp);
+    round_bf16(dlog, T * V);
 
     /* ---------------- backward ---------------- */
     float *gWhead = c->tied ? G + Ly.emb : G + Ly.head;
@@ -814,8 +915,10 @@ float orc_train_step(const orc_model_cfg *c, float *P, float *G, float *Mo, floa
     free(dWtmp);
     float *dhf = falloc(T * d);
     gemm_nn(dlog, V, Whead, d, dhf, d, T, d, V);
+    round_bf16(dhf, T * d);
     float *dx = falloc(T * d);
     norm_bwd(c, x, dhf, P + Ly.nog, meanf, rstdf, dx, G + Ly.nog, c->norm == 0 ? G + Ly.nob : NULL, T);
+    round_bf16(dx, T * d);
     free(dhf);
     float *dtmp = falloc(T * d), *dF = falloc(T * F), *dqkv = falloc(T * 3 * d), *dattn = falloc(T * d);
     float *dr = falloc(T * d);
@@ -825,32 +928,39 @@ float orc_train_step(const orc_model_cfg *c, float *P, float *G, float *Mo, floa
         /* out = norm2(r2) */
         norm_bwd(c, a->r2, dx, P + o[L_N2G], a->mean2, a->rstd2, dr, G + o[L_N2G],
                  c->norm == 0 ? G + o[L_N2B] : NULL, T);
+        round_bf16(dr, T * d);
         /* r2 = h1 + f W2^T + b2 */
         gemm_tn(dr, d, a->f, F, G + o[L_W2], F, T, F, d);
         if (c->bias) colsum_acc(dr, G + o[L_B2], T, d);
-        gemm_nn(dr, d, P + o[L_W2], F, dF, F, T, F, d);
+        gemm_nn(dr, d, Pw + o[L_W2], F, dF, F, T, F, d);
         for (int64_t i = 0; i < T * F; ++i) if (!(a->f[i] > 0.f)) dF[i] = 0.f;
+        round_bf16(dF, T * F);
         gemm_tn(dF, F, a->h1, d, G + o[L_W1], d, T, d, F);
         if (c->bias) colsum_acc(dF, G + o[L_B1], T, F);
-        gemm_nn(dF, F, P + o[L_W1], d, dtmp, d, T, d, F);
+        gemm_nn(dF, F, Pw + o[L_W1], d, dtmp, d, T, d, F);
         for (int64_t i = 0; i < T * d; ++i) dtmp[i] += dr[i];        /* dh1 */
+        round_bf16(dtmp, T * d);
         /* h1 = norm1(r1) */
         norm_bwd(c, a->r1, dtmp, P + o[L_N1G], a->mean1, a->rstd1, dr, G + o[L_N1G],
                  c->norm == 0 ? G + o[L_N1B] : NULL, T);
+        round_bf16(dr, T * d);
         /* r1 = x + attn Wo^T + bo */
         gemm_tn(dr, d, a->attn, d, G + o[L_WO], d, T, d, d);
         if (c->bias) colsum_acc(dr, G + o[L_BO], T, d);
-        gemm_nn(dr, d, P + o[L_WO], d, dattn, d, T, d, d);
+        gemm_nn(dr, d, Pw + o[L_WO], d, dattn, d, T, d, d);
+        round_bf16(dattn, T * d);
         orc_attention_backward(a->qkv, a->qkv + d, a->qkv + 2 * d, (int)(3 * d), a->attn, dattn, (int)d,
                                a->lse, dqkv, dqkv + d, dqkv + 2 * d, (int)(3 * d), B, S, H, Dh);
         if (c->pos == 1) {
             orc_rope_apply(dqkv, T, S, H, Dh, (int)(3 * d), rc, rsn, 1);
             orc_rope_apply(dqkv + d, T, S, H, Dh, (int)(3 * d), rc, rsn, 1);
         }
+        round_bf16(dqkv, T * 3 * d);
         gemm_tn(dqkv, 3 * d, a->x, d, G + o[L_WQKV], d, T, d, 3 * d);
         if (c->bias) colsum_acc(dqkv, G + o[L_BQKV], T, 3 * d);
-        gemm_nn(dqkv, 3 * d, P + o[L_WQKV], d, dx, d, T, d, 3 * d);
+        gemm_nn(dqkv, 3 * d, Pw + o[L_WQKV], d, dx, d, T, d, 3 * d);
         for (int64_t i = 0; i < T * d; ++i) dx[i] += dr[i];
+        round_bf16(dx, T * d);
     }
     /* embedding scatter-add (embedding.cu:33-53) */
     for (int64_t t = 0; t < T; ++t) {
@@ -882,6 +992,6 @@ float orc_train_step(const orc_model_cfg *c, float *P, float *G, float *Mo, floa
     }
     free(A); free(x); free(hf); free(meanf); free(rstdf); free(logits);
     free(dtmp); free(dF); free(dqkv); free(dattn); free(dr); free(dx);
-    free(pos_tab); free(rc); free(rsn);
+    free(pos_tab); free(rc); free(rsn); free(Pw);
     return loss;
 }

@@ -118,6 +118,9 @@ float orc_ce_fused(const float *logits, const int32_t *targets, float *dlogits,
                    int rows, int classes, float eps);
 
 /* ---------------- whole training step ----------------------------------- */
+/* bf16 storage emulation (see oracle.c): 1 rounds every tensor the B200 path
+ * stores in bf16 at the same point of the step; 0 (default) is plain fp32. */
+void orc_set_bf16_emulation(int on);
 typedef struct {
     int vocab, dim, layers, heads, ffn, max_seq;
     int norm;      /* 0 = LayerNorm (reference), 1 = RMSNorm */

@@ -79,6 +79,7 @@ def lib():
             "orc_param_layout": (C.c_int, [C.POINTER(ModelCfg), C.c_void_p, C.c_void_p, C.c_void_p,
                                            C.c_int, C.POINTER(C.c_int64)]),
             "orc_init_params": (None, [C.POINTER(ModelCfg), f32p, C.c_uint64, C.c_float]),
+            "orc_set_bf16_emulation": (None, [C.c_int]),
             "orc_train_step": (C.c_float, [C.POINTER(ModelCfg), f32p, f32p, f32p, f32p, i32p, i32p,
                                            C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
         }
@@ -351,8 +352,11 @@ def init_params(model: Model, seed=0, std=0.02):
 
 
 def train_step(model: Model, params, m, v, ids, targets, B, S, lr=3e-4, beta1=0.9, beta2=0.95,
-               eps=1e-8, weight_decay=0.1, step=1, grad_scale=1.0, update=True, want_logits=False):
-    """Returns (loss, grads); params/m/v are updated in place when update=True."""
+               eps=1e-8, weight_decay=0.1, step=1, grad_scale=1.0, update=True, want_logits=False,
+               bf16_emulation=False):
+    """Returns (loss, grads); params/m/v are updated in place when update=True.
+    bf16_emulation=True rounds to bf16 wherever the B200 path stores bf16."""
+    lib().orc_set_bf16_emulation(int(bf16_emulation))
     grads = np.empty_like(params)
     opt = AdamWCfg(lr, beta1, beta2, eps, weight_decay, step, grad_scale)
     logits = np.empty(B * S * model.vocab, np.float32) if want_logits else None

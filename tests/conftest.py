@@ -24,3 +24,21 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts(request):
+    """After every GPU test: no bounded device wait may have timed out."""
+    yield
+    if "gpu" not in request.keywords:
+        return
+    import ctypes
+
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from zerollm_b200 import lib
+    torch.cuda.synchronize()
+    code = ctypes.c_int(0)
+    lib.load().zl_device_error(ctypes.byref(code))
+    assert code.value == 0, f"device-side bounded wait timed out (code {code.value})"

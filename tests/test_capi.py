@@ -1,0 +1,93 @@
+"""C-ABI boundary checks that need no GPU: the library loads, exports every
+symbol include/zerollm_b200.h declares, and its host-side logic (parameter
+layout, bucket plan, argument validation) behaves."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "zerollm_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(zl_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from zerollm_b200 import lib
+    L = lib.load()
+    syms = declared_symbols()
+    assert len(syms) > 50
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, missing
+    # and the Python binding declares a signature for each
+    assert not [s for s in syms if s not in lib.SIGNATURES], [s for s in syms if s not in lib.SIGNATURES]
+
+
+@pytest.mark.parametrize("norm,pos,tied,bias", [(1, 1, 0, 1), (0, 0, 1, 1), (0, 1, 0, 0), (1, 0, 1, 0)])
+def test_param_layout_matches_oracle(norm, pos, tied, bias):
+    from zerollm_b200 import Config, param_layout
+    c = Config(norm=norm, pos=pos, tied=tied, bias=bias)
+    o, s, k, t = param_layout(c)
+    om = O.Model(norm=norm, pos=pos, tied=tied, bias=bias)
+    oo, ss, kk, tt = O.param_layout(om)
+    assert t == tt and np.array_equal(o, oo) and np.array_equal(s, ss) and np.array_equal(k, kk)
+    assert o[0] == 0 and np.array_equal(o[1:], np.cumsum(s)[:-1])
+
+
+def test_26m_parameter_count():
+    from zerollm_b200 import Config, param_layout
+    # untied head, RMSNorm, biases: 6*(4d^2+2dF + 3d+d+F+d + 2d) + 2*V*d + d
+    *_, t = param_layout(Config.baseline_26m())
+    d, F, V, L = 512, 2048, 6400, 6
+    assert t == L * (4 * d * d + 2 * d * F + 3 * d + d + F + d + 2 * d) + 2 * V * d + d
+
+
+def test_bucket_plan_covers_arena_in_order():
+    from zerollm_b200 import Config, bucket_plan, param_layout
+    o, s, _, t = param_layout(Config.baseline_26m())
+    for budget in (25 * 1024 * 1024 // 4, 1 << 20, 100003, 4099):
+        st, ln = bucket_plan(o, s, budget, max_buckets=1 << 20)
+        assert st[0] == 0 and ln.sum() == t
+        assert np.array_equal(st[1:], st[:-1] + ln[:-1])      # contiguous, ordered
+        assert ln.max() <= budget
+        # bucket boundaries fall on tensor boundaries unless a tensor exceeds the budget
+        bounds = set(o.tolist()) | {t}
+        for a, l in zip(st, ln):
+            if l < budget:
+                assert (a + l) in bounds or (a + l) % 1 == 0
+
+
+def test_bucket_plan_rejects_bad_input():
+    from zerollm_b200 import ZLError, bucket_plan
+    with pytest.raises(ZLError):
+        bucket_plan([0, 5], [4, 4], 10)       # gap between tensors
+    with pytest.raises(ZLError):
+        bucket_plan([0], [4], 0)
+
+
+def test_model_config_validation():
+    from zerollm_b200 import Config, ZLError, param_layout
+    with pytest.raises(ZLError):
+        param_layout(Config(embed_dim=500))   # head_dim must be 64
+    with pytest.raises(ZLError):
+        param_layout(Config(num_layers=0))
+
+
+def test_kernel_entry_points_validate_before_touching_the_device():
+    """Size validation mirrors the reference's throw / silent-return behaviour without a GPU."""
+    from zerollm_b200 import lib
+    L = lib.load()
+    assert L.zl_add_f32(None, None, None, 0, None) == lib.ZL_EINVAL          # add.cu:36-38 throws
+    assert L.zl_softmax_f32(None, None, 0, 5, None) == lib.ZL_EINVAL        # softmax.cu:70-71 throws
+    assert L.zl_relu_forward_f32(None, None, 0, None) == lib.ZL_OK           # relu.cu:23 returns
+    assert L.zl_layernorm_forward_f32(None, None, None, None, None, None, 0, 4, 1e-5, None) == lib.ZL_OK
+    assert L.zl_mha_forward_f32(None, None, None, None, None, None, 0, 1, 1, 1, 1, None) == lib.ZL_EINVAL
+    assert L.zl_adamw_step_f32(None, None, None, None, 0, *([0.0] * 7), None) == lib.ZL_EINVAL
+    assert b"invalid" in L.zl_last_error() or b"size" in L.zl_last_error()

@@ -1,0 +1,370 @@
+"""Kernel parity on the GPU: the CUDA library (through its C ABI) against the
+oracle (CPU restatement of the reference kernels) and, for the bf16 GEMM,
+against a plain torch fp32 product of the same bf16 operands.
+
+Tolerances (normwise: max|got-ref| / max|ref|):
+  * bf16 paths: 2e-2 (BASELINE parity bound under bf16)
+  * fp32 API through tcgen05 kind::tf32 GEMMs: 1e-3 (bound under tf32)
+  * fp32 SIMT paths: 1e-5 relative / bit-exact where the reference order is kept
+  * indexing (embedding gather/skip): bit-exact
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.kat_util import check_case, load_cases
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+TF32_TOL = 1e-3
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def K():
+    from zerollm_b200 import kernels
+    return kernels
+
+
+@pytest.fixture(scope="module")
+def L():
+    from zerollm_b200 import lib
+    lib.load()
+    return lib
+
+
+CASES = load_cases()
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_reference_kats_on_gpu(case, K):
+    check_case(case, K)
+
+
+# ------------------------------------------------------------------ bf16 tcgen05 GEMM
+def _bf(x):
+    return torch.as_tensor(x).to("cuda", torch.bfloat16)
+
+
+def _gemm(L, A, B, M, N, K_, layout, flags=0, epi=None, out=None, ws=None):
+    import ctypes as C
+    if out is None:
+        out = torch.empty(M * N, device="cuda", dtype=torch.float32 if flags & L.EPI_OUT_F32 else torch.bfloat16)
+    e = epi if epi is not None else L.Epilogue()
+    if ws is None:
+        n = L.load().zl_gemm_workspace_floats(M, N, K_, layout, flags)
+        ws = torch.empty(max(int(n), 1), device="cuda", dtype=torch.float32)
+    L.call("zl_gemm_bf16", A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K_, layout, flags, C.byref(e),
+           ws.data_ptr(), None)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("a_k,b_k", [(True, True), (True, False), (False, True), (False, False)])
+@pytest.mark.parametrize("M,N,K_", [(128, 256, 64), (304, 200, 136), (1024, 512, 512), (512, 1536, 512)])
+def test_gemm_bf16_layouts(L, a_k, b_k, M, N, K_):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    A = torch.randn(M, K_, generator=g)
+    B = torch.randn(N, K_, generator=g)
+    Ab, Bb = A.bfloat16(), B.bfloat16()
+    ref = Ab.float() @ Bb.float().T
+    Ad = _bf(Ab if a_k else Ab.T.contiguous())
+    Bd = _bf(Bb if b_k else Bb.T.contiguous())
+    layout = (L.A_KMAJOR if a_k else 0) | (L.B_KMAJOR if b_k else 0)
+    out = _gemm(L, Ad, Bd, M, N, K_, layout, L.EPI_OUT_F32)
+    assert rel(out.cpu().view(M, N), ref) < 1e-4  # fp32 accumulate of identical bf16 operands
+    out16 = _gemm(L, Ad, Bd, M, N, K_, layout, 0)
+    assert rel(out16.float().cpu().view(M, N), ref) < 1e-2
+
+
+def test_gemm_bf16_weight_grad_splitk(L):
+    """dW-shaped product: reduction over 32768 rows, both operands MN-major (split-K path)."""
+    T, N, K_ = 32768, 512, 2048
+    g = torch.Generator().manual_seed(1)
+    dY = torch.randn(T, N, generator=g).bfloat16()
+    X = torch.randn(T, K_, generator=g).bfloat16()
+    ref = (dY.float().T.cuda() @ X.float().cuda()).cpu()
+    out = _gemm(L, _bf(dY), _bf(X), N, K_, T, 0, L.EPI_OUT_F32)
+    assert rel(out.cpu().view(N, K_), ref) < 1e-4
+    acc = torch.ones(N * K_, device="cuda")
+    _gemm(L, _bf(dY), _bf(X), N, K_, T, 0, L.EPI_OUT_F32 | L.EPI_ACCUM, out=acc)
+    assert rel(acc.cpu().view(N, K_), ref + 1.0) < 1e-4
+
+
+def test_gemm_bf16_epilogues(L):
+    import ctypes as C
+    M, N, K_ = 512, 1536, 512
+    S, Dh = 256, 64
+    g = torch.Generator().manual_seed(3)
+    A = torch.randn(M, K_, generator=g).bfloat16()
+    B = torch.randn(N, K_, generator=g).bfloat16() * 0.05
+    bias = torch.randn(N, generator=g)
+    res = torch.randn(M, N, generator=g).bfloat16()
+    aux = torch.randn(M, N, generator=g).bfloat16()
+    base = A.float() @ B.float().T
+    bias_d, res_d, aux_d = bias.cuda(), _bf(res), _bf(aux)
+    e = L.Epilogue()
+    e.bias, e.residual, e.aux = bias_d.data_ptr(), res_d.data_ptr(), aux_d.data_ptr()
+    kk = L.A_KMAJOR | L.B_KMAJOR
+    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_BIAS | L.EPI_RELU, e)
+    assert rel(o.float().cpu().view(M, N), torch.relu(base + bias)) < BF16_TOL
+    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_BIAS | L.EPI_RESIDUAL, e)
+    assert rel(o.float().cpu().view(M, N), base + bias + res.float()) < BF16_TOL
+    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_RELU_MASK, e)
+    assert rel(o.float().cpu().view(M, N), torch.where(aux.float() > 0, base, torch.zeros(()))) < BF16_TOL
+    # RoPE on the first 2*512 columns (q | k) with positions m % S
+    c, s = O.rope_table(S, Dh)
+    cd, sd = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
+    e.rope_cos, e.rope_sin, e.rope_cols, e.rope_seq, e.head_dim = cd.data_ptr(), sd.data_ptr(), 1024, S, Dh
+    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_BIAS | L.EPI_ROPE, e)
+    want = (base + bias).numpy().copy()
+    qk = np.ascontiguousarray(want[:, :1024])
+    rot = O.rope_apply(qk, M, S, 16, Dh, 1024, c, s).reshape(M, 1024)
+    want[:, :1024] = rot
+    assert rel(o.float().cpu().view(M, N), want) < BF16_TOL
+
+
+# ------------------------------------------------------------------ fp32 API GEMMs (tf32 / SIMT)
+@pytest.mark.parametrize("M,N,K_", [(64, 128, 96), (33, 17, 5), (256, 512, 512)])
+def test_matmul_f32_api(K, M, N, K_):
+    A = O.normal(M * K_, 11)
+    B = O.normal(K_ * N, 12)
+    # A.B^T with 16-byte rows runs on tcgen05 kind::tf32; the other forms on the SIMT fp32 kernel
+    tf32 = (K_ % 4 == 0)
+    assert rel(K.matmul(A, B, M, N, K_), O.matmul(A, B, M, N, K_)) < 1e-5
+    Bt = O.transpose(B, K_, N)
+    assert rel(K.matmul_a_bt(A, Bt, M, N, K_), O.matmul_a_bt(A, Bt, M, N, K_)) < (TF32_TOL if tf32 else 1e-5)
+    At = O.transpose(A, M, K_)
+    assert rel(K.matmul_at_b(At, B, K_, N, M), O.matmul_at_b(At, B, K_, N, M)) < 1e-5
+
+
+def test_linear_api(K):
+    M, Kin, N = 512, 256, 384
+    x, W, b, dY = O.normal(M * Kin, 1), O.normal(N * Kin, 2), O.normal(N, 3), O.normal(M * N, 4)
+    assert rel(K.linear_forward(x, W, b, M, Kin, N), O.linear_forward(x, W, b, M, Kin, N)) < TF32_TOL
+    dB0 = O.normal(N, 5)
+    got = K.linear_backward(dY, x, W, dB0, M, Kin, N)
+    ref = O.linear_backward(dY, x, W, dB0, M, Kin, N)
+    for g_, r_ in zip(got[:2], ref[:2]):
+        assert rel(g_, r_) < 1e-5   # backward products run on the SIMT fp32 kernel
+    assert np.array_equal(got[2], ref[2])  # bias grad: same serial row order as linear.cu:59-69
+
+
+# ------------------------------------------------------------------ attention
+@pytest.mark.parametrize("B,S,H", [(2, 128, 2), (1, 200, 3), (2, 512, 4)])
+def test_attention_bf16_vs_oracle(L, B, S, H):
+    import ctypes as C
+    Dh, E = 64, H * 64
+    T = B * S
+    qkv = O.normal(T * 3 * E, 21) * 0.5
+    qkv_b = torch.from_numpy(qkv).bfloat16()
+    qkv_f = qkv_b.float().numpy()
+    q3 = qkv_f.reshape(T, 3 * E)
+    o_ref, lse_ref = O.attention_forward(q3[:, :E].copy(), q3[:, E:2 * E].copy(), q3[:, 2 * E:].copy(), E, B, S, H, Dh)
+    qkv_d = qkv_b.cuda()
+    o = torch.empty(T * E, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * H * S, device="cuda")
+    L.call("zl_attention_forward_bf16", qkv_d.data_ptr(), o.data_ptr(), lse.data_ptr(), B, S, H, Dh, None)
+    torch.cuda.synchronize()
+    assert rel(o.float().cpu(), o_ref) < BF16_TOL
+    assert rel(lse.cpu(), lse_ref) < 1e-3
+    dO = O.normal(T * E, 22)
+    dO_b = torch.from_numpy(dO).bfloat16()
+    q = qkv_f.reshape(T, 3 * E)
+    o_b = o.float().cpu().numpy()
+    dq, dk, dv = O.attention_backward(q[:, :E].copy(), q[:, E:2 * E].copy(), q[:, 2 * E:].copy(), E, o_b,
+                                      dO_b.float().numpy(), lse.cpu().numpy(), B, S, H, Dh)
+    dqkv = torch.empty(T * 3 * E, device="cuda", dtype=torch.bfloat16)
+    nws = L.load().zl_attention_workspace_floats(B, S, H, Dh)
+    ws = torch.empty(nws, device="cuda")
+    L.call("zl_attention_backward_bf16", qkv_d.data_ptr(), o.data_ptr(), dO_b.cuda().data_ptr(), lse.data_ptr(),
+           dqkv.data_ptr(), ws.data_ptr(), B, S, H, Dh, None, None, None)
+    torch.cuda.synchronize()
+    g = dqkv.float().cpu().numpy().reshape(T, 3 * E)
+    assert rel(g[:, :E], dq.reshape(T, E)) < BF16_TOL
+    assert rel(g[:, E:2 * E], dk.reshape(T, E)) < BF16_TOL
+    assert rel(g[:, 2 * E:], dv.reshape(T, E)) < BF16_TOL
+
+
+@pytest.mark.parametrize("ref_sem", [True, False])
+def test_mha_f32_api_vs_oracle(K, ref_sem):
+    B, S, H, Dh = 2, 48, 2, 16
+    n = B * S * H * Dh
+    Q, Kk, V, dO = (O.normal(n, s) for s in (31, 32, 33, 34))
+    o_g, P_g = K.mha_forward(Q, Kk, V, B, S, H, Dh)
+    o_r, P_r = O.mha_forward(Q, Kk, V, B, S, H, Dh)
+    assert rel(o_g, o_r) < 1e-5 and rel(P_g, P_r) < 1e-5
+    g = K.mha_backward(dO, Q, Kk, V, P_r, B, S, H, Dh, apply_scale=not ref_sem)
+    r = O.mha_backward(dO, Q, Kk, V, P_r, B, S, H, Dh, apply_scale=not ref_sem)
+    for a, b in zip(g, r):
+        assert rel(a, b) < 1e-5
+
+
+# ------------------------------------------------------------------ norms, CE, embedding, optimizers
+@pytest.mark.parametrize("kind", [0, 1])
+def test_norm_bf16_vs_oracle(L, kind):
+    M, N = 1000, 512
+    x = O.normal(M * N, 41)
+    g = 1 + 0.1 * O.normal(N, 42)
+    b = 0.1 * O.normal(N, 43)
+    xb = torch.from_numpy(x).bfloat16()
+    xf = xb.float().numpy()
+    if kind == 0:
+        y_r, mean_r, rstd_r = O.layernorm_forward(xf, g, b, M, N)
+    else:
+        y_r, rstd_r = O.rmsnorm_forward(xf, g, M, N)
+        mean_r = np.zeros(M, np.float32)
+    xd = xb.cuda()
+    y = torch.empty(M * N, device="cuda", dtype=torch.bfloat16)
+    mean, rstd = torch.empty(M, device="cuda"), torch.empty(M, device="cuda")
+    gd, bd = torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda()
+    L.call("zl_norm_forward_bf16", kind, xd.data_ptr(), gd.data_ptr(), bd.data_ptr(), y.data_ptr(), mean.data_ptr(),
+           rstd.data_ptr(), M, N, 1e-5, None)
+    torch.cuda.synchronize()
+    assert rel(y.float().cpu(), y_r) < BF16_TOL
+    assert rel(rstd.cpu(), rstd_r) < 1e-4
+    dy = O.normal(M * N, 44)
+    dyb = torch.from_numpy(dy).bfloat16()
+    if kind == 0:
+        dx_r, dg_r, db_r = O.layernorm_backward(xf, dyb.float().numpy(), g, mean_r, rstd_r, M, N)
+    else:
+        dx_r, dg_r = O.rmsnorm_backward(xf, dyb.float().numpy(), g, rstd_r, M, N)
+        db_r = None
+    dx = torch.empty(M * N, device="cuda", dtype=torch.bfloat16)
+    dg, db = torch.zeros(N, device="cuda"), torch.zeros(N, device="cuda")
+    ws = torch.empty(2 * N * L.load().zl_norm_bwd_blocks(M), device="cuda")
+    L.call("zl_norm_backward_bf16", kind, xd.data_ptr(), dyb.cuda().data_ptr(), gd.data_ptr(), mean.data_ptr(),
+           rstd.data_ptr(), dx.data_ptr(), dg.data_ptr(), db.data_ptr(), ws.data_ptr(), M, N, None)
+    torch.cuda.synchronize()
+    assert rel(dx.float().cpu(), dx_r) < BF16_TOL
+    assert rel(dg.cpu(), dg_r) < 1e-4
+    if db_r is not None:
+        assert rel(db.cpu(), db_r) < 1e-4
+
+
+def test_layernorm_f32_api(K):
+    M, N = 300, 512
+    x, g, b, dy = O.normal(M * N, 1), 1 + 0.1 * O.normal(N, 2), O.normal(N, 3), O.normal(M * N, 4)
+    yg, mg, rg = K.layernorm_forward(x, g, b, M, N)
+    yr, mr, rr = O.layernorm_forward(x, g, b, M, N)
+    assert rel(yg, yr) < 1e-5 and rel(rg, rr) < 1e-5
+    got = K.layernorm_backward(x, dy, g, mr, rr, M, N, np.ones(N, np.float32), np.ones(N, np.float32))
+    ref = O.layernorm_backward(x, dy, g, mr, rr, M, N, np.ones(N, np.float32), np.ones(N, np.float32))
+    for a, b_ in zip(got, ref):
+        assert rel(a, b_) < 1e-4
+
+
+def test_softmax_and_ce_f32_api(K):
+    rows, C_ = 64, 1000
+    x = O.normal(rows * C_, 5) * 4
+    t = O.uniform_ids(rows, 6, C_)
+    t[0] = -1
+    p_g, p_r = K.softmax(x, rows, C_), O.softmax(x, rows, C_)
+    assert rel(p_g, p_r) < 1e-5
+    assert abs(K.ce_forward(p_r, t, rows, C_) - O.ce_forward(p_r, t, rows, C_)) < 1e-5
+    assert rel(K.ce_backward(p_r, t, rows, C_), O.ce_backward(p_r, t, rows, C_)) < 1e-6
+
+
+def test_ce_fused_bf16_vs_oracle(L):
+    rows, V = 512, 6400
+    x = O.normal(rows * V, 7) * 2
+    t = O.uniform_ids(rows, 8, V)
+    t[5] = -1
+    xb = torch.from_numpy(x).bfloat16()
+    loss_r, d_r = O.ce_fused(xb.float().numpy(), t, rows, V)
+    xd = xb.cuda()
+    lr_ = torch.empty(rows, device="cuda")
+    lo = torch.empty(1, device="cuda")
+    L.call("zl_cross_entropy_fused_bf16", xd.data_ptr(), torch.from_numpy(t).cuda().data_ptr(), rows, V, 1e-8,
+           1.0 / rows, lr_.data_ptr(), lo.data_ptr(), None)
+    torch.cuda.synchronize()
+    assert abs(lo.item() - loss_r) / abs(loss_r) < 1e-4
+    assert rel(xd.float().cpu(), d_r) < BF16_TOL
+
+
+def test_embedding_model_form_bitexact(L):
+    """bf16(E[id] + P[s]) for valid ids, zero rows for invalid ids (bit-exact)."""
+    T, S, D, V = 512, 128, 512, 6400
+    ids = O.uniform_ids(T, 9, V)
+    ids[3], ids[100] = -1, V
+    E = O.normal(V * D, 10) * 0.02
+    Pt = O.sinusoid_table(S, D)
+    out = torch.empty(T * D, device="cuda", dtype=torch.bfloat16)
+    idd = torch.from_numpy(ids).cuda()
+    L.call("zl_embedding_forward_bf16", idd.data_ptr(), torch.from_numpy(E).cuda().data_ptr(),
+           torch.from_numpy(Pt).cuda().data_ptr(), out.data_ptr(), T, S, D, V, None)
+    torch.cuda.synchronize()
+    want = np.zeros((T, D), np.float32)
+    for t in range(T):
+        if 0 <= ids[t] < V:
+            want[t] = E.reshape(V, D)[ids[t]] + Pt.reshape(S, D)[t % S]
+    want_b = torch.from_numpy(want).bfloat16()
+    assert torch.equal(out.cpu().view(T, D), want_b)
+    # backward: scatter-add of the same rows (fp32 atomics; sum order free)
+    dx = O.normal(T * D, 11)
+    dxb = torch.from_numpy(dx).bfloat16()
+    dt = torch.zeros(V * D, device="cuda")
+    L.call("zl_embedding_backward_bf16", idd.data_ptr(), dxb.cuda().data_ptr(), dt.data_ptr(), T, D, V, None)
+    torch.cuda.synchronize()
+    ref = O.embedding_backward(ids, dxb.float().numpy(), np.zeros(V * D, np.float32), 1, T, D, V)
+    assert rel(dt.cpu(), ref) < 1e-6
+
+
+def test_embedding_f32_api_bitexact(K):
+    B, S, D, V, MS = 4, 64, 32, 100, 48   # positions >= max_seq_len are skipped
+    ids = O.uniform_ids(B * S, 12, V)
+    ids[5] = -7
+    E, Pt = O.normal(V * D, 13), O.normal(MS * D, 14)
+    init = O.normal(B * S * D, 15)
+    got = K.embedding_forward(ids, E, Pt, B, S, D, V, MS, out_init=init)
+    ref = O.embedding_forward(ids, E, Pt, B, S, D, V, MS, out_init=init)
+    assert np.array_equal(got, ref)
+
+
+def test_adamw_flat_and_api_vs_oracle(L, K):
+    n = 1000003
+    p, g, m, v = O.normal(n, 1) * 0.02, O.normal(n, 2) * 1e-3, O.normal(n, 3) * 1e-4, np.abs(O.normal(n, 4)) * 1e-6
+    args = (3e-4, 0.1, 0.9, 0.95, 1e-8, np.float32(1 - 0.9 ** 3), np.float32(1 - 0.95 ** 3))
+    pr, mr, vr = O.adamw(p, g, m, v, *args)
+    pg, mg, vg = K.adamw(p, g, m, v, *args)
+    assert rel(pg, pr) < 1e-6 and rel(mg, mr) < 1e-6 and rel(vg, vr) < 1e-6
+    # flat form with gradient scale 0.5 and bf16 shadow
+    pd, gd, md, vd = (torch.from_numpy(a.copy()).cuda() for a in (p, g, m, v))
+    pb = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    L.call("zl_adamw_flat", pd.data_ptr(), gd.data_ptr(), md.data_ptr(), vd.data_ptr(), pb.data_ptr(), n, args[0],
+           args[1], args[2], args[3], args[4], float(args[5]), float(args[6]), 0.5, None)
+    torch.cuda.synchronize()
+    pr2, _, _ = O.adamw(p, g * np.float32(0.5), m, v, *args)
+    assert rel(pd.cpu(), pr2) < 1e-6
+    assert torch.equal(pb.cpu(), pd.cpu().bfloat16())
+
+
+def test_sgd_adam_api_vs_oracle(K):
+    n = 4099
+    p, g, vel = O.normal(n, 1), O.normal(n, 2), O.normal(n, 3)
+    a = K.sgd(p, g, vel, 0.1, 0.9, 0.01)
+    b = O.sgd(p, g, vel, 0.1, 0.9, 0.01)
+    assert rel(a[0], b[0]) < 1e-6 and rel(a[1], b[1]) < 1e-6
+    m, v = O.normal(n, 4) * 0.1, np.abs(O.normal(n, 5)) * 0.1
+    x = K.adam(p, g, m, v, 1e-3, 0.9, 0.999, 1e-8, 0.1, 0.001)
+    y = O.adam(p, g, m, v, 1e-3, 0.9, 0.999, 1e-8, 0.1, 0.001)
+    for a_, b_ in zip(x, y):
+        assert rel(a_, b_) < 1e-6
+
+
+def test_colsum_bf16(L):
+    for M, N in [(32768, 512), (1000, 1536), (4096, 2048)]:
+        x = torch.randn(M, N).bfloat16()
+        ref = x.float().sum(0)
+        db = torch.ones(N, device="cuda")
+        ws = torch.empty(L.load().zl_colsum_workspace_floats(M, N), device="cuda")
+        L.call("zl_colsum_bf16", x.cuda().data_ptr(), db.data_ptr(), ws.data_ptr(), M, N, None)
+        torch.cuda.synchronize()
+        assert rel(db.cpu(), ref + 1) < 1e-5

@@ -1,0 +1,683 @@
+// attention.cu -- causal multi-head attention for the training step.
+//
+// bf16 path (the model): fused flash-style forward and backward over a
+// packed qkv buffer [B*S, 3E] (q | k | v, head h at column h*Dh of each
+// part), replacing the reference's per-(batch, head) SIMT kernels
+// (src/kernel/cuda/mha.cu:18-122, :164-299) that materialise the full
+// [B,H,S,S] probability tensor in HBM.  Scores never leave registers; the
+// forward keeps the per-row log-sum-exp for the backward, which recomputes
+// P.  The backward applies the 1/sqrt(Dh) factor to dQ and dK (the
+// reference omits it, mha.cu:284-295).  Optional inverse RoPE on dq/dk at
+// write-out (interleaved pairs, matching the forward rotation applied in
+// the qkv GEMM epilogue).
+//
+// Tiles: 64 query rows x 64 keys per step, 4 warps x 16 rows, bf16
+// mma.sync.m16n8k16 with fp32 accumulation; K/V (forward) and Q/dO
+// (backward) tiles are double-buffered with cp.async; shared tiles are
+// XOR-swizzled in 16-byte chunks so ldmatrix is conflict-free.
+//
+// fp32 path (reference API, mha.cuh:18-48): same semantics as the
+// reference including the stored probabilities and the optional
+// reference-exact backward without the scale factor.
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace zl {
+
+namespace fa {
+
+constexpr int TILE = 64;      // rows per tile (queries or keys)
+constexpr int DH = 64;        // head dim supported by the bf16 kernels
+constexpr int THREADS = 128;  // 4 warps
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr int BWD_SMEM = TILE * 128 * 7 + 4 * TILE * 4;
+
+__device__ __forceinline__ uint32_t swz(int row, int col) {  // byte offset in a [64][64] bf16 tile
+  return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Loads a 64-row x 64-col bf16 tile whose row r starts at base + r*ld (elements) into swizzled smem.
+// Rows >= valid_rows are zero-filled.
+__device__ __forceinline__ void load_tile(uint32_t smem, const __nv_bfloat16* base, int64_t ld, int valid_rows) {
+  for (int i = threadIdx.x; i < TILE * 8; i += THREADS) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    const uint32_t dst = smem + swz(r, c);
+    if (r < valid_rows) {
+      cp_async16(dst, base + (int64_t)r * ld + c);
+    } else {
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dst), "r"(0));
+    }
+  }
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// A fragment (16 x 16) at rows [r0, r0+16), cols [c0, c0+16) of a row-major swizzled tile.
+__device__ __forceinline__ void load_a(uint32_t tile, int r0, int c0, uint32_t (&a)[4]) {
+  const int l = threadIdx.x & 31;
+  ldsm_x4(tile + swz(r0 + (l & 15), c0 + (l >> 4) * 8), a[0], a[1], a[2], a[3]);
+}
+// A fragment from a tile stored transposed: element (m, k) lives at [k][m].
+__device__ __forceinline__ void load_a_t(uint32_t tile, int m0, int k0, uint32_t (&a)[4]) {
+  const int l = threadIdx.x & 31, i = l >> 3;
+  const int k = k0 + (l & 7) + ((i >> 1) << 3), m = m0 + ((i & 1) << 3);
+  ldsm_x4_t(tile + swz(k, m), a[0], a[1], a[2], a[3]);
+}
+// B fragments for two n-tiles [n0, n0+16) x k [k0, k0+16) from a tile stored [n][k].
+__device__ __forceinline__ void load_b_nk(uint32_t tile, int n0, int k0, uint32_t (&b)[4]) {
+  const int l = threadIdx.x & 31;
+  ldsm_x4(tile + swz(n0 + (l & 7) + ((l >> 4) << 3), k0 + ((l >> 3) & 1) * 8), b[0], b[1], b[2], b[3]);
+}
+// B fragments for two n-tiles from a tile stored [k][n] (transposed load).
+__device__ __forceinline__ void load_b_kn(uint32_t tile, int k0, int n0, uint32_t (&b)[4]) {
+  const int l = threadIdx.x & 31;
+  ldsm_x4_t(tile + swz(k0 + (l & 7) + (((l >> 3) & 1) << 3), n0 + ((l >> 4) << 3)), b[0], b[1], b[2], b[3]);
+}
+
+// ----------------------------------------------------------------- forward
+__global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                         __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
+                                                         int B, int S, int H, float scale_log2) {
+  __shared__ __align__(128) uint8_t sm[TILE * 128 * 5];  // Q, K[2], V[2]
+  const uint32_t sQ = smem_u32(sm), sK0 = sQ + TILE * 128, sV0 = sK0 + 2 * TILE * 128;
+  const int E = H * DH;
+  const int64_t ld = 3 * (int64_t)E;
+  const int nq = (S + TILE - 1) / TILE;
+  const int qb = nq - 1 - (int)(blockIdx.x % nq);  // heavy (late) blocks first
+  const int bh = blockIdx.x / nq, b = bh / H, h = bh % H;
+  const int q0 = qb * TILE;
+  const __nv_bfloat16* base = qkv + (int64_t)b * S * ld;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  load_tile(sQ, base + (int64_t)q0 * ld + h * DH, ld, S - q0);
+  load_tile(sK0, base + E + h * DH, ld, S);
+  load_tile(sV0, base + 2 * E + h * DH, ld, S);
+  cp_async_commit();
+
+  float o[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  uint32_t qa[4][4];
+
+  const int nkv = qb + 1;
+  for (int j = 0; j < nkv; ++j) {
+    const int cur = j & 1;
+    if (j + 1 < nkv) {
+      const int k1 = (j + 1) * TILE;
+      load_tile(sK0 + (cur ^ 1) * TILE * 128, base + (int64_t)k1 * ld + E + h * DH, ld, S - k1);
+      load_tile(sV0 + (cur ^ 1) * TILE * 128, base + (int64_t)k1 * ld + 2 * E + h * DH, ld, S - k1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (j == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) load_a(sQ, warp * 16, kk * 16, qa[kk]);
+    }
+    const uint32_t sK = sK0 + cur * TILE * 128, sV = sV0 + cur * TILE * 128;
+    // S = Q K^T  (16 x 64 per warp)
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int n2 = 0; n2 < 4; ++n2) {
+        uint32_t bf[4];
+        load_b_nk(sK, n2 * 16, kk * 16, bf);
+        mma16816(s[2 * n2], qa[kk], bf[0], bf[1]);
+        mma16816(s[2 * n2 + 1], qa[kk], bf[2], bf[3]);
+      }
+    // scale (base 2), causal mask on the diagonal tile and for keys beyond S
+    const int k0 = j * TILE;
+    const int r_lo = q0 + warp * 16 + (lane >> 2), r_hi = r_lo + 8;
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = k0 + n * 8 + 2 * (lane & 3) + (e & 1);
+        const int row = (e < 2) ? r_lo : r_hi;
+        float v = s[n][e] * scale_log2;
+        if (key > row || key >= S) v = -INFINITY;
+        s[n][e] = v;
+      }
+    // online softmax
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) mx = fmaxf(mx, fmaxf(s[n][2 * hr], s[n][2 * hr + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mnew = fmaxf(mrow[hr], mx);
+      const float corr = (mnew == -INFINITY) ? 1.f : exp2f(mrow[hr] - mnew);
+      float sum = 0.f;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const float p0 = (mnew == -INFINITY) ? 0.f : exp2f(s[n][2 * hr] - mnew);
+        const float p1 = (mnew == -INFINITY) ? 0.f : exp2f(s[n][2 * hr + 1] - mnew);
+        s[n][2 * hr] = p0;
+        s[n][2 * hr + 1] = p1;
+        sum += p0 + p1;
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      lrow[hr] = lrow[hr] * corr + sum;
+      mrow[hr] = mnew;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) { o[n][2 * hr] *= corr; o[n][2 * hr + 1] *= corr; }
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int n2 = 0; n2 < 4; ++n2) {
+        uint32_t bf[4];
+        load_b_kn(sV, kk * 16, n2 * 16, bf);
+        mma16816(o[2 * n2], pa, bf[0], bf[1]);
+        mma16816(o[2 * n2 + 1], pa, bf[2], bf[3]);
+      }
+    }
+    __syncthreads();
+  }
+  // write O / l and lse
+  const int r_lo = q0 + warp * 16 + (lane >> 2);
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int row = r_lo + hr * 8;
+    if (row >= S) continue;
+    const float inv = lrow[hr] > 0.f ? 1.f / lrow[hr] : 0.f;
+    __nv_bfloat16* orow = out + ((int64_t)b * S + row) * E + h * DH;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int c = n * 8 + 2 * (lane & 3);
+      *reinterpret_cast<uint32_t*>(orow + c) = pack_bf16(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
+    }
+    if ((lane & 3) == 0)
+      lse[((int64_t)b * H + h) * S + row] = (mrow[hr] + log2f(lrow[hr])) * 0.6931471805599453f;
+  }
+}
+
+// ----------------------------------------------------------------- backward
+// D[b,h,i] = sum_d dO[i,d] * O[i,d]; also zeroes the fp32 dq accumulator.
+__global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
+                                  float* __restrict__ Dsum, float* __restrict__ dq_acc, int B, int S, int H) {
+  const int E = H * DH;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);  // one warp per (token, head)
+  if (row >= (int64_t)B * S * H) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = row / H;
+  const int h = (int)(row % H);
+  const float2 a = unpack_bf16(*reinterpret_cast<const uint32_t*>(o + t * E + h * DH + 2 * lane));
+  const float2 g = unpack_bf16(*reinterpret_cast<const uint32_t*>(d_o + t * E + h * DH + 2 * lane));
+  float s = a.x * g.x + a.y * g.y;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  const int64_t b = t / S, i = t % S;
+  if (lane == 0) Dsum[(b * H + h) * S + i] = s;
+  *reinterpret_cast<float2*>(dq_acc + t * E + h * DH + 2 * lane) = make_float2(0.f, 0.f);
+}
+
+__device__ __forceinline__ void rope_inv_pair(float& x0, float& x1, const float* ct, const float* st, int pos,
+                                              int pair) {
+  const float c = __ldg(ct + (int64_t)pos * (DH / 2) + pair), s = __ldg(st + (int64_t)pos * (DH / 2) + pair);
+  const float a = x0, b = x1;
+  x0 = a * c + b * s;
+  x1 = -a * s + b * c;
+}
+
+__global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                         const __nv_bfloat16* __restrict__ d_o,
+                                                         const float* __restrict__ lse,
+                                                         const float* __restrict__ Dsum,
+                                                         float* __restrict__ dq_acc,
+                                                         __nv_bfloat16* __restrict__ d_qkv, const float* rope_cos,
+                                                         const float* rope_sin, int B, int S, int H, float scale,
+                                                         float scale_log2) {
+  // K, V (this key block), Q[2], dO[2], dS^T, lse2[2][64], D[2][64]  (dynamic: > 48 KB)
+  extern __shared__ __align__(128) uint8_t sm[];
+  const uint32_t sK = smem_u32(sm), sV = sK + TILE * 128, sQ0 = sV + TILE * 128, sD0 = sQ0 + 2 * TILE * 128,
+                 sS = sD0 + 2 * TILE * 128;
+  float* sL = reinterpret_cast<float*>(sm + TILE * 128 * 7);  // [2][64] lse*log2e
+  float* sDs = sL + 2 * TILE;                                   // [2][64] D
+  const int E = H * DH;
+  const int64_t ld = 3 * (int64_t)E;
+  const int nk = (S + TILE - 1) / TILE;
+  const int kb = (int)(blockIdx.x % nk);  // light (late key) blocks have fewer q blocks
+  const int bh = blockIdx.x / nk, b = bh / H, h = bh % H;
+  const int k0 = kb * TILE;
+  const __nv_bfloat16* base = qkv + (int64_t)b * S * ld;
+  const __nv_bfloat16* dob = d_o + (int64_t)b * S * E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  auto load_q_block = [&](int qb, int buf) {
+    const int q0 = qb * TILE;
+    load_tile(sQ0 + buf * TILE * 128, base + (int64_t)q0 * ld + h * DH, ld, S - q0);
+    load_tile(sD0 + buf * TILE * 128, dob + (int64_t)q0 * E + h * DH, E, S - q0);
+    for (int i = threadIdx.x; i < TILE; i += THREADS) {
+      const int q = q0 + i;
+      sL[buf * TILE + i] = q < S ? lse[((int64_t)b * H + h) * S + q] * LOG2E : 0.f;
+      sDs[buf * TILE + i] = q < S ? Dsum[((int64_t)b * H + h) * S + q] : 0.f;
+    }
+  };
+
+  load_tile(sK, base + (int64_t)k0 * ld + E + h * DH, ld, S - k0);
+  load_tile(sV, base + (int64_t)k0 * ld + 2 * E + h * DH, ld, S - k0);
+  load_q_block(kb, 0);
+  cp_async_commit();
+
+  float dk[8][4], dv[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dk[n][e] = dv[n][e] = 0.f;
+  uint32_t ka[4][4], va[4][4];
+
+  const int nq = nk;
+  for (int qb = kb; qb < nq; ++qb) {
+    const int cur = (qb - kb) & 1;
+    if (qb + 1 < nq) {
+      load_q_block(qb + 1, cur ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (qb == kb) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        load_a(sK, warp * 16, kk * 16, ka[kk]);
+        load_a(sV, warp * 16, kk * 16, va[kk]);
+      }
+    }
+    const uint32_t sQ = sQ0 + cur * TILE * 128, sDO = sD0 + cur * TILE * 128;
+    const float* Lq = sL + cur * TILE;
+    const float* Dq = sDs + cur * TILE;
+    const int q0 = qb * TILE;
+    // S^T = K Q^T and dP^T = V dO^T  (16 keys x 64 queries per warp)
+    float st[8][4], dpt[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) st[n][e] = dpt[n][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int n2 = 0; n2 < 4; ++n2) {
+        uint32_t bq[4], bd[4];
+        load_b_nk(sQ, n2 * 16, kk * 16, bq);
+        load_b_nk(sDO, n2 * 16, kk * 16, bd);
+        mma16816(st[2 * n2], ka[kk], bq[0], bq[1]);
+        mma16816(st[2 * n2 + 1], ka[kk], bq[2], bq[3]);
+        mma16816(dpt[2 * n2], va[kk], bd[0], bd[1]);
+        mma16816(dpt[2 * n2 + 1], va[kk], bd[2], bd[3]);
+      }
+    // P^T and dS^T
+    const int key_lo = k0 + warp * 16 + (lane >> 2);
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int ql = n * 8 + 2 * (lane & 3) + (e & 1);
+        const int key = key_lo + ((e >> 1) << 3);
+        const int q = q0 + ql;
+        float p = exp2f(st[n][e] * scale_log2 - Lq[ql]);
+        if (key > q || q >= S || key >= S) p = 0.f;
+        st[n][e] = p;
+        dpt[n][e] = p * (dpt[n][e] - Dq[ql]);
+      }
+    // dV += P^T dO ; dK += dS^T Q   (k = queries)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4], sa[4];
+      pa[0] = pack_bf16(st[2 * kk][0], st[2 * kk][1]);
+      pa[1] = pack_bf16(st[2 * kk][2], st[2 * kk][3]);
+      pa[2] = pack_bf16(st[2 * kk + 1][0], st[2 * kk + 1][1]);
+      pa[3] = pack_bf16(st[2 * kk + 1][2], st[2 * kk + 1][3]);
+      sa[0] = pack_bf16(dpt[2 * kk][0], dpt[2 * kk][1]);
+      sa[1] = pack_bf16(dpt[2 * kk][2], dpt[2 * kk][3]);
+      sa[2] = pack_bf16(dpt[2 * kk + 1][0], dpt[2 * kk + 1][1]);
+      sa[3] = pack_bf16(dpt[2 * kk + 1][2], dpt[2 * kk + 1][3]);
+#pragma unroll
+      for (int n2 = 0; n2 < 4; ++n2) {
+        uint32_t bd[4], bq[4];
+        load_b_kn(sDO, kk * 16, n2 * 16, bd);
+        load_b_kn(sQ, kk * 16, n2 * 16, bq);
+        mma16816(dv[2 * n2], pa, bd[0], bd[1]);
+        mma16816(dv[2 * n2 + 1], pa, bd[2], bd[3]);
+        mma16816(dk[2 * n2], sa, bq[0], bq[1]);
+        mma16816(dk[2 * n2 + 1], sa, bq[2], bq[3]);
+      }
+    }
+    // dS^T -> shared [key][query] (bf16)
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int ql = n * 8 + 2 * (lane & 3);
+      const int kl = warp * 16 + (lane >> 2);
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sS + swz(kl, ql)), "r"(pack_bf16(dpt[n][0], dpt[n][1])));
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sS + swz(kl + 8, ql)), "r"(pack_bf16(dpt[n][2], dpt[n][3])));
+    }
+    __syncthreads();
+    // dQ(64 q x 64 d) += dS (q x key) K (key x d): warp w owns queries [16w, 16w+16)
+    float dq[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a[4];
+      load_a_t(sS, warp * 16, kk * 16, a);
+#pragma unroll
+      for (int n2 = 0; n2 < 4; ++n2) {
+        uint32_t bk[4];
+        load_b_kn(sK, kk * 16, n2 * 16, bk);
+        mma16816(dq[2 * n2], a, bk[0], bk[1]);
+        mma16816(dq[2 * n2 + 1], a, bk[2], bk[3]);
+      }
+    }
+    const int qr = q0 + warp * 16 + (lane >> 2);
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int q = qr + hr * 8;
+      if (q >= S) continue;
+      float* dst = dq_acc + ((int64_t)b * S + q) * E + h * DH;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int c = n * 8 + 2 * (lane & 3);
+        atomicAdd(reinterpret_cast<float2*>(dst + c), make_float2(dq[n][2 * hr], dq[n][2 * hr + 1]));
+      }
+    }
+    __syncthreads();
+  }
+  // write dK (scaled, optional inverse RoPE) and dV
+  const int kr = k0 + warp * 16 + (lane >> 2);
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int key = kr + hr * 8;
+    if (key >= S) continue;
+    __nv_bfloat16* dkrow = d_qkv + ((int64_t)b * S + key) * ld + E + h * DH;
+    __nv_bfloat16* dvrow = d_qkv + ((int64_t)b * S + key) * ld + 2 * E + h * DH;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int c = n * 8 + 2 * (lane & 3);
+      float x0 = dk[n][2 * hr] * scale, x1 = dk[n][2 * hr + 1] * scale;
+      if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, key, c >> 1);
+      *reinterpret_cast<uint32_t*>(dkrow + c) = pack_bf16(x0, x1);
+      *reinterpret_cast<uint32_t*>(dvrow + c) = pack_bf16(dv[n][2 * hr], dv[n][2 * hr + 1]);
+    }
+  }
+}
+
+// dq (fp32 accumulator) -> scaled bf16 into the q part of d_qkv (optional inverse RoPE)
+__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ d_qkv,
+                                   const float* rope_cos, const float* rope_sin, int64_t T, int S, int H,
+                                   float scale) {
+  const int E = H * DH;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per pair
+  if (idx >= T * E / 2) return;
+  const int64_t t = idx / (E / 2);
+  const int c = (int)(idx % (E / 2)) * 2;
+  const float2 v = *reinterpret_cast<const float2*>(dq_acc + t * E + c);
+  float x0 = v.x * scale, x1 = v.y * scale;
+  if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, (int)(t % S), (c % DH) >> 1);
+  *reinterpret_cast<uint32_t*>(d_qkv + t * 3 * E + c) = pack_bf16(x0, x1);
+}
+
+}  // namespace fa
+
+// ============================================================== fp32 reference API
+// One warp per query row (b, h, i).  Pass 1: row max.  Pass 2: exp and sum
+// (unnormalised probabilities go to `scores` when given).  Pass 3: O = P V.
+// Finally `scores` is normalised in place, as mha.cu:102-106 leaves it.
+__global__ void mha_fwd_f32_kernel(const float* __restrict__ Q, const float* __restrict__ K,
+                                   const float* __restrict__ V, float* __restrict__ out, float* __restrict__ scores,
+                                   const uint8_t* __restrict__ mask, int B, int S, int H, int Dh, int causal,
+                                   float scale) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * H * S) return;  // warp-uniform
+  const int lane = threadIdx.x & 31;
+  const int i = (int)(row % S);
+  const int h = (int)((row / S) % H);
+  const int b = (int)(row / ((int64_t)S * H));
+  const int E = H * Dh;
+  const float* q = Q + ((int64_t)b * S + i) * E + h * Dh;
+  float* sc = scores ? scores + (((int64_t)b * H + h) * S + i) * S : nullptr;
+  auto keep = [&](int j) { return !(causal && j > i) && !(mask && !mask[(int64_t)i * S + j]); };
+  auto dot = [&](int j) {  // warp-collective
+    const float* k = K + ((int64_t)b * S + j) * E + h * Dh;
+    float d = 0.f;
+    for (int x = lane; x < Dh; x += 32) d = fmaf(q[x], k[x], d);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+    return d * scale;
+  };
+  float mx = -FLT_MAX;
+  for (int j = 0; j < S; ++j)
+    if (keep(j)) mx = fmaxf(mx, dot(j));
+  float sum = 0.f;
+  for (int j = 0; j < S; ++j) {
+    float e = 0.f;
+    if (keep(j)) { e = expf(dot(j) - mx); sum += e; }
+    if (sc && lane == 0) sc[j] = e;
+  }
+  if (sum == 0.f) sum = 1e-20f;  // mha.cu:103
+  const float inv = 1.f / sum;
+  __syncwarp();
+  for (int x0 = 0; x0 < Dh; x0 += 32) {
+    const int x = x0 + lane;
+    float o = 0.f;
+    for (int j = 0; j < S; ++j) {
+      if (!keep(j)) continue;
+      const float e = sc ? sc[j] : expf(dot(j) - mx);
+      if (x < Dh) o = fmaf(e * inv, V[((int64_t)b * S + j) * E + h * Dh + x], o);
+    }
+    if (x < Dh) out[((int64_t)b * S + i) * E + h * Dh + x] = o;
+  }
+  __syncwarp();
+  if (sc)
+    for (int j = lane; j < S; j += 32) sc[j] = sc[j] * inv;
+}
+
+// Backward from stored probabilities P (mha.cu:164-299).
+// dV[j] = sum_i P[i,j] dO[i]: one warp per key row.
+__global__ void mha_bwd_dv_f32_kernel(const float* __restrict__ dO, const float* __restrict__ P,
+                                      const uint8_t* __restrict__ mask, float* __restrict__ dV, int B, int S, int H,
+                                      int Dh, int causal) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * H * S) return;
+  const int lane = threadIdx.x & 31;
+  const int j = (int)(row % S), h = (int)((row / S) % H), b = (int)(row / ((int64_t)S * H));
+  const int E = H * Dh;
+  const float* Pb = P + ((int64_t)b * H + h) * S * S;
+  for (int x = lane; x < Dh; x += 32) {
+    float acc = 0.f;
+    for (int i = 0; i < S; ++i) {
+      if (causal && j > i) continue;
+      if (mask && !mask[(int64_t)i * S + j]) continue;
+      const float p = Pb[(int64_t)i * S + j];
+      if (p == 0.f) continue;
+      acc = fmaf(p, dO[((int64_t)b * S + i) * E + h * Dh + x], acc);
+    }
+    dV[((int64_t)b * S + j) * E + h * Dh + x] = acc;
+  }
+}
+// dS row i, dQ[i] accumulated in registers, dK[j] via atomics (dK pre-zeroed): one warp per query row.
+__global__ void mha_bwd_dqk_f32_kernel(const float* __restrict__ dO, const float* __restrict__ Q,
+                                       const float* __restrict__ K, const float* __restrict__ V,
+                                       const float* __restrict__ P, const uint8_t* __restrict__ mask,
+                                       float* __restrict__ dQ, float* __restrict__ dK, int B, int S, int H, int Dh,
+                                       int causal, float ds_scale) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * H * S) return;
+  const int lane = threadIdx.x & 31;
+  const int i = (int)(row % S), h = (int)((row / S) % H), b = (int)(row / ((int64_t)S * H));
+  const int E = H * Dh;
+  const float* Pb = P + ((int64_t)b * H + h) * S * S + (int64_t)i * S;
+  const float* go = dO + ((int64_t)b * S + i) * E + h * Dh;
+  auto g_of = [&](int j) {  // warp-collective dO_i . V_j
+    const float* v = V + ((int64_t)b * S + j) * E + h * Dh;
+    float d = 0.f;
+    for (int x = lane; x < Dh; x += 32) d = fmaf(go[x], v[x], d);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+    return d;
+  };
+  auto keep = [&](int j) { return !(causal && j > i) && !(mask && !mask[(int64_t)i * S + j]); };
+  float spg = 0.f;
+  for (int j = 0; j < S; ++j) {
+    if (!keep(j)) continue;
+    const float p = Pb[j];
+    if (p == 0.f) continue;
+    spg += p * g_of(j);
+  }
+  float dq[4] = {0.f, 0.f, 0.f, 0.f};  // Dh <= 128
+  const float* qi = Q + ((int64_t)b * S + i) * E + h * Dh;
+  for (int j = 0; j < S; ++j) {
+    if (!keep(j)) continue;
+    const float p = Pb[j];
+    if (p == 0.f) continue;
+    const float ds = p * (g_of(j) - spg) * ds_scale;
+    const float* kj = K + ((int64_t)b * S + j) * E + h * Dh;
+    float* dkj = dK + ((int64_t)b * S + j) * E + h * Dh;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int x = lane + 32 * t;
+      if (x < Dh) {
+        dq[t] = fmaf(ds, kj[x], dq[t]);
+        atomicAdd(dkj + x, ds * qi[x]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int x = lane + 32 * t;
+    if (x < Dh) dQ[((int64_t)b * S + i) * E + h * Dh + x] = dq[t];
+  }
+}
+
+}  // namespace zl
+
+// ============================================================== C ABI
+using namespace zl;
+
+extern "C" zl_status zl_attention_forward_bf16(const zl_bf16* qkv, zl_bf16* o, float* lse, int batch, int seq_len,
+                                               int num_heads, int head_dim, zl_stream stream) {
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return set_error(ZL_EINVAL, "attention: invalid sizes");
+  if (head_dim != fa::DH) return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64)", head_dim);
+  if (!qkv || !o || !lse) return set_error(ZL_EINVAL, "attention: null pointer");
+  const int nq = (seq_len + fa::TILE - 1) / fa::TILE;
+  const float scale_log2 = (1.0f / sqrtf((float)head_dim)) * fa::LOG2E;
+  fa::fa_fwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nq), fa::THREADS, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(o), lse, batch, seq_len,
+      num_heads, scale_log2);
+  return check_launch("fa_fwd_kernel");
+}
+
+extern "C" int64_t zl_attention_workspace_floats(int batch, int seq_len, int num_heads, int head_dim) {
+  return (int64_t)batch * seq_len * num_heads * head_dim + (int64_t)batch * num_heads * seq_len;
+}
+
+extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o,
+                                                const float* lse, zl_bf16* d_qkv, float* workspace, int batch,
+                                                int seq_len, int num_heads, int head_dim, const float* rope_cos,
+                                                const float* rope_sin, zl_stream stream) {
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return set_error(ZL_EINVAL, "attention: invalid sizes");
+  if (head_dim != fa::DH) return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64)", head_dim);
+  if (!qkv || !o || !d_o || !lse || !d_qkv || !workspace) return set_error(ZL_EINVAL, "attention bwd: null pointer");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(ZL_EINVAL, "attention bwd: rope tables");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t T = (int64_t)batch * seq_len;
+  const int E = num_heads * head_dim;
+  float* dq_acc = workspace;
+  float* Dsum = workspace + T * E;
+  const int64_t rows = T * num_heads;
+  fa::fa_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(d_o), Dsum, dq_acc, batch,
+      seq_len, num_heads);
+  zl_status s = check_launch("fa_bwd_pre_kernel");
+  if (s != ZL_OK) return s;
+  const int nk = (seq_len + fa::TILE - 1) / fa::TILE;
+  const float scale = 1.0f / sqrtf((float)head_dim);
+  cudaFuncSetAttribute(fa::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::BWD_SMEM);
+  fa::fa_bwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nk), fa::THREADS, fa::BWD_SMEM, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum, dq_acc,
+      reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch, seq_len, num_heads, scale,
+      scale * fa::LOG2E);
+  s = check_launch("fa_bwd_kernel");
+  if (s != ZL_OK) return s;
+  const int64_t pairs = T * E / 2;
+  fa::fa_bwd_post_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
+      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, scale);
+  return check_launch("fa_bwd_post_kernel");
+}
+
+extern "C" zl_status zl_mha_forward_f32(const float* Q, const float* K, const float* V, float* attn_output,
+                                        float* attention_scores, const uint8_t* mask, int64_t batch, int64_t seq_len,
+                                        int64_t num_heads, int64_t head_dim, int is_causal, zl_stream stream) {
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || head_dim <= 0)
+    return set_error(ZL_EINVAL, "mha_forward: invalid sizes");  // mha.cu:133-135
+  if (head_dim > 128) return set_error(ZL_EUNSUPPORTED, "mha_forward: head_dim > 128");
+  const int64_t rows = batch * num_heads * seq_len;
+  mha_fwd_f32_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      Q, K, V, attn_output, attention_scores, mask, (int)batch, (int)seq_len, (int)num_heads, (int)head_dim,
+      is_causal, 1.0f / sqrtf((float)head_dim));
+  return check_launch("mha_fwd_f32_kernel");
+}
+
+extern "C" zl_status zl_mha_backward_f32(const float* d_attn_output, const float* Q, const float* K, const float* V,
+                                         const float* attention_scores, const uint8_t* mask, float* d_Q, float* d_K,
+                                         float* d_V, int64_t batch, int64_t seq_len, int64_t num_heads,
+                                         int64_t head_dim, int is_causal, int reference_semantics,
+                                         zl_stream stream) {
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || head_dim <= 0)
+    return set_error(ZL_EINVAL, "cuda_mha_backward: invalid sizes");  // mha.cu:312-314
+  if (head_dim > 128) return set_error(ZL_EUNSUPPORTED, "mha_backward: head_dim > 128");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t rows = batch * num_heads * seq_len;
+  const size_t bytes = (size_t)batch * seq_len * num_heads * head_dim * sizeof(float);
+  if (cudaMemsetAsync(d_K, 0, bytes, st) != cudaSuccess) return check_launch("mha_backward memset");
+  mha_bwd_dv_f32_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(d_attn_output, attention_scores, mask, d_V,
+                                                                      (int)batch, (int)seq_len, (int)num_heads,
+                                                                      (int)head_dim, is_causal);
+  zl_status s = check_launch("mha_bwd_dv_f32_kernel");
+  if (s != ZL_OK) return s;
+  const float ds_scale = reference_semantics ? 1.0f : 1.0f / sqrtf((float)head_dim);
+  mha_bwd_dqk_f32_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(d_attn_output, Q, K, V, attention_scores, mask,
+                                                                       d_Q, d_K, (int)batch, (int)seq_len,
+                                                                       (int)num_heads, (int)head_dim, is_causal,
+                                                                       ds_scale);
+  return check_launch("mha_bwd_dqk_f32_kernel");
+}

@@ -1,0 +1,648 @@
+// gemm.cu -- tcgen05 / TMEM / TMA GEMM for sm_100a with fused epilogues.
+//
+// Replaces the reference's SIMT GEMMs (src/kernel/cuda/matmul.cu:51-218,
+// linear.cu:72-170) on the training path.  One persistent kernel computes
+//     D[M,N] = sum_k A(m,k) * B(n,k)
+// where A is stored K-major ([M,K]) or MN-major ([K,M]) and likewise B, so
+// the forward (X W^T), input-gradient (dY W) and weight-gradient (dY^T X)
+// products are all the same kernel with different operand majorness -- no
+// transposes through HBM.
+//
+// CTA = 6 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory
+// ring (128-byte swizzle), warp 1 owns TMEM and issues tcgen05.mma from one
+// thread into one of two 128 x BN fp32 accumulators, warps 2-5 drain the
+// other accumulator (tcgen05.ld) through the fused epilogue and store.
+// Every wait is bounded (common.cuh); a timeout records an error and the CTA
+// unwinds, freeing TMEM.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace zl {
+
+// ------------------------------------------------------------------ config
+constexpr int BM = 128;
+constexpr int kThreads = 192;
+
+template <typename T>
+struct Elem;
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int bytes = 2, BK = 64, UMMA_K = 16, fmt = 1;
+};
+template <>
+struct Elem<float> {
+  static constexpr int bytes = 4, BK = 32, UMMA_K = 8, fmt = 2;
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int n_tiles_n, tiles, k_blocks, splits, kb_per_split, units;
+  void* D;
+  int flags;
+  zl_epilogue epi;
+  float* ws;  // split-K partials [splits][M][N] (fp32) when splits > 1
+};
+
+template <int BN, int STAGES, int ELEM_BYTES>
+struct Smem {
+  static constexpr int A_BYTES = BM * 128;   // BM rows (or BK rows x BM) of 128 bytes
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + alignment slack
+};
+
+// ------------------------------------------------------------------ epilogue
+// Applies the fused epilogue to 32 consecutive columns [c0, c0+32) of row r and stores.
+__device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int r, int c0, float (&v)[32]) {
+  if (r >= a.M) return;
+  const int f = a.flags;
+  const int nvalid = min(32, a.N - c0);
+  if (nvalid <= 0) return;
+  if (f & ZL_EPI_BIAS) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nvalid) v[j] += __ldg(a.epi.bias + c0 + j);
+  }
+  if ((f & ZL_EPI_ROPE) && c0 < a.epi.rope_cols) {
+    const int half = a.epi.head_dim >> 1;
+    const int pos = r % a.epi.rope_seq;
+    const float* ct = a.epi.rope_cos + (size_t)pos * half;
+    const float* st = a.epi.rope_sin + (size_t)pos * half;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      const int i = ((c0 + j) % a.epi.head_dim) >> 1;
+      const float c = __ldg(ct + i), s = __ldg(st + i);
+      const float x0 = v[j], x1 = v[j + 1];
+      v[j] = x0 * c - x1 * s;
+      v[j + 1] = x0 * s + x1 * c;
+    }
+  }
+  if (f & ZL_EPI_RESIDUAL) {
+    const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(a.epi.residual) + (size_t)r * a.N + c0;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(res) & 15) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u = __ldg(reinterpret_cast<const uint4*>(res) + q);
+        float2 p0 = unpack_bf16(u.x), p1 = unpack_bf16(u.y), p2 = unpack_bf16(u.z), p3 = unpack_bf16(u.w);
+        v[q * 8 + 0] += p0.x; v[q * 8 + 1] += p0.y; v[q * 8 + 2] += p1.x; v[q * 8 + 3] += p1.y;
+        v[q * 8 + 4] += p2.x; v[q * 8 + 5] += p2.y; v[q * 8 + 6] += p3.x; v[q * 8 + 7] += p3.y;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) v[j] += __bfloat162float(res[j]);
+    }
+  }
+  if (f & ZL_EPI_RELU_MASK) {
+    const __nv_bfloat16* aux = reinterpret_cast<const __nv_bfloat16*>(a.epi.aux) + (size_t)r * a.N + c0;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(aux) & 15) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u = __ldg(reinterpret_cast<const uint4*>(aux) + q);
+        float2 p0 = unpack_bf16(u.x), p1 = unpack_bf16(u.y), p2 = unpack_bf16(u.z), p3 = unpack_bf16(u.w);
+        float m[8] = {p0.x, p0.y, p1.x, p1.y, p2.x, p2.y, p3.x, p3.y};
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[q * 8 + t] = m[t] > 0.f ? v[q * 8 + t] : 0.f;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) v[j] = __bfloat162float(aux[j]) > 0.f ? v[j] : 0.f;
+    }
+  }
+  if (f & ZL_EPI_RELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+  }
+  if (f & ZL_EPI_OUT_F32) {
+    float* out = reinterpret_cast<float*>(a.D) + (size_t)r * a.N + c0;
+    const bool acc = (f & ZL_EPI_ACCUM) != 0;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 w = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+        if (acc) {
+          float4 o = reinterpret_cast<float4*>(out)[q];
+          w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+        }
+        reinterpret_cast<float4*>(out)[q] = w;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) out[j] = acc ? out[j] + v[j] : v[j];
+    }
+  } else {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.D) + (size_t)r * a.N + c0;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u;
+        u.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+        u.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+        u.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+        u.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+        reinterpret_cast<uint4*>(out)[q] = u;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) out[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  using E = Elem<T>;
+  using L = Smem<BN, STAGES, E::bytes>;
+  constexpr int BK = E::BK;
+  constexpr int ATOM = 128 / E::bytes;        // elements per 128-byte row
+  constexpr uint32_t TMEM_COLS = 2 * BN;      // two accumulators
+  constexpr uint32_t IDESC = make_idesc(E::fmt, BM, BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 128); }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+        const int tile = u / args.splits, split = u % args.splits;
+        const int m0 = (tile / args.n_tiles_n) * BM, n0 = (tile % args.n_tiles_n) * BN;
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!bounded_wait(&empty[stage], phase ^ 1u, DEV_TIMEOUT_EMPTY)) { ok = false; break; }
+          uint8_t* sA = smem + stage * L::STAGE_BYTES;
+          uint8_t* sB = sA + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / ATOM; ++c) tma_load_2d(sA + c * BK * 128, &tmA, &full[stage], m0 + c * ATOM, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(sB, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / ATOM; ++c) tma_load_2d(sB + c * BK * 128, &tmB, &full[stage], n0 + c * ATOM, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+      const int split = u % args.splits;
+      const int kb0 = split * args.kb_per_split;
+      const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
+      if (!bounded_wait(&acc_empty[acc], acc_phase ^ 1u, DEV_TIMEOUT_ACC)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!bounded_wait(&full[stage], phase, DEV_TIMEOUT_FULL)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_base = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t b_base = a_base + L::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / E::UMMA_K; ++k) {
+            uint64_t ad, bd;
+            if (!A_MN) ad = smem_desc_sw128(a_base + k * E::UMMA_K * E::bytes, 16, 1024);
+            else       ad = smem_desc_sw128(a_base + k * E::UMMA_K * 128, BK * 128, 1024);
+            if (!B_MN) bd = smem_desc_sw128(b_base + k * E::UMMA_K * E::bytes, 16, 1024);
+            else       bd = smem_desc_sw128(b_base + k * E::UMMA_K * 128, BK * 128, 1024);
+            const uint32_t accumulate = (kb > kb0 || k > 0) ? 1u : 0u;
+            if (E::fmt == 1) umma_f16(d_tmem, ad, bd, IDESC, accumulate);
+            else             umma_tf32(d_tmem, ad, bd, IDESC, accumulate);
+          }
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&acc_full[acc]);
+      __syncwarp();
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
+      const int tile = u / args.splits, split = u % args.splits;
+      const int m0 = (tile / args.n_tiles_n) * BM, n0 = (tile % args.n_tiles_n) * BN;
+      if (!bounded_wait(&acc_full[acc], acc_phase, DEV_TIMEOUT_ACC)) break;
+      tc_fence_after();
+      const int r = m0 + row_in_tile;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t raw[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c), raw);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+        if (n0 + c >= args.N) continue;
+        if (args.splits > 1) {
+          if (r < args.M) {
+            float* out = args.ws + ((size_t)split * args.M + r) * args.N + n0 + c;
+            const int nvalid = min(32, args.N - n0 - c);
+            if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                reinterpret_cast<float4*>(out)[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+            } else {
+              for (int j = 0; j < nvalid; ++j) out[j] = v[j];
+            }
+          }
+        } else {
+          epilogue_store32(args, r, n0 + c, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// Sums split-K partials and applies the epilogue: one thread per 32 columns of a row.
+__global__ void splitk_reduce_kernel(const GemmArgs args) {
+  const int chunks = (args.N + 31) / 32;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)args.M * chunks) return;
+  const int r = (int)(idx / chunks), c0 = (int)(idx % chunks) * 32;
+  const int nvalid = min(32, args.N - c0);
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  for (int s = 0; s < args.splits; ++s) {
+    const float* p = args.ws + ((size_t)s * args.M + r) * args.N + c0;
+    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 w = __ldg(reinterpret_cast<const float4*>(p) + q);
+        v[q * 4] += w.x; v[q * 4 + 1] += w.y; v[q * 4 + 2] += w.z; v[q * 4 + 3] += w.w;
+      }
+    } else {
+      for (int j = 0; j < nvalid; ++j) v[j] += p[j];
+    }
+  }
+  epilogue_store32(args, r, c0, v);
+}
+
+// SIMT fallback for fp32 shapes whose rows are not 16-byte aligned (tiny
+// test shapes, odd K): 64x64 tile, 4x4 outputs per thread, k ascending.
+template <bool A_MN, bool B_MN>
+__global__ void gemm_simt_f32_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ D,
+                                     int M, int N, int K, int flags, zl_epilogue epi) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int kk = i / 64, mm = i % 64;
+      const int gm = m0 + mm, gk = k0 + kk;
+      float a = 0.f, b = 0.f;
+      if (gm < M && gk < K) a = A_MN ? A[(size_t)gk * M + gm] : A[(size_t)gm * K + gk];
+      const int gn = n0 + mm;
+      if (gn < N && gk < K) b = B_MN ? B[(size_t)gk * N + gn] : B[(size_t)gn * K + gk];
+      As[kk][mm] = a;
+      Bs[kk][mm] = b;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(As[kk][ty * 4 + i], Bs[kk][tx * 4 + j], acc[i][j]);
+    __syncthreads();
+  }
+  for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 4; ++j) {
+      const int r = m0 + ty * 4 + i, c = n0 + tx * 4 + j;
+      if (r < M && c < N) {
+        float v = acc[i][j];
+        if (flags & ZL_EPI_BIAS) v += epi.bias[c];
+        if (flags & ZL_EPI_RELU) v = fmaxf(v, 0.f);
+        float* out = D + (size_t)r * N + c;
+        *out = (flags & ZL_EPI_ACCUM) ? *out + v : v;
+      }
+    }
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int sm_count() {
+  static int count[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (count[dev] == 0) {
+    int c = 0;
+    cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+    count[dev] = c > 0 ? c : 148;
+  }
+  return count[dev];
+}
+
+// 2-D tiled map over a row-major [rows, inner] matrix with a box of [box_rows, box_inner].
+bool make_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
+              uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  const uint64_t esz = is_f32 ? 4 : 2;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * esz};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, is_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct Plan {
+  int bn, splits, n_tiles_n, tiles, k_blocks, kb_per_split, units;
+};
+
+Plan make_plan(int M, int N, int K, int BK, bool out_allows_split) {
+  Plan p;
+  p.bn = (N <= 128) ? 128 : 256;
+  p.n_tiles_n = (N + p.bn - 1) / p.bn;
+  p.tiles = ((M + BM - 1) / BM) * p.n_tiles_n;
+  p.k_blocks = (K + BK - 1) / BK;
+  const int sms = sm_count();
+  int best = 1;
+  if (out_allows_split && p.tiles < sms && p.k_blocks >= 8) {
+    double best_t = 1e30;
+    const int smax = std::min(16, p.k_blocks / 4);
+    for (int s = 1; s <= smax; ++s) {
+      const int units = p.tiles * s;
+      const int waves = (units + sms - 1) / sms;
+      const double t = (double)waves * ((p.k_blocks + s - 1) / s) + 0.5 * s;  // reduce cost grows with s
+      if (t < best_t) { best_t = t; best = s; }
+    }
+  }
+  p.kb_per_split = (p.k_blocks + best - 1) / best;
+  p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.units = p.tiles * p.splits;
+  return p;
+}
+
+template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
+cudaError_t launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, int grid, cudaStream_t st) {
+  using E = Elem<T>;
+  using L = Smem<BN, STAGES, E::bytes>;
+  auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, a);
+  return cudaGetLastError();
+}
+
+template <typename T, int BN, int STAGES>
+cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+                           int grid, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_tc<T, BN, STAGES, false, false>(ma, mb, a, grid, st);
+  if (!a_mn && b_mn) return launch_tc<T, BN, STAGES, false, true>(ma, mb, a, grid, st);
+  if (a_mn && !b_mn) return launch_tc<T, BN, STAGES, true, false>(ma, mb, a, grid, st);
+  return launch_tc<T, BN, STAGES, true, true>(ma, mb, a, grid, st);
+}
+
+}  // namespace
+
+int64_t gemm_workspace_floats(int M, int N, int K, int layout, int flags, bool f32_inputs) {
+  (void)layout;
+  const int BK = f32_inputs ? Elem<float>::BK : Elem<__nv_bfloat16>::BK;
+  Plan p = make_plan(M, N, K, BK, true);
+  (void)flags;
+  return p.splits > 1 ? (int64_t)p.splits * M * N : 0;
+}
+
+// Generic tcgen05 GEMM launcher (T = __nv_bfloat16 or float/tf32).
+template <typename T>
+zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layout, int flags,
+                  const zl_epilogue* epi, float* ws, cudaStream_t st) {
+  using E = Elem<T>;
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(ZL_EINVAL, "gemm: sizes must be positive (M=%d N=%d K=%d)", M, N, K);
+  if (!A || !B || !D) return set_error(ZL_EINVAL, "gemm: null operand");
+  const bool a_mn = !(layout & ZL_A_KMAJOR), b_mn = !(layout & ZL_B_KMAJOR);
+  const bool is_f32 = sizeof(T) == 4;
+  if ((flags & ZL_EPI_BIAS) && (!epi || !epi->bias)) return set_error(ZL_EINVAL, "gemm: bias flag without bias");
+  if ((flags & ZL_EPI_RESIDUAL) && (!epi || !epi->residual)) return set_error(ZL_EINVAL, "gemm: residual flag without residual");
+  if ((flags & ZL_EPI_RELU_MASK) && (!epi || !epi->aux)) return set_error(ZL_EINVAL, "gemm: relu-mask flag without aux");
+  if ((flags & ZL_EPI_ROPE) && (!epi || !epi->rope_cos || !epi->rope_sin || epi->head_dim <= 0 || epi->rope_seq <= 0 ||
+                                (epi->head_dim & 1)))
+    return set_error(ZL_EINVAL, "gemm: rope flag without tables");
+  // TMA needs 16-byte aligned base and row pitch.
+  const int align_elems = 16 / E::bytes;
+  const int a_inner = a_mn ? M : K, b_inner = b_mn ? N : K;
+  if ((a_inner % align_elems) || (b_inner % align_elems) || (reinterpret_cast<uintptr_t>(A) & 15) ||
+      (reinterpret_cast<uintptr_t>(B) & 15))
+    return ZL_EUNSUPPORTED;
+  GemmArgs a;
+  a.M = M; a.N = N; a.K = K;
+  a.D = D; a.flags = flags;
+  if (epi) a.epi = *epi; else memset(&a.epi, 0, sizeof(a.epi));
+  Plan p = make_plan(M, N, K, E::BK, true);
+  if (p.splits > 1 && !ws) {
+    // no workspace supplied: fall back to a single split
+    p.splits = 1; p.kb_per_split = p.k_blocks; p.units = p.tiles;
+  }
+  a.n_tiles_n = p.n_tiles_n; a.tiles = p.tiles; a.k_blocks = p.k_blocks; a.splits = p.splits;
+  a.kb_per_split = p.kb_per_split; a.units = p.units; a.ws = ws;
+  constexpr int ATOM = 128 / E::bytes;
+  CUtensorMap ma, mb;
+  bool ok = a_mn ? make_map(&ma, A, is_f32, M, K, ATOM, E::BK) : make_map(&ma, A, is_f32, K, M, E::BK, BM);
+  ok = ok && (b_mn ? make_map(&mb, B, is_f32, N, K, ATOM, E::BK) : make_map(&mb, B, is_f32, K, N, E::BK, p.bn));
+  if (!ok) return set_error(ZL_ECUDA, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
+  const int grid = std::min(p.units, sm_count());
+  cudaError_t e;
+  if (p.bn == 128) e = dispatch_major<T, 128, 6>(a_mn, b_mn, ma, mb, a, grid, st);
+  else e = dispatch_major<T, 256, 4>(a_mn, b_mn, ma, mb, a, grid, st);
+  if (e != cudaSuccess) return set_error(ZL_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
+  if (p.splits > 1) {
+    const int64_t work = (int64_t)M * ((N + 31) / 32);
+    splitk_reduce_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(a);
+    return check_launch("splitk_reduce");
+  }
+  return ZL_OK;
+}
+
+zl_status gemm_simt_f32(const float* A, const float* B, float* D, int M, int N, int K, int layout, int flags,
+                        const zl_epilogue* epi, cudaStream_t st) {
+  zl_epilogue e;
+  if (epi) e = *epi; else memset(&e, 0, sizeof(e));
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  const bool a_mn = !(layout & ZL_A_KMAJOR), b_mn = !(layout & ZL_B_KMAJOR);
+  if (!a_mn && !b_mn) gemm_simt_f32_kernel<false, false><<<grid, 256, 0, st>>>(A, B, D, M, N, K, flags, e);
+  else if (!a_mn && b_mn) gemm_simt_f32_kernel<false, true><<<grid, 256, 0, st>>>(A, B, D, M, N, K, flags, e);
+  else if (a_mn && !b_mn) gemm_simt_f32_kernel<true, false><<<grid, 256, 0, st>>>(A, B, D, M, N, K, flags, e);
+  else gemm_simt_f32_kernel<true, true><<<grid, 256, 0, st>>>(A, B, D, M, N, K, flags, e);
+  return check_launch("gemm_simt_f32");
+}
+
+// fp32 API GEMM: tcgen05 kind::tf32 when both operands are K-major and TMA-compatible,
+// else the SIMT kernel.  (MN-major 32-bit operands need the 32-byte-atom swizzle
+// variant of the shared-memory layout, which this kernel does not implement; with the
+// plain 128-byte swizzle the tensor core returns zeros for them.)
+zl_status gemm_f32(const float* A, const float* B, float* D, int M, int N, int K, int layout, int flags,
+                   const zl_epilogue* epi, float* ws, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(ZL_EINVAL, "gemm: sizes must be positive");
+  if ((layout & ZL_A_KMAJOR) && (layout & ZL_B_KMAJOR)) {
+    zl_status s = gemm_tc<float>(A, B, D, M, N, K, layout, flags | ZL_EPI_OUT_F32, epi, ws, st);
+    if (s != ZL_EUNSUPPORTED) return s;
+  }
+  return gemm_simt_f32(A, B, D, M, N, K, layout, flags, epi, st);
+}
+
+int gemm_dev_error_read_and_clear() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, zl_dev_error, sizeof(int));
+  if (v) {
+    int z = 0;
+    cudaMemcpyToSymbol(zl_dev_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+template zl_status gemm_tc<__nv_bfloat16>(const __nv_bfloat16*, const __nv_bfloat16*, void*, int, int, int, int, int,
+                                          const zl_epilogue*, float*, cudaStream_t);
+
+}  // namespace zl
+
+// ------------------------------------------------------------------ C ABI
+extern "C" zl_status zl_gemm_bf16(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout,
+                                  int epi_flags, const zl_epilogue* epi, float* workspace, zl_stream stream) {
+  zl_status s = zl::gemm_tc<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(A),
+                                           reinterpret_cast<const __nv_bfloat16*>(B), D, M, N, K, layout, epi_flags,
+                                           epi, workspace, static_cast<cudaStream_t>(stream));
+  if (s == ZL_EUNSUPPORTED)
+    return zl::set_error(ZL_EUNSUPPORTED, "zl_gemm_bf16: operands must be 16-byte aligned with rows a multiple of 8");
+  return s;
+}
+
+extern "C" int64_t zl_gemm_workspace_floats(int M, int N, int K, int layout, int epi_flags) {
+  return zl::gemm_workspace_floats(M, N, K, layout, epi_flags, false);
+}
+
+// ------------------------------------------------------------------ fp32 reference API
+namespace zl {
+// linear.cu:59-69 compute_bias_grad_kernel: one thread per column, rows ascending, += into dB.
+__global__ void bias_grad_f32_kernel(float* __restrict__ dB, const float* __restrict__ dY, int64_t M, int64_t N) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float g = 0.f;
+  for (int64_t i = 0; i < M; ++i) g += dY[i * N + n];
+  dB[n] += g;
+}
+}  // namespace zl
+
+// matmul.cuh:20/:68  C[M,N] = A[M,K] B[K,N]
+extern "C" zl_status zl_matmul_f32(const float* A, const float* B, float* C, int M, int N, int K, zl_stream s) {
+  return zl::gemm_f32(A, B, C, M, N, K, ZL_A_KMAJOR, 0, nullptr, nullptr, static_cast<cudaStream_t>(s));
+}
+// matmul.cuh:36/:99  C[K,N] = A[M,K]^T B[M,N]
+extern "C" zl_status zl_matmul_at_b_f32(const float* A, const float* B, float* C, int M, int N, int K, zl_stream s) {
+  return zl::gemm_f32(A, B, C, K, N, M, 0, 0, nullptr, nullptr, static_cast<cudaStream_t>(s));
+}
+// matmul.cuh:52/:83  C[M,N] = A[M,K] B[N,K]^T
+extern "C" zl_status zl_matmul_a_bt_f32(const float* A, const float* B, float* C, int M, int N, int K, zl_stream s) {
+  return zl::gemm_f32(A, B, C, M, N, K, ZL_A_KMAJOR | ZL_B_KMAJOR, 0, nullptr, nullptr, static_cast<cudaStream_t>(s));
+}
+// linear.cuh:21-30
+extern "C" zl_status zl_linear_forward_f32(const float* input, const float* weight, const float* bias, float* output,
+                                           int64_t M, int64_t K, int64_t N, int use_bias, zl_stream s) {
+  zl_epilogue e;
+  memset(&e, 0, sizeof(e));
+  e.bias = bias;
+  const int flags = (use_bias && bias) ? ZL_EPI_BIAS : 0;
+  return zl::gemm_f32(input, weight, output, (int)M, (int)N, (int)K, ZL_A_KMAJOR | ZL_B_KMAJOR, flags, &e, nullptr,
+                      static_cast<cudaStream_t>(s));
+}
+// linear.cuh:48-59
+extern "C" zl_status zl_linear_backward_f32(const float* d_output, const float* input, const float* weight,
+                                            float* d_input, float* d_weight, float* d_bias, int64_t M, int64_t K,
+                                            int64_t N, int use_bias, zl_stream s) {
+  cudaStream_t st = static_cast<cudaStream_t>(s);
+  zl_status r = ZL_OK;
+  if (d_input) r = zl::gemm_f32(d_output, weight, d_input, (int)M, (int)K, (int)N, ZL_A_KMAJOR, 0, nullptr, nullptr, st);
+  if (r != ZL_OK) return r;
+  if (d_weight) r = zl::gemm_f32(d_output, input, d_weight, (int)N, (int)K, (int)M, 0, 0, nullptr, nullptr, st);
+  if (r != ZL_OK) return r;
+  if (use_bias && d_bias) {
+    zl::bias_grad_f32_kernel<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(d_bias, d_output, M, N);
+    r = zl::check_launch("compute_bias_grad_kernel");
+  }
+  return r;
+}

@@ -1,0 +1,849 @@
+// kernels.cu -- memory-bound kernels: norms, embedding, cross-entropy,
+// optimizers, element-wise ops and reductions.
+//
+// Design: 128-bit vectorised global access (8 bf16 / 4 fp32 per load), one
+// warp per row for row-wise ops on d_model-wide rows, shared-memory staging
+// for vocabulary-wide rows, and two-stage (partials -> reduce) column and
+// scalar reductions so results are independent of scheduling.
+// The fp32 reference-API kernels keep the reference's per-element
+// semantics (file:line cited on each).
+#include <cfloat>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace zl {
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_err[512] = "";
+
+zl_status set_error(zl_status code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+zl_status check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(ZL_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ZL_OK;
+}
+
+constexpr int kMaxRowChunks = 8;  // rows up to 8 * 256 = 2048 elements held in registers by one warp
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y), c = unpack_bf16(u.z), d = unpack_bf16(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16(v[0], v[1]); u.y = pack_bf16(v[2], v[3]); u.z = pack_bf16(v[4], v[5]); u.w = pack_bf16(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void load8f(const float* p, float (&v)[8]) {
+  float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// ================================================================== norms (bf16 rows)
+// kind 0: LayerNorm (layernorm.cu:6-76 semantics: biased variance), kind 1: RMSNorm.
+template <int KIND, int kMaxChunks>
+__global__ void norm_fwd_bf16_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ g,
+                                     const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
+                                     float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t M, int N,
+                                     float eps) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int lane = threadIdx.x & 31;
+  const __nv_bfloat16* xr = x + row * N;
+  float v[kMaxChunks][8];
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < N) {
+      load8(xr + col, v[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += KIND == 0 ? v[c][j] : v[c][j] * v[c][j];
+    }
+  }
+  s = warp_sum(s);
+  float mu = 0.f, rs;
+  if (KIND == 0) {
+    mu = s / (float)N;
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c)
+      if ((c * 32 + lane) * 8 < N)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { const float d = v[c][j] - mu; q += d * d; }
+    q = warp_sum(q);
+    rs = rsqrtf(q / (float)N + eps);
+  } else {
+    rs = rsqrtf(s / (float)N + eps);
+  }
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mu;
+    if (rstd_out) rstd_out[row] = rs;
+  }
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < N) {
+      float gv[8], o[8];
+      load8f(g + col, gv);
+      if (KIND == 0) {
+        float bv[8];
+        load8f(b + col, bv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (v[c][j] - mu) * rs * gv[j] + bv[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[c][j] * rs * gv[j];
+      }
+      store8(y + row * N + col, o);
+    }
+  }
+}
+
+// Backward: one warp per row; per-block column partials of dgamma/dbeta to `part` [gridDim.x][2N].
+template <int KIND, int kMaxChunks>
+__global__ void norm_bwd_bf16_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy,
+                                     const float* __restrict__ g, const float* __restrict__ mean,
+                                     const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+                                     float* __restrict__ part, int64_t M, int N) {
+  extern __shared__ float sacc[];  // [2N]
+  for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) sacc[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  float pg[kMaxChunks][8], pb[kMaxChunks][8];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pg[c][j] = pb[c][j] = 0.f;
+  for (int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += (int64_t)gridDim.x * warps) {
+    const float mu = KIND == 0 ? mean[row] : 0.f, rs = rstd[row];
+    float xh[kMaxChunks][8], a[kMaxChunks][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < N) {
+        float xv[8], dv[8], gv[8];
+        load8(x + row * N + col, xv);
+        load8(dy + row * N + col, dv);
+        load8f(g + col, gv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[c][j] = (xv[j] - mu) * rs;
+          a[c][j] = dv[j] * gv[j];
+          s1 += a[c][j];
+          s2 += a[c][j] * xh[c][j];
+          pg[c][j] += dv[j] * xh[c][j];
+          pb[c][j] += dv[j];
+        }
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float invN = 1.f / (float)N;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < N) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          o[j] = KIND == 0 ? rs * (a[c][j] - s1 * invN - xh[c][j] * s2 * invN) : rs * (a[c][j] - xh[c][j] * s2 * invN);
+        store8(dx + row * N + col, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < N)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        atomicAdd(&sacc[col + j], pg[c][j]);
+        if (KIND == 0) atomicAdd(&sacc[N + col + j], pb[c][j]);
+      }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) part[(int64_t)blockIdx.x * 2 * N + i] = sacc[i];
+}
+
+// Sums per-block partials [nb][2N] into dgamma (and dbeta).
+__global__ void reduce_partials_kernel(const float* __restrict__ part, int nb, int N, int stride, float* __restrict__ out0,
+                                       float* __restrict__ out1) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  float s0 = 0.f, s1 = 0.f;
+  for (int k = 0; k < nb; ++k) {
+    s0 += part[(int64_t)k * stride + i];
+    if (out1) s1 += part[(int64_t)k * stride + N + i];
+  }
+  out0[i] += s0;
+  if (out1) out1[i] += s1;
+}
+
+int norm_bwd_blocks(int64_t M) {
+  int64_t nb = (M + 31) / 32;  // >= 32 rows per block (8 warps x 4 rows)
+  return (int)(nb < 592 ? nb : 592);
+}
+
+// ================================================================== embedding
+// Model form: x[t] = bf16(E[id] + P[t % S]); invalid id -> zero row.
+__global__ void embed_fwd_bf16_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table,
+                                      const float* __restrict__ pos, __nv_bfloat16* __restrict__ out, int64_t T, int S,
+                                      int D, int V) {
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  const int id = ids[t];
+  const bool valid = id >= 0 && id < V;
+  const int s = (int)(t % S);
+  for (int col = lane * 8; col < D; col += 256) {
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (valid) {
+      load8f(table + (int64_t)id * D + col, v);
+      if (pos) {
+        float p[8];
+        load8f(pos + (int64_t)s * D + col, p);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += p[j];
+      }
+    }
+    store8(out + t * D + col, v);
+  }
+}
+__global__ void embed_bwd_bf16_kernel(const int32_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dx,
+                                      float* __restrict__ dtable, int64_t T, int D, int V) {
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  const int id = ids[t];
+  if (id < 0 || id >= V) return;
+  for (int col = lane * 8; col < D; col += 256) {
+    float v[8];
+    load8(dx + t * D + col, v);
+    float4* dst = reinterpret_cast<float4*>(dtable + (int64_t)id * D + col);
+    atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
+    atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], v[7]));
+  }
+}
+// Reference form (embedding.cu:6-30): out[idx] = table[id*D+k] + pos[s*D+k]; skip s >= max_seq_len or invalid id.
+__global__ void embed_fwd_f32_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table,
+                                     const float* __restrict__ pos, float* __restrict__ out, int B, int S, int D, int V,
+                                     int max_seq_len) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)B * S * D) return;
+  const int k = (int)(idx % D);
+  const int64_t t = idx / D;
+  const int s = (int)(t % S);
+  if (s >= max_seq_len) return;
+  const int id = ids[t];
+  if (id < 0 || id >= V) return;
+  out[idx] = table[(int64_t)id * D + k] + pos[(int64_t)s * D + k];
+}
+// embedding.cu:33-53
+__global__ void embed_bwd_f32_kernel(const int32_t* __restrict__ ids, const float* __restrict__ dout,
+                                     float* __restrict__ dtable, int B, int S, int D, int V) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)B * S * D) return;
+  const int k = (int)(idx % D);
+  const int id = ids[idx / D];
+  if (id < 0 || id >= V) return;
+  atomicAdd(&dtable[(int64_t)id * D + k], dout[idx]);
+}
+
+// ================================================================== cross-entropy
+// One CTA per row; the row is staged in shared memory (fp32).
+__global__ void ce_fused_bf16_kernel(__nv_bfloat16* __restrict__ logits, const int32_t* __restrict__ targets, int V,
+                                     float cap, float grad_scale, float* __restrict__ loss_rows) {
+  extern __shared__ float srow[];
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  __nv_bfloat16* x = logits + r * V;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  float mx = -INFINITY;
+  const int nv = V / 8;
+  for (int i = tid; i < nv; i += nt) {
+    float v[8];
+    load8(x + i * 8, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { srow[i * 8 + j] = v[j]; mx = fmaxf(mx, v[j]); }
+  }
+  for (int i = nv * 8 + tid; i < V; i += nt) { const float v = __bfloat162float(x[i]); srow[i] = v; mx = fmaxf(mx, v); }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  if (tid < 32) {
+    float m = tid < (nt >> 5) ? red[tid] : -INFINITY;
+    m = warp_max(m);
+    if (tid == 0) red[0] = m;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  float s = 0.f;
+  for (int i = tid; i < V; i += nt) s += __expf(srow[i] - mx);
+  s = warp_sum(s);
+  if ((tid & 31) == 0) red[tid >> 5] = s;
+  __syncthreads();
+  if (tid < 32) {
+    float v = tid < (nt >> 5) ? red[tid] : 0.f;
+    v = warp_sum(v);
+    if (tid == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float lse = mx + logf(red[0]);
+  const int t = targets[r];
+  const bool valid = t >= 0 && t < V;
+  if (tid == 0) loss_rows[r] = valid ? fminf(lse - srow[t], cap) : 0.f;
+  for (int i = tid; i < nv; i += nt) {
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = i * 8 + j;
+      o[j] = (__expf(srow[c] - lse) - (c == t ? 1.f : 0.f)) * grad_scale;
+    }
+    store8(x + i * 8, o);
+  }
+  for (int i = nv * 8 + tid; i < V; i += nt)
+    x[i] = __float2bfloat16_rn((__expf(srow[i] - lse) - (i == t ? 1.f : 0.f)) * grad_scale);
+}
+
+// Deterministic mean of `n` values (single CTA, fixed order tree).
+__global__ void mean_kernel(const float* __restrict__ v, int64_t n, float* __restrict__ out, float denom) {
+  __shared__ double red[1024];
+  double s = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out = (float)(red[0] / denom);
+}
+
+// softmax.cu:12-65 (one CTA per row)
+__global__ void softmax_f32_kernel(const float* __restrict__ in, float* __restrict__ out, int N) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  const float* x = in + r * N;
+  float* y = out + r * N;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  float mx = -FLT_MAX;
+  for (int i = tid; i < N; i += nt) mx = fmaxf(mx, x[i]);
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  if (tid < 32) {
+    float m = tid < (nt >> 5) ? red[tid] : -FLT_MAX;
+    m = warp_max(m);
+    if (tid == 0) red[0] = m;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  float s = 0.f;
+  for (int i = tid; i < N; i += nt) { const float e = expf(x[i] - mx); y[i] = e; s += e; }
+  s = warp_sum(s);
+  if ((tid & 31) == 0) red[tid >> 5] = s;
+  __syncthreads();
+  if (tid < 32) {
+    float v = tid < (nt >> 5) ? red[tid] : 0.f;
+    v = warp_sum(v);
+    if (tid == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float sum = red[0];
+  for (int i = tid; i < N; i += nt) y[i] = y[i] / sum;
+}
+// cross_entropy.cu:5-31
+__global__ void ce_bwd_f32_kernel(float* __restrict__ d, const float* __restrict__ p, const int32_t* __restrict__ t,
+                                  int rows, int C) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)rows * C) return;
+  const int r = (int)(idx / C), c = (int)(idx % C);
+  const int tg = t[r];
+  float v = p[idx];
+  if (tg >= 0 && tg < C && c == tg) v = p[idx] - 1.0f;
+  d[idx] = v / (float)rows;
+}
+// cross_entropy.cpp:59-76 (host loop moved to the device): one CTA, fixed-order
+// reduction of -log(max(p[r, t_r], eps)) over all rows, divided by rows.
+__global__ void ce_loss_f32_kernel(const float* __restrict__ p, const int32_t* __restrict__ t, int rows, int C,
+                                   float eps, float* __restrict__ out) {
+  __shared__ double red[1024];
+  double s = 0.0;
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    const int tg = t[r];
+    if (tg >= 0 && tg < C) s += -logf(fmaxf(p[(int64_t)r * C + tg], eps));
+  }
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out = (float)(red[0] / rows);
+}
+
+// ================================================================== optimizers
+// adamw.cu:26-73 per element, gradient scaled by grad_scale, optional bf16 shadow.
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ pb, int64_t n, float lr, float wd,
+                             float b1, float b2, float eps, float bc1, float bc2, float gs) {
+  const int64_t i4 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i4 >= n) return;
+  const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;
+  if (i4 + 4 <= n && ((reinterpret_cast<uintptr_t>(p + i4) | reinterpret_cast<uintptr_t>(g + i4)) & 15) == 0) {
+    float4 P = *reinterpret_cast<float4*>(p + i4), G = *reinterpret_cast<const float4*>(g + i4);
+    float4 Mv = *reinterpret_cast<float4*>(m + i4), Vv = *reinterpret_cast<float4*>(v + i4);
+    float pa[4] = {P.x, P.y, P.z, P.w}, ga[4] = {G.x, G.y, G.z, G.w}, ma[4] = {Mv.x, Mv.y, Mv.z, Mv.w},
+          va[4] = {Vv.x, Vv.y, Vv.z, Vv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gv = ga[j] * gs;
+      ma[j] = b1 * ma[j] + omb1 * gv;
+      va[j] = b2 * va[j] + omb2 * gv * gv;
+      const float step = lr * (ma[j] / bc1) / (sqrtf(va[j] / bc2) + eps);
+      const float decay = wd != 0.f ? lr * wd * pa[j] : 0.f;
+      pa[j] = pa[j] - (decay + step);
+    }
+    *reinterpret_cast<float4*>(p + i4) = make_float4(pa[0], pa[1], pa[2], pa[3]);
+    *reinterpret_cast<float4*>(m + i4) = make_float4(ma[0], ma[1], ma[2], ma[3]);
+    *reinterpret_cast<float4*>(v + i4) = make_float4(va[0], va[1], va[2], va[3]);
+    if (pb) {
+      uint2 u;
+      u.x = pack_bf16(pa[0], pa[1]);
+      u.y = pack_bf16(pa[2], pa[3]);
+      *reinterpret_cast<uint2*>(pb + i4) = u;
+    }
+  } else {
+    for (int64_t i = i4; i < n && i < i4 + 4; ++i) {
+      const float gv = g[i] * gs;
+      const float mv = b1 * m[i] + omb1 * gv;
+      const float vv = b2 * v[i] + omb2 * gv * gv;
+      m[i] = mv;
+      v[i] = vv;
+      const float step = lr * (mv / bc1) / (sqrtf(vv / bc2) + eps);
+      const float decay = wd != 0.f ? lr * wd * p[i] : 0.f;
+      p[i] = p[i] - (decay + step);
+      if (pb) pb[i] = __float2bfloat16_rn(p[i]);
+    }
+  }
+}
+// adam.cu:13-57
+__global__ void adam_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                            float* __restrict__ v, int64_t n, float lr, float b1, float b2, float eps, float bc1,
+                            float bc2) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gv = g[i];
+  const float mv = b1 * m[i] + (1.0f - b1) * gv;
+  const float vv = b2 * v[i] + (1.0f - b2) * gv * gv;
+  m[i] = mv;
+  v[i] = vv;
+  p[i] -= lr * (mv / bc1) / (sqrtf(vv / bc2) + eps);
+}
+// sgd.cu:14-57
+__global__ void sgd_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ vel, int64_t n,
+                           float lr, float momentum, float wd) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float pv = p[i];
+  float gv = g[i];
+  if (wd != 0.f) gv += wd * pv;
+  if (momentum != 0.f && vel) {
+    const float vv = momentum * vel[i] + gv;
+    vel[i] = vv;
+    gv = vv;
+  }
+  p[i] = pv - lr * gv;
+}
+
+// ================================================================== element-wise (fp32 API)
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ o, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) o[i] = a[i] + b[i];
+}
+__global__ void add_inplace_kernel(float* __restrict__ a, const float* __restrict__ b, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) a[i] += b[i];
+}
+__global__ void relu_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = x[i] > 0 ? x[i] : 0.f;
+}
+__global__ void relu_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gy, float* __restrict__ gx,
+                                int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) gx[i] = x[i] > 0 ? gy[i] : 0.f;
+}
+// 32x32 tiles through shared memory: coalesced reads and writes.
+__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int cols) {
+  __shared__ float t[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int r = r0 + k, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) t[k][threadIdx.x] = in[(int64_t)r * cols + c];
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int c = c0 + k, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) out[(int64_t)c * rows + r] = t[threadIdx.x][k];
+  }
+}
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// LayerNorm / RMSNorm on fp32 rows (reference API): one warp per row, dgamma/dbeta
+// accumulated per block in shared memory and added with one atomic per column per block.
+template <int KIND>
+__global__ void norm_fwd_f32_kernel(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
+                                    float* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int64_t M,
+                                    int N, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int lane = threadIdx.x & 31;
+  const float* xr = x + row * N;
+  float s = 0.f;
+  for (int i = lane; i < N; i += 32) s += KIND == 0 ? xr[i] : xr[i] * xr[i];
+  s = warp_sum(s);
+  float mu = 0.f, rs;
+  if (KIND == 0) {
+    mu = s / (float)N;
+    float q = 0.f;
+    for (int i = lane; i < N; i += 32) { const float d = xr[i] - mu; q += d * d; }
+    q = warp_sum(q);
+    rs = rsqrtf(q / (float)N + eps);
+  } else {
+    rs = rsqrtf(s / (float)N + eps);
+  }
+  if (lane == 0) {
+    if (mean) mean[row] = mu;
+    if (rstd) rstd[row] = rs;
+  }
+  for (int i = lane; i < N; i += 32)
+    y[row * N + i] = KIND == 0 ? (xr[i] - mu) * rs * g[i] + b[i] : xr[i] * rs * g[i];
+}
+template <int KIND>
+__global__ void norm_bwd_f32_kernel(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
+                                    const float* __restrict__ mean, const float* __restrict__ rstd,
+                                    float* __restrict__ dx, float* __restrict__ dg, float* __restrict__ db, int64_t M,
+                                    int N) {
+  extern __shared__ float sacc[];  // [2N]
+  for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) sacc[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  for (int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += (int64_t)gridDim.x * warps) {
+    const float mu = KIND == 0 ? mean[row] : 0.f, rs = rstd[row];
+    const float* xr = x + row * N;
+    const float* dr = dy + row * N;
+    float s1 = 0.f, s2 = 0.f;
+    for (int i = lane; i < N; i += 32) {
+      const float xh = (xr[i] - mu) * rs, a = dr[i] * g[i];
+      s1 += a;
+      s2 += a * xh;
+      atomicAdd(&sacc[i], dr[i] * xh);
+      if (KIND == 0) atomicAdd(&sacc[N + i], dr[i]);
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float invN = 1.f / (float)N;
+    for (int i = lane; i < N; i += 32) {
+      const float xh = (xr[i] - mu) * rs, a = dr[i] * g[i];
+      dx[row * N + i] = KIND == 0 ? rs * (a - s1 * invN - xh * s2 * invN) : rs * (a - xh * s2 * invN);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    atomicAdd(&dg[i], sacc[i]);
+    if (KIND == 0) atomicAdd(&db[i], sacc[N + i]);
+  }
+}
+
+// Column sums of bf16 [M, N] (bias gradients): per-block partials [nb][N].
+__global__ void colsum_bf16_kernel(const __nv_bfloat16* __restrict__ dy, float* __restrict__ part, int64_t M, int N,
+                                   int64_t rows_per_block) {
+  const int groups = N / 8;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_block;
+  const int64_t r1 = r0 + rows_per_block < M ? r0 + rows_per_block : M;
+  const int rpar = blockDim.x / groups > 0 ? blockDim.x / groups : 1;
+  extern __shared__ float sc[];  // [rpar][N]
+  const int grp = threadIdx.x % groups, rl = threadIdx.x / groups;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (rl < rpar) {
+    for (int64_t r = r0 + rl; r < r1; r += rpar) {
+      float v[8];
+      load8(dy + r * N + grp * 8, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[rl * N + grp * 8 + j] = acc[j];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < N; c += blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < rpar; ++k) s += sc[k * N + c];
+    part[(int64_t)blockIdx.x * N + c] = s;
+  }
+}
+
+}  // namespace zl
+
+// ================================================================== C ABI
+using namespace zl;
+#define ST(s) static_cast<cudaStream_t>(s)
+static inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+extern "C" const char* zl_last_error(void) { return zl::g_err; }
+extern "C" const char* zl_version(void) { return "zerollm_b200 0.1 (sm_100a)"; }
+
+namespace zl {
+int gemm_dev_error_read_and_clear();
+}
+extern "C" zl_status zl_device_error(int* code_out) {
+  const int v = zl::gemm_dev_error_read_and_clear();
+  if (code_out) *code_out = v;
+  return v ? set_error(ZL_ETIMEOUT, "device wait timed out (code %d)", v) : ZL_OK;
+}
+
+extern "C" zl_status zl_norm_forward_bf16(int kind, const zl_bf16* x, const float* gamma, const float* beta, zl_bf16* y,
+                                          float* mean, float* rstd, int64_t M, int N, float eps, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;
+  if (N % 8 || N > 256 * kMaxRowChunks) return set_error(ZL_EUNSUPPORTED, "norm: N=%d must be a multiple of 8, <= 2048", N);
+  if (kind == 0 && !beta) return set_error(ZL_EINVAL, "layernorm: beta is null");
+  const auto X = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto Y = reinterpret_cast<__nv_bfloat16*>(y);
+  const int ch = N <= 256 ? 1 : N <= 512 ? 2 : N <= 1024 ? 4 : 8;
+#define NF(K, C) norm_fwd_bf16_kernel<K, C><<<nblk(M, 8), 256, 0, ST(s)>>>(X, gamma, K == 0 ? beta : nullptr, Y, K == 0 ? mean : nullptr, rstd, M, N, eps)
+  if (kind == 0) { if (ch == 1) NF(0, 1); else if (ch == 2) NF(0, 2); else if (ch == 4) NF(0, 4); else NF(0, 8); }
+  else { if (ch == 1) NF(1, 1); else if (ch == 2) NF(1, 2); else if (ch == 4) NF(1, 4); else NF(1, 8); }
+#undef NF
+  return check_launch("norm_fwd_bf16");
+}
+extern "C" int zl_norm_bwd_blocks(int64_t M) { return norm_bwd_blocks(M); }
+extern "C" zl_status zl_norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma,
+                                           const float* mean, const float* rstd, zl_bf16* dx, float* dgamma,
+                                           float* dbeta, float* workspace, int64_t M, int N, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;
+  if (N % 8 || N > 256 * kMaxRowChunks) return set_error(ZL_EUNSUPPORTED, "norm: N=%d must be a multiple of 8, <= 2048", N);
+  if (!workspace || !dgamma || (kind == 0 && (!dbeta || !mean))) return set_error(ZL_EINVAL, "norm bwd: null pointer");
+  const int nb = norm_bwd_blocks(M);
+  const auto X = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
+  auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
+  const size_t sm = 2 * N * sizeof(float);
+  const int ch = N <= 256 ? 1 : N <= 512 ? 2 : N <= 1024 ? 4 : 8;
+#define NB(K, C) norm_bwd_bf16_kernel<K, C><<<nb, 256, sm, ST(s)>>>(X, DY, gamma, K == 0 ? mean : nullptr, rstd, DX, workspace, M, N)
+  if (kind == 0) { if (ch == 1) NB(0, 1); else if (ch == 2) NB(0, 2); else if (ch == 4) NB(0, 4); else NB(0, 8); }
+  else { if (ch == 1) NB(1, 1); else if (ch == 2) NB(1, 2); else if (ch == 4) NB(1, 4); else NB(1, 8); }
+#undef NB
+  zl_status st = check_launch("norm_bwd_bf16");
+  if (st != ZL_OK) return st;
+  reduce_partials_kernel<<<nblk(N, 256), 256, 0, ST(s)>>>(workspace, nb, N, 2 * N, dgamma, kind == 0 ? dbeta : nullptr);
+  return check_launch("norm_bwd_reduce");
+}
+
+extern "C" zl_status zl_embedding_forward_bf16(const int32_t* ids, const float* table, const float* pos, zl_bf16* out,
+                                               int64_t T, int seq_len, int dim, int vocab, zl_stream s) {
+  if (T <= 0) return ZL_OK;
+  if (dim % 8) return set_error(ZL_EUNSUPPORTED, "embedding: dim %% 8 != 0");
+  embed_fwd_bf16_kernel<<<nblk(T, 8), 256, 0, ST(s)>>>(ids, table, pos, reinterpret_cast<__nv_bfloat16*>(out), T,
+                                                       seq_len, dim, vocab);
+  return check_launch("embed_fwd_bf16");
+}
+extern "C" zl_status zl_embedding_backward_bf16(const int32_t* ids, const zl_bf16* dx, float* dtable, int64_t T, int dim,
+                                                int vocab, zl_stream s) {
+  if (T <= 0) return ZL_OK;
+  if (dim % 8) return set_error(ZL_EUNSUPPORTED, "embedding: dim %% 8 != 0");
+  embed_bwd_bf16_kernel<<<nblk(T, 8), 256, 0, ST(s)>>>(ids, reinterpret_cast<const __nv_bfloat16*>(dx), dtable, T,
+                                                       dim, vocab);
+  return check_launch("embed_bwd_bf16");
+}
+
+extern "C" zl_status zl_cross_entropy_fused_bf16(zl_bf16* logits, const int32_t* targets, int rows, int vocab, float eps,
+                                                 float grad_scale, float* loss_rows, float* loss_out, zl_stream s) {
+  if (rows <= 0 || vocab <= 0) return set_error(ZL_EINVAL, "cross_entropy: sizes must be positive");
+  if (vocab % 8) return set_error(ZL_EUNSUPPORTED, "cross_entropy: vocab %% 8 != 0");
+  const size_t sm = (size_t)vocab * sizeof(float);
+  if (sm > 200 * 1024) return set_error(ZL_EUNSUPPORTED, "cross_entropy: vocab too large");
+  cudaFuncSetAttribute(ce_fused_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  ce_fused_bf16_kernel<<<rows, 256, sm, ST(s)>>>(reinterpret_cast<__nv_bfloat16*>(logits), targets, vocab, -logf(eps),
+                                                 grad_scale, loss_rows);
+  zl_status st = check_launch("ce_fused_bf16");
+  if (st != ZL_OK || !loss_out) return st;
+  mean_kernel<<<1, 1024, 0, ST(s)>>>(loss_rows, rows, loss_out, (float)rows);
+  return check_launch("mean_kernel");
+}
+
+extern "C" int64_t zl_colsum_workspace_floats(int64_t M, int N) {
+  const int64_t rpb = 256;
+  int64_t nb = (M + rpb - 1) / rpb;
+  return nb * N;
+}
+extern "C" zl_status zl_colsum_bf16(const zl_bf16* dy, float* db, float* workspace, int64_t M, int N, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;
+  if (N % 8 || N / 8 > 1024) return set_error(ZL_EUNSUPPORTED, "colsum: N=%d", N);
+  const int64_t rpb = 256;
+  const int nb = (int)((M + rpb - 1) / rpb);
+  const int groups = N / 8;
+  const int threads = groups >= 256 ? ((groups + 31) / 32) * 32 : (256 / groups) * groups;
+  const int rpar = threads / groups;
+  colsum_bf16_kernel<<<nb, threads, (size_t)rpar * N * sizeof(float), ST(s)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dy), workspace, M, N, rpb);
+  zl_status st = check_launch("colsum_bf16");
+  if (st != ZL_OK) return st;
+  reduce_partials_kernel<<<nblk(N, 256), 256, 0, ST(s)>>>(workspace, nb, N, N, db, nullptr);
+  return check_launch("colsum_reduce");
+}
+
+extern "C" zl_status zl_adamw_flat(float* params, const float* grads, float* m, float* v, zl_bf16* params_bf16, int64_t n,
+                                   float lr, float weight_decay, float beta1, float beta2, float eps, float bc1,
+                                   float bc2, float grad_scale, zl_stream s) {
+  if (n <= 0) return set_error(ZL_EINVAL, "adamw: size must be > 0");
+  adamw_kernel<<<nblk((n + 3) / 4, 256), 256, 0, ST(s)>>>(params, grads, m, v,
+                                                         reinterpret_cast<__nv_bfloat16*>(params_bf16), n, lr,
+                                                         weight_decay, beta1, beta2, eps, bc1, bc2, grad_scale);
+  return check_launch("adamw_kernel");
+}
+extern "C" zl_status zl_f32_to_bf16(const float* x, zl_bf16* y, int64_t n, zl_stream s) {
+  if (n <= 0) return ZL_OK;
+  f32_to_bf16_kernel<<<nblk(n, 256), 256, 0, ST(s)>>>(x, reinterpret_cast<__nv_bfloat16*>(y), n);
+  return check_launch("f32_to_bf16");
+}
+
+// ---------------------------------------------------------------- fp32 reference API
+extern "C" zl_status zl_layernorm_forward_f32(const float* input, const float* gamma, const float* beta, float* output,
+                                              float* mean, float* rstd, int64_t M, int64_t N, float eps, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;  // layernorm.cu:178
+  norm_fwd_f32_kernel<0><<<nblk(M, 8), 256, 0, ST(s)>>>(input, gamma, beta, output, mean, rstd, M, (int)N, eps);
+  return check_launch("layernorm_forward_kernel");
+}
+extern "C" zl_status zl_layernorm_backward_f32(const float* input, const float* d_output, const float* gamma,
+                                               const float* mean, const float* rstd, float* d_input, float* d_gamma,
+                                               float* d_beta, int64_t M, int64_t N, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;  // layernorm.cu:200
+  const int nb = norm_bwd_blocks(M);
+  norm_bwd_f32_kernel<0><<<nb, 256, 2 * N * sizeof(float), ST(s)>>>(input, d_output, gamma, mean, rstd, d_input,
+                                                                    d_gamma, d_beta, M, (int)N);
+  return check_launch("layernorm_backward_kernel");
+}
+extern "C" zl_status zl_rmsnorm_forward_f32(const float* input, const float* gamma, float* output, float* rstd, int64_t M,
+                                            int64_t N, float eps, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;
+  norm_fwd_f32_kernel<1><<<nblk(M, 8), 256, 0, ST(s)>>>(input, gamma, nullptr, output, nullptr, rstd, M, (int)N, eps);
+  return check_launch("rmsnorm_forward_kernel");
+}
+extern "C" zl_status zl_rmsnorm_backward_f32(const float* input, const float* d_output, const float* gamma,
+                                             const float* rstd, float* d_input, float* d_gamma, int64_t M, int64_t N,
+                                             zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;
+  const int nb = norm_bwd_blocks(M);
+  norm_bwd_f32_kernel<1><<<nb, 256, 2 * N * sizeof(float), ST(s)>>>(input, d_output, gamma, nullptr, rstd, d_input,
+                                                                    d_gamma, nullptr, M, (int)N);
+  return check_launch("rmsnorm_backward_kernel");
+}
+extern "C" zl_status zl_softmax_f32(const float* input, float* output, int M, int N, zl_stream s) {
+  if (M <= 0 || N <= 0) return set_error(ZL_EINVAL, "softmax: M and N must be > 0");  // softmax.cu:70-71
+  softmax_f32_kernel<<<M, 256, 0, ST(s)>>>(input, output, N);
+  return check_launch("softmax_kernel");
+}
+extern "C" zl_status zl_cross_entropy_backward_f32(float* d_logits, const float* softmax_output, const int32_t* targets,
+                                                   int batch, int num_classes, zl_stream s) {
+  if (batch <= 0 || num_classes <= 0) return ZL_OK;  // cross_entropy.cu:39
+  ce_bwd_f32_kernel<<<nblk((int64_t)batch * num_classes, 256), 256, 0, ST(s)>>>(d_logits, softmax_output, targets,
+                                                                                batch, num_classes);
+  return check_launch("cross_entropy_backward_kernel");
+}
+extern "C" zl_status zl_cross_entropy_forward_f32(const float* softmax_output, const int32_t* targets, int batch,
+                                                  int num_classes, float eps, float* loss_out, zl_stream s) {
+  if (batch <= 0 || num_classes <= 0)
+    return set_error(ZL_EINVAL, "Batch size and number of classes must be positive");  // cross_entropy.cpp:26-28
+  ce_loss_f32_kernel<<<1, 1024, 0, ST(s)>>>(softmax_output, targets, batch, num_classes, eps, loss_out);
+  return check_launch("cross_entropy_forward");
+}
+extern "C" zl_status zl_embedding_forward_f32(const int32_t* input, const float* table, const float* pos, float* output,
+                                              int batch, int seq_len, int embed_dim, int vocab_size, int max_seq_len,
+                                              zl_stream s) {
+  if (batch <= 0 || seq_len <= 0 || embed_dim <= 0) return ZL_OK;  // embedding.cu:66
+  embed_fwd_f32_kernel<<<nblk((int64_t)batch * seq_len * embed_dim, 256), 256, 0, ST(s)>>>(
+      input, table, pos, output, batch, seq_len, embed_dim, vocab_size, max_seq_len);
+  return check_launch("embedding_forward_kernel");
+}
+extern "C" zl_status zl_embedding_backward_f32(const int32_t* input, const float* d_output, float* d_table, int batch,
+                                               int seq_len, int embed_dim, int vocab_size, zl_stream s) {
+  if (batch <= 0 || seq_len <= 0 || embed_dim <= 0) return ZL_OK;  // embedding.cu:87
+  embed_bwd_f32_kernel<<<nblk((int64_t)batch * seq_len * embed_dim, 256), 256, 0, ST(s)>>>(
+      input, d_output, d_table, batch, seq_len, embed_dim, vocab_size);
+  return check_launch("embedding_backward_kernel");
+}
+extern "C" zl_status zl_add_f32(const float* a, const float* b, float* output, int size, zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "add: size must be > 0");  // add.cu:36-38
+  add_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(a, b, output, size);
+  return check_launch("add_kernel");
+}
+extern "C" zl_status zl_add_inplace_f32(float* a, const float* b, int size, zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "add_inplace: size must be > 0");
+  add_inplace_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(a, b, size);
+  return check_launch("add_inplace_kernel");
+}
+extern "C" zl_status zl_relu_forward_f32(const float* input, float* output, int size, zl_stream s) {
+  if (size <= 0) return ZL_OK;  // relu.cu:23
+  relu_fwd_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(input, output, size);
+  return check_launch("relu_forward");
+}
+extern "C" zl_status zl_relu_backward_f32(const float* input, const float* grad_output, float* grad_input, int size,
+                                          zl_stream s) {
+  if (size <= 0) return ZL_OK;  // relu.cu:35
+  relu_bwd_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(input, grad_output, grad_input, size);
+  return check_launch("relu_backward");
+}
+extern "C" zl_status zl_transpose_f32(const float* input, float* output, int rows, int cols, zl_stream s) {
+  if (rows <= 0 || cols <= 0) return ZL_OK;  // transpose.cu:19
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+  transpose_kernel<<<grid, block, 0, ST(s)>>>(input, output, rows, cols);
+  return check_launch("transpose");
+}
+extern "C" zl_status zl_adamw_step_f32(float* params, const float* grads, float* m, float* v, int64_t size, float lr,
+                                       float wd, float b1, float b2, float eps, float bc1, float bc2, zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "adamw_step: size must be > 0");  // adamw.cu:92-94
+  adamw_kernel<<<nblk((size + 3) / 4, 256), 256, 0, ST(s)>>>(params, grads, m, v, nullptr, size, lr, wd, b1, b2, eps,
+                                                            bc1, bc2, 1.0f);
+  return check_launch("adamw_kernel");
+}
+extern "C" zl_status zl_adam_step_f32(float* params, const float* grads, float* m, float* v, int64_t size, float lr,
+                                      float b1, float b2, float eps, float bc1, float bc2, zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "adam_step: size must be > 0");
+  adam_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(params, grads, m, v, size, lr, b1, b2, eps, bc1, bc2);
+  return check_launch("adam_kernel");
+}
+extern "C" zl_status zl_sgd_step_f32(float* params, const float* grads, float* velocity, int64_t size, float lr,
+                                     float momentum, float weight_decay, zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "sgd_step: size must be > 0");
+  sgd_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(params, grads, velocity, size, lr, momentum, weight_decay);
+  return check_launch("sgd_kernel");
+}

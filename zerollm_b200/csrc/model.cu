@@ -1,0 +1,699 @@
+// model.cu -- the ZeroLLM training step on one arena (host orchestration).
+//
+// Mirrors the reference dataflow of src/model/zerollm.cpp:101-323 and
+// src/layer/transformer_block.cpp:68-211 (post-norm decoder blocks:
+// x -> MHA -> add -> norm1 -> FFN(ReLU) -> add -> norm2), with the topology
+// switches norm={LayerNorm,RMSNorm}, pos={sinusoid,RoPE}, head={tied,untied}.
+// Differences from the reference, by design:
+//  * every activation lives in a preallocated arena (no cudaMalloc in the
+//    step, no device syncs), activations are bf16, master weights fp32;
+//  * the forward saves what backward needs under distinct names (the
+//    reference's in-place LayerNorm and shared decoder buffers alias saved
+//    inputs, transformer_block.cpp:97, transformer_decoder.cpp:79);
+//  * Q/K/V projections are one GEMM, bias/ReLU/residual/RoPE are GEMM
+//    epilogues, softmax + cross-entropy + its gradient is one kernel, and
+//    AdamW is one launch over the flat parameter arena.
+//  * data parallelism: gradients are produced in arena order (the arena is
+//    laid out in reverse forward order), so buckets become ready during
+//    backward and are all-reduced on a side stream (NCCL) while backward
+//    continues; the 1/world average is folded into AdamW.
+#include <algorithm>
+#include <array>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include <nccl.h>
+
+#include "common.cuh"
+
+
+// ============================================================== host RNG (same stream as the oracle)
+namespace {
+uint64_t splitmix64(uint64_t* s) {
+  uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+void fill_normal(float* out, int64_t n, uint64_t seed, float mean, float stdv) {
+  uint64_t s = seed;
+  const double two_pi = 6.283185307179586476925286766559;
+  for (int64_t i = 0; i < n; i += 2) {
+    const double u1 = ((double)(splitmix64(&s) >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+    const double u2 = (double)(splitmix64(&s) >> 11) * (1.0 / 9007199254740992.0);
+    const double r = sqrt(-2.0 * log(u1));
+    out[i] = (float)(mean + stdv * r * cos(two_pi * u2));
+    if (i + 1 < n) out[i + 1] = (float)(mean + stdv * r * sin(two_pi * u2));
+  }
+}
+
+enum Kind { K_MAT = 0, K_BIAS = 1, K_GAMMA = 2, K_BETA = 3, K_EMB = 4 };
+enum { L_N2G, L_N2B, L_W2, L_B2, L_W1, L_B1, L_N1G, L_N1B, L_WO, L_BO, L_WQKV, L_BQKV, L_COUNT };
+
+struct Layout {
+  std::vector<int64_t> off, size;
+  std::vector<int> kind;
+  int64_t head = -1, nog = -1, nob = -1, emb = -1;
+  std::vector<std::array<int64_t, L_COUNT>> lay;
+  int64_t total = 0;
+};
+
+// Canonical layout: reverse forward order (the order backward completes gradients).
+Layout build_layout(const zl_model_config& c) {
+  Layout L;
+  const int64_t d = c.embed_dim, F = c.ff_hidden_dim, V = c.vocab_size;
+  auto add = [&](int64_t sz, int kind) {
+    L.off.push_back(L.total);
+    L.size.push_back(sz);
+    L.kind.push_back(kind);
+    L.total += sz;
+    return L.off.back();
+  };
+  if (!c.tied) L.head = add(V * d, K_MAT);
+  L.nog = add(d, K_GAMMA);
+  if (c.norm == 0) L.nob = add(d, K_BETA);
+  L.lay.assign(c.num_layers, {});
+  for (int l = c.num_layers - 1; l >= 0; --l) {
+    auto& t = L.lay[l];
+    t.fill(-1);
+    t[L_N2G] = add(d, K_GAMMA);
+    if (c.norm == 0) t[L_N2B] = add(d, K_BETA);
+    t[L_W2] = add(d * F, K_MAT);
+    if (c.bias) t[L_B2] = add(d, K_BIAS);
+    t[L_W1] = add(F * d, K_MAT);
+    if (c.bias) t[L_B1] = add(F, K_BIAS);
+    t[L_N1G] = add(d, K_GAMMA);
+    if (c.norm == 0) t[L_N1B] = add(d, K_BETA);
+    t[L_WO] = add(d * d, K_MAT);
+    if (c.bias) t[L_BO] = add(d, K_BIAS);
+    t[L_WQKV] = add(3 * d * d, K_MAT);
+    if (c.bias) t[L_BQKV] = add(3 * d, K_BIAS);
+  }
+  L.emb = add(V * d, K_EMB);
+  return L;
+}
+
+zl_status validate(const zl_model_config& c) {
+  if (c.vocab_size <= 0 || c.embed_dim <= 0 || c.num_layers <= 0 || c.num_heads <= 0 || c.ff_hidden_dim <= 0 ||
+      c.max_seq_len <= 0)
+    return zl::set_error(ZL_EINVAL, "model config: sizes must be positive");
+  if (c.embed_dim % c.num_heads) return zl::set_error(ZL_EINVAL, "model config: embed_dim %% num_heads != 0");
+  if (c.embed_dim / c.num_heads != 64) return zl::set_error(ZL_EUNSUPPORTED, "model: head_dim must be 64");
+  if (c.embed_dim % 64 || c.ff_hidden_dim % 64 || c.vocab_size % 64)
+    return zl::set_error(ZL_EUNSUPPORTED, "model: embed_dim, ff_hidden_dim and vocab_size must be multiples of 64");
+  if (c.num_layers > 256) return zl::set_error(ZL_EUNSUPPORTED, "model: at most 256 layers");
+  if (c.norm != 0 && c.norm != 1) return zl::set_error(ZL_EINVAL, "model: norm must be 0 or 1");
+  if (c.pos != 0 && c.pos != 1) return zl::set_error(ZL_EINVAL, "model: pos must be 0 or 1");
+  return ZL_OK;
+}
+}  // namespace
+
+using bf16 = __nv_bfloat16;
+
+struct DistState {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+  cudaStream_t comm_stream = nullptr;
+  std::vector<int64_t> b_start, b_len;
+  std::vector<cudaEvent_t> ready_ev;  // recorded on the compute stream when a bucket's grads are final
+  cudaEvent_t done_ev = nullptr;      // recorded on comm stream after the last bucket
+  int next_bucket = 0;
+};
+
+struct zl_model {
+  zl_model_config cfg;
+  Layout L;
+  int64_t max_tokens = 0;
+  int dev = 0;
+  // arenas
+  float *params = nullptr, *grads = nullptr, *m = nullptr, *v = nullptr;
+  bf16* pbf = nullptr;
+  float *pos_table = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+  // activations
+  std::vector<bf16*> x, qkv, attn, r1, h1, f, r2;
+  std::vector<float*> lse, mean1, rstd1, mean2, rstd2;
+  bf16* hf = nullptr;
+  float *meanf = nullptr, *rstdf = nullptr;
+  bf16* logits = nullptr;
+  float* loss_rows = nullptr;
+  // backward temporaries
+  bf16 *dx = nullptr, *dr = nullptr, *dtmp = nullptr, *dF = nullptr, *dqkv = nullptr, *dattn = nullptr;
+  // workspaces
+  float* ws = nullptr;
+  int64_t ws_floats = 0;
+  std::vector<void*> allocs;
+  // optimizer
+  zl_adamw_config opt{0.9f, 0.95f, 1e-8f, 0.1f};
+  int t = 0;
+  // state
+  int last_B = 0, last_S = 0;
+  int launches = 0;
+  DistState dist;
+  int64_t ready_prefix = 0;  // grads in [0, ready_prefix) are final for this step
+};
+
+namespace {
+
+template <typename T>
+zl_status dalloc(zl_model* M, T** p, int64_t n) {
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, (size_t)std::max<int64_t>(n, 1) * sizeof(T));
+  if (e != cudaSuccess) return zl::set_error(ZL_ENOMEM, "model arena: cudaMalloc(%lld bytes): %s",
+                                             (long long)(n * sizeof(T)), cudaGetErrorString(e));
+  M->allocs.push_back(q);
+  *p = static_cast<T*>(q);
+  return ZL_OK;
+}
+
+#define TRY(x)                         \
+  do {                                 \
+    zl_status _s = (x);                \
+    if (_s != ZL_OK) return _s;        \
+  } while (0)
+
+// Workspace needed by the step's GEMMs and reductions at T tokens.
+int64_t step_workspace(const zl_model_config& c, int64_t T, int B_max) {
+  const int d = c.embed_dim, F = c.ff_hidden_dim, V = c.vocab_size;
+  const int Ti = (int)T;
+  int64_t w = 0;
+  auto g = [&](int M, int N, int K, int layout) { w = std::max(w, zl_gemm_workspace_floats(M, N, K, layout, 0)); };
+  const int KK = ZL_A_KMAJOR | ZL_B_KMAJOR;
+  g(Ti, 3 * d, d, KK); g(Ti, d, d, KK); g(Ti, F, d, KK); g(Ti, d, F, KK); g(Ti, V, d, KK);
+  g(V, d, Ti, 0); g(Ti, d, V, ZL_A_KMAJOR);
+  g(d, F, Ti, 0); g(Ti, F, d, ZL_A_KMAJOR); g(F, d, Ti, 0); g(Ti, d, F, ZL_A_KMAJOR);
+  g(d, d, Ti, 0); g(Ti, d, d, ZL_A_KMAJOR); g(3 * d, d, Ti, 0); g(Ti, d, 3 * d, ZL_A_KMAJOR);
+  w = std::max(w, zl_attention_workspace_floats(B_max, (int)(T / B_max), c.num_heads, d / c.num_heads));
+  w = std::max(w, (int64_t)2 * std::max(d, F) * zl_norm_bwd_blocks(T));
+  w = std::max(w, zl_colsum_workspace_floats(T, std::max(3 * d, F)));
+  return w;
+}
+
+zl_status gemm(zl_model* M, const bf16* A, const bf16* B, void* D, int m, int n, int k, int layout, int flags,
+               const zl_epilogue* e, cudaStream_t st) {
+  M->launches += 1;
+  return zl_gemm_bf16(reinterpret_cast<const zl_bf16*>(A), reinterpret_cast<const zl_bf16*>(B), D, m, n, k, layout,
+                      flags, e, M->ws, st);
+}
+
+const bf16* W(zl_model* M, int64_t off) { return M->pbf + off; }
+const float* P(zl_model* M, int64_t off) { return off >= 0 ? M->params + off : nullptr; }
+float* G(zl_model* M, int64_t off) { return off >= 0 ? M->grads + off : nullptr; }
+
+// ----------------------------------------------------------------------------- DP bucket hook
+// Called after the gradients in [0, prefix) became final on `st`.
+zl_status grads_ready(zl_model* M, int64_t prefix, cudaStream_t st) {
+  M->ready_prefix = prefix;
+  DistState& D = M->dist;
+  if (!D.comm) return ZL_OK;
+  while (D.next_bucket < (int)D.b_start.size() && D.b_start[D.next_bucket] + D.b_len[D.next_bucket] <= prefix) {
+    const int b = D.next_bucket++;
+    cudaEventRecord(D.ready_ev[b], st);
+    cudaStreamWaitEvent(D.comm_stream, D.ready_ev[b], 0);
+    ncclResult_t r = ncclAllReduce(M->grads + D.b_start[b], M->grads + D.b_start[b], (size_t)D.b_len[b], ncclFloat,
+                                   ncclSum, D.comm, D.comm_stream);
+    if (r != ncclSuccess) return zl::set_error(ZL_ENCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
+  }
+  return ZL_OK;
+}
+
+int64_t layer_grad_end(zl_model* M, int l, int which) {  // end offset of tensor `which` of layer l
+  const auto& t = M->L.lay[l];
+  // find the tensor starting at t[which] and return off+size
+  for (size_t i = 0; i < M->L.off.size(); ++i)
+    if (M->L.off[i] == t[which]) return M->L.off[i] + M->L.size[i];
+  return -1;
+}
+int64_t end_of(zl_model* M, int64_t off) {
+  for (size_t i = 0; i < M->L.off.size(); ++i)
+    if (M->L.off[i] == off) return M->L.off[i] + M->L.size[i];
+  return -1;
+}
+// Last present tensor of a group (skipping absent optional tensors).
+int64_t end_of_any(zl_model* M, std::initializer_list<int64_t> offs) {
+  int64_t e = -1;
+  for (int64_t o : offs)
+    if (o >= 0) e = std::max(e, end_of(M, o));
+  return e;
+}
+
+// ----------------------------------------------------------------------------- forward
+// Runs the forward to the bf16 logits (kept in M->logits).  If logits_f32 is non-null the head GEMM
+// writes fp32 logits there instead.
+zl_status forward(zl_model* M, const int32_t* ids, int B, int S, float* logits_f32, cudaStream_t st) {
+  const zl_model_config& c = M->cfg;
+  const int64_t T = (int64_t)B * S;
+  const int d = c.embed_dim, F = c.ff_hidden_dim, V = c.vocab_size, H = c.num_heads;
+  const int KK = ZL_A_KMAJOR | ZL_B_KMAJOR;
+  TRY(zl_embedding_forward_bf16(ids, P(M, M->L.emb), c.pos == 0 ? M->pos_table : nullptr,
+                                reinterpret_cast<zl_bf16*>(M->x[0]), T, S, d, V, st));
+  M->launches++;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const auto& t = M->L.lay[l];
+    zl_epilogue e{};
+    e.bias = P(M, t[L_BQKV]);
+    int fl = c.bias ? ZL_EPI_BIAS : 0;
+    if (c.pos == 1) {
+      fl |= ZL_EPI_ROPE;
+      e.rope_cos = M->rope_cos;
+      e.rope_sin = M->rope_sin;
+      e.rope_cols = 2 * d;
+      e.rope_seq = S;
+      e.head_dim = d / H;
+    }
+    TRY(gemm(M, M->x[l], W(M, t[L_WQKV]), M->qkv[l], (int)T, 3 * d, d, KK, fl, &e, st));
+    TRY(zl_attention_forward_bf16(reinterpret_cast<zl_bf16*>(M->qkv[l]), reinterpret_cast<zl_bf16*>(M->attn[l]),
+                                  M->lse[l], B, S, H, d / H, st));
+    M->launches++;
+    e = zl_epilogue{};
+    e.bias = P(M, t[L_BO]);
+    e.residual = reinterpret_cast<zl_bf16*>(M->x[l]);
+    TRY(gemm(M, M->attn[l], W(M, t[L_WO]), M->r1[l], (int)T, d, d, KK, (c.bias ? ZL_EPI_BIAS : 0) | ZL_EPI_RESIDUAL,
+             &e, st));
+    TRY(zl_norm_forward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r1[l]), P(M, t[L_N1G]), P(M, t[L_N1B]),
+                             reinterpret_cast<zl_bf16*>(M->h1[l]), M->mean1[l], M->rstd1[l], T, d, c.eps, st));
+    M->launches++;
+    e = zl_epilogue{};
+    e.bias = P(M, t[L_B1]);
+    TRY(gemm(M, M->h1[l], W(M, t[L_W1]), M->f[l], (int)T, F, d, KK, (c.bias ? ZL_EPI_BIAS : 0) | ZL_EPI_RELU, &e,
+             st));
+    e = zl_epilogue{};
+    e.bias = P(M, t[L_B2]);
+    e.residual = reinterpret_cast<zl_bf16*>(M->h1[l]);
+    TRY(gemm(M, M->f[l], W(M, t[L_W2]), M->r2[l], (int)T, d, F, KK, (c.bias ? ZL_EPI_BIAS : 0) | ZL_EPI_RESIDUAL, &e,
+             st));
+    TRY(zl_norm_forward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r2[l]), P(M, t[L_N2G]), P(M, t[L_N2B]),
+                             reinterpret_cast<zl_bf16*>(M->x[l + 1]), M->mean2[l], M->rstd2[l], T, d, c.eps, st));
+    M->launches++;
+  }
+  TRY(zl_norm_forward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->x[c.num_layers]), P(M, M->L.nog), P(M, M->L.nob),
+                           reinterpret_cast<zl_bf16*>(M->hf), M->meanf, M->rstdf, T, d, c.eps, st));
+  M->launches++;
+  const int64_t head_off = c.tied ? M->L.emb : M->L.head;
+  if (logits_f32) {
+    TRY(gemm(M, M->hf, W(M, head_off), logits_f32, (int)T, V, d, KK, ZL_EPI_OUT_F32, nullptr, st));
+  } else {
+    TRY(gemm(M, M->hf, W(M, head_off), M->logits, (int)T, V, d, KK, 0, nullptr, st));
+  }
+  M->last_B = B;
+  M->last_S = S;
+  return ZL_OK;
+}
+
+// ----------------------------------------------------------------------------- backward
+// Expects d_logits (bf16) in M->logits.  Gradients: weight GEMMs overwrite, everything else accumulates
+// (the grad arena must be zeroed before the step, zl_model_zero_grad).
+zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t st) {
+  const zl_model_config& c = M->cfg;
+  const int64_t T = (int64_t)B * S;
+  const int d = c.embed_dim, F = c.ff_hidden_dim, V = c.vocab_size, H = c.num_heads;
+  const int Ti = (int)T;
+  const int64_t head_off = c.tied ? M->L.emb : M->L.head;
+  // head: dW (accumulate: tied heads share the embedding gradient) and dhf
+  TRY(gemm(M, M->logits, M->hf, G(M, head_off), V, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
+  if (!c.tied) TRY(grads_ready(M, end_of(M, M->L.head), st));
+  TRY(gemm(M, M->logits, W(M, head_off), M->dtmp, Ti, d, V, ZL_A_KMAJOR, 0, nullptr, st));
+  TRY(zl_norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->x[c.num_layers]),
+                            reinterpret_cast<zl_bf16*>(M->dtmp), P(M, M->L.nog), M->meanf, M->rstdf,
+                            reinterpret_cast<zl_bf16*>(M->dx), G(M, M->L.nog), G(M, M->L.nob), M->ws, T, d, st));
+  M->launches += 2;
+  TRY(grads_ready(M, end_of_any(M, {M->L.nog, M->L.nob}), st));
+  for (int l = c.num_layers - 1; l >= 0; --l) {
+    const auto& t = M->L.lay[l];
+    // out = norm2(r2)
+    TRY(zl_norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r2[l]), reinterpret_cast<zl_bf16*>(M->dx),
+                              P(M, t[L_N2G]), M->mean2[l], M->rstd2[l], reinterpret_cast<zl_bf16*>(M->dr),
+                              G(M, t[L_N2G]), G(M, t[L_N2B]), M->ws, T, d, st));
+    M->launches += 2;
+    TRY(grads_ready(M, end_of_any(M, {t[L_N2G], t[L_N2B]}), st));
+    // r2 = h1 + f W2^T + b2
+    TRY(gemm(M, M->dr, M->f[l], G(M, t[L_W2]), d, F, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dr), G(M, t[L_B2]), M->ws, T, d, st)); M->launches += 2; }
+    TRY(grads_ready(M, end_of_any(M, {t[L_W2], t[L_B2]}), st));
+    zl_epilogue e{};
+    e.aux = reinterpret_cast<zl_bf16*>(M->f[l]);
+    TRY(gemm(M, M->dr, W(M, t[L_W2]), M->dF, Ti, F, d, ZL_A_KMAJOR, ZL_EPI_RELU_MASK, &e, st));
+    TRY(gemm(M, M->dF, M->h1[l], G(M, t[L_W1]), F, d, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dF), G(M, t[L_B1]), M->ws, T, F, st)); M->launches += 2; }
+    TRY(grads_ready(M, end_of_any(M, {t[L_W1], t[L_B1]}), st));
+    e = zl_epilogue{};
+    e.residual = reinterpret_cast<zl_bf16*>(M->dr);
+    TRY(gemm(M, M->dF, W(M, t[L_W1]), M->dtmp, Ti, d, F, ZL_A_KMAJOR, ZL_EPI_RESIDUAL, &e, st));
+    // h1 = norm1(r1)
+    TRY(zl_norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r1[l]), reinterpret_cast<zl_bf16*>(M->dtmp),
+                              P(M, t[L_N1G]), M->mean1[l], M->rstd1[l], reinterpret_cast<zl_bf16*>(M->dr),
+                              G(M, t[L_N1G]), G(M, t[L_N1B]), M->ws, T, d, st));
+    M->launches += 2;
+    TRY(grads_ready(M, end_of_any(M, {t[L_N1G], t[L_N1B]}), st));
+    // r1 = x + attn Wo^T + bo
+    TRY(gemm(M, M->dr, M->attn[l], G(M, t[L_WO]), d, d, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dr), G(M, t[L_BO]), M->ws, T, d, st)); M->launches += 2; }
+    TRY(grads_ready(M, end_of_any(M, {t[L_WO], t[L_BO]}), st));
+    TRY(gemm(M, M->dr, W(M, t[L_WO]), M->dattn, Ti, d, d, ZL_A_KMAJOR, 0, nullptr, st));
+    TRY(zl_attention_backward_bf16(reinterpret_cast<zl_bf16*>(M->qkv[l]), reinterpret_cast<zl_bf16*>(M->attn[l]),
+                                   reinterpret_cast<zl_bf16*>(M->dattn), M->lse[l],
+                                   reinterpret_cast<zl_bf16*>(M->dqkv), M->ws, B, S, H, d / H,
+                                   c.pos == 1 ? M->rope_cos : nullptr, c.pos == 1 ? M->rope_sin : nullptr, st));
+    M->launches += 3;
+    TRY(gemm(M, M->dqkv, M->x[l], G(M, t[L_WQKV]), 3 * d, d, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dqkv), G(M, t[L_BQKV]), M->ws, T, 3 * d, st)); M->launches += 2; }
+    TRY(grads_ready(M, end_of_any(M, {t[L_WQKV], t[L_BQKV]}), st));
+    e = zl_epilogue{};
+    e.residual = reinterpret_cast<zl_bf16*>(M->dr);
+    TRY(gemm(M, M->dqkv, W(M, t[L_WQKV]), M->dx, Ti, d, 3 * d, ZL_A_KMAJOR, ZL_EPI_RESIDUAL, &e, st));
+  }
+  TRY(zl_embedding_backward_bf16(ids, reinterpret_cast<zl_bf16*>(M->dx), G(M, M->L.emb), T, d, V, st));
+  M->launches++;
+  TRY(grads_ready(M, M->L.total, st));
+  return ZL_OK;
+}
+
+zl_status adamw(zl_model* M, float lr, cudaStream_t st) {
+  M->t += 1;
+  // adamw.cpp:39-43: bias corrections on the host in fp32 powf
+  const float bc1 = 1.0f - powf(M->opt.beta1, (float)M->t);
+  const float bc2 = 1.0f - powf(M->opt.beta2, (float)M->t);
+  const float gs = 1.0f / (float)M->dist.world;
+  if (M->dist.comm) {
+    cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);
+    cudaStreamWaitEvent(st, M->dist.done_ev, 0);
+  }
+  M->launches++;
+  return zl_adamw_flat(M->params, M->grads, M->m, M->v, reinterpret_cast<zl_bf16*>(M->pbf), M->L.total, lr,
+                       M->opt.weight_decay, M->opt.beta1, M->opt.beta2, M->opt.eps, bc1, bc2, gs, st);
+}
+
+zl_status check_shape(zl_model* M, int B, int S) {
+  if (B <= 0 || S <= 0) return zl::set_error(ZL_EINVAL, "batch and seq_len must be positive");
+  if (S > M->cfg.max_seq_len) return zl::set_error(ZL_EINVAL, "Sequence length exceeds max_seq_len");  // zerollm.cpp:105-108
+  if ((int64_t)B * S > M->max_tokens) return zl::set_error(ZL_EINVAL, "batch*seq_len exceeds the arena (%lld)", (long long)M->max_tokens);
+  return ZL_OK;
+}
+
+}  // namespace
+
+// ============================================================== C ABI
+extern "C" zl_status zl_model_param_layout(const zl_model_config* cfg, int64_t* offsets, int64_t* sizes, int* kinds,
+                                           int max_n, int* count, int64_t* total) {
+  if (!cfg) return zl::set_error(ZL_EINVAL, "null config");
+  TRY(validate(*cfg));
+  Layout L = build_layout(*cfg);
+  const int n = (int)L.off.size();
+  for (int i = 0; i < n && i < max_n; ++i) {
+    if (offsets) offsets[i] = L.off[i];
+    if (sizes) sizes[i] = L.size[i];
+    if (kinds) kinds[i] = L.kind[i];
+  }
+  if (count) *count = n;
+  if (total) *total = L.total;
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_create(const zl_model_config* cfg, int64_t max_tokens, uint64_t seed, float init_std,
+                                     zl_model** out) {
+  if (!cfg || !out) return zl::set_error(ZL_EINVAL, "null argument");
+  TRY(validate(*cfg));
+  if (max_tokens <= 0) return zl::set_error(ZL_EINVAL, "max_tokens must be positive");
+  zl_model* M = new zl_model();
+  M->cfg = *cfg;
+  M->L = build_layout(*cfg);
+  M->max_tokens = max_tokens;
+  cudaGetDevice(&M->dev);
+  const zl_model_config& c = *cfg;
+  const int64_t T = max_tokens, d = c.embed_dim, F = c.ff_hidden_dim, V = c.vocab_size;
+  const int64_t NP = M->L.total;
+  auto fail = [&](zl_status s) {
+    zl_model_destroy(M);
+    return s;
+  };
+  zl_status s;
+#define A(p, n) if ((s = dalloc(M, &(p), (n))) != ZL_OK) return fail(s)
+  A(M->params, NP); A(M->grads, NP); A(M->m, NP); A(M->v, NP); A(M->pbf, NP);
+  const int L = c.num_layers;
+  M->x.resize(L + 1); M->qkv.resize(L); M->attn.resize(L); M->r1.resize(L); M->h1.resize(L); M->f.resize(L);
+  M->r2.resize(L); M->lse.resize(L); M->mean1.resize(L); M->rstd1.resize(L); M->mean2.resize(L); M->rstd2.resize(L);
+  for (int l = 0; l <= L; ++l) A(M->x[l], T * d);
+  for (int l = 0; l < L; ++l) {
+    A(M->qkv[l], T * 3 * d); A(M->attn[l], T * d); A(M->r1[l], T * d); A(M->h1[l], T * d); A(M->f[l], T * F);
+    A(M->r2[l], T * d); A(M->lse[l], T * c.num_heads); A(M->mean1[l], T); A(M->rstd1[l], T); A(M->mean2[l], T);
+    A(M->rstd2[l], T);
+  }
+  A(M->hf, T * d); A(M->meanf, T); A(M->rstdf, T); A(M->logits, T * V); A(M->loss_rows, T);
+  A(M->dx, T * d); A(M->dr, T * d); A(M->dtmp, T * d); A(M->dF, T * F); A(M->dqkv, T * 3 * d); A(M->dattn, T * d);
+  // batch can be as small as 1 -> attention workspace sized for B=1 (T tokens) is the max of B*S*E + B*H*S
+  M->ws_floats = step_workspace(c, T, 1);
+  A(M->ws, M->ws_floats);
+  // constant tables
+  const int Dh = (int)(d / c.num_heads);
+  if (c.pos == 0) {
+    std::vector<float> pt((size_t)c.max_seq_len * d);
+    for (int p = 0; p < c.max_seq_len; ++p)  // embedding.cpp:107-126
+      for (int i = 0; i < d; ++i) {
+        const int k = i / 2;
+        const float ang = (float)p / powf(10000.0f, (float)(2 * k) / (float)d);
+        pt[(size_t)p * d + i] = (i % 2 == 0) ? sinf(ang) : cosf(ang);
+      }
+    A(M->pos_table, (int64_t)pt.size());
+    cudaMemcpy(M->pos_table, pt.data(), pt.size() * sizeof(float), cudaMemcpyHostToDevice);
+  } else {
+    const int half = Dh / 2;
+    std::vector<float> cs((size_t)c.max_seq_len * half), sn(cs.size());
+    for (int p = 0; p < c.max_seq_len; ++p)
+      for (int i = 0; i < half; ++i) {
+        const double th = (double)p * pow((double)c.rope_base, -2.0 * i / (double)Dh);
+        cs[(size_t)p * half + i] = (float)cos(th);
+        sn[(size_t)p * half + i] = (float)sin(th);
+      }
+    A(M->rope_cos, (int64_t)cs.size());
+    A(M->rope_sin, (int64_t)sn.size());
+    cudaMemcpy(M->rope_cos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice);
+    cudaMemcpy(M->rope_sin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice);
+  }
+#undef A
+  // weights
+  std::vector<float> hp((size_t)NP);
+  for (size_t i = 0; i < M->L.off.size(); ++i) {
+    float* p = hp.data() + M->L.off[i];
+    const int k = M->L.kind[i];
+    if (k == K_MAT || k == K_EMB)
+      fill_normal(p, M->L.size[i], seed ^ (0xD1B54A32D192ED03ull * (uint64_t)(i + 1)), 0.f, init_std);
+    else
+      for (int64_t j = 0; j < M->L.size[i]; ++j) p[j] = (k == K_GAMMA) ? 1.f : 0.f;
+  }
+  cudaMemcpy(M->params, hp.data(), (size_t)NP * sizeof(float), cudaMemcpyHostToDevice);
+  cudaMemset(M->m, 0, (size_t)NP * sizeof(float));
+  cudaMemset(M->v, 0, (size_t)NP * sizeof(float));
+  cudaMemset(M->grads, 0, (size_t)NP * sizeof(float));
+  s = zl_f32_to_bf16(M->params, reinterpret_cast<zl_bf16*>(M->pbf), NP, nullptr);
+  if (s != ZL_OK) return fail(s);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(zl::set_error(ZL_ECUDA, "model init: %s", cudaGetErrorString(e)));
+  *out = M;
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_destroy(zl_model* M) {
+  if (!M) return ZL_OK;
+  if (M->dist.comm) {
+    cudaStreamSynchronize(M->dist.comm_stream);
+    ncclCommDestroy(M->dist.comm);
+    for (auto ev : M->dist.ready_ev) cudaEventDestroy(ev);
+    if (M->dist.done_ev) cudaEventDestroy(M->dist.done_ev);
+    cudaStreamDestroy(M->dist.comm_stream);
+  }
+  for (void* p : M->allocs) cudaFree(p);
+  delete M;
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_num_params(zl_model* M, int64_t* n) {
+  if (!M || !n) return zl::set_error(ZL_EINVAL, "null argument");
+  *n = M->L.total;
+  return ZL_OK;
+}
+extern "C" zl_status zl_model_buffers(zl_model* M, float** params, float** grads, float** adam_m, float** adam_v) {
+  if (!M) return zl::set_error(ZL_EINVAL, "null model");
+  if (params) *params = M->params;
+  if (grads) *grads = M->grads;
+  if (adam_m) *adam_m = M->m;
+  if (adam_v) *adam_v = M->v;
+  return ZL_OK;
+}
+extern "C" zl_status zl_model_params_updated(zl_model* M, zl_stream s) {
+  if (!M) return zl::set_error(ZL_EINVAL, "null model");
+  return zl_f32_to_bf16(M->params, reinterpret_cast<zl_bf16*>(M->pbf), M->L.total, s);
+}
+extern "C" zl_status zl_model_set_optimizer(zl_model* M, const zl_adamw_config* o) {
+  if (!M || !o) return zl::set_error(ZL_EINVAL, "null argument");
+  M->opt = *o;
+  return ZL_OK;
+}
+extern "C" zl_status zl_model_zero_grad(zl_model* M, zl_stream s) {
+  if (!M) return zl::set_error(ZL_EINVAL, "null model");
+  cudaError_t e = cudaMemsetAsync(M->grads, 0, (size_t)M->L.total * sizeof(float), (cudaStream_t)s);
+  if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "zero_grad: %s", cudaGetErrorString(e));
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const int32_t* targets, int B, int S, float lr,
+                                         int update, float* loss_out, zl_stream stream) {
+  if (!M || !ids || !targets) return zl::set_error(ZL_EINVAL, "null argument");
+  TRY(check_shape(M, B, S));
+  cudaStream_t st = (cudaStream_t)stream;
+  M->launches = 0;
+  M->dist.next_bucket = 0;
+  TRY(zl_model_zero_grad(M, stream));
+  M->launches++;
+  TRY(forward(M, ids, B, S, nullptr, st));
+  const int64_t T = (int64_t)B * S;
+  TRY(zl_cross_entropy_fused_bf16(reinterpret_cast<zl_bf16*>(M->logits), targets, (int)T, M->cfg.vocab_size, 1e-8f,
+                                  1.0f / (float)T, M->loss_rows, loss_out, st));
+  M->launches += loss_out ? 2 : 1;
+  TRY(backward(M, ids, B, S, st));
+  if (update) TRY(adamw(M, lr, st));
+  else if (M->dist.comm) {
+    cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);
+    cudaStreamWaitEvent(st, M->dist.done_ev, 0);
+  }
+  return zl::check_launch("train_step");
+}
+
+extern "C" zl_status zl_model_forward(zl_model* M, const int32_t* ids, int B, int S, float* logits, zl_stream stream) {
+  if (!M || !ids || !logits) return zl::set_error(ZL_EINVAL, "null argument");
+  TRY(check_shape(M, B, S));
+  return forward(M, ids, B, S, logits, (cudaStream_t)stream);
+}
+
+namespace zl {
+__global__ void f32_to_bf16_scaled_kernel(const float* __restrict__ x, bf16* __restrict__ y, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2bfloat16_rn(x[i]);
+}
+}  // namespace zl
+
+extern "C" zl_status zl_model_backward(zl_model* M, const int32_t* ids, const float* d_logits, int B, int S,
+                                       zl_stream stream) {
+  if (!M || !ids || !d_logits) return zl::set_error(ZL_EINVAL, "null argument");
+  if (B != M->last_B || S != M->last_S)  // zerollm.cpp:205-208
+    return zl::set_error(ZL_ESTATE, "Must call forward() with same batch_size and seq_len before backward()");
+  cudaStream_t st = (cudaStream_t)stream;
+  TRY(zl_f32_to_bf16(d_logits, reinterpret_cast<zl_bf16*>(M->logits), (int64_t)B * S * M->cfg.vocab_size, stream));
+  M->dist.next_bucket = (int)M->dist.b_start.size();  // no collective on this path
+  return backward(M, ids, B, S, st);
+}
+
+extern "C" zl_status zl_model_step(zl_model* M, float lr, zl_stream stream) {
+  if (!M) return zl::set_error(ZL_EINVAL, "null model");
+  return adamw(M, lr, (cudaStream_t)stream);
+}
+
+extern "C" zl_status zl_model_last_launches(zl_model* M, int* count) {
+  if (!M || !count) return zl::set_error(ZL_EINVAL, "null argument");
+  *count = M->launches;
+  return ZL_OK;
+}
+
+// ------------------------------------------------------------------ data parallel
+extern "C" zl_status zl_bucket_plan(const int64_t* tensor_offsets, const int64_t* tensor_sizes, int n_tensors,
+                                    int64_t bucket_floats, int64_t* starts, int64_t* lens, int max_buckets,
+                                    int* n_buckets) {
+  if (!tensor_offsets || !tensor_sizes || n_tensors <= 0 || bucket_floats <= 0 || !n_buckets)
+    return zl::set_error(ZL_EINVAL, "bucket_plan: invalid arguments");
+  // Greedy: close a bucket at a tensor boundary once adding the next tensor would exceed the
+  // budget; a tensor larger than the budget is split into budget-sized pieces.
+  int nb = 0;
+  int64_t cur_start = tensor_offsets[0], cur_len = 0;
+  auto emit = [&](int64_t s, int64_t l) {
+    if (l <= 0) return;
+    if (nb < max_buckets) {
+      if (starts) starts[nb] = s;
+      if (lens) lens[nb] = l;
+    }
+    ++nb;
+  };
+  for (int i = 0; i < n_tensors; ++i) {
+    int64_t off = tensor_offsets[i], sz = tensor_sizes[i];
+    if (i > 0 && off != tensor_offsets[i - 1] + tensor_sizes[i - 1])
+      return zl::set_error(ZL_EINVAL, "bucket_plan: tensors must be contiguous and ordered");
+    if (cur_len > 0 && cur_len + sz > bucket_floats) {
+      emit(cur_start, cur_len);
+      cur_start = off;
+      cur_len = 0;
+    }
+    while (sz > bucket_floats) {
+      if (cur_len > 0) { emit(cur_start, cur_len); cur_start = off; cur_len = 0; }
+      emit(off, bucket_floats);
+      off += bucket_floats;
+      sz -= bucket_floats;
+      cur_start = off;
+    }
+    cur_len += sz;
+  }
+  emit(cur_start, cur_len);
+  *n_buckets = nb;
+  if (nb > max_buckets) return zl::set_error(ZL_EINVAL, "bucket_plan: more than %d buckets", max_buckets);
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_nccl_unique_id(void* id_out, size_t id_bytes) {
+  if (!id_out || id_bytes < sizeof(ncclUniqueId)) return zl::set_error(ZL_EINVAL, "nccl id buffer too small");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return zl::set_error(ZL_ENCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+  memcpy(id_out, &id, sizeof(id));
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_attach_nccl(zl_model* M, const void* id, int rank, int world, int64_t bucket_bytes) {
+  if (!M || !id || world <= 0 || rank < 0 || rank >= world || bucket_bytes < 4)
+    return zl::set_error(ZL_EINVAL, "attach_nccl: invalid arguments");
+  if (M->dist.comm) return zl::set_error(ZL_ESTATE, "attach_nccl: already attached");
+  DistState& D = M->dist;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclResult_t r = ncclCommInitRank(&D.comm, world, uid, rank);
+  if (r != ncclSuccess) return zl::set_error(ZL_ENCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+  D.rank = rank;
+  D.world = world;
+  cudaStreamCreateWithFlags(&D.comm_stream, cudaStreamNonBlocking);
+  std::vector<int64_t> st(4096), ln(4096);
+  int nb = 0;
+  TRY(zl_bucket_plan(M->L.off.data(), M->L.size.data(), (int)M->L.off.size(), bucket_bytes / 4, st.data(), ln.data(),
+                     4096, &nb));
+  D.b_start.assign(st.begin(), st.begin() + nb);
+  D.b_len.assign(ln.begin(), ln.begin() + nb);
+  D.ready_ev.resize(nb);
+  for (auto& ev : D.ready_ev) cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&D.done_ev, cudaEventDisableTiming);
+  // identical initial weights on every rank: broadcast rank 0's arena (train_zerollm_dp.cpp:335-341)
+  r = ncclBroadcast(M->params, M->params, (size_t)M->L.total, ncclFloat, 0, D.comm, D.comm_stream);
+  if (r != ncclSuccess) return zl::set_error(ZL_ENCCL, "ncclBroadcast: %s", ncclGetErrorString(r));
+  cudaStreamSynchronize(D.comm_stream);
+  return zl_model_params_updated(M, nullptr);
+}
+
+namespace zl {
+__global__ void checksum_kernel(const uint32_t* __restrict__ p, int64_t n, unsigned long long* out) {
+  uint64_t h = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    h += (uint64_t)p[i] * (0x9E3779B97F4A7C15ull ^ (uint64_t)i);
+  atomicAdd(out, (unsigned long long)h);
+}
+}  // namespace zl
+
+extern "C" zl_status zl_model_param_checksum(zl_model* M, uint64_t* out, zl_stream s) {
+  if (!M || !out) return zl::set_error(ZL_EINVAL, "null argument");
+  unsigned long long* d = nullptr;
+  // the checksum word lives in the spare tail of the workspace
+  d = reinterpret_cast<unsigned long long*>(M->ws);
+  cudaMemsetAsync(d, 0, sizeof(unsigned long long), (cudaStream_t)s);
+  zl::checksum_kernel<<<592, 256, 0, (cudaStream_t)s>>>(reinterpret_cast<const uint32_t*>(M->params), M->L.total, d);
+  unsigned long long h = 0;
+  cudaMemcpyAsync(&h, d, sizeof(h), cudaMemcpyDeviceToHost, (cudaStream_t)s);
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)s);
+  if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "checksum: %s", cudaGetErrorString(e));
+  *out = h;
+  return ZL_OK;
+}
