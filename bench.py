@@ -136,8 +136,8 @@ def kernel_breakdown(B, S, reps=5):
         res[name] = {"ms": ms, "per_step": launches, "work": work, "kind": kind}
 
     KK = L.A_KMAJOR | L.B_KMAJOR
-    # operand buffers large enough for every shape below: A up to [T, V], B up to [V, F]
-    x, w = rnd(T * V), rnd(V * F, scale=0.02)
+    # operand buffers large enough for every shape below: A up to [T, V], B up to [T, F]
+    x, w = rnd(T * V), rnd(T * max(F, 3 * d), scale=0.02)
     out = torch.empty(T * V, device="cuda", dtype=bf)
     out32 = torch.empty(V * F, device="cuda")
     bias = torch.zeros(max(F, 3 * d), device="cuda")

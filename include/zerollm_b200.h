@@ -242,6 +242,10 @@ zl_status zl_model_set_optimizer(zl_model *m, const zl_adamw_config *opt);
  * rank's batch.  update=0 skips AdamW (gradients stay in the grad arena). */
 zl_status zl_model_train_step(zl_model *m, const int32_t *ids, const int32_t *targets, int batch, int seq_len,
                               float lr, int update, float *loss_out, zl_stream stream);
+/* Step as a CUDA graph (default on, single process): the second call with the same ids/targets/loss
+ * pointers and shape captures zero_grad -> forward -> CE -> backward into a graph that later calls replay
+ * (AdamW stays a separate launch so lr may change).  0 disables. */
+zl_status zl_model_set_graph(zl_model *m, int enabled);
 /* Reference-API pieces: forward to fp32 logits [batch*seq, V] (zerollm.cpp:101-195) ... */
 zl_status zl_model_forward(zl_model *m, const int32_t *ids, int batch, int seq_len, float *logits,
                            zl_stream stream);

@@ -91,3 +91,10 @@ def test_kernel_entry_points_validate_before_touching_the_device():
     assert L.zl_mha_forward_f32(None, None, None, None, None, None, 0, 1, 1, 1, 1, None) == lib.ZL_EINVAL
     assert L.zl_adamw_step_f32(None, None, None, None, 0, *([0.0] * 7), None) == lib.ZL_EINVAL
     assert b"invalid" in L.zl_last_error() or b"size" in L.zl_last_error()
+
+
+def test_cpp_api_program_builds():
+    """The C++ drop-in headers compile against the C ABI (nvcc cross-compiles without a GPU)."""
+    from zerollm_b200 import build
+    path = build.build_api_test()
+    assert os.path.exists(path)

@@ -84,9 +84,10 @@ def test_gemm_bf16_layouts(L, a_k, b_k, M, N, K_):
     assert rel(out16.float().cpu().view(M, N), ref) < 1e-2
 
 
-def test_gemm_bf16_weight_grad_splitk(L):
-    """dW-shaped product: reduction over 32768 rows, both operands MN-major (split-K path)."""
-    T, N, K_ = 32768, 512, 2048
+@pytest.mark.parametrize("T,N,K_", [(32768, 512, 2048), (2048, 2048, 512), (2048, 512, 2048), (2048, 1536, 512)])
+def test_gemm_bf16_weight_grad_splitk(L, T, N, K_):
+    """dW-shaped products dW[N,K] = dY[T,N]^T X[T,K]: reduction over T, both operands MN-major
+    (split-K path), in both orientations of the FFN weights."""
     g = torch.Generator().manual_seed(1)
     dY = torch.randn(T, N, generator=g).bfloat16()
     X = torch.randn(T, K_, generator=g).bfloat16()

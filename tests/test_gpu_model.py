@@ -1,24 +1,28 @@
 """Whole training step on the GPU against the oracle.
 
-Two comparisons per configuration:
+The bars (BASELINE parity under bf16) are applied in two settings.
 
-1. Against the oracle in bf16-storage emulation (the same fp32 arithmetic,
-   with every tensor the GPU keeps in bf16 rounded at the same point, and the
-   attention forward in the kernel's block order).  This isolates
-   implementation errors from rounding:
+A. Smooth setting: every FFN bias is set to +3 before the step, so every ReLU
+   is active (pre-activations ~ 3 +- 0.45) and the step is a smooth function
+   of its inputs.  Against both the plain fp32 oracle and the oracle in bf16
+   storage emulation (same fp32 arithmetic, every tensor the GPU keeps in bf16
+   rounded at the same point, attention forward in the kernel's block order):
      * step loss within 1e-3 relative;
      * every tensor's gradient within 2e-2 (max|got-ref| / max|ref|);
      * AdamW-updated weights within 2e-2 over the elements whose reference
-       gradient is above that floor (|g| >= 2e-2 max|g|): at step 1 the update
-       is lr*g/(|g|+eps), i.e. +-lr whatever |g| is, so an element whose
-       gradient is below the rounding floor can take either sign.
-2. Against the plain fp32 oracle (the reference semantics):
+       gradient is above the rounding floor and in the sign regime of the step
+       (|g| >= max(2e-2 max|g|, 100 eps)): at step 1 the update is
+       lr*g/(|g|+eps), i.e. +-lr for |g| >> eps whatever |g| is, so an element
+       whose gradient is below the floor may take either sign, and one with
+       |g| ~ eps moves by an amount that tracks |g| itself.
+B. Default initialisation (biases 0), against the plain fp32 oracle:
      * step loss within 1e-3 relative;
-     * each gradient within max(2e-2, 2 x s_t), where s_t is the oracle's own
-       change of that gradient when only its weights are rounded to bf16.  For
-       most tensors s_t < 5e-3 and the bound is 2e-2; the ReLU-gated W1/b1
-       gradients have s_t ~ 0.1 (bf16-level noise in the pre-activations flips
-       ReLU mask decisions), and there the bound is the intrinsic one.
+     * each gradient within max(2e-2, 2 * n_t), where n_t is the oracle's own
+       fp32-vs-bf16-storage difference for that tensor.  n_t < 5e-3 for most
+       tensors; for the ReLU-gated W1/b1 gradients n_t ~ 0.1, because any
+       bf16-level difference in a pre-activation near zero flips that ReLU's
+       mask, and dW1/db1 sum such flips over every token.  Setting A is what
+       pins those tensors tightly.
 Initial weights are checked bit-exact (same seeded generator).
 """
 import numpy as np
@@ -31,6 +35,7 @@ pytestmark = pytest.mark.gpu
 
 GRAD_TOL = 2e-2
 LOSS_TOL = 1e-3
+ADAM_EPS = 1e-8
 
 
 def rel(a, b):
@@ -63,43 +68,73 @@ def _batch(B, S, V, seed):
     return ids[:, :S].ravel().copy(), ids[:, 1:].ravel().copy()
 
 
-def _compare_step(c, B, S):
+def _ffn_bias_slices(om):
+    """Offsets of every b1 (FFN hidden bias) in the parameter arena."""
+    offs, sizes, kinds, _ = O.param_layout(om)
+    F = om.ffn
+    return [(int(o), int(s)) for o, s, k in zip(offs, sizes, kinds) if k == 1 and s == F]
+
+
+def _check(tag, g_gpu, p_gpu, g_ref, p_ref, om, bound=None):
+    offs, sizes, kinds, _ = O.param_layout(om)
+    rows, bad = [], []
+    for i, (o, s, k) in enumerate(zip(offs, sizes, kinds)):
+        gr = g_ref[o:o + s]
+        eg = rel(g_gpu[o:o + s], gr)
+        tol = GRAD_TOL if bound is None else bound[i]
+        ew = 0.0
+        if p_ref is not None:
+            sel = np.abs(gr) >= max(GRAD_TOL * np.max(np.abs(gr)), 100 * ADAM_EPS)
+            if sel.any():
+                ew = float(np.max(np.abs(p_gpu[o:o + s][sel] - p_ref[o:o + s][sel])) /
+                           max(np.max(np.abs(p_ref[o:o + s])), 1e-30))
+        rows.append(f"  @{o:>9} n={s:>8} kind {k}: grad {eg:.4f} (bound {tol:.3f}) weights {ew:.4f}")
+        if eg >= tol or ew >= GRAD_TOL:
+            bad.append(o)
+    assert not bad, f"[{tag}] tensors over their bound:\n" + "\n".join(rows)
+
+
+def _run(c, B, S, smooth):
     from zerollm_b200 import ZeroLLM
     om = _oracle_model(c)
+    p0 = O.init_params(om, seed=0, std=0.02)
     m = ZeroLLM(c, B * S, seed=0, init_std=0.02)
     m.set_optimizer(0.9, 0.95, 1e-8, 0.1)
-    p0 = O.init_params(om, seed=0, std=0.02)
     assert np.array_equal(m.params(), p0), "initial weights differ from the oracle's generator"
+    if smooth:
+        for o, s in _ffn_bias_slices(om):
+            p0[o:o + s] = 3.0
+        m.set_params(p0)
     inp, tgt = _batch(B, S, c.vocab_size, 1)
     loss = m.train_step(torch.from_numpy(inp).cuda(), torch.from_numpy(tgt).cuda(), B, S, lr=3e-4).item()
     g_gpu, p_gpu = m.grads(), m.params()
     m.close()
-    offs, sizes, kinds, _ = O.param_layout(om)
-    # 1. bf16-storage emulation
-    pe, zm, zv = p0.copy(), np.zeros_like(p0), np.zeros_like(p0)
-    loss_e, g_e = O.train_step(om, pe, zm, zv, inp, tgt, B, S, lr=3e-4, beta1=0.9, beta2=0.95, weight_decay=0.1,
-                               bf16_emulation=True)
-    assert abs(loss - loss_e) / abs(loss_e) < LOSS_TOL, (loss, loss_e)
-    report = []
-    for o, s, k in zip(offs, sizes, kinds):
-        eg = rel(g_gpu[o:o + s], g_e[o:o + s])
-        gr = g_e[o:o + s]
-        sel = np.abs(gr) >= GRAD_TOL * np.max(np.abs(gr))
-        ew = float(np.max(np.abs(p_gpu[o:o + s][sel] - pe[o:o + s][sel])) / max(np.max(np.abs(pe[o:o + s])), 1e-30))
-        report.append((int(o), int(k), eg, ew))
-        assert eg < GRAD_TOL, f"[emulated] grad tensor @{o} kind {k}: rel err {eg}"
-        assert ew < GRAD_TOL, f"[emulated] weights @{o} kind {k}: rel err {ew}"
-    # 2. plain fp32 reference semantics
-    loss_r, g_r = O.train_step(om, p0.copy(), zm * 0, zv * 0, inp, tgt, B, S, update=False)
-    pb = torch.from_numpy(p0).bfloat16().float().numpy()
-    _, g_b = O.train_step(om, pb, zm * 0, zv * 0, inp, tgt, B, S, update=False)
+    return om, p0, inp, tgt, loss, g_gpu, p_gpu
+
+
+def _oracle(om, p0, inp, tgt, B, S, emulate):
+    p = p0.copy()
+    loss, g = O.train_step(om, p, np.zeros_like(p), np.zeros_like(p), inp, tgt, B, S, lr=3e-4, beta1=0.9,
+                           beta2=0.95, weight_decay=0.1, bf16_emulation=emulate)
+    return loss, g, p
+
+
+def _compare_step(c, B, S):
+    # A. smooth setting: every tensor within 2e-2 of both oracles
+    om, p0, inp, tgt, loss, g_gpu, p_gpu = _run(c, B, S, smooth=True)
+    for emulate in (True, False):
+        loss_r, g_r, p_r = _oracle(om, p0, inp, tgt, B, S, emulate)
+        tag = "smooth, bf16-emulated oracle" if emulate else "smooth, fp32 oracle"
+        assert abs(loss - loss_r) / abs(loss_r) < LOSS_TOL, (tag, loss, loss_r)
+        _check(tag, g_gpu, p_gpu, g_r, p_r, om)
+    # B. default init against fp32, bounded by the oracle's own bf16-storage effect
+    om, p0, inp, tgt, loss, g_gpu, p_gpu = _run(c, B, S, smooth=False)
+    loss_r, g_r, _ = _oracle(om, p0, inp, tgt, B, S, False)
+    _, g_e, _ = _oracle(om, p0, inp, tgt, B, S, True)
     assert abs(loss - loss_r) / abs(loss_r) < LOSS_TOL, (loss, loss_r)
-    for o, s, k in zip(offs, sizes, kinds):
-        sens = rel(g_b[o:o + s], g_r[o:o + s])
-        tol = max(GRAD_TOL, 2 * sens)
-        e = rel(g_gpu[o:o + s], g_r[o:o + s])
-        assert e < tol, f"[fp32] grad tensor @{o} kind {k}: rel err {e} (bound {tol}, bf16 self-sensitivity {sens})"
-    return loss, loss_r, report
+    offs, sizes, _, _ = O.param_layout(om)
+    bound = [max(GRAD_TOL, 2 * rel(g_e[o:o + s], g_r[o:o + s])) for o, s in zip(offs, sizes)]
+    _check("default init, fp32 oracle", g_gpu, None, g_r, None, om, bound)
 
 
 @pytest.mark.parametrize("idx", [0, 1])
@@ -138,3 +173,24 @@ def test_full_context_step_properties():
         losses.append(m.train_step(ids, tg, B, S, lr=1e-3).item())
     assert losses[-1] < losses[0] - 0.1, losses
     m.close()
+
+
+def test_graph_replay_matches_eager():
+    """Steps replayed from the captured CUDA graph equal eagerly launched steps (up to the
+    summation-order freedom of the fp32 atomics in the embedding and dQ accumulation)."""
+    from zerollm_b200 import ZeroLLM
+    c = _cfgs(True)[0]
+    B, S = 4, 128
+    inp, tgt = _batch(B, S, c.vocab_size, 7)
+    ids, tg = torch.from_numpy(inp).cuda(), torch.from_numpy(tgt).cuda()
+    out = []
+    for graph in (False, True):
+        m = ZeroLLM(c, B * S, seed=0)
+        m.set_optimizer()
+        m.set_graph(graph)
+        losses = [m.train_step(ids, tg, B, S, lr=1e-3).item() for _ in range(4)]
+        out.append((losses, m.params()))
+        m.close()
+    (l0, p0), (l1, p1) = out
+    assert np.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
+    assert rel(p1, p0) < 1e-5

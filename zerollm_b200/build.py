@@ -47,7 +47,26 @@ def build(jobs: int = 4, verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_api_test()
     return LIB
+
+
+API_TEST_SRC = os.path.join(ROOT, "tests", "cpp", "api_test.cpp")
+API_TEST_BIN = os.path.join(OUT_DIR, "api_test")
+
+
+def build_api_test() -> str:
+    """Compiles tests/cpp/api_test.cpp against the C++ drop-in headers and the library."""
+    deps = [API_TEST_SRC, LIB] + [os.path.join(CSRC, "api", f) for f in os.listdir(os.path.join(CSRC, "api"))]
+    if os.path.exists(API_TEST_BIN) and os.path.getmtime(API_TEST_BIN) >= max(os.path.getmtime(d) for d in deps):
+        return API_TEST_BIN
+    cmd = [NVCC, "-O2", "-std=c++17", "-ccbin", "g++", "-x", "cu", *ARCH, "-I", os.path.join(ROOT, "include"),
+           "-I", os.path.join(CSRC, "api"), API_TEST_SRC, "-o", API_TEST_BIN, "-L", HERE, "-lzerollm_b200",
+           f"-Xlinker=-rpath,{HERE}", "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"api_test build failed:\n{r.stdout}\n{r.stderr}")
+    return API_TEST_BIN
 
 
 if __name__ == "__main__":

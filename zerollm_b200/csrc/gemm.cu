@@ -25,7 +25,10 @@ namespace zl {
 
 // ------------------------------------------------------------------ config
 constexpr int BM = 128;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                       // two warps per TMEM lane quarter
+constexpr int kThreads = 64 + kEpiWarps * 32;      // producer warp + MMA warp + epilogue
+constexpr int kStgStride = 80;                     // bytes per staged row: 64 B of data + 16 B pad
+constexpr int kStgBytes = 32 * kStgStride;         // per epilogue warp
 
 template <typename T>
 struct Elem;
@@ -52,63 +55,166 @@ struct Smem {
   static constexpr int A_BYTES = BM * 128;   // BM rows (or BK rows x BM) of 128 bytes
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;            // per-warp staging for coalesced epilogue I/O
+  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kStgBytes;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + alignment slack
 };
 
 // ------------------------------------------------------------------ epilogue
-// Applies the fused epilogue to 32 consecutive columns [c0, c0+32) of row r and stores.
+// Per-thread fused epilogue for 32 consecutive columns [c0, c0+32) of row r (used for
+// partial chunks and by the split-K reduction).  Every loop is fully unrolled with a
+// column predicate so the value array stays in registers.
 __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int r, int c0, float (&v)[32]) {
   if (r >= a.M) return;
   const int f = a.flags;
   const int nvalid = min(32, a.N - c0);
   if (nvalid <= 0) return;
+  const size_t rowoff = (size_t)r * a.N + c0;
+  const int hd = a.epi.head_dim;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < nvalid) {
+      if (f & ZL_EPI_BIAS) v[j] += __ldg(a.epi.bias + c0 + j);
+    }
+  }
+  if ((f & ZL_EPI_ROPE) && c0 < a.epi.rope_cols) {
+    const int half = hd >> 1;
+    const int pos = r % a.epi.rope_seq;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      if (j + 1 < nvalid && c0 + j < a.epi.rope_cols) {
+        const int i = ((c0 + j) % hd) >> 1;
+        const float c = __ldg(a.epi.rope_cos + (size_t)pos * half + i), s = __ldg(a.epi.rope_sin + (size_t)pos * half + i);
+        const float x0 = v[j], x1 = v[j + 1];
+        v[j] = x0 * c - x1 * s;
+        v[j + 1] = x0 * s + x1 * c;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < nvalid) {
+      if (f & ZL_EPI_RESIDUAL)
+        v[j] += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.epi.residual)[rowoff + j]);
+      if (f & ZL_EPI_RELU_MASK)
+        v[j] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.epi.aux)[rowoff + j]) > 0.f ? v[j] : 0.f;
+      if (f & ZL_EPI_RELU) v[j] = fmaxf(v[j], 0.f);
+      if (f & ZL_EPI_OUT_F32) {
+        float* out = reinterpret_cast<float*>(a.D) + rowoff + j;
+        *out = (f & ZL_EPI_ACCUM) ? *out + v[j] : v[j];
+      } else {
+        reinterpret_cast<__nv_bfloat16*>(a.D)[rowoff + j] = __float2bfloat16_rn(v[j]);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ coalesced epilogue
+// A warp owns 32 consecutive rows (one TMEM lane quarter) and walks 32-column
+// chunks.  Row-wise data (residual / mask in, results out) moves between
+// registers and global memory through a per-warp staging buffer in shared
+// memory, so every global access instruction of the warp covers 8 full
+// 64-byte row segments instead of 32 scattered 16-byte pieces.
+__device__ __forceinline__ void stg_put_row(uint32_t stg, int lane, const uint4 (&u)[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stg + lane * kStgStride + q * 16), "r"(u[q].x),
+                 "r"(u[q].y), "r"(u[q].z), "r"(u[q].w));
+}
+__device__ __forceinline__ void stg_get_row(uint32_t stg, int lane, uint4 (&u)[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(u[q].x), "=r"(u[q].y), "=r"(u[q].z), "=r"(u[q].w)
+                 : "r"(stg + lane * kStgStride + q * 16));
+}
+// Global -> staging: 32 rows x 64 bytes starting at `base` (row pitch `pitch` bytes), rows < nrows.
+__device__ __forceinline__ void stg_load(uint32_t stg, int lane, const uint8_t* base, size_t pitch, int nrows) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int p = i * 32 + lane, row = p >> 2, q = p & 3;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (row < nrows) u = __ldg(reinterpret_cast<const uint4*>(base + (size_t)row * pitch + q * 16));
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stg + row * kStgStride + q * 16), "r"(u.x), "r"(u.y),
+                 "r"(u.z), "r"(u.w));
+  }
+}
+// Staging -> global, same geometry.
+__device__ __forceinline__ void stg_store(uint32_t stg, int lane, uint8_t* base, size_t pitch, int nrows) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int p = i * 32 + lane, row = p >> 2, q = p & 3;
+    uint4 u;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                 : "r"(stg + row * kStgStride + q * 16));
+    if (row < nrows) *reinterpret_cast<uint4*>(base + (size_t)row * pitch + q * 16) = u;
+  }
+}
+__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
+  float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y), c = unpack_bf16(u.z), d = unpack_bf16(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+
+// Fused epilogue for one 32 x 32 chunk: rows [r0, r0+32) (this lane: r0+lane), columns [c0, c0+32).
+// Requires N % 8 == 0 (bf16 out) / N % 4 == 0 (fp32 out) and c0 + 32 <= N; other chunks use
+// epilogue_store32 (per-thread path).
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, uint32_t stg, int lane, int r0, int c0,
+                                               float (&v)[32]) {
+  const int f = a.flags;
+  const int r = r0 + lane;
+  const int nrows = min(32, a.M - r0);
   if (f & ZL_EPI_BIAS) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nvalid) v[j] += __ldg(a.epi.bias + c0 + j);
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(a.epi.bias + c0) + q);
+      v[q * 4] += b.x; v[q * 4 + 1] += b.y; v[q * 4 + 2] += b.z; v[q * 4 + 3] += b.w;
+    }
   }
   if ((f & ZL_EPI_ROPE) && c0 < a.epi.rope_cols) {
     const int half = a.epi.head_dim >> 1;
     const int pos = r % a.epi.rope_seq;
     const float* ct = a.epi.rope_cos + (size_t)pos * half;
     const float* st = a.epi.rope_sin + (size_t)pos * half;
+    const int i0 = (c0 % a.epi.head_dim) >> 1;
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
-      const int i = ((c0 + j) % a.epi.head_dim) >> 1;
-      const float c = __ldg(ct + i), s = __ldg(st + i);
+      const float c = __ldg(ct + i0 + (j >> 1)), s = __ldg(st + i0 + (j >> 1));
       const float x0 = v[j], x1 = v[j + 1];
       v[j] = x0 * c - x1 * s;
       v[j + 1] = x0 * s + x1 * c;
     }
   }
   if (f & ZL_EPI_RESIDUAL) {
-    const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(a.epi.residual) + (size_t)r * a.N + c0;
-    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(res) & 15) == 0)) {
+    __syncwarp();
+    stg_load(stg, lane, reinterpret_cast<const uint8_t*>(reinterpret_cast<const __nv_bfloat16*>(a.epi.residual) +
+                                                         (size_t)r0 * a.N + c0),
+             (size_t)a.N * 2, nrows);
+    __syncwarp();
+    uint4 u[4];
+    stg_get_row(stg, lane, u);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 u = __ldg(reinterpret_cast<const uint4*>(res) + q);
-        float2 p0 = unpack_bf16(u.x), p1 = unpack_bf16(u.y), p2 = unpack_bf16(u.z), p3 = unpack_bf16(u.w);
-        v[q * 8 + 0] += p0.x; v[q * 8 + 1] += p0.y; v[q * 8 + 2] += p1.x; v[q * 8 + 3] += p1.y;
-        v[q * 8 + 4] += p2.x; v[q * 8 + 5] += p2.y; v[q * 8 + 6] += p3.x; v[q * 8 + 7] += p3.y;
-      }
-    } else {
-      for (int j = 0; j < nvalid; ++j) v[j] += __bfloat162float(res[j]);
+    for (int q = 0; q < 4; ++q) {
+      float t[8];
+      unpack8(u[q], t);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[q * 8 + k] += t[k];
     }
   }
   if (f & ZL_EPI_RELU_MASK) {
-    const __nv_bfloat16* aux = reinterpret_cast<const __nv_bfloat16*>(a.epi.aux) + (size_t)r * a.N + c0;
-    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(aux) & 15) == 0)) {
+    __syncwarp();
+    stg_load(stg, lane, reinterpret_cast<const uint8_t*>(reinterpret_cast<const __nv_bfloat16*>(a.epi.aux) +
+                                                         (size_t)r0 * a.N + c0),
+             (size_t)a.N * 2, nrows);
+    __syncwarp();
+    uint4 u[4];
+    stg_get_row(stg, lane, u);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 u = __ldg(reinterpret_cast<const uint4*>(aux) + q);
-        float2 p0 = unpack_bf16(u.x), p1 = unpack_bf16(u.y), p2 = unpack_bf16(u.z), p3 = unpack_bf16(u.w);
-        float m[8] = {p0.x, p0.y, p1.x, p1.y, p2.x, p2.y, p3.x, p3.y};
+    for (int q = 0; q < 4; ++q) {
+      float t[8];
+      unpack8(u[q], t);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) v[q * 8 + t] = m[t] > 0.f ? v[q * 8 + t] : 0.f;
-      }
-    } else {
-      for (int j = 0; j < nvalid; ++j) v[j] = __bfloat162float(aux[j]) > 0.f ? v[j] : 0.f;
+      for (int k = 0; k < 8; ++k) v[q * 8 + k] = t[k] > 0.f ? v[q * 8 + k] : 0.f;
     }
   }
   if (f & ZL_EPI_RELU) {
@@ -116,36 +222,67 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int r, int c
     for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
   }
   if (f & ZL_EPI_OUT_F32) {
-    float* out = reinterpret_cast<float*>(a.D) + (size_t)r * a.N + c0;
+    float* out = reinterpret_cast<float*>(a.D) + (size_t)r0 * a.N + c0;
     const bool acc = (f & ZL_EPI_ACCUM) != 0;
-    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float4 w = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-        if (acc) {
-          float4 o = reinterpret_cast<float4*>(out)[q];
-          w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+    for (int h = 0; h < 2; ++h) {  // 16 fp32 columns = 64 bytes per staged row
+      if (acc) {
+        __syncwarp();
+        stg_load(stg, lane, reinterpret_cast<const uint8_t*>(out + h * 16), (size_t)a.N * 4, nrows);
+        __syncwarp();
+        uint4 u[4];
+        stg_get_row(stg, lane, u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[h * 16 + q * 4 + 0] += __uint_as_float(u[q].x);
+          v[h * 16 + q * 4 + 1] += __uint_as_float(u[q].y);
+          v[h * 16 + q * 4 + 2] += __uint_as_float(u[q].z);
+          v[h * 16 + q * 4 + 3] += __uint_as_float(u[q].w);
         }
-        reinterpret_cast<float4*>(out)[q] = w;
       }
-    } else {
-      for (int j = 0; j < nvalid; ++j) out[j] = acc ? out[j] + v[j] : v[j];
+      uint4 u[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        u[q] = make_uint4(__float_as_uint(v[h * 16 + q * 4]), __float_as_uint(v[h * 16 + q * 4 + 1]),
+                          __float_as_uint(v[h * 16 + q * 4 + 2]), __float_as_uint(v[h * 16 + q * 4 + 3]));
+      __syncwarp();
+      stg_put_row(stg, lane, u);
+      __syncwarp();
+      stg_store(stg, lane, reinterpret_cast<uint8_t*>(out + h * 16), (size_t)a.N * 4, nrows);
     }
   } else {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.D) + (size_t)r * a.N + c0;
-    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.D) + (size_t)r0 * a.N + c0;
+    uint4 u[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 u;
-        u.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
-        u.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
-        u.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
-        u.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
-        reinterpret_cast<uint4*>(out)[q] = u;
-      }
-    } else {
-      for (int j = 0; j < nvalid; ++j) out[j] = __float2bfloat16_rn(v[j]);
+    for (int q = 0; q < 4; ++q) {
+      u[q].x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+      u[q].y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+      u[q].z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+      u[q].w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
     }
+    __syncwarp();
+    stg_put_row(stg, lane, u);
+    __syncwarp();
+    stg_store(stg, lane, reinterpret_cast<uint8_t*>(out), (size_t)a.N * 2, nrows);
+  }
+}
+
+// Split-K partial chunk: raw fp32 accumulators to ws[split] (coalesced through staging).
+__device__ __forceinline__ void partial_chunk(const GemmArgs& a, uint32_t stg, int lane, int split, int r0, int c0,
+                                              const float (&v)[32]) {
+  const int nrows = min(32, a.M - r0);
+  float* out = a.ws + ((size_t)split * a.M + r0) * a.N + c0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint4 u[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      u[q] = make_uint4(__float_as_uint(v[h * 16 + q * 4]), __float_as_uint(v[h * 16 + q * 4 + 1]),
+                        __float_as_uint(v[h * 16 + q * 4 + 2]), __float_as_uint(v[h * 16 + q * 4 + 3]));
+    __syncwarp();
+    stg_put_row(stg, lane, u);
+    __syncwarp();
+    stg_store(stg, lane, reinterpret_cast<uint8_t*>(out + h * 16), (size_t)a.N * 4, nrows);
   }
 }
 
@@ -174,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 128); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps * 32); }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -263,9 +400,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 2..5)
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = quarter * 32 + lane;
+    // ------------------------------------------------ epilogue (warps 2 .. 2+kEpiWarps)
+    const int ew = warp - 2;
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int col_half = ew >> 2;            // which half of the BN columns this warp drains
+    const uint32_t stg = smem_u32(smem + L::EPI_OFF + ew * kStgBytes);
+    const bool fast_ok = ((args.flags & ZL_EPI_OUT_F32) ? (args.N % 4 == 0) : (args.N % 8 == 0)) &&
+                         (!(args.flags & ZL_EPI_ROPE) || args.epi.head_dim % 32 == 0);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
@@ -273,30 +414,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (tile / args.n_tiles_n) * BM, n0 = (tile % args.n_tiles_n) * BN;
       if (!bounded_wait(&acc_full[acc], acc_phase, DEV_TIMEOUT_ACC)) break;
       tc_fence_after();
-      const int r = m0 + row_in_tile;
+      const int r0 = m0 + quarter * 32;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = col_half * (BN / 2); c < (col_half + 1) * (BN / 2); c += 32) {
         uint32_t raw[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c), raw);
+        tmem_ld32(t_row + (uint32_t)c, raw);
         tmem_ld_wait();
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-        if (n0 + c >= args.N) continue;
+        const int c0 = n0 + c;
+        if (c0 >= args.N || r0 >= args.M) continue;
+        const bool full_chunk = fast_ok && (c0 + 32 <= args.N);
         if (args.splits > 1) {
-          if (r < args.M) {
-            float* out = args.ws + ((size_t)split * args.M + r) * args.N + n0 + c;
-            const int nvalid = min(32, args.N - n0 - c);
-            if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+          if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v);
+          else if (r0 + lane < args.M) {
+            float* out = args.ws + ((size_t)split * args.M + r0 + lane) * args.N + c0;
 #pragma unroll
-              for (int q = 0; q < 8; ++q)
-                reinterpret_cast<float4*>(out)[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-            } else {
-              for (int j = 0; j < nvalid; ++j) out[j] = v[j];
-            }
+            for (int j = 0; j < 32; ++j)
+              if (c0 + j < args.N) out[j] = v[j];
           }
+        } else if (full_chunk) {
+          epilogue_chunk(args, stg, lane, r0, c0, v);
         } else {
-          epilogue_store32(args, r, n0 + c, v);
+          epilogue_store32(args, r0 + lane, c0, v);
         }
       }
       tc_fence_before();

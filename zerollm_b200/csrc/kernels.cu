@@ -585,17 +585,33 @@ __global__ void norm_bwd_f32_kernel(const float* __restrict__ x, const float* __
 }
 
 // Column sums of bf16 [M, N] (bias gradients): per-block partials [nb][N].
-__global__ void colsum_bf16_kernel(const __nv_bfloat16* __restrict__ dy, float* __restrict__ part, int64_t M, int N,
-                                   int64_t rows_per_block) {
+// A block covers `rows_per_block` rows; its threads are laid out as
+// (N/8 column groups) x (256 / (N/8) row lanes) so every row is read with
+// coalesced 16-byte loads, four rows in flight per thread.
+__global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                          float* __restrict__ part, int64_t M, int N,
+                                                          int64_t rows_per_block) {
   const int groups = N / 8;
+  const int rpar = blockDim.x / groups;
+  const int grp = threadIdx.x % groups, rl = threadIdx.x / groups;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per_block;
   const int64_t r1 = r0 + rows_per_block < M ? r0 + rows_per_block : M;
-  const int rpar = blockDim.x / groups > 0 ? blockDim.x / groups : 1;
   extern __shared__ float sc[];  // [rpar][N]
-  const int grp = threadIdx.x % groups, rl = threadIdx.x / groups;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (rl < rpar) {
-    for (int64_t r = r0 + rl; r < r1; r += rpar) {
+    int64_t r = r0 + rl;
+    for (; r + 3 * rpar < r1; r += 4 * rpar) {
+      uint4 u[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) u[k] = __ldg(reinterpret_cast<const uint4*>(dy + (r + k * rpar) * N + grp * 8));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 a = unpack_bf16(u[k].x), b = unpack_bf16(u[k].y), c = unpack_bf16(u[k].z), d = unpack_bf16(u[k].w);
+        acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
+        acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
+      }
+    }
+    for (; r < r1; r += rpar) {
       float v[8];
       load8(dy + r * N + grp * 8, v);
 #pragma unroll
@@ -700,19 +716,25 @@ extern "C" zl_status zl_cross_entropy_fused_bf16(zl_bf16* logits, const int32_t*
   return check_launch("mean_kernel");
 }
 
+namespace {
+// ~4 waves of 148 SMs x 2 resident blocks; at least 64 rows per block.
+int64_t colsum_rows_per_block(int64_t M) {
+  int64_t rpb = (M + 1183) / 1184;
+  return rpb < 64 ? 64 : rpb;
+}
+}  // namespace
 extern "C" int64_t zl_colsum_workspace_floats(int64_t M, int N) {
-  const int64_t rpb = 256;
-  int64_t nb = (M + rpb - 1) / rpb;
-  return nb * N;
+  const int64_t rpb = colsum_rows_per_block(M);
+  return ((M + rpb - 1) / rpb) * N;
 }
 extern "C" zl_status zl_colsum_bf16(const zl_bf16* dy, float* db, float* workspace, int64_t M, int N, zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;
-  if (N % 8 || N / 8 > 1024) return set_error(ZL_EUNSUPPORTED, "colsum: N=%d", N);
-  const int64_t rpb = 256;
+  if (N % 8 || N / 8 > 256) return set_error(ZL_EUNSUPPORTED, "colsum: N=%d (multiple of 8, <= 2048)", N);
+  const int64_t rpb = colsum_rows_per_block(M);
   const int nb = (int)((M + rpb - 1) / rpb);
   const int groups = N / 8;
-  const int threads = groups >= 256 ? ((groups + 31) / 32) * 32 : (256 / groups) * groups;
-  const int rpar = threads / groups;
+  const int rpar = 256 / groups;
+  const int threads = rpar * groups;
   colsum_bf16_kernel<<<nb, threads, (size_t)rpar * N * sizeof(float), ST(s)>>>(
       reinterpret_cast<const __nv_bfloat16*>(dy), workspace, M, N, rpb);
   zl_status st = check_launch("colsum_bf16");

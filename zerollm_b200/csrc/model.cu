@@ -153,6 +153,12 @@ struct zl_model {
   int launches = 0;
   DistState dist;
   int64_t ready_prefix = 0;  // grads in [0, ready_prefix) are final for this step
+  // CUDA graph of zero_grad -> forward -> CE -> backward for one (ids, targets, loss, B, S) binding
+  int use_graph = 1;
+  cudaStream_t cap_stream = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  const void *g_ids = nullptr, *g_tgt = nullptr, *g_loss = nullptr;
+  int g_B = 0, g_S = 0, g_seen = 0, g_launches = 0;
 };
 
 namespace {
@@ -496,6 +502,8 @@ extern "C" zl_status zl_model_create(const zl_model_config* cfg, int64_t max_tok
 
 extern "C" zl_status zl_model_destroy(zl_model* M) {
   if (!M) return ZL_OK;
+  if (M->graph_exec) cudaGraphExecDestroy(M->graph_exec);
+  if (M->cap_stream) cudaStreamDestroy(M->cap_stream);
   if (M->dist.comm) {
     cudaStreamSynchronize(M->dist.comm_stream);
     ncclCommDestroy(M->dist.comm);
@@ -537,21 +545,85 @@ extern "C" zl_status zl_model_zero_grad(zl_model* M, zl_stream s) {
   return ZL_OK;
 }
 
-extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const int32_t* targets, int B, int S, float lr,
-                                         int update, float* loss_out, zl_stream stream) {
-  if (!M || !ids || !targets) return zl::set_error(ZL_EINVAL, "null argument");
-  TRY(check_shape(M, B, S));
-  cudaStream_t st = (cudaStream_t)stream;
+namespace {
+// zero_grad -> forward -> fused CE -> backward on `st` (gradient buckets are all-reduced on the
+// side stream as they become final when a communicator is attached).
+zl_status step_body(zl_model* M, const int32_t* ids, const int32_t* targets, int B, int S, float* loss_out,
+                    cudaStream_t st) {
   M->launches = 0;
   M->dist.next_bucket = 0;
-  TRY(zl_model_zero_grad(M, stream));
+  TRY(zl_model_zero_grad(M, st));
   M->launches++;
   TRY(forward(M, ids, B, S, nullptr, st));
   const int64_t T = (int64_t)B * S;
   TRY(zl_cross_entropy_fused_bf16(reinterpret_cast<zl_bf16*>(M->logits), targets, (int)T, M->cfg.vocab_size, 1e-8f,
                                   1.0f / (float)T, M->loss_rows, loss_out, st));
   M->launches += loss_out ? 2 : 1;
-  TRY(backward(M, ids, B, S, st));
+  return backward(M, ids, B, S, st);
+}
+
+// Replays (or captures, the second time a binding is seen) the step body as one CUDA graph.
+zl_status step_graph(zl_model* M, const int32_t* ids, const int32_t* targets, int B, int S, float* loss_out,
+                     cudaStream_t st) {
+  const bool same = M->graph_exec && M->g_ids == ids && M->g_tgt == targets && M->g_loss == loss_out &&
+                    M->g_B == B && M->g_S == S;
+  if (same) {
+    cudaError_t e = cudaGraphLaunch(M->graph_exec, st);
+    if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "cudaGraphLaunch: %s", cudaGetErrorString(e));
+    M->launches = M->g_launches;
+    return ZL_OK;
+  }
+  const bool seen = M->g_ids == ids && M->g_tgt == targets && M->g_loss == loss_out && M->g_B == B && M->g_S == S;
+  M->g_ids = ids; M->g_tgt = targets; M->g_loss = loss_out; M->g_B = B; M->g_S = S;
+  if (!seen) return step_body(M, ids, targets, B, S, loss_out, st);  // first sighting: run eagerly (warm-up)
+  if (M->graph_exec) { cudaGraphExecDestroy(M->graph_exec); M->graph_exec = nullptr; }
+  if (!M->cap_stream) cudaStreamCreateWithFlags(&M->cap_stream, cudaStreamNonBlocking);
+  cudaEvent_t ev;
+  cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  cudaEventRecord(ev, st);
+  cudaStreamWaitEvent(M->cap_stream, ev, 0);  // order capture-time work after the caller's stream
+  cudaStreamSynchronize(M->cap_stream);
+  cudaEventDestroy(ev);
+  cudaError_t e = cudaStreamBeginCapture(M->cap_stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "cudaStreamBeginCapture: %s", cudaGetErrorString(e));
+  zl_status body = step_body(M, ids, targets, B, S, loss_out, M->cap_stream);
+  cudaGraph_t graph = nullptr;
+  e = cudaStreamEndCapture(M->cap_stream, &graph);
+  if (body != ZL_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return body;
+  }
+  if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&M->graph_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    M->graph_exec = nullptr;
+    return zl::set_error(ZL_ECUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+  }
+  M->g_launches = M->launches;
+  e = cudaGraphLaunch(M->graph_exec, st);
+  if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "cudaGraphLaunch: %s", cudaGetErrorString(e));
+  return ZL_OK;
+}
+}  // namespace
+
+extern "C" zl_status zl_model_set_graph(zl_model* M, int enabled) {
+  if (!M) return zl::set_error(ZL_EINVAL, "null model");
+  M->use_graph = enabled;
+  if (!enabled && M->graph_exec) {
+    cudaGraphExecDestroy(M->graph_exec);
+    M->graph_exec = nullptr;
+  }
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const int32_t* targets, int B, int S, float lr,
+                                         int update, float* loss_out, zl_stream stream) {
+  if (!M || !ids || !targets) return zl::set_error(ZL_EINVAL, "null argument");
+  TRY(check_shape(M, B, S));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M->use_graph && !M->dist.comm) TRY(step_graph(M, ids, targets, B, S, loss_out, st));
+  else TRY(step_body(M, ids, targets, B, S, loss_out, st));
   if (update) TRY(adamw(M, lr, st));
   else if (M->dist.comm) {
     cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);

@@ -135,6 +135,9 @@ class ZeroLLM:
     def step(self, lr: float, stream=None):
         L.call("zl_model_step", self.h, lr, _stream(stream))
 
+    def set_graph(self, enabled: bool):
+        L.call("zl_model_set_graph", self.h, int(enabled))
+
     def last_launches(self) -> int:
         n = C.c_int(0)
         L.call("zl_model_last_launches", self.h, C.byref(n))
