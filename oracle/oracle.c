@@ -624,16 +624,18 @@ void orc_attention_backward(const float *q, const float *k, const float *v, int 
         }
 }
 
-/* Flash-style causal attention forward with the B200 kernel's order: 64-key
- * blocks, running max in base 2, probabilities rounded to bf16 before the
- * P.V product, row sum of the unrounded probabilities, output / sum. */
+/* Flash-style causal attention forward with the B200 kernels' order: key
+ * blocks of 128 when S is a multiple of 128 (tcgen05 kernel), else 64
+ * (mma.sync kernel); running max in base 2, probabilities rounded to bf16
+ * before the P.V product, row sum of the unrounded probabilities, output / sum. */
 static void attention_forward_blockwise(const float *q, const float *k, const float *v, int ld, float *o, int ldo,
                                         float *lse, int B, int S, int H, int Dh) {
     const float scale_log2 = (1.0f / sqrtf((float)Dh)) * 1.4426950408889634f;
 #pragma omp parallel
     {
         float *acc = (float *)malloc((size_t)Dh * sizeof(float));
-        float *sv = (float *)malloc(64 * sizeof(float));
+        const int KB = (S % 128 == 0) ? 128 : 64;
+        float *sv = (float *)malloc(128 * sizeof(float));
 #pragma omp for collapse(3) schedule(dynamic, 16)
         for (int b = 0; b < B; ++b)
             for (int h = 0; h < H; ++h)
@@ -641,8 +643,8 @@ static void attention_forward_blockwise(const float *q, const float *k, const fl
                     const float *qi = q + ((int64_t)b * S + i) * ld + (int64_t)h * Dh;
                     float m = -INFINITY, l = 0.f;
                     for (int d = 0; d < Dh; ++d) acc[d] = 0.f;
-                    for (int j0 = 0; j0 <= i; j0 += 64) {
-                        const int j1 = (j0 + 64 <= i + 1) ? j0 + 64 : i + 1;
+                    for (int j0 = 0; j0 <= i; j0 += KB) {
+                        const int j1 = (j0 + KB <= i + 1) ? j0 + KB : i + 1;
                         float mx = -INFINITY;
                         for (int j = j0; j < j1; ++j) {
                             const float *kj = k + ((int64_t)b * S + j) * ld + (int64_t)h * Dh;

@@ -159,9 +159,16 @@ def test_linear_api(K):
 
 
 # ------------------------------------------------------------------ attention
-@pytest.mark.parametrize("B,S,H", [(2, 128, 2), (1, 200, 3), (2, 512, 4)])
-def test_attention_bf16_vs_oracle(L, B, S, H):
-    import ctypes as C
+@pytest.mark.parametrize("kernel", ["default", "mma"])
+@pytest.mark.parametrize("B,S,H", [(2, 128, 2), (1, 200, 3), (2, 512, 4), (1, 1024, 2)])
+def test_attention_bf16_vs_oracle(L, B, S, H, kernel, monkeypatch):
+    """Flash attention fwd+bwd against the oracle.  "default" runs the tcgen05
+    kernels where the shape allows (S % 128 == 0) and mma.sync otherwise;
+    "mma" forces the mma.sync kernels."""
+    if kernel == "mma":
+        monkeypatch.setenv("ZL_ATTENTION_KERNEL", "mma")
+    else:
+        monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
     Dh, E = 64, H * 64
     T = B * S
     qkv = O.normal(T * 3 * E, 21) * 0.5
@@ -192,6 +199,39 @@ def test_attention_bf16_vs_oracle(L, B, S, H):
     assert rel(g[:, :E], dq.reshape(T, E)) < BF16_TOL
     assert rel(g[:, E:2 * E], dk.reshape(T, E)) < BF16_TOL
     assert rel(g[:, 2 * E:], dv.reshape(T, E)) < BF16_TOL
+
+
+def _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d):
+    Dh, E = 64, H * 64
+    dqkv = torch.empty(B * S * 3 * E, device="cuda", dtype=torch.bfloat16)
+    ws = torch.empty(L.load().zl_attention_workspace_floats(B, S, H, Dh), device="cuda")
+    L.call("zl_attention_backward_bf16", qkv_d.data_ptr(), o.data_ptr(), dO_d.data_ptr(), lse.data_ptr(),
+           dqkv.data_ptr(), ws.data_ptr(), B, S, H, Dh, cos_d.data_ptr(), sin_d.data_ptr(), None)
+    torch.cuda.synchronize()
+    return dqkv.float().cpu().numpy().reshape(B * S, 3 * E)
+
+
+@pytest.mark.parametrize("B,S,H", [(2, 256, 4), (1, 2048, 1)])
+def test_attention_bwd_rope_tcgen05_vs_mma(L, B, S, H, monkeypatch):
+    """The two backward kernels fold the inverse RoPE of dQ/dK in different
+    places (tcgen05: dK in the key-block epilogue; mma.sync: in its own
+    epilogue); both must give the same gradient as the forward's rotation."""
+    Dh, E = 64, H * 64
+    T = B * S
+    qkv_d = (torch.from_numpy(O.normal(T * 3 * E, 31)) * 0.5).bfloat16().cuda()
+    dO_d = torch.from_numpy(O.normal(T * E, 32)).bfloat16().cuda()
+    c, s_ = O.rope_table(S, Dh)
+    cos_d, sin_d = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+    monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
+    o = torch.empty(T * E, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * H * S, device="cuda")
+    L.call("zl_attention_forward_bf16", qkv_d.data_ptr(), o.data_ptr(), lse.data_ptr(), B, S, H, Dh, None)
+    g_tc = _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d)
+    monkeypatch.setenv("ZL_ATTENTION_KERNEL", "mma")
+    g_mma = _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d)
+    for part in range(3):
+        sl = slice(part * E, (part + 1) * E)
+        assert rel(g_tc[:, sl], g_mma[:, sl]) < BF16_TOL, part
 
 
 @pytest.mark.parametrize("ref_sem", [True, False])

@@ -4,9 +4,9 @@ The bars (BASELINE parity under bf16) are applied in two settings.
 
 A. Smooth setting: every FFN bias is set to +3 before the step, so every ReLU
    is active (pre-activations ~ 3 +- 0.45) and the step is a smooth function
-   of its inputs.  Against both the plain fp32 oracle and the oracle in bf16
-   storage emulation (same fp32 arithmetic, every tensor the GPU keeps in bf16
-   rounded at the same point, attention forward in the kernel's block order):
+   of its inputs.  Against the oracle in bf16 storage emulation (same fp32
+   arithmetic, every tensor the GPU keeps in bf16 rounded at the same point,
+   attention forward in the kernel's block order):
      * step loss within 1e-3 relative;
      * every tensor's gradient within 2e-2 (max|got-ref| / max|ref|);
      * AdamW-updated weights within 2e-2 over the elements whose reference
@@ -15,14 +15,17 @@ A. Smooth setting: every FFN bias is set to +3 before the step, so every ReLU
        lr*g/(|g|+eps), i.e. +-lr for |g| >> eps whatever |g| is, so an element
        whose gradient is below the floor may take either sign, and one with
        |g| ~ eps moves by an amount that tracks |g| itself.
-B. Default initialisation (biases 0), against the plain fp32 oracle:
+   Against the plain fp32 oracle (the reference semantics), in this setting
+   and in B:
      * step loss within 1e-3 relative;
      * each gradient within max(2e-2, 2 * n_t), where n_t is the oracle's own
-       fp32-vs-bf16-storage difference for that tensor.  n_t < 5e-3 for most
-       tensors; for the ReLU-gated W1/b1 gradients n_t ~ 0.1, because any
-       bf16-level difference in a pre-activation near zero flips that ReLU's
-       mask, and dW1/db1 sum such flips over every token.  Setting A is what
-       pins those tensors tightly.
+       fp32-vs-bf16-storage difference for that tensor (the effect of storing
+       activations in bf16 at all, measured without the GPU).  In the smooth
+       26M setting n_t is 0.018-0.033 (median 0.02) after six layers.
+B. Default initialisation (biases 0): for the ReLU-gated W1/b1 gradients
+   n_t ~ 0.1, because any bf16-level difference in a pre-activation near zero
+   flips that ReLU's mask and dW1/db1 sum such flips over every token; setting
+   A is what pins those tensors tightly.
 Initial weights are checked bit-exact (same seeded generator).
 """
 import numpy as np
@@ -119,22 +122,25 @@ def _oracle(om, p0, inp, tgt, B, S, emulate):
     return loss, g, p
 
 
-def _compare_step(c, B, S):
-    # A. smooth setting: every tensor within 2e-2 of both oracles
-    om, p0, inp, tgt, loss, g_gpu, p_gpu = _run(c, B, S, smooth=True)
-    for emulate in (True, False):
-        loss_r, g_r, p_r = _oracle(om, p0, inp, tgt, B, S, emulate)
-        tag = "smooth, bf16-emulated oracle" if emulate else "smooth, fp32 oracle"
-        assert abs(loss - loss_r) / abs(loss_r) < LOSS_TOL, (tag, loss, loss_r)
-        _check(tag, g_gpu, p_gpu, g_r, p_r, om)
-    # B. default init against fp32, bounded by the oracle's own bf16-storage effect
-    om, p0, inp, tgt, loss, g_gpu, p_gpu = _run(c, B, S, smooth=False)
+def _against_fp32(tag, om, p0, inp, tgt, B, S, loss, g_gpu, g_e):
     loss_r, g_r, _ = _oracle(om, p0, inp, tgt, B, S, False)
-    _, g_e, _ = _oracle(om, p0, inp, tgt, B, S, True)
-    assert abs(loss - loss_r) / abs(loss_r) < LOSS_TOL, (loss, loss_r)
+    assert abs(loss - loss_r) / abs(loss_r) < LOSS_TOL, (tag, loss, loss_r)
     offs, sizes, _, _ = O.param_layout(om)
     bound = [max(GRAD_TOL, 2 * rel(g_e[o:o + s], g_r[o:o + s])) for o, s in zip(offs, sizes)]
-    _check("default init, fp32 oracle", g_gpu, None, g_r, None, om, bound)
+    _check(tag, g_gpu, None, g_r, None, om, bound)
+
+
+def _compare_step(c, B, S):
+    # A. smooth setting: every tensor within 2e-2 of the bf16-storage oracle
+    om, p0, inp, tgt, loss, g_gpu, p_gpu = _run(c, B, S, smooth=True)
+    loss_e, g_e, p_e = _oracle(om, p0, inp, tgt, B, S, True)
+    assert abs(loss - loss_e) / abs(loss_e) < LOSS_TOL, (loss, loss_e)
+    _check("smooth, bf16-storage oracle", g_gpu, p_gpu, g_e, p_e, om)
+    _against_fp32("smooth, fp32 oracle", om, p0, inp, tgt, B, S, loss, g_gpu, g_e)
+    # B. default init against fp32, bounded by the oracle's own bf16-storage effect
+    om, p0, inp, tgt, loss, g_gpu, p_gpu = _run(c, B, S, smooth=False)
+    _, g_e, _ = _oracle(om, p0, inp, tgt, B, S, True)
+    _against_fp32("default init, fp32 oracle", om, p0, inp, tgt, B, S, loss, g_gpu, g_e)
 
 
 @pytest.mark.parametrize("idx", [0, 1])

@@ -21,6 +21,7 @@
 // reference-exact backward without the scale factor.
 #include <cfloat>
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -591,13 +592,35 @@ __global__ void mha_bwd_dqk_f32_kernel(const float* __restrict__ dO, const float
 }  // namespace zl
 
 // ============================================================== C ABI
+namespace zl {
+bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh,
+                      cudaStream_t st, zl_status* status);
+bool fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* lse, const float* Dsum,
+                      float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B, int S,
+                      int H, int Dh, cudaStream_t st, zl_status* status);
+}
 using namespace zl;
+
+namespace {
+// ZL_ATTENTION_KERNEL=mma forces the mma.sync kernels (kept for shapes the tcgen05 kernels do not
+// cover); read on every call so that one process can run both.
+bool force_mma_sync() {
+  const char* e = getenv("ZL_ATTENTION_KERNEL");
+  return e && e[0] == 'm';
+}
+}  // namespace
 
 extern "C" zl_status zl_attention_forward_bf16(const zl_bf16* qkv, zl_bf16* o, float* lse, int batch, int seq_len,
                                                int num_heads, int head_dim, zl_stream stream) {
   if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return set_error(ZL_EINVAL, "attention: invalid sizes");
   if (head_dim != fa::DH) return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64)", head_dim);
   if (!qkv || !o || !lse) return set_error(ZL_EINVAL, "attention: null pointer");
+  if (!force_mma_sync()) {
+    zl_status st = ZL_OK;
+    if (fa_fwd_tc_launch(reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(o), lse, batch,
+                         seq_len, num_heads, head_dim, (cudaStream_t)stream, &st))
+      return st;
+  }
   const int nq = (seq_len + fa::TILE - 1) / fa::TILE;
   const float scale_log2 = (1.0f / sqrtf((float)head_dim)) * fa::LOG2E;
   fa::fa_fwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nq), fa::THREADS, 0, (cudaStream_t)stream>>>(
@@ -631,13 +654,23 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
   if (s != ZL_OK) return s;
   const int nk = (seq_len + fa::TILE - 1) / fa::TILE;
   const float scale = 1.0f / sqrtf((float)head_dim);
-  cudaFuncSetAttribute(fa::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::BWD_SMEM);
-  fa::fa_bwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nk), fa::THREADS, fa::BWD_SMEM, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum, dq_acc,
-      reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch, seq_len, num_heads, scale,
-      scale * fa::LOG2E);
-  s = check_launch("fa_bwd_kernel");
-  if (s != ZL_OK) return s;
+  bool done = false;
+  if (!force_mma_sync()) {
+    zl_status ts = ZL_OK;
+    done = fa_bwd_tc_launch(reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o),
+                            lse, Dsum, dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch,
+                            seq_len, num_heads, head_dim, st, &ts);
+    if (done && ts != ZL_OK) return ts;
+  }
+  if (!done) {
+    cudaFuncSetAttribute(fa::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::BWD_SMEM);
+    fa::fa_bwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nk), fa::THREADS, fa::BWD_SMEM, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum, dq_acc,
+        reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch, seq_len, num_heads, scale,
+        scale * fa::LOG2E);
+    s = check_launch("fa_bwd_kernel");
+    if (s != ZL_OK) return s;
+  }
   const int64_t pairs = T * E / 2;
   fa::fa_bwd_post_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
       dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, scale);

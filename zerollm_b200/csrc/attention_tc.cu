@@ -1,0 +1,585 @@
+// attention_tc.cu -- causal flash-attention forward on tcgen05 / TMEM (sm_100a).
+//
+// One CTA computes 128 query rows of one (batch, head) against key blocks of
+// 128 (causal: blocks 0..q_block).  Per key block j:
+//   MMA warp:      S = Q K_j^T             (M=128, N=128, K=64; A, B K-major in smem; S fp32 in TMEM)
+//   softmax warps: row max / exp2 / row sum from S (two passes over TMEM), P = bf16(exp2(S - m))
+//                  written back over the S columns of TMEM; O rescaled in TMEM by exp2(m_old - m_new)
+//   MMA warp:      O += P V_j              (M=128, N=64, K=128; A = P from TMEM, B = V MN-major in smem)
+// Q/K/V tiles arrive by TMA (128-byte swizzle) straight from the packed qkv
+// activation [B*S, 3E]; K/V are double buffered.  TMEM holds two S/P buffers
+// (128 columns each) and O (64 columns): the MMA warp computes S for block j+1
+// while the softmax warps work on block j.  The softmax reads all 128 scores
+// of its row with one TMEM round trip and uses the MUFU ex2 instruction.
+// Every wait is bounded (common.cuh).  The result matches the mma.sync kernel's definition:
+// probabilities rounded to bf16 before P.V, row sums from the unrounded
+// values, lse = natural log-sum-exp of the scaled scores.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace zl {
+bool make_tma_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                  uint32_t box_rows);
+int sm_count_current();
+
+namespace fatc {
+
+constexpr int BQ = 128, BKV = 128, D = 64;
+constexpr int THREADS = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 softmax / epilogue
+constexpr int TILE_BYTES = 128 * 128; // 128 rows x 64 bf16
+constexpr int SMEM_Q = 0, SMEM_K = TILE_BYTES, SMEM_V = 3 * TILE_BYTES, SMEM_BAR = 5 * TILE_BYTES;
+constexpr int SMEM_TOTAL = SMEM_BAR + 128 + 1024;
+constexpr uint32_t TMEM_COLS = 512;   // S/P buffer b at [128 b, 128 b + 128), O at [256, 320)
+constexpr uint32_t O_COL = 256;
+constexpr uint32_t IDESC_S = make_idesc(1, 128, 128, 0, 0);  // bf16, M=128, N=128, A/B K-major
+constexpr uint32_t IDESC_O = make_idesc(1, 128, 64, 0, 1);   // bf16, M=128, N=64, A (TMEM) K-major, B MN-major
+
+enum : int { DEV_TIMEOUT_ATTN = 11 };
+
+__device__ __forceinline__ float fast_exp2(float x) {  // MUFU ex2 (inputs <= 0 here; -inf -> 0)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out,
+                     float* __restrict__ lse, int S, int H, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;   // [2]
+  uint64_t* kv_empty = bar + 3;  // [2]
+  uint64_t* s_full = bar + 5;    // [2]
+  uint64_t* p_full = bar + 7;
+  uint64_t* o_full = bar + 8;
+  uint64_t* drain = bar + 9;     // final commit: every MMA of this CTA has retired
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
+
+  const int E = H * D;
+  const int nq = S / BQ;
+  const int qb = nq - 1 - (int)(blockIdx.x % nq);  // heavy blocks first
+  const int bh = blockIdx.x / nq, b = bh / H, h = bh % H;
+  const int row0 = b * S + qb * BQ;                // first query row in the packed activation
+  const int nkv = qb + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_2d(smem + SMEM_Q, &tm, q_full, h * D, row0);
+      int issued = 0;
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!bounded_wait(&kv_empty[st], ph ^ 1u, DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        const int krow = b * S + j * BKV;
+        tma_load_2d(smem + SMEM_K + st * TILE_BYTES, &tm, &kv_full[st], E + h * D, krow);
+        tma_load_2d(smem + SMEM_V + st * TILE_BYTES, &tm, &kv_full[st], 2 * E + h * D, krow);
+        issued = j + 1;
+      }
+      // no copy may still be landing in shared memory when the CTA exits
+      bounded_wait(q_full, 0, DEV_TIMEOUT_ATTN);
+      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j)
+        bounded_wait(&kv_full[j & 1], (j >> 1) & 1, DEV_TIMEOUT_ATTN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t sq = smem_u32(smem + SMEM_Q);
+    auto issue_s = [&](int j) {  // S_j = Q K_j^T into buffer j & 1
+      const int st = j & 1;
+      const uint32_t sk = smem_u32(smem + SMEM_K + st * TILE_BYTES);
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16(tmem + (uint32_t)(st * BKV), smem_desc_sw128(sq + k * 32, 16, 1024),
+                   smem_desc_sw128(sk + k * 32, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[st]);
+      }
+      __syncwarp();
+    };
+    bool ok = bounded_wait_warp(q_full, 0, DEV_TIMEOUT_ATTN) && bounded_wait_warp(&kv_full[0], 0, DEV_TIMEOUT_ATTN);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+    }
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int st = j & 1;
+      if (j + 1 < nkv) {
+        // K_{j+1} resident, and buffer (j+1)&1 free: P_{j-1} (in that buffer) consumed by P.V of block j-1
+        if (!bounded_wait_warp(&kv_full[st ^ 1], ((j + 1) >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        if (j >= 1 && !bounded_wait_warp(o_full, (j - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        issue_s(j + 1);
+      }
+      if (!bounded_wait_warp(p_full, j & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t sv = smem_u32(smem + SMEM_V + st * TILE_BYTES);
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA: P columns k*8.., V rows k*16..
+          umma_f16_ts(tmem + O_COL, tmem + (uint32_t)(st * BKV + k * 8),
+                      smem_desc_sw128(sv + k * 16 * 128, TILE_BYTES, 1024), IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(o_full);
+        umma_commit(&kv_empty[st]);
+      }
+      __syncwarp();
+    }
+    // TMEM is freed below only after every MMA issued here has retired
+    if (lane == 0) umma_commit(drain);
+    __syncwarp();
+    bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (one row per thread)
+    const int quarter = warp & 3;
+    const int r_local = quarter * 32 + lane;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int q_pos = qb * BQ + r_local;  // position inside the sequence
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      if (!bounded_wait_warp(&s_full[st], (j >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t t_s = t_lane + (uint32_t)(st * BKV);
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + (uint32_t)(c * 32), r[c]);
+      tmem_ld_wait();
+      const bool diag = (j == nkv - 1);
+      const int key0 = j * BKV;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(r[c][i]) * scale_log2;
+          if (diag && key0 + c * 32 + i > q_pos) v = -INFINITY;
+          r[c][i] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
+        }
+      const float m_new = fmaxf(m, mx);
+      const float corr = fast_exp2(m - m_new);  // m = -inf on the first block -> 0
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = fast_exp2(__uint_as_float(r[c][i]) - m_new);
+          const float p1 = fast_exp2(__uint_as_float(r[c][i + 1]) - m_new);
+          sum += p0 + p1;
+          pk[i >> 1] = pack_bf16(p0, p1);
+        }
+        tmem_st16(t_s + (uint32_t)(c * 16), pk);  // P over the consumed S columns
+      }
+      l = l * corr + sum;
+      m = m_new;
+      if (j > 0) {  // O *= corr once the previous P.V has landed
+        if (!bounded_wait_warp(o_full, (j - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t o[2][32];
+        tmem_ld32(t_lane + O_COL, o[0]);
+        tmem_ld32(t_lane + O_COL + 32, o[1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * corr);
+        tmem_st32(t_lane + O_COL, o[0]);
+        tmem_st32(t_lane + O_COL + 32, o[1]);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // epilogue: O / l -> bf16, lse
+    if (ok && bounded_wait_warp(o_full, (nkv - 1) & 1, DEV_TIMEOUT_ATTN)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = out + (size_t)(row0 + r_local) * E + h * D;
+      uint32_t o[2][32];
+      tmem_ld32(t_lane + O_COL, o[0]);
+      tmem_ld32(t_lane + O_COL + 32, o[1]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 u;
+          u.x = pack_bf16(__uint_as_float(o[c][q * 8 + 0]) * inv, __uint_as_float(o[c][q * 8 + 1]) * inv);
+          u.y = pack_bf16(__uint_as_float(o[c][q * 8 + 2]) * inv, __uint_as_float(o[c][q * 8 + 3]) * inv);
+          u.z = pack_bf16(__uint_as_float(o[c][q * 8 + 4]) * inv, __uint_as_float(o[c][q * 8 + 5]) * inv);
+          u.w = pack_bf16(__uint_as_float(o[c][q * 8 + 6]) * inv, __uint_as_float(o[c][q * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) = u;
+        }
+      lse[((size_t)b * H + h) * S + qb * BQ + r_local] = (m + log2f(l)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+
+// ============================================================== backward
+// One CTA per (batch, head, 128-key block); it walks the query blocks from
+// the diagonal to the end of the sequence.  Per query block i:
+//   MMA:     S^T = K Q_i^T, dP^T = V dO_i^T                      (TMEM, fp32)
+//   softmax: P^T = exp2(S^T * scale_log2 - lse2[q]) (causal mask), dS^T = P^T (dP^T - D[q]);
+//            P^T and dS^T as bf16 back into TMEM (A operands), dS^T also into shared memory
+//   MMA:     dV += P^T dO_i, dK += dS^T Q_i  (A from TMEM, B MN-major in smem)
+//            dQ_i = dS K                      (A = dS^T in smem read MN-major, B = K MN-major)
+//   softmax warps: dQ_i (TMEM) -> fp32 vector atomics into the dq accumulator
+// At the end dK (times the softmax scale, optionally rotated back by RoPE) and dV
+// go to the packed gradient buffer.  The 1/sqrt(Dh) of dQ is applied by the caller's
+// post-processing pass together with its inverse RoPE.
+namespace bwd {
+constexpr int SM_K = 0, SM_V = TILE_BYTES, SM_Q = 2 * TILE_BYTES, SM_DO = 4 * TILE_BYTES, SM_DS = 6 * TILE_BYTES;
+constexpr int SM_VEC = 8 * TILE_BYTES;            // lse2[2][128], D[2][128]
+constexpr int SM_BAR = SM_VEC + 4 * 128 * 4;
+constexpr int SMEM_TOTAL = SM_BAR + 128 + 1024;
+constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
+constexpr uint32_t IDESC_SD = make_idesc(1, 128, 128, 0, 0);   // K Q^T / V dO^T: both K-major
+constexpr uint32_t IDESC_VK = make_idesc(1, 128, 64, 0, 1);    // dV/dK: A TMEM, B MN-major
+constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);     // dQ: A MN-major (dS^T), B MN-major (K)
+
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__global__ void __launch_bounds__(THREADS, 1)
+    fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                     const float* __restrict__ lse, const float* __restrict__ Dsum, float* __restrict__ dq_acc,
+                     __nv_bfloat16* __restrict__ d_qkv, const float* __restrict__ rope_cos,
+                     const float* __restrict__ rope_sin, int S, int H, float scale, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+  uint64_t* kv_full = bar + 0;
+  uint64_t* q_full = bar + 1;   // [2]
+  uint64_t* q_empty = bar + 3;  // [2]
+  uint64_t* sd_full = bar + 5;
+  uint64_t* ds_ready = bar + 6;
+  uint64_t* mm_done = bar + 7;
+  uint64_t* dq_free = bar + 8;
+  uint64_t* drain = bar + 9;    // final commit: every MMA of this CTA has retired
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
+  float* vec = reinterpret_cast<float*>(smem + SM_VEC);  // lse2[buf][128] at vec + buf*256, D at +128
+
+  const int E = H * D;
+  const int nk = S / BKV;
+  // key-block-major order: the CTAs of key block 0 (most query blocks) are launched first
+  const int nbh = (int)gridDim.x / nk;
+  const int kb = (int)blockIdx.x / nbh;
+  const int bh = (int)blockIdx.x % nbh, b = bh / H, h = bh % H;
+  const int krow0 = b * S + kb * BKV;
+  const int niter = nk - kb;               // query blocks kb .. nk-1
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
+    mbar_init(sd_full, 1);
+    mbar_init(ds_ready, 128);
+    mbar_init(mm_done, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_do);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_2d(smem + SM_K, &tm_qkv, kv_full, E + h * D, krow0);
+      tma_load_2d(smem + SM_V, &tm_qkv, kv_full, 2 * E + h * D, krow0);
+      int issued = 0;
+      for (int i = 0; i < niter; ++i) {
+        const int st = i & 1;
+        if (!bounded_wait(&q_empty[st], ((i >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES);
+        const int qrow = b * S + (kb + i) * BQ;
+        tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_qkv, &q_full[st], h * D, qrow);
+        tma_load_2d(smem + SM_DO + st * TILE_BYTES, &tm_do, &q_full[st], h * D, qrow);
+        issued = i + 1;
+      }
+      // no copy may still be landing in shared memory when the CTA exits
+      bounded_wait(kv_full, 0, DEV_TIMEOUT_ATTN);
+      for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i)
+        bounded_wait(&q_full[i & 1], (i >> 1) & 1, DEV_TIMEOUT_ATTN);
+    }
+  } else if (warp == 1) {
+    const uint32_t sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
+    bool ok = bounded_wait_warp(kv_full, 0, DEV_TIMEOUT_ATTN);
+    for (int i = 0; i < niter && ok; ++i) {
+      const int st = i & 1;
+      if (!bounded_wait_warp(&q_full[st], (i >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      if (i > 0 && !bounded_wait_warp(mm_done, (i - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          umma_f16(tmem + C_S, smem_desc_sw128(sk + k * 32, 16, 1024), smem_desc_sw128(sq + k * 32, 16, 1024),
+                   IDESC_SD, k > 0 ? 1u : 0u);
+          umma_f16(tmem + C_DP, smem_desc_sw128(sv + k * 32, 16, 1024), smem_desc_sw128(sdo + k * 32, 16, 1024),
+                   IDESC_SD, k > 0 ? 1u : 0u);
+        }
+        umma_commit(sd_full);
+      }
+      __syncwarp();
+      if (!bounded_wait_warp(ds_ready, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      if (i > 0 && !bounded_wait_warp(dq_free, (i - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < BQ / 16; ++k) {  // 16 queries per MMA
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          umma_f16_ts(tmem + C_DV, tmem + C_S + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
+                      IDESC_VK, acc);
+          umma_f16_ts(tmem + C_DK, tmem + C_DP + (uint32_t)(k * 8), smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024),
+                      IDESC_VK, acc);
+        }
+#pragma unroll
+        for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA
+          umma_f16(tmem + C_DQ, smem_desc_sw128(sds + k * 2048, TILE_BYTES, 1024),
+                   smem_desc_sw128(sk + k * 2048, TILE_BYTES, 1024), IDESC_Q, k > 0 ? 1u : 0u);
+        umma_commit(mm_done);
+        umma_commit(&q_empty[st]);
+      }
+      __syncwarp();
+    }
+    // TMEM is freed below only after every MMA issued here has retired
+    if (lane == 0) umma_commit(drain);
+    __syncwarp();
+    bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
+  } else {
+    const int quarter = warp & 3;
+    const int r_local = quarter * 32 + lane;      // key row (S^T / dP^T / dV / dK) and query row (dQ)
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int key = kb * BKV + r_local;           // position of this thread's key
+    uint8_t* sds = smem + SM_DS;
+    bool ok = true;
+    for (int i = 0; i < niter; ++i) {
+      const int qb = kb + i;
+      const int vb = i & 1;
+      // stage lse2 / D of this query block (read by every row)
+      {
+        const size_t base = ((size_t)b * H + h) * S + (size_t)qb * BQ + r_local;
+        vec[vb * 256 + r_local] = lse[base] * 1.4426950408889634f;
+        vec[vb * 256 + 128 + r_local] = Dsum[base];
+      }
+      // every softmax thread passes this barrier once per query block, also after a
+      // timeout (then it skips the work), so no thread is left waiting in it
+      named_sync_softmax();
+      ok = ok && bounded_wait_warp(sd_full, i & 1, DEV_TIMEOUT_ATTN);
+      if (!ok) continue;
+      tc_fence_after();
+      const float* lse2 = vec + vb * 256;
+      const float* Dv = lse2 + 128;
+      const bool diag = (i == 0);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rs[32], rd[32];
+        tmem_ld32(t_lane + C_S + (uint32_t)(c * 32), rs);
+        tmem_ld32(t_lane + C_DP + (uint32_t)(c * 32), rd);
+        tmem_ld_wait();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float p2[2], d2[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int q = c * 32 + j + t;
+            float p = fast_exp2(__uint_as_float(rs[j + t]) * scale_log2 - lse2[q]);
+            if (diag && key > qb * BQ + q) p = 0.f;
+            p2[t] = p;
+            d2[t] = p * (__uint_as_float(rd[j + t]) - Dv[q]);
+          }
+          pp[j >> 1] = pack_bf16(p2[0], p2[1]);
+          dd[j >> 1] = pack_bf16(d2[0], d2[1]);
+        }
+        tmem_st16(t_lane + C_S + (uint32_t)(c * 16), pp);
+        tmem_st16(t_lane + C_DP + (uint32_t)(c * 16), dd);
+        // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout the dQ MMA reads
+        const int half = c >> 1, jj0 = (c & 1) * 32;
+        uint8_t* rowp = sds + half * TILE_BYTES + r_local * 128;
+#pragma unroll
+        for (int pc = 0; pc < 4; ++pc) {
+          const int chunk = ((jj0 >> 3) + pc) ^ (r_local & 7);
+          *reinterpret_cast<uint4*>(rowp + chunk * 16) = make_uint4(dd[pc * 4], dd[pc * 4 + 1], dd[pc * 4 + 2], dd[pc * 4 + 3]);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      fence_async_smem();
+      mbar_arrive(ds_ready);
+      // dQ_i -> atomics (this thread: query row qb*128 + r_local)
+      ok = bounded_wait_warp(mm_done, i & 1, DEV_TIMEOUT_ATTN);
+      if (!ok) continue;
+      tc_fence_after();
+      {
+        uint32_t dq[2][32];
+        tmem_ld32(t_lane + C_DQ, dq[0]);
+        tmem_ld32(t_lane + C_DQ + 32, dq[1]);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(dq_free);
+        float* dst = dq_acc + ((size_t)b * S + (size_t)qb * BQ + r_local) * E + h * D;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + q * 4),
+                      make_float4(__uint_as_float(dq[c][q * 4]), __uint_as_float(dq[c][q * 4 + 1]),
+                                  __uint_as_float(dq[c][q * 4 + 2]), __uint_as_float(dq[c][q * 4 + 3])));
+      }
+    }
+    // dK (scaled, inverse RoPE) and dV for this key block
+    if (ok) {
+      tc_fence_after();
+      uint32_t dk[2][32], dv[2][32];
+      tmem_ld32(t_lane + C_DK, dk[0]);
+      tmem_ld32(t_lane + C_DK + 32, dk[1]);
+      tmem_ld32(t_lane + C_DV, dv[0]);
+      tmem_ld32(t_lane + C_DV + 32, dv[1]);
+      tmem_ld_wait();
+      const size_t row = (size_t)b * S + key;
+      __nv_bfloat16* dkrow = d_qkv + row * 3 * E + E + h * D;
+      __nv_bfloat16* dvrow = d_qkv + row * 3 * E + 2 * E + h * D;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float x[8], y[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            x[t] = __uint_as_float(dk[c][q * 8 + t]) * scale;
+            y[t] = __uint_as_float(dv[c][q * 8 + t]);
+          }
+          if (rope_cos) {
+#pragma unroll
+            for (int t = 0; t < 8; t += 2) {
+              const int pair = (c * 32 + q * 8 + t) >> 1;
+              const float cs = __ldg(rope_cos + (size_t)key * (D / 2) + pair);
+              const float sn = __ldg(rope_sin + (size_t)key * (D / 2) + pair);
+              const float a0 = x[t], a1 = x[t + 1];
+              x[t] = a0 * cs + a1 * sn;
+              x[t + 1] = -a0 * sn + a1 * cs;
+            }
+          }
+          uint4 uk, uv;
+          uk.x = pack_bf16(x[0], x[1]); uk.y = pack_bf16(x[2], x[3]); uk.z = pack_bf16(x[4], x[5]); uk.w = pack_bf16(x[6], x[7]);
+          uv.x = pack_bf16(y[0], y[1]); uv.y = pack_bf16(y[2], y[3]); uv.z = pack_bf16(y[4], y[5]); uv.w = pack_bf16(y[6], y[7]);
+          *reinterpret_cast<uint4*>(dkrow + c * 32 + q * 8) = uk;
+          *reinterpret_cast<uint4*>(dvrow + c * 32 + q * 8) = uv;
+        }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+}  // namespace bwd
+}  // namespace fatc
+
+// Returns true if the tcgen05 kernel handled the call.
+bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh,
+                      cudaStream_t st, zl_status* status) {
+  if (Dh != fatc::D || S % fatc::BQ != 0 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return false;
+  CUtensorMap tm;
+  const int E = H * Dh;
+  if (!make_tma_map(&tm, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128)) {
+    *status = set_error(ZL_ECUDA, "attention: cuTensorMapEncodeTiled failed");
+    return true;
+  }
+  cudaFuncSetAttribute(fatc::fa_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM_TOTAL);
+  const float scale_log2 = (1.0f / sqrtf((float)Dh)) * 1.4426950408889634f;
+  const int grid = B * H * (S / fatc::BQ);
+  fatc::fa_fwd_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM_TOTAL, st>>>(tm, out, lse, S, H, scale_log2);
+  *status = check_launch("fa_fwd_tc_kernel");
+  return true;
+}
+
+// Backward main pass (the caller runs the D / dq-zeroing pre-pass before and the dq post-pass after).
+bool fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* lse, const float* Dsum,
+                      float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B, int S,
+                      int H, int Dh, cudaStream_t st, zl_status* status) {
+  // TMA sources, the float4 dQ atomics and the 16-byte dK/dV stores all need 16-byte alignment
+  if (Dh != fatc::D || S % fatc::BQ != 0 ||
+      ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(d_o) | reinterpret_cast<uintptr_t>(dq_acc) |
+        reinterpret_cast<uintptr_t>(d_qkv)) & 15))
+    return false;
+  CUtensorMap tq, tdo;
+  const int E = H * Dh;
+  if (!make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128) ||
+      !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, 128)) {
+    *status = set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
+    return true;
+  }
+  cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       fatc::bwd::SMEM_TOTAL);
+  const float scale = 1.0f / sqrtf((float)Dh);
+  const int grid = B * H * (S / fatc::BKV);
+  fatc::bwd::fa_bwd_tc_kernel<<<grid, fatc::THREADS, fatc::bwd::SMEM_TOTAL, st>>>(
+      tq, tdo, lse, Dsum, dq_acc, d_qkv, rope_cos, rope_sin, S, H, scale, scale * 1.4426950408889634f);
+  *status = check_launch("fa_bwd_tc_kernel");
+  return true;
+}
+
+int attn_tc_dev_error_read_and_clear() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, zl_dev_error, sizeof(int));
+  if (v) {
+    int z = 0;
+    cudaMemcpyToSymbol(zl_dev_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace zl

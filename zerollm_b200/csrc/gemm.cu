@@ -623,6 +623,12 @@ cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CU
 
 }  // namespace
 
+bool make_tma_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                  uint32_t box_rows) {
+  return make_map(map, ptr, is_f32, inner, rows, box_inner, box_rows);
+}
+int sm_count_current() { return sm_count(); }
+
 int64_t gemm_workspace_floats(int M, int N, int K, int layout, int flags, bool f32_inputs) {
   (void)layout;
   const int BK = f32_inputs ? Elem<float>::BK : Elem<__nv_bfloat16>::BK;

@@ -640,9 +640,12 @@ extern "C" const char* zl_version(void) { return "zerollm_b200 0.1 (sm_100a)"; }
 
 namespace zl {
 int gemm_dev_error_read_and_clear();
+int attn_tc_dev_error_read_and_clear();
 }
 extern "C" zl_status zl_device_error(int* code_out) {
-  const int v = zl::gemm_dev_error_read_and_clear();
+  int v = zl::gemm_dev_error_read_and_clear();
+  const int a = zl::attn_tc_dev_error_read_and_clear();
+  if (!v) v = a;
   if (code_out) *code_out = v;
   return v ? set_error(ZL_ETIMEOUT, "device wait timed out (code %d)", v) : ZL_OK;
 }
