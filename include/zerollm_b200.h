@@ -192,6 +192,19 @@ zl_status zl_cross_entropy_fused_bf16(zl_bf16 *logits, const int32_t *targets, i
 /* Column sums of a bf16 [M, N] matrix accumulated into db (fp32): bias gradients. */
 zl_status zl_colsum_bf16(const zl_bf16 *dy, float *db, float *workspace, int64_t M, int N, zl_stream stream);
 int64_t zl_colsum_workspace_floats(int64_t M, int N);
+/* zl_colsum_bf16 without a workspace argument (no counterpart in the reference, whose bias
+ * gradients come from its own kernels).  It is for callers that cannot hand over device
+ * memory: code that must not call cudaMalloc/cudaFree because they can synchronise the whole
+ * device and stall work on other streams, and plugins whose host framework owns every device
+ * allocation.  The partial sums go to a fixed 4 MiB device array inside the library
+ * (zl_colsum_noalloc_max_floats() floats); the call allocates nothing.  Sizes whose
+ * zl_colsum_workspace_floats(M, N) exceeds that maximum return ZL_EINVAL with a message
+ * (e.g. M <= 32768 fits at N = 2048).  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) and keeps it; make that first call before any stream
+ * capture.  Calls on one device share the array: calls that overlap on the GPU (two streams,
+ * or two host threads) race and give wrong sums, so order them on one stream. */
+zl_status zl_colsum_bf16_noalloc(const zl_bf16 *dy, float *db, int64_t M, int N, zl_stream stream);
+int64_t zl_colsum_noalloc_max_floats(void);
 /* Flat AdamW over the whole parameter arena (adamw.cu:26-73 per element) with the gradient
  * multiplied by grad_scale (1/world for data parallelism), writing a bf16 shadow of the
  * updated parameters (may be NULL). */

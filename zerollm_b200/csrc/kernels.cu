@@ -12,6 +12,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -744,6 +745,53 @@ extern "C" zl_status zl_colsum_bf16(const zl_bf16* dy, float* db, float* workspa
   if (st != ZL_OK) return st;
   reduce_partials_kernel<<<nblk(N, 256), 256, 0, ST(s)>>>(workspace, nb, N, N, db, nullptr);
   return check_launch("colsum_reduce");
+}
+
+// ---------------------------------------------------------------- colsum without a caller workspace
+// The partial sums of zl_colsum_bf16 live in this fixed device array instead of a caller buffer.
+// Its device address is looked up once per device (cudaGetSymbolAddress) and kept; every partial
+// is written by the column-sum kernel before the reduction reads it, so nothing needs clearing.
+namespace {
+constexpr int64_t kColsumScratchFloats = int64_t(1) << 20;  // 4 MiB
+constexpr int kMaxDevices = 64;
+static __device__ __align__(256) float colsum_scratch[kColsumScratchFloats];
+std::mutex g_colsum_scratch_mu;
+float* g_colsum_scratch_ptr[kMaxDevices] = {};
+
+zl_status colsum_scratch_for_current_device(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ZL_ECUDA, "colsum_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(ZL_EUNSUPPORTED, "colsum_noalloc: device %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_colsum_scratch_mu);
+  if (!g_colsum_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, colsum_scratch);
+    if (e != cudaSuccess)
+      return set_error(ZL_ECUDA, "colsum_noalloc: cudaGetSymbolAddress on device %d: %s", dev, cudaGetErrorString(e));
+    g_colsum_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_colsum_scratch_ptr[dev];
+  return ZL_OK;
+}
+}  // namespace
+
+extern "C" int64_t zl_colsum_noalloc_max_floats(void) { return kColsumScratchFloats; }
+
+extern "C" zl_status zl_colsum_bf16_noalloc(const zl_bf16* dy, float* db, int64_t M, int N, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;
+  if (N % 8 || N / 8 > 256) return set_error(ZL_EUNSUPPORTED, "colsum_noalloc: N=%d (multiple of 8, <= 2048)", N);
+  if (!dy || !db) return set_error(ZL_EINVAL, "colsum_noalloc: null pointer");
+  const int64_t need = zl_colsum_workspace_floats(M, N);
+  if (need > kColsumScratchFloats)
+    return set_error(ZL_EINVAL,
+                     "colsum_noalloc: M=%lld, N=%d needs %lld floats of scratch; the static maximum is %lld "
+                     "(use zl_colsum_bf16 with a workspace)",
+                     (long long)M, N, (long long)need, (long long)kColsumScratchFloats);
+  float* scratch = nullptr;
+  const zl_status st = colsum_scratch_for_current_device(&scratch);
+  if (st != ZL_OK) return st;
+  return zl_colsum_bf16(dy, db, scratch, M, N, s);
 }
 
 extern "C" zl_status zl_adamw_flat(float* params, const float* grads, float* m, float* v, zl_bf16* params_bf16, int64_t n,

@@ -83,6 +83,8 @@ SIGNATURES = {
     "zl_cross_entropy_fused_bf16": (i32, [vp, vp, i32, i32, f32, f32, vp, vp, vp]),
     "zl_colsum_bf16": (i32, [vp, vp, vp, i64, i32, vp]),
     "zl_colsum_workspace_floats": (i64, [i64, i32]),
+    "zl_colsum_bf16_noalloc": (i32, [vp, vp, i64, i32, vp]),
+    "zl_colsum_noalloc_max_floats": (i64, []),
     "zl_adamw_flat": (i32, [vp, vp, vp, vp, vp, i64] + [f32] * 8 + [vp]),
     "zl_f32_to_bf16": (i32, [vp, vp, i64, vp]),
     "zl_model_create": (i32, [C.POINTER(ModelConfig), i64, u64, f32, C.POINTER(vp)]),
