@@ -384,7 +384,7 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform ids in [0,6400), N(0,0.02) weights)",
-        "config": {"workload": "26M ZeroLLM training step (RMSNorm, RoPE, untied head), batch 16 x seq 2048 per GPU",
+        "config": {"workload": f"26M ZeroLLM training step (RMSNorm, RoPE, untied head), batch {B} x seq {S} per GPU",
                    "model": "zerollm-26m", "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2 (per-step working set ~3 GB)"},
         "mfu": round(value * FLOP_PER_TOKEN / world / (pk["bf16_tflops"] * 1e12), 4),
