@@ -233,9 +233,11 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
 }
 
 // ----------------------------------------------------------------- backward
-// D[b,h,i] = sum_d dO[i,d] * O[i,d]; also zeroes the fp32 dq accumulator.
+// D[b,h,i] = sum_d dO[i,d] * O[i,d]; also zeroes the fp32 dq accumulator and, when `nl` is
+// given, writes nl[b,h,i] = -lse[b,h,i] * log2(e) (the exponent offset the tcgen05 kernel reads).
 __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
-                                  float* __restrict__ Dsum, float* __restrict__ dq_acc, int B, int S, int H) {
+                                  const float* __restrict__ lse, float* __restrict__ Dsum, float* __restrict__ nl,
+                                  float* __restrict__ dq_acc, int B, int S, int H) {
   const int E = H * DH;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);  // one warp per (token, head)
   if (row >= (int64_t)B * S * H) return;
@@ -248,7 +250,10 @@ __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __n
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   const int64_t b = t / S, i = t % S;
-  if (lane == 0) Dsum[(b * H + h) * S + i] = s;
+  if (lane == 0) {
+    Dsum[(b * H + h) * S + i] = s;
+    if (nl) nl[(b * H + h) * S + i] = -lse[(b * H + h) * S + i] * LOG2E;
+  }
   *reinterpret_cast<float2*>(dq_acc + t * E + h * DH + 2 * lane) = make_float2(0.f, 0.f);
 }
 
@@ -443,15 +448,18 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
 }
 
 // dq (fp32 accumulator) -> scaled bf16 into the q part of d_qkv (optional inverse RoPE)
+// dQ = scale * dq_acc, rotated back by RoPE, into the Q columns of d_qkv.  dq_acc is [T, E]
+// (token-major, the mma.sync kernel) or [B, H, S, Dh] (head-major, the tcgen05 kernel).
 __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ d_qkv,
                                    const float* rope_cos, const float* rope_sin, int64_t T, int S, int H,
-                                   float scale) {
+                                   float scale, int head_major) {
   const int E = H * DH;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per pair
   if (idx >= T * E / 2) return;
   const int64_t t = idx / (E / 2);
   const int c = (int)(idx % (E / 2)) * 2;
-  const float2 v = *reinterpret_cast<const float2*>(dq_acc + t * E + c);
+  const int64_t src = head_major ? (((t / S) * H + c / DH) * S + t % S) * DH + c % DH : t * E + c;
+  const float2 v = *reinterpret_cast<const float2*>(dq_acc + src);
   float x0 = v.x * scale, x1 = v.y * scale;
   if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, (int)(t % S), (c % DH) >> 1);
   *reinterpret_cast<uint32_t*>(d_qkv + t * 3 * E + c) = pack_bf16(x0, x1);
@@ -595,9 +603,10 @@ __global__ void mha_bwd_dqk_f32_kernel(const float* __restrict__ dO, const float
 namespace zl {
 bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh,
                       cudaStream_t st, zl_status* status);
-bool fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* lse, const float* Dsum,
-                      float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B, int S,
-                      int H, int Dh, cudaStream_t st, zl_status* status);
+bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, const void* d_qkv, int S, int Dh);
+zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
+                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
+                           int S, int H, int Dh, cudaStream_t st);
 }
 using namespace zl;
 
@@ -630,7 +639,7 @@ extern "C" zl_status zl_attention_forward_bf16(const zl_bf16* qkv, zl_bf16* o, f
 }
 
 extern "C" int64_t zl_attention_workspace_floats(int batch, int seq_len, int num_heads, int head_dim) {
-  return (int64_t)batch * seq_len * num_heads * head_dim + (int64_t)batch * num_heads * seq_len;
+  return (int64_t)batch * seq_len * num_heads * head_dim + 2 * (int64_t)batch * num_heads * seq_len;
 }
 
 extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o,
@@ -646,23 +655,22 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
   const int E = num_heads * head_dim;
   float* dq_acc = workspace;
   float* Dsum = workspace + T * E;
+  float* nl = Dsum + (int64_t)batch * num_heads * seq_len;
+  const bool tc = !force_mma_sync() && fa_bwd_tc_supported(qkv, d_o, dq_acc, d_qkv, seq_len, head_dim);
   const int64_t rows = T * num_heads;
   fa::fa_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(d_o), Dsum, dq_acc, batch,
-      seq_len, num_heads);
+      reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum,
+      tc ? nl : nullptr, dq_acc, batch, seq_len, num_heads);
   zl_status s = check_launch("fa_bwd_pre_kernel");
   if (s != ZL_OK) return s;
-  const int nk = (seq_len + fa::TILE - 1) / fa::TILE;
   const float scale = 1.0f / sqrtf((float)head_dim);
-  bool done = false;
-  if (!force_mma_sync()) {
-    zl_status ts = ZL_OK;
-    done = fa_bwd_tc_launch(reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o),
-                            lse, Dsum, dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch,
-                            seq_len, num_heads, head_dim, st, &ts);
-    if (done && ts != ZL_OK) return ts;
-  }
-  if (!done) {
+  if (tc) {
+    s = fa_bwd_tc_launch(reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), nl,
+                         Dsum, dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch, seq_len,
+                         num_heads, head_dim, st);
+    if (s != ZL_OK) return s;
+  } else {
+    const int nk = (seq_len + fa::TILE - 1) / fa::TILE;
     cudaFuncSetAttribute(fa::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::BWD_SMEM);
     fa::fa_bwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nk), fa::THREADS, fa::BWD_SMEM, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum, dq_acc,
@@ -673,7 +681,7 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
   }
   const int64_t pairs = T * E / 2;
   fa::fa_bwd_post_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
-      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, scale);
+      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, scale, tc ? 1 : 0);
   return check_launch("fa_bwd_post_kernel");
 }
 

@@ -254,33 +254,59 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 
 // ============================================================== backward
-// One CTA per (batch, head, 128-key block); it walks the query blocks from
-// the diagonal to the end of the sequence.  Per query block i:
-//   MMA:     S^T = K Q_i^T, dP^T = V dO_i^T                      (TMEM, fp32)
-//   softmax: P^T = exp2(S^T * scale_log2 - lse2[q]) (causal mask), dS^T = P^T (dP^T - D[q]);
-//            P^T and dS^T as bf16 back into TMEM (A operands), dS^T also into shared memory
-//   MMA:     dV += P^T dO_i, dK += dS^T Q_i  (A from TMEM, B MN-major in smem)
-//            dQ_i = dS K                      (A = dS^T in smem read MN-major, B = K MN-major)
-//   softmax warps: dQ_i (TMEM) -> fp32 vector atomics into the dq accumulator
-// At the end dK (times the softmax scale, optionally rotated back by RoPE) and dV
-// go to the packed gradient buffer.  The 1/sqrt(Dh) of dQ is applied by the caller's
-// post-processing pass together with its inverse RoPE.
+// One CTA per (batch, head, 128-key block); it walks the query blocks from the diagonal to the end
+// of the sequence.  Per query block i:
+//   MMA:     S^T = K Q_i^T, dP^T = V dO_i^T                                      (TMEM, fp32)
+//   softmax: P^T = exp2(S^T * scale_log2 - lse2[q]) with the causal mask, dS^T = P^T (dP^T - D[q]);
+//            P^T and dS^T go back into TMEM as bf16 (A operands of the next MMAs), dS^T also to
+//            shared memory
+//   MMA:     dV += P^T dO_i, dK += dS^T Q_i  (A from TMEM, B MN-major in shared memory)
+//            dQ_i = dS K                      (A = dS^T read MN-major, B = K MN-major)
+//   softmax warps: dQ_i (TMEM) -> shared memory -> one bulk reduce-add into the fp32 dQ accumulator
+//            ([B, H, S, Dh], so the 128 x 64 tile is contiguous)
+// Eight softmax warps: warps w and w+4 share the TMEM lanes of quadrant w % 4 and split the 128
+// query columns into halves.  Each half packs its bf16 P^T / dS^T into its own 64-column range
+// (queries 0-63 -> columns 0-31, queries 64-127 -> columns 64-95), so the two warps never touch
+// each other's columns; the MMA for query chunk k reads its A operand at (k/4)*64 + (k%4)*8.
+// The per-query rows nl = -lse*log2(e) and D = rowsum(dO*O) arrive by bulk copy with Q_i / dO_i.
+// At the end dK (times the softmax scale, rotated back by RoPE when tables are given) and dV go to
+// the packed gradient buffer.  dQ's scale and inverse RoPE are applied by the caller's post pass.
 namespace bwd {
+constexpr int NSOFT = 8;
+constexpr int THREADS_B = 64 + 32 * NSOFT;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
 constexpr int SM_K = 0, SM_V = TILE_BYTES, SM_Q = 2 * TILE_BYTES, SM_DO = 4 * TILE_BYTES, SM_DS = 6 * TILE_BYTES;
-constexpr int SM_VEC = 8 * TILE_BYTES;            // lse2[2][128], D[2][128]
-constexpr int SM_BAR = SM_VEC + 4 * 128 * 4;
+constexpr int DQ_BYTES = BQ * D * 4;                 // one fp32 dQ tile: two [128][32] boxes, 128-byte swizzle
+constexpr int SM_DQ = 8 * TILE_BYTES;                // [2] dQ tiles
+constexpr int VEC_BYTES = 2 * BQ * 4;                // nl[128], D[128] of one query block
+constexpr int SM_VEC = SM_DQ + 2 * DQ_BYTES;         // [2] stages
+constexpr int SM_BAR = SM_VEC + 2 * VEC_BYTES;
 constexpr int SMEM_TOTAL = SM_BAR + 128 + 1024;
+static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
 constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
-constexpr uint32_t IDESC_SD = make_idesc(1, 128, 128, 0, 0);   // K Q^T / V dO^T: both K-major
-constexpr uint32_t IDESC_VK = make_idesc(1, 128, 64, 0, 1);    // dV/dK: A TMEM, B MN-major
-constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);     // dQ: A MN-major (dS^T), B MN-major (K)
+constexpr uint32_t IDESC_SD = make_idesc(1, 128, 128, 0, 0);  // K Q^T / V dO^T: both K-major
+constexpr uint32_t IDESC_VK = make_idesc(1, 128, 64, 0, 1);   // dV/dK: A TMEM, B MN-major
+constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);    // dQ: A MN-major (dS^T), B MN-major (K)
 
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// Element-wise add of a shared-memory box into global memory through the tensor map (fp32).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+// P^T / dS^T column of query chunk k (16 queries, 8 packed columns)
+__device__ __forceinline__ uint32_t packed_col(int k) { return (uint32_t)((k >> 2) * 64 + (k & 3) * 8); }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS_B, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                     const float* __restrict__ lse, const float* __restrict__ Dsum, float* __restrict__ dq_acc,
+                     const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ nl_g,
+                     const float* __restrict__ Dsum,
                      __nv_bfloat16* __restrict__ d_qkv, const float* __restrict__ rope_cos,
                      const float* __restrict__ rope_sin, int S, int H, float scale, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
@@ -296,7 +322,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* dq_free = bar + 8;
   uint64_t* drain = bar + 9;    // final commit: every MMA of this CTA has retired
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
-  float* vec = reinterpret_cast<float*>(smem + SM_VEC);  // lse2[buf][128] at vec + buf*256, D at +128
 
   const int E = H * D;
   const int nk = S / BKV;
@@ -305,20 +330,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int kb = (int)blockIdx.x / nbh;
   const int bh = (int)blockIdx.x % nbh, b = bh / H, h = bh % H;
   const int krow0 = b * S + kb * BKV;
-  const int niter = nk - kb;               // query blocks kb .. nk-1
+  const int niter = nk - kb;  // query blocks kb .. nk-1
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t row_base = (size_t)bh * S;  // (b, h) rows of nl, D and the dQ accumulator
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
     mbar_init(sd_full, 1);
-    mbar_init(ds_ready, 128);
+    mbar_init(ds_ready, 32 * NSOFT);
     mbar_init(mm_done, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, 32 * NSOFT);
     mbar_init(drain, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -338,10 +365,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int i = 0; i < niter; ++i) {
         const int st = i & 1;
         if (!bounded_wait(&q_empty[st], ((i >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES);
-        const int qrow = b * S + (kb + i) * BQ;
+        mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES + VEC_BYTES);
+        const int qb = kb + i;
+        const int qrow = b * S + qb * BQ;
         tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_qkv, &q_full[st], h * D, qrow);
         tma_load_2d(smem + SM_DO + st * TILE_BYTES, &tm_do, &q_full[st], h * D, qrow);
+        float* vec = reinterpret_cast<float*>(smem + SM_VEC + st * VEC_BYTES);
+        bulk_load(vec, nl_g + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
+        bulk_load(vec + BQ, Dsum + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
         issued = i + 1;
       }
       // no copy may still be landing in shared memory when the CTA exits
@@ -355,6 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int i = 0; i < niter && ok; ++i) {
       const int st = i & 1;
       if (!bounded_wait_warp(&q_full[st], (i >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      // S / dP regions are read (as P^T / dS^T) by the previous block's dV / dK MMAs
       if (i > 0 && !bounded_wait_warp(mm_done, (i - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
       tc_fence_after();
       const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
@@ -376,9 +408,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int k = 0; k < BQ / 16; ++k) {  // 16 queries per MMA
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          umma_f16_ts(tmem + C_DV, tmem + C_S + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
+          umma_f16_ts(tmem + C_DV, tmem + C_S + packed_col(k), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
                       IDESC_VK, acc);
-          umma_f16_ts(tmem + C_DK, tmem + C_DP + (uint32_t)(k * 8), smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024),
+          umma_f16_ts(tmem + C_DK, tmem + C_DP + packed_col(k), smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024),
                       IDESC_VK, acc);
         }
 #pragma unroll
@@ -396,125 +428,127 @@ __global__ void __launch_bounds__(THREADS, 1)
     bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
   } else {
     const int quarter = warp & 3;
+    const int col_half = (warp - 2) >> 2;         // query columns [64*col_half, 64*col_half + 64)
     const int r_local = quarter * 32 + lane;      // key row (S^T / dP^T / dV / dK) and query row (dQ)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     const int key = kb * BKV + r_local;           // position of this thread's key
+    const bool elected = (threadIdx.x == 64);     // issues the dQ bulk reductions
     uint8_t* sds = smem + SM_DS;
     bool ok = true;
     for (int i = 0; i < niter; ++i) {
       const int qb = kb + i;
-      const int vb = i & 1;
-      // stage lse2 / D of this query block (read by every row)
-      {
-        const size_t base = ((size_t)b * H + h) * S + (size_t)qb * BQ + r_local;
-        vec[vb * 256 + r_local] = lse[base] * 1.4426950408889634f;
-        vec[vb * 256 + 128 + r_local] = Dsum[base];
-      }
-      // every softmax thread passes this barrier once per query block, also after a
-      // timeout (then it skips the work), so no thread is left waiting in it
-      named_sync_softmax();
-      ok = ok && bounded_wait_warp(sd_full, i & 1, DEV_TIMEOUT_ATTN);
-      if (!ok) continue;
-      tc_fence_after();
-      const float* lse2 = vec + vb * 256;
-      const float* Dv = lse2 + 128;
+      const int st = i & 1;
+      const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + st * VEC_BYTES);
       const bool diag = (i == 0);
+      ok = ok && bounded_wait_warp(sd_full, i & 1, DEV_TIMEOUT_ATTN);
+      if (ok) {
+        tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t rs[32], rd[32];
-        tmem_ld32(t_lane + C_S + (uint32_t)(c * 32), rs);
-        tmem_ld32(t_lane + C_DP + (uint32_t)(c * 32), rd);
-        tmem_ld_wait();
-        uint32_t pp[16], dd[16];
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = col_half * 2 + cc;        // 32-query chunk
+          uint32_t rs[32], rd[32];
+          tmem_ld32(t_lane + C_S + (uint32_t)(c * 32), rs);
+          tmem_ld32(t_lane + C_DP + (uint32_t)(c * 32), rd);
+          tmem_ld_wait();
+          uint32_t pp[16], dd[16];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          float p2[2], d2[2];
+          for (int j = 0; j < 32; j += 4) {
+            const float4 nl4 = *reinterpret_cast<const float4*>(vec + c * 32 + j);
+            const float4 d4 = *reinterpret_cast<const float4*>(vec + BQ + c * 32 + j);
+            const float nlv[4] = {nl4.x, nl4.y, nl4.z, nl4.w};
+            const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+            float p[4], d[4];
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int q = c * 32 + j + t;
-            float p = fast_exp2(__uint_as_float(rs[j + t]) * scale_log2 - lse2[q]);
-            if (diag && key > qb * BQ + q) p = 0.f;
-            p2[t] = p;
-            d2[t] = p * (__uint_as_float(rd[j + t]) - Dv[q]);
+            for (int t = 0; t < 4; ++t) {
+              p[t] = fast_exp2(fmaf(__uint_as_float(rs[j + t]), scale_log2, nlv[t]));
+              if (diag && r_local > c * 32 + j + t) p[t] = 0.f;
+              d[t] = p[t] * (__uint_as_float(rd[j + t]) - dv[t]);
+            }
+            pp[j >> 1] = pack_bf16(p[0], p[1]);
+            pp[(j >> 1) + 1] = pack_bf16(p[2], p[3]);
+            dd[j >> 1] = pack_bf16(d[0], d[1]);
+            dd[(j >> 1) + 1] = pack_bf16(d[2], d[3]);
           }
-          pp[j >> 1] = pack_bf16(p2[0], p2[1]);
-          dd[j >> 1] = pack_bf16(d2[0], d2[1]);
-        }
-        tmem_st16(t_lane + C_S + (uint32_t)(c * 16), pp);
-        tmem_st16(t_lane + C_DP + (uint32_t)(c * 16), dd);
-        // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout the dQ MMA reads
-        const int half = c >> 1, jj0 = (c & 1) * 32;
-        uint8_t* rowp = sds + half * TILE_BYTES + r_local * 128;
+          const uint32_t pcol = (uint32_t)(col_half * 64 + cc * 16);
+          tmem_st16(t_lane + C_S + pcol, pp);
+          tmem_st16(t_lane + C_DP + pcol, dd);
+          // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout the dQ MMA reads
+          uint8_t* rowp = sds + col_half * TILE_BYTES + r_local * 128;
 #pragma unroll
-        for (int pc = 0; pc < 4; ++pc) {
-          const int chunk = ((jj0 >> 3) + pc) ^ (r_local & 7);
-          *reinterpret_cast<uint4*>(rowp + chunk * 16) = make_uint4(dd[pc * 4], dd[pc * 4 + 1], dd[pc * 4 + 2], dd[pc * 4 + 3]);
+          for (int pc = 0; pc < 4; ++pc) {
+            const int chunk = (cc * 4 + pc) ^ (r_local & 7);
+            *reinterpret_cast<uint4*>(rowp + chunk * 16) =
+                make_uint4(dd[pc * 4], dd[pc * 4 + 1], dd[pc * 4 + 2], dd[pc * 4 + 3]);
+          }
         }
+        tmem_st_wait();
+        tc_fence_before();
+        fence_async_smem();
+        mbar_arrive(ds_ready);
       }
-      tmem_st_wait();
-      tc_fence_before();
-      fence_async_smem();
-      mbar_arrive(ds_ready);
-      // dQ_i -> atomics (this thread: query row qb*128 + r_local)
-      ok = bounded_wait_warp(mm_done, i & 1, DEV_TIMEOUT_ATTN);
-      if (!ok) continue;
-      tc_fence_after();
-      {
-        uint32_t dq[2][32];
-        tmem_ld32(t_lane + C_DQ, dq[0]);
-        tmem_ld32(t_lane + C_DQ + 32, dq[1]);
+      // dQ_i: TMEM -> two swizzled [128][32] boxes (row = query) -> TMA reduce-add into dq_acc
+      ok = ok && bounded_wait_warp(mm_done, i & 1, DEV_TIMEOUT_ATTN);
+      uint8_t* dq_tile = smem + SM_DQ + st * DQ_BYTES;
+      if (ok) {
+        tc_fence_after();
+        uint32_t dq[32];
+        tmem_ld32(t_lane + C_DQ + (uint32_t)(col_half * 32), dq);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(dq_free);
-        float* dst = dq_acc + ((size_t)b * S + (size_t)qb * BQ + r_local) * E + h * D;
+        uint8_t* rowp = dq_tile + col_half * (DQ_BYTES / 2) + r_local * 128;
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + q * 4),
-                      make_float4(__uint_as_float(dq[c][q * 4]), __uint_as_float(dq[c][q * 4 + 1]),
-                                  __uint_as_float(dq[c][q * 4 + 2]), __uint_as_float(dq[c][q * 4 + 3])));
+        for (int k = 0; k < 8; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
+          *reinterpret_cast<uint4*>(rowp + ((k ^ (r_local & 7)) * 16)) =
+              make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
+      }
+      fence_async_smem();
+      named_sync_softmax();  // every softmax thread, every block (also after a timeout)
+      if (elected && ok) {
+        const int y = (int)(row_base + (size_t)qb * BQ);
+        tma_reduce_add_2d(&tm_dq, dq_tile, 0, y);
+        tma_reduce_add_2d(&tm_dq, dq_tile + DQ_BYTES / 2, 32, y);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        // the tile written two blocks from now reuses the buffer of the reductions before these
+        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
       }
     }
-    // dK (scaled, inverse RoPE) and dV for this key block
+    if (elected) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    // dK (scaled, inverse RoPE) and dV for this key block: columns [32*col_half, 32*col_half + 32)
     if (ok) {
       tc_fence_after();
-      uint32_t dk[2][32], dv[2][32];
-      tmem_ld32(t_lane + C_DK, dk[0]);
-      tmem_ld32(t_lane + C_DK + 32, dk[1]);
-      tmem_ld32(t_lane + C_DV, dv[0]);
-      tmem_ld32(t_lane + C_DV + 32, dv[1]);
+      uint32_t dk[32], dv[32];
+      tmem_ld32(t_lane + C_DK + (uint32_t)(col_half * 32), dk);
+      tmem_ld32(t_lane + C_DV + (uint32_t)(col_half * 32), dv);
       tmem_ld_wait();
       const size_t row = (size_t)b * S + key;
-      __nv_bfloat16* dkrow = d_qkv + row * 3 * E + E + h * D;
-      __nv_bfloat16* dvrow = d_qkv + row * 3 * E + 2 * E + h * D;
+      __nv_bfloat16* dkrow = d_qkv + row * 3 * E + E + h * D + col_half * 32;
+      __nv_bfloat16* dvrow = d_qkv + row * 3 * E + 2 * E + h * D + col_half * 32;
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int q = 0; q < 4; ++q) {
+        float x[8], y[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float x[8], y[8];
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            x[t] = __uint_as_float(dk[c][q * 8 + t]) * scale;
-            y[t] = __uint_as_float(dv[c][q * 8 + t]);
-          }
-          if (rope_cos) {
-#pragma unroll
-            for (int t = 0; t < 8; t += 2) {
-              const int pair = (c * 32 + q * 8 + t) >> 1;
-              const float cs = __ldg(rope_cos + (size_t)key * (D / 2) + pair);
-              const float sn = __ldg(rope_sin + (size_t)key * (D / 2) + pair);
-              const float a0 = x[t], a1 = x[t + 1];
-              x[t] = a0 * cs + a1 * sn;
-              x[t + 1] = -a0 * sn + a1 * cs;
-            }
-          }
-          uint4 uk, uv;
-          uk.x = pack_bf16(x[0], x[1]); uk.y = pack_bf16(x[2], x[3]); uk.z = pack_bf16(x[4], x[5]); uk.w = pack_bf16(x[6], x[7]);
-          uv.x = pack_bf16(y[0], y[1]); uv.y = pack_bf16(y[2], y[3]); uv.z = pack_bf16(y[4], y[5]); uv.w = pack_bf16(y[6], y[7]);
-          *reinterpret_cast<uint4*>(dkrow + c * 32 + q * 8) = uk;
-          *reinterpret_cast<uint4*>(dvrow + c * 32 + q * 8) = uv;
+        for (int t = 0; t < 8; ++t) {
+          x[t] = __uint_as_float(dk[q * 8 + t]) * scale;
+          y[t] = __uint_as_float(dv[q * 8 + t]);
         }
+        if (rope_cos) {
+#pragma unroll
+          for (int t = 0; t < 8; t += 2) {
+            const int pair = (col_half * 32 + q * 8 + t) >> 1;
+            const float cs = __ldg(rope_cos + (size_t)key * (D / 2) + pair);
+            const float sn = __ldg(rope_sin + (size_t)key * (D / 2) + pair);
+            const float a0 = x[t], a1 = x[t + 1];
+            x[t] = a0 * cs + a1 * sn;
+            x[t + 1] = -a0 * sn + a1 * cs;
+          }
+        }
+        uint4 uk, uv;
+        uk.x = pack_bf16(x[0], x[1]); uk.y = pack_bf16(x[2], x[3]); uk.z = pack_bf16(x[4], x[5]); uk.w = pack_bf16(x[6], x[7]);
+        uv.x = pack_bf16(y[0], y[1]); uv.y = pack_bf16(y[2], y[3]); uv.z = pack_bf16(y[4], y[5]); uv.w = pack_bf16(y[6], y[7]);
+        *reinterpret_cast<uint4*>(dkrow + q * 8) = uk;
+        *reinterpret_cast<uint4*>(dvrow + q * 8) = uv;
+      }
     }
   }
 
@@ -546,30 +580,32 @@ bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, 
   return true;
 }
 
-// Backward main pass (the caller runs the D / dq-zeroing pre-pass before and the dq post-pass after).
-bool fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* lse, const float* Dsum,
-                      float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B, int S,
-                      int H, int Dh, cudaStream_t st, zl_status* status) {
-  // TMA sources, the float4 dQ atomics and the 16-byte dK/dV stores all need 16-byte alignment
-  if (Dh != fatc::D || S % fatc::BQ != 0 ||
-      ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(d_o) | reinterpret_cast<uintptr_t>(dq_acc) |
-        reinterpret_cast<uintptr_t>(d_qkv)) & 15))
-    return false;
-  CUtensorMap tq, tdo;
+// Whether the tcgen05 backward takes this call: head_dim 64, S a multiple of 128, and 16-byte
+// aligned TMA sources, dQ accumulator and gradient rows.
+bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, const void* d_qkv, int S, int Dh) {
+  return Dh == fatc::D && S % fatc::BQ == 0 &&
+         ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(d_o) | reinterpret_cast<uintptr_t>(dq_acc) |
+           reinterpret_cast<uintptr_t>(d_qkv)) & 15) == 0;
+}
+
+// Backward main pass.  Before it the caller's pre pass writes nl = -lse*log2(e) and D = rowsum(dO*O)
+// ([B, H, S]) and zeroes dq_acc; after it the post pass turns dq_acc ([B, H, S, Dh] fp32) into dQ.
+zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
+                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
+                           int S, int H, int Dh, cudaStream_t st) {
+  CUtensorMap tq, tdo, tdq;
   const int E = H * Dh;
   if (!make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128) ||
-      !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, 128)) {
-    *status = set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
-    return true;
-  }
+      !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, 128) ||
+      !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 128))
+    return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
   cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        fatc::bwd::SMEM_TOTAL);
   const float scale = 1.0f / sqrtf((float)Dh);
   const int grid = B * H * (S / fatc::BKV);
-  fatc::bwd::fa_bwd_tc_kernel<<<grid, fatc::THREADS, fatc::bwd::SMEM_TOTAL, st>>>(
-      tq, tdo, lse, Dsum, dq_acc, d_qkv, rope_cos, rope_sin, S, H, scale, scale * 1.4426950408889634f);
-  *status = check_launch("fa_bwd_tc_kernel");
-  return true;
+  fatc::bwd::fa_bwd_tc_kernel<<<grid, fatc::bwd::THREADS_B, fatc::bwd::SMEM_TOTAL, st>>>(
+      tq, tdo, tdq, nl, Dsum, d_qkv, rope_cos, rope_sin, S, H, scale, scale * 1.4426950408889634f);
+  return check_launch("fa_bwd_tc_kernel");
 }
 
 int attn_tc_dev_error_read_and_clear() {
