@@ -258,19 +258,22 @@ __global__ void __launch_bounds__(THREADS, 1)
 // of the sequence.  Per query block i:
 //   MMA:     S^T = K Q_i^T, dP^T = V dO_i^T                                      (TMEM, fp32)
 //   softmax: P^T = exp2(S^T * scale_log2 - lse2[q]) with the causal mask, dS^T = P^T (dP^T - D[q]);
-//            P^T and dS^T go back into TMEM as bf16 (A operands of the next MMAs), dS^T also to
-//            shared memory
-//   MMA:     dV += P^T dO_i, dK += dS^T Q_i  (A from TMEM, B MN-major in shared memory)
-//            dQ_i = dS K                      (A = dS^T read MN-major, B = K MN-major)
-//   softmax warps: dQ_i (TMEM) -> shared memory -> one bulk reduce-add into the fp32 dQ accumulator
-//            ([B, H, S, Dh], so the 128 x 64 tile is contiguous)
+//            P^T goes back to TMEM as bf16 (A operand of dV), dS^T to shared memory
+//   MMA:     dV += P^T dO_i   (A from TMEM)
+//            dK += dS^T Q_i   (A = dS^T in shared memory, K-major)
+//            dQ_i = dS K      (A = the same dS^T read MN-major, B = K MN-major)
+//   dQ_i:    TMEM -> two swizzled [128][32] shared boxes -> TMA reduce-add into the fp32 accumulator
+//            ([B, H, S, Dh]), done by the softmax warps one block later
+// The tensor core and the softmax warps overlap across blocks: once the softmax of block i has
+// consumed S^T / dP^T, the MMA warp issues S^T / dP^T of block i+1 and then dV / dK / dQ of block i,
+// while the softmax warps read out dQ of block i-1 and start on block i+1.  Only the writes of P^T
+// (TMEM) and dS^T (shared memory) of block i+1 wait for block i's MMAs to finish reading them.
+// TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ [384,448), P^T [448,512).
 // Eight softmax warps: warps w and w+4 share the TMEM lanes of quadrant w % 4 and split the 128
-// query columns into halves.  Each half packs its bf16 P^T / dS^T into its own 64-column range
-// (queries 0-63 -> columns 0-31, queries 64-127 -> columns 64-95), so the two warps never touch
-// each other's columns; the MMA for query chunk k reads its A operand at (k/4)*64 + (k%4)*8.
-// The per-query rows nl = -lse*log2(e) and D = rowsum(dO*O) arrive by bulk copy with Q_i / dO_i.
-// At the end dK (times the softmax scale, rotated back by RoPE when tables are given) and dV go to
-// the packed gradient buffer.  dQ's scale and inverse RoPE are applied by the caller's post pass.
+// query columns into halves.  The per-query rows nl = -lse*log2(e) and D = rowsum(dO*O) arrive by
+// bulk copy with Q_i / dO_i.  At the end dK (times the softmax scale, rotated back by RoPE when
+// tables are given) and dV go to the packed gradient buffer; dQ's scale and inverse RoPE are
+// applied by the caller's post pass.
 namespace bwd {
 constexpr int NSOFT = 8;
 constexpr int THREADS_B = 64 + 32 * NSOFT;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
@@ -282,9 +285,9 @@ constexpr int SM_VEC = SM_DQ + 2 * DQ_BYTES;         // [2] stages
 constexpr int SM_BAR = SM_VEC + 2 * VEC_BYTES;
 constexpr int SMEM_TOTAL = SM_BAR + 128 + 1024;
 static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
-constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
+constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384, C_P = 448;
 constexpr uint32_t IDESC_SD = make_idesc(1, 128, 128, 0, 0);  // K Q^T / V dO^T: both K-major
-constexpr uint32_t IDESC_VK = make_idesc(1, 128, 64, 0, 1);   // dV/dK: A TMEM, B MN-major
+constexpr uint32_t IDESC_VK = make_idesc(1, 128, 64, 0, 1);   // dV / dK: A (TMEM or K-major), B MN-major
 constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);    // dQ: A MN-major (dS^T), B MN-major (K)
 
 __device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -300,8 +303,6 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
                ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
-// P^T / dS^T column of query chunk k (16 queries, 8 packed columns)
-__device__ __forceinline__ uint32_t packed_col(int k) { return (uint32_t)((k >> 2) * 64 + (k & 3) * 8); }
 
 __global__ void __launch_bounds__(THREADS_B, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
@@ -382,14 +383,10 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     }
   } else if (warp == 1) {
     const uint32_t sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
-    bool ok = bounded_wait_warp(kv_full, 0, DEV_TIMEOUT_ATTN);
-    for (int i = 0; i < niter && ok; ++i) {
-      const int st = i & 1;
-      if (!bounded_wait_warp(&q_full[st], (i >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-      // S / dP regions are read (as P^T / dS^T) by the previous block's dV / dK MMAs
-      if (i > 0 && !bounded_wait_warp(mm_done, (i - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
+    // S^T / dP^T of query block j (stage j & 1) -> sd_full
+    auto issue_sd = [&](int j) {
+      const uint32_t sq = smem_u32(smem + SM_Q + (j & 1) * TILE_BYTES);
+      const uint32_t sdo = smem_u32(smem + SM_DO + (j & 1) * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -401,18 +398,38 @@ __global__ void __launch_bounds__(THREADS_B, 1)
         umma_commit(sd_full);
       }
       __syncwarp();
-      if (!bounded_wait_warp(ds_ready, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-      if (i > 0 && !bounded_wait_warp(dq_free, (i - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+    };
+    bool ok = bounded_wait_warp(kv_full, 0, DEV_TIMEOUT_ATTN) && bounded_wait_warp(&q_full[0], 0, DEV_TIMEOUT_ATTN);
+    if (ok) {
       tc_fence_after();
+      issue_sd(0);
+    }
+    for (int i = 0; i < niter && ok; ++i) {
+      const int st = i & 1;
+      // softmax of block i is done: S^T / dP^T are free, P^T (TMEM) and dS^T (smem) are ready
+      if (!bounded_wait_warp(ds_ready, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      if (i + 1 < niter) {
+        if (!bounded_wait_warp(&q_full[st ^ 1], ((i + 1) >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        issue_sd(i + 1);
+      }
+      const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < BQ / 16; ++k) {  // 16 queries per MMA
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          umma_f16_ts(tmem + C_DV, tmem + C_S + packed_col(k), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
+          umma_f16_ts(tmem + C_DV, tmem + C_P + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
                       IDESC_VK, acc);
-          umma_f16_ts(tmem + C_DK, tmem + C_DP + packed_col(k), smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024),
-                      IDESC_VK, acc);
+          umma_f16(tmem + C_DK, smem_desc_sw128(sds + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
+                   smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024), IDESC_VK, acc);
         }
+      }
+      __syncwarp();
+      // dQ of block i-1 has been read out of TMEM
+      if (i > 0 && !bounded_wait_warp(dq_free, (i - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA
           umma_f16(tmem + C_DQ, smem_desc_sw128(sds + k * 2048, TILE_BYTES, 1024),
@@ -432,15 +449,44 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     const int r_local = quarter * 32 + lane;      // key row (S^T / dP^T / dV / dK) and query row (dQ)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     const int key = kb * BKV + r_local;           // position of this thread's key
-    const bool elected = (threadIdx.x == 64);     // issues the dQ bulk reductions
+    const bool elected = (threadIdx.x == 64);     // issues the dQ reductions
     uint8_t* sds = smem + SM_DS;
     bool ok = true;
+    // dQ of block j: TMEM -> shared boxes (buffer j & 1); the caller syncs and reduces
+    auto dq_readout = [&](int j) {
+      tc_fence_after();
+      uint32_t dq[32];
+      tmem_ld32(t_lane + C_DQ + (uint32_t)(col_half * 32), dq);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(dq_free);
+      uint8_t* rowp = smem + SM_DQ + (j & 1) * DQ_BYTES + col_half * (DQ_BYTES / 2) + r_local * 128;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
+        *reinterpret_cast<uint4*>(rowp + ((k ^ (r_local & 7)) * 16)) =
+            make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
+    };
+    // every softmax thread runs this once per block (also after a timeout), so the named barrier
+    // always completes.  Before it, the elected thread makes sure the reduction issued last time
+    // (from the other buffer) has finished reading, so that buffer can be refilled next time.
+    auto dq_reduce = [&](int j, bool have) {
+      if (elected) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      fence_async_smem();
+      named_sync_softmax();
+      if (elected && have) {
+        const uint8_t* tile = smem + SM_DQ + (j & 1) * DQ_BYTES;
+        const int y = (int)(row_base + (size_t)(kb + j) * BQ);
+        tma_reduce_add_2d(&tm_dq, tile, 0, y);
+        tma_reduce_add_2d(&tm_dq, tile + DQ_BYTES / 2, 32, y);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+    };
     for (int i = 0; i < niter; ++i) {
-      const int qb = kb + i;
       const int st = i & 1;
       const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + st * VEC_BYTES);
       const bool diag = (i == 0);
       ok = ok && bounded_wait_warp(sd_full, i & 1, DEV_TIMEOUT_ATTN);
+      bool have_dq = false;
       if (ok) {
         tc_fence_after();
 #pragma unroll 1
@@ -469,10 +515,15 @@ __global__ void __launch_bounds__(THREADS_B, 1)
             dd[j >> 1] = pack_bf16(d[0], d[1]);
             dd[(j >> 1) + 1] = pack_bf16(d[2], d[3]);
           }
-          const uint32_t pcol = (uint32_t)(col_half * 64 + cc * 16);
-          tmem_st16(t_lane + C_S + pcol, pp);
-          tmem_st16(t_lane + C_DP + pcol, dd);
-          // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout the dQ MMA reads
+          if (cc == 0 && i > 0) {
+            // block i-1's dV / dK / dQ MMAs have finished reading P^T and dS^T
+            ok = bounded_wait_warp(mm_done, (i - 1) & 1, DEV_TIMEOUT_ATTN);
+            if (!ok) break;
+            tc_fence_after();
+            have_dq = true;
+          }
+          tmem_st16(t_lane + C_P + (uint32_t)(col_half * 32 + cc * 16), pp);
+          // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout
           uint8_t* rowp = sds + col_half * TILE_BYTES + r_local * 128;
 #pragma unroll
           for (int pc = 0; pc < 4; ++pc) {
@@ -481,38 +532,19 @@ __global__ void __launch_bounds__(THREADS_B, 1)
                 make_uint4(dd[pc * 4], dd[pc * 4 + 1], dd[pc * 4 + 2], dd[pc * 4 + 3]);
           }
         }
-        tmem_st_wait();
-        tc_fence_before();
-        fence_async_smem();
-        mbar_arrive(ds_ready);
+        if (ok) {
+          tmem_st_wait();
+          tc_fence_before();
+          fence_async_smem();
+          mbar_arrive(ds_ready);
+          if (have_dq) dq_readout(i - 1);
+        }
       }
-      // dQ_i: TMEM -> two swizzled [128][32] boxes (row = query) -> TMA reduce-add into dq_acc
-      ok = ok && bounded_wait_warp(mm_done, i & 1, DEV_TIMEOUT_ATTN);
-      uint8_t* dq_tile = smem + SM_DQ + st * DQ_BYTES;
-      if (ok) {
-        tc_fence_after();
-        uint32_t dq[32];
-        tmem_ld32(t_lane + C_DQ + (uint32_t)(col_half * 32), dq);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(dq_free);
-        uint8_t* rowp = dq_tile + col_half * (DQ_BYTES / 2) + r_local * 128;
-#pragma unroll
-        for (int k = 0; k < 8; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
-          *reinterpret_cast<uint4*>(rowp + ((k ^ (r_local & 7)) * 16)) =
-              make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
-      }
-      fence_async_smem();
-      named_sync_softmax();  // every softmax thread, every block (also after a timeout)
-      if (elected && ok) {
-        const int y = (int)(row_base + (size_t)qb * BQ);
-        tma_reduce_add_2d(&tm_dq, dq_tile, 0, y);
-        tma_reduce_add_2d(&tm_dq, dq_tile + DQ_BYTES / 2, 32, y);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        // the tile written two blocks from now reuses the buffer of the reductions before these
-        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-      }
+      dq_reduce(i - 1, ok && have_dq);
     }
+    ok = ok && bounded_wait_warp(mm_done, (niter - 1) & 1, DEV_TIMEOUT_ATTN);
+    if (ok) dq_readout(niter - 1);
+    dq_reduce(niter - 1, ok);
     if (elected) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     // dK (scaled, inverse RoPE) and dV for this key block: columns [32*col_half, 32*col_half + 32)
     if (ok) {

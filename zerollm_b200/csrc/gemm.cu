@@ -480,6 +480,39 @@ __global__ void splitk_reduce_kernel(const GemmArgs args) {
   epilogue_store32(args, r, c0, v);
 }
 
+// Split-K sum for plain fp32 outputs (no epilogue beyond OUT_F32 / ACCUM), N % 4 == 0: one
+// thread per 4 columns of a row, the splits summed with four loads in flight.
+__global__ void splitk_reduce_f32_kernel(const float* __restrict__ ws, float* __restrict__ out, int M, int N, int splits,
+                                         int accum) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t n4 = (int64_t)M * N / 4;
+  if (idx >= n4) return;
+  const float4* p = reinterpret_cast<const float4*>(ws) + idx;
+  const int64_t sstride = (int64_t)M * N / 4;
+  float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0, a2 = a0, a3 = a0;
+  int s = 0;
+  for (; s + 3 < splits; s += 4) {
+    const float4 u0 = __ldg(p + s * sstride), u1 = __ldg(p + (s + 1) * sstride), u2 = __ldg(p + (s + 2) * sstride),
+                 u3 = __ldg(p + (s + 3) * sstride);
+    a0.x += u0.x; a0.y += u0.y; a0.z += u0.z; a0.w += u0.w;
+    a1.x += u1.x; a1.y += u1.y; a1.z += u1.z; a1.w += u1.w;
+    a2.x += u2.x; a2.y += u2.y; a2.z += u2.z; a2.w += u2.w;
+    a3.x += u3.x; a3.y += u3.y; a3.z += u3.z; a3.w += u3.w;
+  }
+  for (; s < splits; ++s) {
+    const float4 u = __ldg(p + s * sstride);
+    a0.x += u.x; a0.y += u.y; a0.z += u.z; a0.w += u.w;
+  }
+  float4 r = make_float4((a0.x + a1.x) + (a2.x + a3.x), (a0.y + a1.y) + (a2.y + a3.y),
+                         (a0.z + a1.z) + (a2.z + a3.z), (a0.w + a1.w) + (a2.w + a3.w));
+  float4* o = reinterpret_cast<float4*>(out) + idx;
+  if (accum) {
+    const float4 prev = *o;
+    r.x += prev.x; r.y += prev.y; r.z += prev.z; r.w += prev.w;
+  }
+  *o = r;
+}
+
 // SIMT fallback for fp32 shapes whose rows are not 16-byte aligned (tiny
 // test shapes, odd K): 64x64 tile, 4x4 outputs per thread, k ascending.
 template <bool A_MN, bool B_MN>
@@ -680,6 +713,14 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   else e = dispatch_major<T, 256, 4>(a_mn, b_mn, ma, mb, a, grid, st);
   if (e != cudaSuccess) return set_error(ZL_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
   if (p.splits > 1) {
+    const bool plain_f32 = (flags & ~(ZL_EPI_OUT_F32 | ZL_EPI_ACCUM)) == 0 && (flags & ZL_EPI_OUT_F32) && N % 4 == 0 &&
+                           ((reinterpret_cast<uintptr_t>(D) | reinterpret_cast<uintptr_t>(ws)) & 15) == 0;
+    if (plain_f32) {
+      const int64_t n4 = (int64_t)M * N / 4;
+      splitk_reduce_f32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(ws, static_cast<float*>(D), M, N, p.splits,
+                                                                            (flags & ZL_EPI_ACCUM) ? 1 : 0);
+      return check_launch("splitk_reduce_f32");
+    }
     const int64_t work = (int64_t)M * ((N + 31) / 32);
     splitk_reduce_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(a);
     return check_launch("splitk_reduce");

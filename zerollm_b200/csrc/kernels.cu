@@ -189,18 +189,44 @@ __global__ void norm_bwd_bf16_kernel(const __nv_bfloat16* __restrict__ x, const 
   for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) part[(int64_t)blockIdx.x * 2 * N + i] = sacc[i];
 }
 
-// Sums per-block partials [nb][2N] into dgamma (and dbeta).
-__global__ void reduce_partials_kernel(const float* __restrict__ part, int nb, int N, int stride, float* __restrict__ out0,
-                                       float* __restrict__ out1) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= N) return;
-  float s0 = 0.f, s1 = 0.f;
-  for (int k = 0; k < nb; ++k) {
-    s0 += part[(int64_t)k * stride + i];
-    if (out1) s1 += part[(int64_t)k * stride + N + i];
+// Sums per-block partials [nb][stride] into out0 (columns [0, N)) and, when out1 is given, out1
+// (columns [N, 2N)), accumulating.  One block per 32 columns: its 32 warps take every 32nd
+// partial row (four loads in flight), then warp 0 adds the 32 warp sums in a fixed order, so the
+// result does not depend on timing.
+constexpr int kReduceWarps = 32;
+__global__ void __launch_bounds__(kReduceWarps * 32) reduce_partials_kernel(const float* __restrict__ part, int nb, int N,
+                                                                         int stride, float* __restrict__ out0,
+                                                                         float* __restrict__ out1) {
+  __shared__ float red[kReduceWarps][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int ncols = out1 ? 2 * N : N;
+  const int c = blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (c < ncols) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int k = w;
+    for (; k + 3 * kReduceWarps < nb; k += 4 * kReduceWarps) {
+      a0 += part[(int64_t)k * stride + c];
+      a1 += part[(int64_t)(k + kReduceWarps) * stride + c];
+      a2 += part[(int64_t)(k + 2 * kReduceWarps) * stride + c];
+      a3 += part[(int64_t)(k + 3 * kReduceWarps) * stride + c];
+    }
+    for (; k < nb; k += kReduceWarps) a0 += part[(int64_t)k * stride + c];
+    s = (a0 + a1) + (a2 + a3);
   }
-  out0[i] += s0;
-  if (out1) out1[i] += s1;
+  red[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && c < ncols) {
+    float t = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < kReduceWarps; ++j) t += red[j][lane];
+    if (c < N) out0[c] += t;
+    else out1[c - N] += t;
+  }
+}
+void launch_reduce_partials(const float* part, int nb, int N, int stride, float* out0, float* out1, cudaStream_t st) {
+  const int ncols = out1 ? 2 * N : N;
+  reduce_partials_kernel<<<(ncols + 31) / 32, kReduceWarps * 32, 0, st>>>(part, nb, N, stride, out0, out1);
 }
 
 int norm_bwd_blocks(int64_t M) {
@@ -684,7 +710,7 @@ extern "C" zl_status zl_norm_backward_bf16(int kind, const zl_bf16* x, const zl_
 #undef NB
   zl_status st = check_launch("norm_bwd_bf16");
   if (st != ZL_OK) return st;
-  reduce_partials_kernel<<<nblk(N, 256), 256, 0, ST(s)>>>(workspace, nb, N, 2 * N, dgamma, kind == 0 ? dbeta : nullptr);
+  launch_reduce_partials(workspace, nb, N, 2 * N, dgamma, kind == 0 ? dbeta : nullptr, ST(s));
   return check_launch("norm_bwd_reduce");
 }
 
@@ -743,7 +769,7 @@ extern "C" zl_status zl_colsum_bf16(const zl_bf16* dy, float* db, float* workspa
       reinterpret_cast<const __nv_bfloat16*>(dy), workspace, M, N, rpb);
   zl_status st = check_launch("colsum_bf16");
   if (st != ZL_OK) return st;
-  reduce_partials_kernel<<<nblk(N, 256), 256, 0, ST(s)>>>(workspace, nb, N, N, db, nullptr);
+  launch_reduce_partials(workspace, nb, N, N, db, nullptr, ST(s));
   return check_launch("colsum_reduce");
 }
 
