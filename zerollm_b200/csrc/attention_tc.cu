@@ -16,6 +16,8 @@
 // values, lse = natural log-sum-exp of the scaled scores.
 #include <cmath>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace zl {
@@ -264,10 +266,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 //            dQ_i = dS K      (A = the same dS^T read MN-major, B = K MN-major)
 //   dQ_i:    TMEM -> two swizzled [128][32] shared boxes -> TMA reduce-add into the fp32 accumulator
 //            ([B, H, S, Dh]), done by the softmax warps one block later
-// The tensor core and the softmax warps overlap across blocks: once the softmax of block i has
-// consumed S^T / dP^T, the MMA warp issues S^T / dP^T of block i+1 and then dV / dK / dQ of block i,
-// while the softmax warps read out dQ of block i-1 and start on block i+1.  Only the writes of P^T
-// (TMEM) and dS^T (shared memory) of block i+1 wait for block i's MMAs to finish reading them.
+// The tensor core and the softmax warps overlap across blocks: as soon as the softmax warps hold
+// S^T / dP^T of block i in registers (sd_used), the MMA warp issues S^T / dP^T of block i+1; once
+// P^T / dS^T of block i are written (ds_ready) it issues dV / dK / dQ of block i, while the softmax
+// warps read out dQ of block i-1 and start on block i+1.  Only the writes of P^T (TMEM) and dS^T
+// (shared memory) of block i+1 wait for block i's MMAs to finish reading them.  Q / dO run in three
+// stages, so their loads are issued two blocks ahead.
 // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ [384,448), P^T [448,512).
 // Eight softmax warps: warps w and w+4 share the TMEM lanes of quadrant w % 4 and split the 128
 // query columns into halves.  The per-query rows nl = -lse*log2(e) and D = rowsum(dO*O) arrive by
@@ -277,12 +281,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 namespace bwd {
 constexpr int NSOFT = 8;
 constexpr int THREADS_B = 64 + 32 * NSOFT;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
-constexpr int SM_K = 0, SM_V = TILE_BYTES, SM_Q = 2 * TILE_BYTES, SM_DO = 4 * TILE_BYTES, SM_DS = 6 * TILE_BYTES;
-constexpr int DQ_BYTES = BQ * D * 4;                 // one fp32 dQ tile: two [128][32] boxes, 128-byte swizzle
-constexpr int SM_DQ = 8 * TILE_BYTES;                // [2] dQ tiles
+constexpr int QST = 3;                               // Q / dO / row-vector stages (loads run two blocks ahead)
+constexpr int SM_K = 0, SM_V = TILE_BYTES, SM_Q = 2 * TILE_BYTES, SM_DO = SM_Q + QST * TILE_BYTES;
+constexpr int SM_DS = SM_DO + QST * TILE_BYTES;
+constexpr int DQ_BYTES = BQ * D * 4;                 // the fp32 dQ tile: two [128][32] boxes, 128-byte swizzle
+constexpr int SM_DQ = SM_DS + 2 * TILE_BYTES;
 constexpr int VEC_BYTES = 2 * BQ * 4;                // nl[128], D[128] of one query block
-constexpr int SM_VEC = SM_DQ + 2 * DQ_BYTES;         // [2] stages
-constexpr int SM_BAR = SM_VEC + 2 * VEC_BYTES;
+constexpr int SM_VEC = SM_DQ + DQ_BYTES;             // [QST] stages
+constexpr int SM_BAR = SM_VEC + QST * VEC_BYTES;
 constexpr int SMEM_TOTAL = SM_BAR + 128 + 1024;
 static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
 constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384, C_P = 448;
@@ -315,14 +321,15 @@ __global__ void __launch_bounds__(THREADS_B, 1)
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM_BAR);
   uint64_t* kv_full = bar + 0;
-  uint64_t* q_full = bar + 1;   // [2]
-  uint64_t* q_empty = bar + 3;  // [2]
-  uint64_t* sd_full = bar + 5;
-  uint64_t* ds_ready = bar + 6;
-  uint64_t* mm_done = bar + 7;
-  uint64_t* dq_free = bar + 8;
-  uint64_t* drain = bar + 9;    // final commit: every MMA of this CTA has retired
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* q_full = bar + 1;         // [QST]
+  uint64_t* q_empty = bar + 1 + QST;  // [QST]
+  uint64_t* sd_full = bar + 1 + 2 * QST;
+  uint64_t* ds_ready = sd_full + 1;
+  uint64_t* mm_done = sd_full + 2;
+  uint64_t* dq_free = sd_full + 3;
+  uint64_t* drain = sd_full + 4;      // final commit: every MMA of this CTA has retired
+  uint64_t* sd_used = sd_full + 5;    // the softmax warps have loaded S^T / dP^T into registers
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sd_full + 6);
 
   const int E = H * D;
   const int nk = S / BKV;
@@ -337,12 +344,13 @@ __global__ void __launch_bounds__(THREADS_B, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
+    for (int i = 0; i < QST; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
     mbar_init(sd_full, 1);
     mbar_init(ds_ready, 32 * NSOFT);
     mbar_init(mm_done, 1);
     mbar_init(dq_free, 32 * NSOFT);
     mbar_init(drain, 1);
+    mbar_init(sd_used, 32 * NSOFT);
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
@@ -364,8 +372,8 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       tma_load_2d(smem + SM_V, &tm_qkv, kv_full, 2 * E + h * D, krow0);
       int issued = 0;
       for (int i = 0; i < niter; ++i) {
-        const int st = i & 1;
-        if (!bounded_wait(&q_empty[st], ((i >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
+        const int st = i % QST;
+        if (!bounded_wait(&q_empty[st], ((i / QST) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
         mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES + VEC_BYTES);
         const int qb = kb + i;
         const int qrow = b * S + qb * BQ;
@@ -378,15 +386,15 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       }
       // no copy may still be landing in shared memory when the CTA exits
       bounded_wait(kv_full, 0, DEV_TIMEOUT_ATTN);
-      for (int i = issued - 2 < 0 ? 0 : issued - 2; i < issued; ++i)
-        bounded_wait(&q_full[i & 1], (i >> 1) & 1, DEV_TIMEOUT_ATTN);
+      for (int i = issued - QST < 0 ? 0 : issued - QST; i < issued; ++i)
+        bounded_wait(&q_full[i % QST], (i / QST) & 1, DEV_TIMEOUT_ATTN);
     }
   } else if (warp == 1) {
     const uint32_t sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
-    // S^T / dP^T of query block j (stage j & 1) -> sd_full
+    // S^T / dP^T of query block j (stage j % QST) -> sd_full
     auto issue_sd = [&](int j) {
-      const uint32_t sq = smem_u32(smem + SM_Q + (j & 1) * TILE_BYTES);
-      const uint32_t sdo = smem_u32(smem + SM_DO + (j & 1) * TILE_BYTES);
+      const uint32_t sq = smem_u32(smem + SM_Q + (j % QST) * TILE_BYTES);
+      const uint32_t sdo = smem_u32(smem + SM_DO + (j % QST) * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -405,15 +413,18 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       issue_sd(0);
     }
     for (int i = 0; i < niter && ok; ++i) {
-      const int st = i & 1;
-      // softmax of block i is done: S^T / dP^T are free, P^T (TMEM) and dS^T (smem) are ready
-      if (!bounded_wait_warp(ds_ready, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-      tc_fence_after();
+      const int st = i % QST;
       if (i + 1 < niter) {
-        if (!bounded_wait_warp(&q_full[st ^ 1], ((i + 1) >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        // the softmax warps hold S^T / dP^T of block i in registers: block i+1 can overwrite them
+        if (!bounded_wait_warp(sd_used, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        const int sn = (i + 1) % QST;
+        if (!bounded_wait_warp(&q_full[sn], ((i + 1) / QST) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
         tc_fence_after();
         issue_sd(i + 1);
       }
+      // softmax of block i is done: P^T (TMEM) and dS^T (smem) are ready
+      if (!bounded_wait_warp(ds_ready, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
       const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
@@ -452,29 +463,32 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     const bool elected = (threadIdx.x == 64);     // issues the dQ reductions
     uint8_t* sds = smem + SM_DS;
     bool ok = true;
-    // dQ of block j: TMEM -> shared boxes (buffer j & 1); the caller syncs and reduces
-    auto dq_readout = [&](int j) {
-      tc_fence_after();
-      uint32_t dq[32];
-      tmem_ld32(t_lane + C_DQ + (uint32_t)(col_half * 32), dq);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(dq_free);
-      uint8_t* rowp = smem + SM_DQ + (j & 1) * DQ_BYTES + col_half * (DQ_BYTES / 2) + r_local * 128;
-#pragma unroll
-      for (int k = 0; k < 8; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
-        *reinterpret_cast<uint4*>(rowp + ((k ^ (r_local & 7)) * 16)) =
-            make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
-    };
-    // every softmax thread runs this once per block (also after a timeout), so the named barrier
-    // always completes.  Before it, the elected thread makes sure the reduction issued last time
-    // (from the other buffer) has finished reading, so that buffer can be refilled next time.
-    auto dq_reduce = [&](int j, bool have) {
+    // dQ of block j: TMEM -> shared boxes.  The reduction of the previous tile must have finished
+    // reading the buffer first: the elected thread waits for it, and a named barrier passes that on.
+    auto dq_readout = [&](int j, bool have) {
       if (elected) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      named_sync_softmax();
+      if (have) {
+        uint32_t dq[32];
+        tc_fence_after();
+        tmem_ld32(t_lane + C_DQ + (uint32_t)(col_half * 32), dq);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(dq_free);
+        uint8_t* rowp = smem + SM_DQ + col_half * (DQ_BYTES / 2) + r_local * 128;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
+          *reinterpret_cast<uint4*>(rowp + ((k ^ (r_local & 7)) * 16)) =
+              make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
+      }
+    };
+    // every softmax thread runs dq_readout and dq_reduce once per block (also after a timeout), so
+    // the named barriers always complete
+    auto dq_reduce = [&](int j, bool have) {
       fence_async_smem();
       named_sync_softmax();
       if (elected && have) {
-        const uint8_t* tile = smem + SM_DQ + (j & 1) * DQ_BYTES;
+        const uint8_t* tile = smem + SM_DQ;
         const int y = (int)(row_base + (size_t)(kb + j) * BQ);
         tma_reduce_add_2d(&tm_dq, tile, 0, y);
         tma_reduce_add_2d(&tm_dq, tile + DQ_BYTES / 2, 32, y);
@@ -482,68 +496,82 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       }
     };
     for (int i = 0; i < niter; ++i) {
-      const int st = i & 1;
-      const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + st * VEC_BYTES);
+      const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + (i % QST) * VEC_BYTES);
       const bool diag = (i == 0);
       ok = ok && bounded_wait_warp(sd_full, i & 1, DEV_TIMEOUT_ATTN);
       bool have_dq = false;
       if (ok) {
         tc_fence_after();
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = col_half * 2 + cc;        // 32-query chunk
-          uint32_t rs[32], rd[32];
-          tmem_ld32(t_lane + C_S + (uint32_t)(c * 32), rs);
-          tmem_ld32(t_lane + C_DP + (uint32_t)(c * 32), rd);
+        // P^T / dS^T of this thread's 64 queries are computed into registers first (4 sub-chunks of 16;
+        // the TMEM loads of sub-chunk g+1 are in flight while g is computed), and only then does the
+        // thread wait for block i-1's MMAs to release the P^T columns and the dS^T buffer.
+        auto chunks = [&](auto diag_tag) {
+          constexpr bool DIAG = decltype(diag_tag)::value;
+          uint32_t rs[2][16], rd[2][16];
+          uint32_t pp[32], dd[32];
+          const uint32_t c0 = (uint32_t)(col_half * 64);
+          tmem_ld16(t_lane + C_S + c0, rs[0]);
+          tmem_ld16(t_lane + C_DP + c0, rd[0]);
           tmem_ld_wait();
-          uint32_t pp[16], dd[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 nl4 = *reinterpret_cast<const float4*>(vec + c * 32 + j);
-            const float4 d4 = *reinterpret_cast<const float4*>(vec + BQ + c * 32 + j);
-            const float nlv[4] = {nl4.x, nl4.y, nl4.z, nl4.w};
-            const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
-            float p[4], d[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              p[t] = fast_exp2(fmaf(__uint_as_float(rs[j + t]), scale_log2, nlv[t]));
-              if (diag && r_local > c * 32 + j + t) p[t] = 0.f;
-              d[t] = p[t] * (__uint_as_float(rd[j + t]) - dv[t]);
+          for (int g = 0; g < 4; ++g) {
+            if (g + 1 < 4) {
+              tmem_ld16(t_lane + C_S + c0 + (uint32_t)((g + 1) * 16), rs[(g + 1) & 1]);
+              tmem_ld16(t_lane + C_DP + c0 + (uint32_t)((g + 1) * 16), rd[(g + 1) & 1]);
             }
-            pp[j >> 1] = pack_bf16(p[0], p[1]);
-            pp[(j >> 1) + 1] = pack_bf16(p[2], p[3]);
-            dd[j >> 1] = pack_bf16(d[0], d[1]);
-            dd[(j >> 1) + 1] = pack_bf16(d[2], d[3]);
+            const int q0 = col_half * 64 + g * 16;  // first query of the sub-chunk
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const float4 nl4 = *reinterpret_cast<const float4*>(vec + q0 + j);
+              const float4 d4 = *reinterpret_cast<const float4*>(vec + BQ + q0 + j);
+              const float nlv[4] = {nl4.x, nl4.y, nl4.z, nl4.w};
+              const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+              float p[4], d[4];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                p[t] = fast_exp2(fmaf(__uint_as_float(rs[g & 1][j + t]), scale_log2, nlv[t]));
+                if (DIAG && r_local > q0 + j + t) p[t] = 0.f;
+                d[t] = p[t] * (__uint_as_float(rd[g & 1][j + t]) - dv[t]);
+              }
+              pp[g * 8 + (j >> 1)] = pack_bf16(p[0], p[1]);
+              pp[g * 8 + (j >> 1) + 1] = pack_bf16(p[2], p[3]);
+              dd[g * 8 + (j >> 1)] = pack_bf16(d[0], d[1]);
+              dd[g * 8 + (j >> 1) + 1] = pack_bf16(d[2], d[3]);
+            }
+            if (g + 1 < 4) tmem_ld_wait();
           }
-          if (cc == 0 && i > 0) {
+          tc_fence_before();
+          mbar_arrive(sd_used);
+          if (i > 0) {
             // block i-1's dV / dK / dQ MMAs have finished reading P^T and dS^T
             ok = bounded_wait_warp(mm_done, (i - 1) & 1, DEV_TIMEOUT_ATTN);
-            if (!ok) break;
+            if (!ok) return;
             tc_fence_after();
             have_dq = true;
           }
-          tmem_st16(t_lane + C_P + (uint32_t)(col_half * 32 + cc * 16), pp);
+          tmem_st32(t_lane + C_P + (uint32_t)(col_half * 32), pp);
           // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout
           uint8_t* rowp = sds + col_half * TILE_BYTES + r_local * 128;
 #pragma unroll
-          for (int pc = 0; pc < 4; ++pc) {
-            const int chunk = (cc * 4 + pc) ^ (r_local & 7);
-            *reinterpret_cast<uint4*>(rowp + chunk * 16) =
-                make_uint4(dd[pc * 4], dd[pc * 4 + 1], dd[pc * 4 + 2], dd[pc * 4 + 3]);
-          }
-        }
+          for (int t = 0; t < 8; ++t)
+            *reinterpret_cast<uint4*>(rowp + ((t ^ (r_local & 7)) * 16)) =
+                make_uint4(dd[t * 4], dd[t * 4 + 1], dd[t * 4 + 2], dd[t * 4 + 3]);
+        };
+        if (diag) chunks(std::integral_constant<bool, true>{});
+        else chunks(std::integral_constant<bool, false>{});
         if (ok) {
           tmem_st_wait();
           tc_fence_before();
           fence_async_smem();
           mbar_arrive(ds_ready);
-          if (have_dq) dq_readout(i - 1);
         }
       }
-      dq_reduce(i - 1, ok && have_dq);
+      have_dq = have_dq && ok;
+      dq_readout(i - 1, have_dq);
+      dq_reduce(i - 1, have_dq);
     }
     ok = ok && bounded_wait_warp(mm_done, (niter - 1) & 1, DEV_TIMEOUT_ATTN);
-    if (ok) dq_readout(niter - 1);
+    dq_readout(niter - 1, ok);
     dq_reduce(niter - 1, ok);
     if (elected) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     // dK (scaled, inverse RoPE) and dV for this key block: columns [32*col_half, 32*col_half + 32)
