@@ -18,6 +18,10 @@
 
 #include <type_traits>
 
+#ifndef ZL_ATTN_BWD_SOFTMAX_WARPS
+#define ZL_ATTN_BWD_SOFTMAX_WARPS 8
+#endif
+
 #include "common.cuh"
 
 namespace zl {
@@ -30,7 +34,9 @@ namespace fatc {
 constexpr int BQ = 128, BKV = 128, D = 64;
 constexpr int THREADS = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 softmax / epilogue
 constexpr int TILE_BYTES = 128 * 128; // 128 rows x 64 bf16
-constexpr int SMEM_Q = 0, SMEM_K = TILE_BYTES, SMEM_V = 3 * TILE_BYTES, SMEM_BAR = 5 * TILE_BYTES;
+constexpr int KVST = 4;               // K / V stages (loads run three blocks ahead)
+constexpr int SMEM_Q = 0, SMEM_K = TILE_BYTES, SMEM_V = SMEM_K + KVST * TILE_BYTES;
+constexpr int SMEM_BAR = SMEM_V + KVST * TILE_BYTES;
 constexpr int SMEM_TOTAL = SMEM_BAR + 128 + 1024;
 constexpr uint32_t TMEM_COLS = 512;   // S/P buffer b at [128 b, 128 b + 128), O at [256, 320)
 constexpr uint32_t O_COL = 256;
@@ -53,13 +59,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;   // [2]
-  uint64_t* kv_empty = bar + 3;  // [2]
-  uint64_t* s_full = bar + 5;    // [2]
-  uint64_t* p_full = bar + 7;
-  uint64_t* o_full = bar + 8;
-  uint64_t* drain = bar + 9;     // final commit: every MMA of this CTA has retired
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* kv_full = bar + 1;              // [KVST]
+  uint64_t* kv_empty = bar + 1 + KVST;      // [KVST]
+  uint64_t* s_full = bar + 1 + 2 * KVST;    // [2]
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = s_full + 3;
+  uint64_t* drain = s_full + 4;             // final commit: every MMA of this CTA has retired
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 5);
 
   const int E = H * D;
   const int nq = S / BQ;
@@ -71,11 +77,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KVST; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
     }
+    for (int i = 0; i < 2; ++i) mbar_init(&s_full[i], 1);
     mbar_init(p_full, 128);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
@@ -98,8 +104,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       tma_load_2d(smem + SMEM_Q, &tm, q_full, h * D, row0);
       int issued = 0;
       for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % KVST;
+        const uint32_t ph = (j / KVST) & 1;
         if (!bounded_wait(&kv_empty[st], ph ^ 1u, DEV_TIMEOUT_ATTN)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
         const int krow = b * S + j * BKV;
@@ -109,21 +115,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // no copy may still be landing in shared memory when the CTA exits
       bounded_wait(q_full, 0, DEV_TIMEOUT_ATTN);
-      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j)
-        bounded_wait(&kv_full[j & 1], (j >> 1) & 1, DEV_TIMEOUT_ATTN);
+      for (int j = issued - KVST < 0 ? 0 : issued - KVST; j < issued; ++j)
+        bounded_wait(&kv_full[j % KVST], (j / KVST) & 1, DEV_TIMEOUT_ATTN);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t sq = smem_u32(smem + SMEM_Q);
-    auto issue_s = [&](int j) {  // S_j = Q K_j^T into buffer j & 1
-      const int st = j & 1;
-      const uint32_t sk = smem_u32(smem + SMEM_K + st * TILE_BYTES);
+    auto issue_s = [&](int j) {  // S_j = Q K_j^T into TMEM buffer j & 1 (K from stage j % KVST)
+      const int sb = j & 1;
+      const uint32_t sk = smem_u32(smem + SMEM_K + (j % KVST) * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
-          umma_f16(tmem + (uint32_t)(st * BKV), smem_desc_sw128(sq + k * 32, 16, 1024),
+          umma_f16(tmem + (uint32_t)(sb * BKV), smem_desc_sw128(sq + k * 32, 16, 1024),
                    smem_desc_sw128(sk + k * 32, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[sb]);
       }
       __syncwarp();
     };
@@ -133,10 +139,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       issue_s(0);
     }
     for (int j = 0; j < nkv && ok; ++j) {
-      const int st = j & 1;
+      const int sb = j & 1, st = j % KVST;
       if (j + 1 < nkv) {
         // K_{j+1} resident, and buffer (j+1)&1 free: P_{j-1} (in that buffer) consumed by P.V of block j-1
-        if (!bounded_wait_warp(&kv_full[st ^ 1], ((j + 1) >> 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        if (!bounded_wait_warp(&kv_full[(j + 1) % KVST], ((j + 1) / KVST) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
         if (j >= 1 && !bounded_wait_warp(o_full, (j - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
         tc_fence_after();
         issue_s(j + 1);
@@ -147,7 +153,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA: P columns k*8.., V rows k*16..
-          umma_f16_ts(tmem + O_COL, tmem + (uint32_t)(st * BKV + k * 8),
+          umma_f16_ts(tmem + O_COL, tmem + (uint32_t)(sb * BKV + k * 8),
                       smem_desc_sw128(sv + k * 16 * 128, TILE_BYTES, 1024), IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(&kv_empty[st]);
@@ -177,34 +183,58 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_ld_wait();
       const bool diag = (j == nkv - 1);
       const int key0 = j * BKV;
-      float mx = -INFINITY;
+      float corr = 1.f;
+      bool raise = false;
+      // The diagonal block (the only one with masked keys) is a separate instance, so the others
+      // carry no per-element mask.
+      auto block = [&](auto diag_tag) {
+        constexpr bool DIAG = decltype(diag_tag)::value;
+        auto val = [&](int c, int i) {
+          const float v = __uint_as_float(r[c][i]);
+          return (DIAG && key0 + c * 32 + i > q_pos) ? -INFINITY : v;
+        };
+        // row maximum of the raw scores (the scale is positive, so it commutes with max); eight
+        // independent partial maxima keep the dependency chains short
+        float mxp[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int k = 0; k < 8; ++k) mxp[k] = val(0, k);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(r[c][i]) * scale_log2;
-          if (diag && key0 + c * 32 + i > q_pos) v = -INFINITY;
-          r[c][i] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c > 0 || i >= 8) mxp[i & 7] = fmaxf(mxp[i & 7], val(c, i));
+        const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        // Lazy rescaling: the running maximum m (log2 units) is only raised when a lane's new
+        // maximum exceeds it by more than 8, so P = exp2(s - m) stays below 2^8 and O needs no
+        // correction in most blocks.  The decision is per warp (TMEM access is warp-wide).
+        const float m_cand = fmaxf(m, mx * scale_log2);
+        raise = __any_sync(0xffffffffu, m_cand > m + 8.f);
+        if (raise) {
+          corr = fast_exp2(m - m_cand);  // m = -inf on the first block -> 0
+          m = m_cand;
         }
-      const float m_new = fmaxf(m, mx);
-      const float corr = fast_exp2(m - m_new);  // m = -inf on the first block -> 0
-      float sum = 0.f;
+        const float neg_m = -m;
+        float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = fast_exp2(__uint_as_float(r[c][i]) - m_new);
-          const float p1 = fast_exp2(__uint_as_float(r[c][i + 1]) - m_new);
-          sum += p0 + p1;
-          pk[i >> 1] = pack_bf16(p0, p1);
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = fast_exp2(fmaf(val(c, i), scale_log2, neg_m));
+            const float p1 = fast_exp2(fmaf(val(c, i + 1), scale_log2, neg_m));
+            sp[i & 7] += p0;
+            sp[(i + 1) & 7] += p1;
+            pk[i >> 1] = pack_bf16(p0, p1);
+          }
+          tmem_st16(t_s + (uint32_t)(c * 16), pk);  // P over the consumed S columns
         }
-        tmem_st16(t_s + (uint32_t)(c * 16), pk);  // P over the consumed S columns
-      }
-      l = l * corr + sum;
-      m = m_new;
-      if (j > 0) {  // O *= corr once the previous P.V has landed
+        const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+        l = l * corr + sum;
+      };
+      if (diag) block(std::integral_constant<bool, true>{});
+      else block(std::integral_constant<bool, false>{});
+      if (raise && j > 0) {  // O *= corr once the previous P.V has landed
         if (!bounded_wait_warp(o_full, (j - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
         tc_fence_after();
         uint32_t o[2][32];
@@ -279,8 +309,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 // tables are given) and dV go to the packed gradient buffer; dQ's scale and inverse RoPE are
 // applied by the caller's post pass.
 namespace bwd {
-constexpr int NSOFT = 8;
-constexpr int THREADS_B = 64 + 32 * NSOFT;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
+constexpr int NSOFT = ZL_ATTN_BWD_SOFTMAX_WARPS;
+constexpr int THREADS_B = 64 + 32 * NSOFT;  // warp 0 TMA, warp 1 MMA, warps 2.. softmax
+constexpr int WPQ = NSOFT / 4;              // softmax warps per TMEM lane quadrant
+constexpr int QCOLS = BQ / WPQ;             // query columns (of S^T / dP^T) per softmax warp
+constexpr int DCOLS = D / WPQ;              // head-dim columns (of dQ / dK / dV) per softmax warp
+static_assert(NSOFT == 8 || NSOFT == 16, "softmax warps");
 constexpr int QST = 3;                               // Q / dO / row-vector stages (loads run two blocks ahead)
 constexpr int SM_K = 0, SM_V = TILE_BYTES, SM_Q = 2 * TILE_BYTES, SM_DO = SM_Q + QST * TILE_BYTES;
 constexpr int SM_DS = SM_DO + QST * TILE_BYTES;
@@ -296,7 +330,7 @@ constexpr uint32_t IDESC_SD = make_idesc(1, 128, 128, 0, 0);  // K Q^T / V dO^T:
 constexpr uint32_t IDESC_VK = make_idesc(1, 128, 64, 0, 1);   // dV / dK: A (TMEM or K-major), B MN-major
 constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);    // dQ: A MN-major (dS^T), B MN-major (K)
 
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, %0;" ::"n"(32 * NSOFT) : "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -308,6 +342,17 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
                ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
+}
+
+template <int N> __device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 32, "columns");
+  if constexpr (N == 32) tmem_ld32(taddr, r);
+  else tmem_ld16(taddr, r);
+}
+template <int N> __device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 32, "columns");
+  if constexpr (N == 32) tmem_st32(taddr, r);
+  else tmem_st16(taddr, r);
 }
 
 __global__ void __launch_bounds__(THREADS_B, 1)
@@ -456,7 +501,7 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
   } else {
     const int quarter = warp & 3;
-    const int col_half = (warp - 2) >> 2;         // query columns [64*col_half, 64*col_half + 64)
+    const int cs = (warp - 2) >> 2;               // column slice: queries [QCOLS*cs, +QCOLS), head dims [DCOLS*cs, +DCOLS)
     const int r_local = quarter * 32 + lane;      // key row (S^T / dP^T / dV / dK) and query row (dQ)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     const int key = kb * BKV + r_local;           // position of this thread's key
@@ -469,16 +514,18 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       if (elected) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       named_sync_softmax();
       if (have) {
-        uint32_t dq[32];
+        uint32_t dq[DCOLS];
         tc_fence_after();
-        tmem_ld32(t_lane + C_DQ + (uint32_t)(col_half * 32), dq);
+        tmem_ld_n<DCOLS>(t_lane + C_DQ + (uint32_t)(cs * DCOLS), dq);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(dq_free);
-        uint8_t* rowp = smem + SM_DQ + col_half * (DQ_BYTES / 2) + r_local * 128;
+        // box (cs*DCOLS)/32, 16-byte chunks from ((cs*DCOLS) % 32) / 4
+        uint8_t* rowp = smem + SM_DQ + ((cs * DCOLS) >> 5) * (DQ_BYTES / 2) + r_local * 128;
+        const int k0 = ((cs * DCOLS) & 31) >> 2;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
-          *reinterpret_cast<uint4*>(rowp + ((k ^ (r_local & 7)) * 16)) =
+        for (int k = 0; k < DCOLS / 4; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
+          *reinterpret_cast<uint4*>(rowp + (((k0 + k) ^ (r_local & 7)) * 16)) =
               make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
       }
     };
@@ -507,19 +554,33 @@ __global__ void __launch_bounds__(THREADS_B, 1)
         // thread wait for block i-1's MMAs to release the P^T columns and the dS^T buffer.
         auto chunks = [&](auto diag_tag) {
           constexpr bool DIAG = decltype(diag_tag)::value;
-          uint32_t rs[2][16], rd[2][16];
-          uint32_t pp[32], dd[32];
-          const uint32_t c0 = (uint32_t)(col_half * 64);
-          tmem_ld16(t_lane + C_S + c0, rs[0]);
-          tmem_ld16(t_lane + C_DP + c0, rd[0]);
-          tmem_ld_wait();
+          constexpr int NG = QCOLS / 16;          // sub-chunks of 16 queries
+          // with two softmax warps per sub-partition the TMEM loads of sub-chunk g+1 are issued
+          // before g is computed; with four, the other warps hide the load latency instead
+          constexpr bool PREFETCH = (WPQ == 2);
+          constexpr int NB = PREFETCH ? 2 : 1;
+          uint32_t rs[NB][16], rd[NB][16];
+          uint32_t pp[QCOLS / 2], dd[QCOLS / 2];
+          const uint32_t c0 = (uint32_t)(cs * QCOLS);
+          if constexpr (PREFETCH) {
+            tmem_ld16(t_lane + C_S + c0, rs[0]);
+            tmem_ld16(t_lane + C_DP + c0, rd[0]);
+            tmem_ld_wait();
+          }
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            if (g + 1 < 4) {
-              tmem_ld16(t_lane + C_S + c0 + (uint32_t)((g + 1) * 16), rs[(g + 1) & 1]);
-              tmem_ld16(t_lane + C_DP + c0 + (uint32_t)((g + 1) * 16), rd[(g + 1) & 1]);
+          for (int g = 0; g < NG; ++g) {
+            const int b = PREFETCH ? (g & 1) : 0;
+            if constexpr (PREFETCH) {
+              if (g + 1 < NG) {
+                tmem_ld16(t_lane + C_S + c0 + (uint32_t)((g + 1) * 16), rs[(g + 1) & 1]);
+                tmem_ld16(t_lane + C_DP + c0 + (uint32_t)((g + 1) * 16), rd[(g + 1) & 1]);
+              }
+            } else {
+              tmem_ld16(t_lane + C_S + c0 + (uint32_t)(g * 16), rs[0]);
+              tmem_ld16(t_lane + C_DP + c0 + (uint32_t)(g * 16), rd[0]);
+              tmem_ld_wait();
             }
-            const int q0 = col_half * 64 + g * 16;  // first query of the sub-chunk
+            const int q0 = cs * QCOLS + g * 16;  // first query of the sub-chunk
 #pragma unroll
             for (int j = 0; j < 16; j += 4) {
               const float4 nl4 = *reinterpret_cast<const float4*>(vec + q0 + j);
@@ -529,16 +590,18 @@ __global__ void __launch_bounds__(THREADS_B, 1)
               float p[4], d[4];
 #pragma unroll
               for (int t = 0; t < 4; ++t) {
-                p[t] = fast_exp2(fmaf(__uint_as_float(rs[g & 1][j + t]), scale_log2, nlv[t]));
+                p[t] = fast_exp2(fmaf(__uint_as_float(rs[b][j + t]), scale_log2, nlv[t]));
                 if (DIAG && r_local > q0 + j + t) p[t] = 0.f;
-                d[t] = p[t] * (__uint_as_float(rd[g & 1][j + t]) - dv[t]);
+                d[t] = p[t] * (__uint_as_float(rd[b][j + t]) - dv[t]);
               }
               pp[g * 8 + (j >> 1)] = pack_bf16(p[0], p[1]);
               pp[g * 8 + (j >> 1) + 1] = pack_bf16(p[2], p[3]);
               dd[g * 8 + (j >> 1)] = pack_bf16(d[0], d[1]);
               dd[g * 8 + (j >> 1) + 1] = pack_bf16(d[2], d[3]);
             }
-            if (g + 1 < 4) tmem_ld_wait();
+            if constexpr (PREFETCH) {
+              if (g + 1 < NG) tmem_ld_wait();
+            }
           }
           tc_fence_before();
           mbar_arrive(sd_used);
@@ -549,12 +612,13 @@ __global__ void __launch_bounds__(THREADS_B, 1)
             tc_fence_after();
             have_dq = true;
           }
-          tmem_st32(t_lane + C_P + (uint32_t)(col_half * 32), pp);
+          tmem_st_n<QCOLS / 2>(t_lane + C_P + (uint32_t)(cs * (QCOLS / 2)), pp);
           // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout
-          uint8_t* rowp = sds + col_half * TILE_BYTES + r_local * 128;
+          uint8_t* rowp = sds + ((cs * QCOLS) >> 6) * TILE_BYTES + r_local * 128;
+          const int t0 = ((cs * QCOLS) & 63) >> 3;
 #pragma unroll
-          for (int t = 0; t < 8; ++t)
-            *reinterpret_cast<uint4*>(rowp + ((t ^ (r_local & 7)) * 16)) =
+          for (int t = 0; t < QCOLS / 8; ++t)
+            *reinterpret_cast<uint4*>(rowp + (((t0 + t) ^ (r_local & 7)) * 16)) =
                 make_uint4(dd[t * 4], dd[t * 4 + 1], dd[t * 4 + 2], dd[t * 4 + 3]);
         };
         if (diag) chunks(std::integral_constant<bool, true>{});
@@ -574,18 +638,18 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     dq_readout(niter - 1, ok);
     dq_reduce(niter - 1, ok);
     if (elected) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    // dK (scaled, inverse RoPE) and dV for this key block: columns [32*col_half, 32*col_half + 32)
+    // dK (scaled, inverse RoPE) and dV for this key block: head-dim columns [DCOLS*cs, +DCOLS)
     if (ok) {
       tc_fence_after();
-      uint32_t dk[32], dv[32];
-      tmem_ld32(t_lane + C_DK + (uint32_t)(col_half * 32), dk);
-      tmem_ld32(t_lane + C_DV + (uint32_t)(col_half * 32), dv);
+      uint32_t dk[DCOLS], dv[DCOLS];
+      tmem_ld_n<DCOLS>(t_lane + C_DK + (uint32_t)(cs * DCOLS), dk);
+      tmem_ld_n<DCOLS>(t_lane + C_DV + (uint32_t)(cs * DCOLS), dv);
       tmem_ld_wait();
       const size_t row = (size_t)b * S + key;
-      __nv_bfloat16* dkrow = d_qkv + row * 3 * E + E + h * D + col_half * 32;
-      __nv_bfloat16* dvrow = d_qkv + row * 3 * E + 2 * E + h * D + col_half * 32;
+      __nv_bfloat16* dkrow = d_qkv + row * 3 * E + E + h * D + cs * DCOLS;
+      __nv_bfloat16* dvrow = d_qkv + row * 3 * E + 2 * E + h * D + cs * DCOLS;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < DCOLS / 8; ++q) {
         float x[8], y[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
@@ -595,7 +659,7 @@ __global__ void __launch_bounds__(THREADS_B, 1)
         if (rope_cos) {
 #pragma unroll
           for (int t = 0; t < 8; t += 2) {
-            const int pair = (col_half * 32 + q * 8 + t) >> 1;
+            const int pair = (cs * DCOLS + q * 8 + t) >> 1;
             const float cs = __ldg(rope_cos + (size_t)key * (D / 2) + pair);
             const float sn = __ldg(rope_sin + (size_t)key * (D / 2) + pair);
             const float a0 = x[t], a1 = x[t + 1];
