@@ -121,6 +121,7 @@ struct DistState {
   std::vector<cudaEvent_t> ready_ev;  // recorded on the compute stream when a bucket's grads are final
   cudaEvent_t done_ev = nullptr;      // recorded on comm stream after the last bucket
   int next_bucket = 0;
+  bool joined = false;  // the last step ran as a graph that already waits for its all-reduces
 };
 
 struct zl_model {
@@ -382,7 +383,7 @@ zl_status adamw(zl_model* M, float lr, cudaStream_t st) {
   const float bc1 = 1.0f - powf(M->opt.beta1, (float)M->t);
   const float bc2 = 1.0f - powf(M->opt.beta2, (float)M->t);
   const float gs = 1.0f / (float)M->dist.world;
-  if (M->dist.comm) {
+  if (M->dist.comm && !M->dist.joined) {
     cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);
     cudaStreamWaitEvent(st, M->dist.done_ev, 0);
   }
@@ -567,10 +568,12 @@ zl_status step_graph(zl_model* M, const int32_t* ids, const int32_t* targets, in
                      cudaStream_t st) {
   const bool same = M->graph_exec && M->g_ids == ids && M->g_tgt == targets && M->g_loss == loss_out &&
                     M->g_B == B && M->g_S == S;
+  M->dist.joined = false;
   if (same) {
     cudaError_t e = cudaGraphLaunch(M->graph_exec, st);
     if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "cudaGraphLaunch: %s", cudaGetErrorString(e));
     M->launches = M->g_launches;
+    M->dist.joined = true;
     return ZL_OK;
   }
   const bool seen = M->g_ids == ids && M->g_tgt == targets && M->g_loss == loss_out && M->g_B == B && M->g_S == S;
@@ -587,6 +590,12 @@ zl_status step_graph(zl_model* M, const int32_t* ids, const int32_t* targets, in
   cudaError_t e = cudaStreamBeginCapture(M->cap_stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "cudaStreamBeginCapture: %s", cudaGetErrorString(e));
   zl_status body = step_body(M, ids, targets, B, S, loss_out, M->cap_stream);
+  if (body == ZL_OK && M->dist.comm) {
+    // the gradient all-reduces on the side stream rejoin the captured stream, so one graph launch
+    // covers the whole exchange
+    cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);
+    cudaStreamWaitEvent(M->cap_stream, M->dist.done_ev, 0);
+  }
   cudaGraph_t graph = nullptr;
   e = cudaStreamEndCapture(M->cap_stream, &graph);
   if (body != ZL_OK) {
@@ -603,6 +612,7 @@ zl_status step_graph(zl_model* M, const int32_t* ids, const int32_t* targets, in
   M->g_launches = M->launches;
   e = cudaGraphLaunch(M->graph_exec, st);
   if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "cudaGraphLaunch: %s", cudaGetErrorString(e));
+  M->dist.joined = true;
   return ZL_OK;
 }
 }  // namespace
@@ -622,10 +632,11 @@ extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const 
   if (!M || !ids || !targets) return zl::set_error(ZL_EINVAL, "null argument");
   TRY(check_shape(M, B, S));
   cudaStream_t st = (cudaStream_t)stream;
-  if (M->use_graph && !M->dist.comm) TRY(step_graph(M, ids, targets, B, S, loss_out, st));
+  M->dist.joined = false;
+  if (M->use_graph) TRY(step_graph(M, ids, targets, B, S, loss_out, st));
   else TRY(step_body(M, ids, targets, B, S, loss_out, st));
   if (update) TRY(adamw(M, lr, st));
-  else if (M->dist.comm) {
+  else if (M->dist.comm && !M->dist.joined) {
     cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);
     cudaStreamWaitEvent(st, M->dist.done_ev, 0);
   }
@@ -653,6 +664,7 @@ extern "C" zl_status zl_model_backward(zl_model* M, const int32_t* ids, const fl
   cudaStream_t st = (cudaStream_t)stream;
   TRY(zl_f32_to_bf16(d_logits, reinterpret_cast<zl_bf16*>(M->logits), (int64_t)B * S * M->cfg.vocab_size, stream));
   M->dist.next_bucket = (int)M->dist.b_start.size();  // no collective on this path
+  M->dist.joined = false;
   return backward(M, ids, B, S, st);
 }
 
