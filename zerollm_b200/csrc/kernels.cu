@@ -7,6 +7,7 @@
 // scalar reductions so results are independent of scheduling.
 // The fp32 reference-API kernels keep the reference's per-element
 // semantics (file:line cited on each).
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <cstdarg>
@@ -17,6 +18,7 @@
 #include "common.cuh"
 
 namespace zl {
+int sm_count_current();  // gemm.cu
 
 // ------------------------------------------------------------------ errors
 static thread_local char g_err[512] = "";
@@ -51,6 +53,10 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
   float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y), c = unpack_bf16(u.z), d = unpack_bf16(u.w);
   v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
 }
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y), c = unpack_bf16(u.z), d = unpack_bf16(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
   uint4 u;
   u.x = pack_bf16(v[0], v[1]); u.y = pack_bf16(v[2], v[3]); u.z = pack_bf16(v[4], v[5]); u.w = pack_bf16(v[6], v[7]);
@@ -63,100 +69,146 @@ __device__ __forceinline__ void load8f(const float* p, float (&v)[8]) {
 
 // ================================================================== norms (bf16 rows)
 // kind 0: LayerNorm (layernorm.cu:6-76 semantics: biased variance), kind 1: RMSNorm.
+// One warp per row; the warps stay resident (grid-stride over rows) and fetch the next row's
+// packed input while the current one is reduced and written, so each SM keeps a row per warp in
+// flight.
 template <int KIND, int kMaxChunks>
-__global__ void norm_fwd_bf16_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ g,
-                                     const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
-                                     float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t M, int N,
-                                     float eps) {
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= M) return;
+__global__ void __launch_bounds__(256) norm_fwd_bf16_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const float* __restrict__ g, const float* __restrict__ b,
+                                                          __nv_bfloat16* __restrict__ y, float* __restrict__ mean_out,
+                                                          float* __restrict__ rstd_out, int64_t M, int N, float eps) {
   const int lane = threadIdx.x & 31;
-  const __nv_bfloat16* xr = x + row * N;
-  float v[kMaxChunks][8];
-  float s = 0.f;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  uint4 nxt[kMaxChunks];
+  auto fetch = [&](int64_t r) {
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < N) {
-      load8(xr + col, v[c]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) s += KIND == 0 ? v[c][j] : v[c][j] * v[c][j];
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < N) nxt[c] = __ldg(reinterpret_cast<const uint4*>(x + r * N + col));
     }
-  }
-  s = warp_sum(s);
-  float mu = 0.f, rs;
-  if (KIND == 0) {
-    mu = s / (float)N;
-    float q = 0.f;
+  };
+  if (row < M) fetch(row);
+  for (; row < M; row += nwarps) {
+    float v[kMaxChunks][8];
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c)
+      if ((c * 32 + lane) * 8 < N) unpack8(nxt[c], v[c]);
+    if (row + nwarps < M) fetch(row + nwarps);
+    float s = 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c)
       if ((c * 32 + lane) * 8 < N)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { const float d = v[c][j] - mu; q += d * d; }
-    q = warp_sum(q);
-    rs = rsqrtf(q / (float)N + eps);
-  } else {
-    rs = rsqrtf(s / (float)N + eps);
-  }
-  if (lane == 0) {
-    if (mean_out) mean_out[row] = mu;
-    if (rstd_out) rstd_out[row] = rs;
-  }
+        for (int j = 0; j < 8; ++j) s += KIND == 0 ? v[c][j] : v[c][j] * v[c][j];
+    s = warp_sum(s);
+    float mu = 0.f, rs;
+    if (KIND == 0) {
+      mu = s / (float)N;
+      float q = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < N) {
-      float gv[8], o[8];
-      load8f(g + col, gv);
-      if (KIND == 0) {
-        float bv[8];
-        load8f(b + col, bv);
+      for (int c = 0; c < kMaxChunks; ++c)
+        if ((c * 32 + lane) * 8 < N)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = (v[c][j] - mu) * rs * gv[j] + bv[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = v[c][j] * rs * gv[j];
-      }
-      store8(y + row * N + col, o);
+          for (int j = 0; j < 8; ++j) { const float d = v[c][j] - mu; q += d * d; }
+      q = warp_sum(q);
+      rs = rsqrtf(q / (float)N + eps);
+    } else {
+      rs = rsqrtf(s / (float)N + eps);
     }
-  }
-}
-
-// Backward: one warp per row; per-block column partials of dgamma/dbeta to `part` [gridDim.x][2N].
-template <int KIND, int kMaxChunks>
-__global__ void norm_bwd_bf16_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy,
-                                     const float* __restrict__ g, const float* __restrict__ mean,
-                                     const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-                                     float* __restrict__ part, int64_t M, int N) {
-  extern __shared__ float sacc[];  // [2N]
-  for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) sacc[i] = 0.f;
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-  float pg[kMaxChunks][8], pb[kMaxChunks][8];
-#pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) pg[c][j] = pb[c][j] = 0.f;
-  for (int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += (int64_t)gridDim.x * warps) {
-    const float mu = KIND == 0 ? mean[row] : 0.f, rs = rstd[row];
-    float xh[kMaxChunks][8], a[kMaxChunks][8];
-    float s1 = 0.f, s2 = 0.f;
+    if (lane == 0) {
+      if (mean_out) mean_out[row] = mu;
+      if (rstd_out) rstd_out[row] = rs;
+    }
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < N) {
-        float xv[8], dv[8], gv[8];
-        load8(x + row * N + col, xv);
-        load8(dy + row * N + col, dv);
+        float gv[8], o[8];
+        load8f(g + col, gv);
+        if (KIND == 0) {
+          float bv[8];
+          load8f(b + col, bv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = (v[c][j] - mu) * rs * gv[j] + bv[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = v[c][j] * rs * gv[j];
+        }
+        store8(y + row * N + col, o);
+      }
+    }
+  }
+}
+
+// Backward: one warp per row (resident warps, next row prefetched).  Per-block column partials go
+// to `part` [gridDim.x][NP] with NP = N * (1 + LayerNorm + COL): dgamma | dbeta (LayerNorm) |
+// column sums of dx (COL: the bias gradient of the layer whose output this norm consumed).
+// Rows of up to 512 columns combine their eight warps' partials in shared memory; wider rows use
+// shared-memory atomics.
+template <int KIND, int kMaxChunks, bool COL>
+__global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ dy,
+                                                          const float* __restrict__ g, const float* __restrict__ mean,
+                                                          const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+                                                          float* __restrict__ part, int64_t M, int N) {
+  constexpr int NK = 1 + (KIND == 0 ? 1 : 0) + (COL ? 1 : 0);  // partial sets
+  extern __shared__ float sacc[];                               // [8][NK*N] (tree) or [NK*N] (atomics)
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const bool tree = N <= 512;
+  const int NP = NK * N;
+  if (!tree) {
+    for (int i = threadIdx.x; i < NP; i += blockDim.x) sacc[i] = 0.f;
+    __syncthreads();
+  }
+  float pg[kMaxChunks][8], pb[kMaxChunks][8], pc[kMaxChunks][8];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pg[c][j] = pb[c][j] = pc[c][j] = 0.f;
+  const int64_t nwarps = (int64_t)gridDim.x * warps;
+  int64_t row = (int64_t)blockIdx.x * warps + w;
+  // rows of up to 512 columns prefetch the next row; wider rows would run out of registers
+  constexpr bool PREFETCH = kMaxChunks <= 2;
+  uint4 nx[kMaxChunks], nd[kMaxChunks];
+  auto fetch = [&](int64_t r) {
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < N) {
+        nx[c] = __ldg(reinterpret_cast<const uint4*>(x + r * N + col));
+        nd[c] = __ldg(reinterpret_cast<const uint4*>(dy + r * N + col));
+      }
+    }
+  };
+  if (PREFETCH && row < M) fetch(row);
+  for (; row < M; row += nwarps) {
+    const float mu = KIND == 0 ? mean[row] : 0.f, rs = rstd[row];
+    float xh[kMaxChunks][8], a[kMaxChunks][8];
+    float s1 = 0.f, s2 = 0.f;
+    float dv[kMaxChunks][8];
+    if (!PREFETCH) fetch(row);
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c)
+      if ((c * 32 + lane) * 8 < N) {
+        unpack8(nx[c], xh[c]);
+        unpack8(nd[c], dv[c]);
+      }
+    if (PREFETCH && row + nwarps < M) fetch(row + nwarps);
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < N) {
+        float gv[8];
         load8f(g + col, gv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          xh[c][j] = (xv[j] - mu) * rs;
-          a[c][j] = dv[j] * gv[j];
+          xh[c][j] = (xh[c][j] - mu) * rs;
+          a[c][j] = dv[c][j] * gv[j];
           s1 += a[c][j];
           s2 += a[c][j] * xh[c][j];
-          pg[c][j] += dv[j] * xh[c][j];
-          pb[c][j] += dv[j];
+          pg[c][j] += dv[c][j] * xh[c][j];
+          pb[c][j] += dv[c][j];
         }
       }
     }
@@ -169,24 +221,42 @@ __global__ void norm_bwd_bf16_kernel(const __nv_bfloat16* __restrict__ x, const 
       if (col < N) {
         float o[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 8; ++j) {
           o[j] = KIND == 0 ? rs * (a[c][j] - s1 * invN - xh[c][j] * s2 * invN) : rs * (a[c][j] - xh[c][j] * s2 * invN);
+          if (COL) pc[c][j] += o[j];
+        }
         store8(dx + row * N + col, o);
       }
     }
   }
+  // block partials: [dgamma | dbeta | column sums]
+  auto put = [&](float* base, bool atomic) {
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < N)
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < N)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        atomicAdd(&sacc[col + j], pg[c][j]);
-        if (KIND == 0) atomicAdd(&sacc[N + col + j], pb[c][j]);
-      }
+        for (int j = 0; j < 8; ++j) {
+          int k = 0;
+          if (atomic) atomicAdd(&base[col + j], pg[c][j]); else base[col + j] = pg[c][j];
+          if (KIND == 0) { ++k; if (atomic) atomicAdd(&base[k * N + col + j], pb[c][j]); else base[k * N + col + j] = pb[c][j]; }
+          if (COL) { ++k; if (atomic) atomicAdd(&base[k * N + col + j], pc[c][j]); else base[k * N + col + j] = pc[c][j]; }
+        }
+    }
+  };
+  if (tree) {
+    put(sacc + w * NP, false);
+    __syncthreads();
+    for (int i = threadIdx.x; i < NP; i += blockDim.x) {
+      float t = 0.f;
+      for (int k = 0; k < warps; ++k) t += sacc[k * NP + i];
+      part[(int64_t)blockIdx.x * NP + i] = t;
+    }
+  } else {
+    put(sacc, true);
+    __syncthreads();
+    for (int i = threadIdx.x; i < NP; i += blockDim.x) part[(int64_t)blockIdx.x * NP + i] = sacc[i];
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) part[(int64_t)blockIdx.x * 2 * N + i] = sacc[i];
 }
 
 // Sums per-block partials [nb][stride] into out0 (columns [0, N)) and, when out1 is given, out1
@@ -614,7 +684,7 @@ __global__ void norm_bwd_f32_kernel(const float* __restrict__ x, const float* __
 // Column sums of bf16 [M, N] (bias gradients): per-block partials [nb][N].
 // A block covers `rows_per_block` rows; its threads are laid out as
 // (N/8 column groups) x (256 / (N/8) row lanes) so every row is read with
-// coalesced 16-byte loads, four rows in flight per thread.
+// coalesced 16-byte loads, eight rows in flight per thread.
 __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* __restrict__ dy,
                                                           float* __restrict__ part, int64_t M, int N,
                                                           int64_t rows_per_block) {
@@ -627,12 +697,12 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (rl < rpar) {
     int64_t r = r0 + rl;
-    for (; r + 3 * rpar < r1; r += 4 * rpar) {
-      uint4 u[4];
+    for (; r + 7 * rpar < r1; r += 8 * rpar) {
+      uint4 u[8];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) u[k] = __ldg(reinterpret_cast<const uint4*>(dy + (r + k * rpar) * N + grp * 8));
+      for (int k = 0; k < 8; ++k) u[k] = __ldg(reinterpret_cast<const uint4*>(dy + (r + k * rpar) * N + grp * 8));
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 8; ++k) {
         float2 a = unpack_bf16(u[k].x), b = unpack_bf16(u[k].y), c = unpack_bf16(u[k].z), d = unpack_bf16(u[k].w);
         acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
         acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
@@ -685,16 +755,22 @@ extern "C" zl_status zl_norm_forward_bf16(int kind, const zl_bf16* x, const floa
   const auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   auto Y = reinterpret_cast<__nv_bfloat16*>(y);
   const int ch = N <= 256 ? 1 : N <= 512 ? 2 : N <= 1024 ? 4 : 8;
-#define NF(K, C) norm_fwd_bf16_kernel<K, C><<<nblk(M, 8), 256, 0, ST(s)>>>(X, gamma, K == 0 ? beta : nullptr, Y, K == 0 ? mean : nullptr, rstd, M, N, eps)
+  // resident warps: 8 blocks of 8 warps per SM, each warp walks rows with the next one prefetched
+  const int64_t nbf = std::min<int64_t>(nblk(M, 8), (int64_t)sm_count_current() * 8);
+#define NF(K, C) norm_fwd_bf16_kernel<K, C><<<(unsigned)nbf, 256, 0, ST(s)>>>(X, gamma, K == 0 ? beta : nullptr, Y, K == 0 ? mean : nullptr, rstd, M, N, eps)
   if (kind == 0) { if (ch == 1) NF(0, 1); else if (ch == 2) NF(0, 2); else if (ch == 4) NF(0, 4); else NF(0, 8); }
   else { if (ch == 1) NF(1, 1); else if (ch == 2) NF(1, 2); else if (ch == 4) NF(1, 4); else NF(1, 8); }
 #undef NF
   return check_launch("norm_fwd_bf16");
 }
 extern "C" int zl_norm_bwd_blocks(int64_t M) { return norm_bwd_blocks(M); }
-extern "C" zl_status zl_norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma,
-                                           const float* mean, const float* rstd, zl_bf16* dx, float* dgamma,
-                                           float* dbeta, float* workspace, int64_t M, int N, zl_stream s) {
+namespace zl {
+// Norm backward with optional column sums of dx (`dcol`, accumulated): the bias gradient of the
+// layer whose output feeds this norm, so the model needs no separate column-sum pass for it.
+// `workspace` holds nb * N * (1 + LayerNorm + (dcol != null)) floats.
+zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma, const float* mean,
+                             const float* rstd, zl_bf16* dx, float* dgamma, float* dbeta, float* dcol,
+                             float* workspace, int64_t M, int N, cudaStream_t s) {
   if (M <= 0 || N <= 0) return ZL_OK;
   if (N % 8 || N > 256 * kMaxRowChunks) return set_error(ZL_EUNSUPPORTED, "norm: N=%d must be a multiple of 8, <= 2048", N);
   if (!workspace || !dgamma || (kind == 0 && (!dbeta || !mean))) return set_error(ZL_EINVAL, "norm bwd: null pointer");
@@ -702,16 +778,26 @@ extern "C" zl_status zl_norm_backward_bf16(int kind, const zl_bf16* x, const zl_
   const auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   const auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
   auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
-  const size_t sm = 2 * N * sizeof(float);
+  const int NK = 1 + (kind == 0 ? 1 : 0) + (dcol ? 1 : 0);
+  const size_t sm = (size_t)(N <= 512 ? 8 : 1) * NK * N * sizeof(float);
   const int ch = N <= 256 ? 1 : N <= 512 ? 2 : N <= 1024 ? 4 : 8;
-#define NB(K, C) norm_bwd_bf16_kernel<K, C><<<nb, 256, sm, ST(s)>>>(X, DY, gamma, K == 0 ? mean : nullptr, rstd, DX, workspace, M, N)
-  if (kind == 0) { if (ch == 1) NB(0, 1); else if (ch == 2) NB(0, 2); else if (ch == 4) NB(0, 4); else NB(0, 8); }
-  else { if (ch == 1) NB(1, 1); else if (ch == 2) NB(1, 2); else if (ch == 4) NB(1, 4); else NB(1, 8); }
+#define NB(K, C, COL) norm_bwd_bf16_kernel<K, C, COL><<<nb, 256, sm, s>>>(X, DY, gamma, K == 0 ? mean : nullptr, rstd, DX, workspace, M, N)
+#define NBC(K, COL) { if (ch == 1) NB(K, 1, COL); else if (ch == 2) NB(K, 2, COL); else if (ch == 4) NB(K, 4, COL); else NB(K, 8, COL); }
+  if (kind == 0) { if (dcol) NBC(0, true) else NBC(0, false) }
+  else { if (dcol) NBC(1, true) else NBC(1, false) }
+#undef NBC
 #undef NB
   zl_status st = check_launch("norm_bwd_bf16");
   if (st != ZL_OK) return st;
-  launch_reduce_partials(workspace, nb, N, 2 * N, dgamma, kind == 0 ? dbeta : nullptr, ST(s));
+  launch_reduce_partials(workspace, nb, N, NK * N, dgamma, kind == 0 ? dbeta : nullptr, s);
+  if (dcol) launch_reduce_partials(workspace + (NK - 1) * N, nb, N, NK * N, dcol, nullptr, s);
   return check_launch("norm_bwd_reduce");
+}
+}  // namespace zl
+extern "C" zl_status zl_norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma,
+                                           const float* mean, const float* rstd, zl_bf16* dx, float* dgamma,
+                                           float* dbeta, float* workspace, int64_t M, int N, zl_stream s) {
+  return zl::norm_backward_bf16(kind, x, dy, gamma, mean, rstd, dx, dgamma, dbeta, nullptr, workspace, M, N, ST(s));
 }
 
 extern "C" zl_status zl_embedding_forward_bf16(const int32_t* ids, const float* table, const float* pos, zl_bf16* out,

@@ -29,6 +29,13 @@
 
 #include "common.cuh"
 
+namespace zl {
+// kernels.cu: norm backward that also accumulates column sums of its output (a bias gradient)
+zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma, const float* mean,
+                             const float* rstd, zl_bf16* dx, float* dgamma, float* dbeta, float* dcol,
+                             float* workspace, int64_t M, int N, cudaStream_t s);
+}  // namespace zl
+
 
 // ============================================================== host RNG (same stream as the oracle)
 namespace {
@@ -193,7 +200,7 @@ int64_t step_workspace(const zl_model_config& c, int64_t T, int B_max) {
   g(d, F, Ti, 0); g(Ti, F, d, ZL_A_KMAJOR); g(F, d, Ti, 0); g(Ti, d, F, ZL_A_KMAJOR);
   g(d, d, Ti, 0); g(Ti, d, d, ZL_A_KMAJOR); g(3 * d, d, Ti, 0); g(Ti, d, 3 * d, ZL_A_KMAJOR);
   w = std::max(w, zl_attention_workspace_floats(B_max, (int)(T / B_max), c.num_heads, d / c.num_heads));
-  w = std::max(w, (int64_t)2 * std::max(d, F) * zl_norm_bwd_blocks(T));
+  w = std::max(w, (int64_t)3 * d * zl_norm_bwd_blocks(T));  // dgamma | dbeta | bias column sums
   w = std::max(w, zl_colsum_workspace_floats(T, std::max(3 * d, F)));
   return w;
 }
@@ -330,14 +337,14 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
   for (int l = c.num_layers - 1; l >= 0; --l) {
     const auto& t = M->L.lay[l];
     // out = norm2(r2)
-    TRY(zl_norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r2[l]), reinterpret_cast<zl_bf16*>(M->dx),
-                              P(M, t[L_N2G]), M->mean2[l], M->rstd2[l], reinterpret_cast<zl_bf16*>(M->dr),
-                              G(M, t[L_N2G]), G(M, t[L_N2B]), M->ws, T, d, st));
-    M->launches += 2;
+    // also the FF2 bias gradient: column sums of this norm's output dr
+    TRY(zl::norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r2[l]), reinterpret_cast<zl_bf16*>(M->dx),
+                               P(M, t[L_N2G]), M->mean2[l], M->rstd2[l], reinterpret_cast<zl_bf16*>(M->dr),
+                               G(M, t[L_N2G]), G(M, t[L_N2B]), c.bias ? G(M, t[L_B2]) : nullptr, M->ws, T, d, st));
+    M->launches += c.bias ? 3 : 2;
     TRY(grads_ready(M, end_of_any(M, {t[L_N2G], t[L_N2B]}), st));
     // r2 = h1 + f W2^T + b2
     TRY(gemm(M, M->dr, M->f[l], G(M, t[L_W2]), d, F, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
-    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dr), G(M, t[L_B2]), M->ws, T, d, st)); M->launches += 2; }
     TRY(grads_ready(M, end_of_any(M, {t[L_W2], t[L_B2]}), st));
     zl_epilogue e{};
     e.aux = reinterpret_cast<zl_bf16*>(M->f[l]);
@@ -349,14 +356,14 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     e.residual = reinterpret_cast<zl_bf16*>(M->dr);
     TRY(gemm(M, M->dF, W(M, t[L_W1]), M->dtmp, Ti, d, F, ZL_A_KMAJOR, ZL_EPI_RESIDUAL, &e, st));
     // h1 = norm1(r1)
-    TRY(zl_norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r1[l]), reinterpret_cast<zl_bf16*>(M->dtmp),
-                              P(M, t[L_N1G]), M->mean1[l], M->rstd1[l], reinterpret_cast<zl_bf16*>(M->dr),
-                              G(M, t[L_N1G]), G(M, t[L_N1B]), M->ws, T, d, st));
-    M->launches += 2;
+    // also the output-projection bias gradient: column sums of this norm's output dr
+    TRY(zl::norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r1[l]), reinterpret_cast<zl_bf16*>(M->dtmp),
+                               P(M, t[L_N1G]), M->mean1[l], M->rstd1[l], reinterpret_cast<zl_bf16*>(M->dr),
+                               G(M, t[L_N1G]), G(M, t[L_N1B]), c.bias ? G(M, t[L_BO]) : nullptr, M->ws, T, d, st));
+    M->launches += c.bias ? 3 : 2;
     TRY(grads_ready(M, end_of_any(M, {t[L_N1G], t[L_N1B]}), st));
     // r1 = x + attn Wo^T + bo
     TRY(gemm(M, M->dr, M->attn[l], G(M, t[L_WO]), d, d, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
-    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dr), G(M, t[L_BO]), M->ws, T, d, st)); M->launches += 2; }
     TRY(grads_ready(M, end_of_any(M, {t[L_WO], t[L_BO]}), st));
     TRY(gemm(M, M->dr, W(M, t[L_WO]), M->dattn, Ti, d, d, ZL_A_KMAJOR, 0, nullptr, st));
     TRY(zl_attention_backward_bf16(reinterpret_cast<zl_bf16*>(M->qkv[l]), reinterpret_cast<zl_bf16*>(M->attn[l]),
