@@ -160,16 +160,17 @@ def test_linear_api(K):
 
 # ------------------------------------------------------------------ attention
 @pytest.mark.parametrize("kernel", ["default", "mma"])
-@pytest.mark.parametrize("B,S,H", [(2, 128, 2), (1, 200, 3), (2, 512, 4), (1, 1024, 2)])
-def test_attention_bf16_vs_oracle(L, B, S, H, kernel, monkeypatch):
+@pytest.mark.parametrize("B,S,H,Dh", [(2, 128, 2, 64), (1, 200, 3, 64), (2, 512, 4, 64), (1, 1024, 2, 64),
+                                      (2, 256, 2, 128), (1, 200, 1, 128)])
+def test_attention_bf16_vs_oracle(L, B, S, H, Dh, kernel, monkeypatch):
     """Flash attention fwd+bwd against the oracle.  "default" runs the tcgen05
-    kernels where the shape allows (S % 128 == 0) and mma.sync otherwise;
+    kernels where the shape allows (S % 128 == 0, head dim 64) and mma.sync otherwise;
     "mma" forces the mma.sync kernels."""
     if kernel == "mma":
         monkeypatch.setenv("ZL_ATTENTION_KERNEL", "mma")
     else:
         monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
-    Dh, E = 64, H * 64
+    E = H * Dh
     T = B * S
     qkv = O.normal(T * 3 * E, 21) * 0.5
     qkv_b = torch.from_numpy(qkv).bfloat16()

@@ -156,6 +156,14 @@ def test_step_matches_oracle_26m_seq256(idx):
     _compare_step(c, 8, 256)
 
 
+def test_step_matches_oracle_head_dim_128():
+    """Head dim 128, the attention shape of the scaled configuration (d_model 2048, 16 heads):
+    a small model with 2 heads of 128 and the baseline topology (RMSNorm, RoPE, untied head)."""
+    from zerollm_b200 import Config
+    c = Config(vocab_size=512, embed_dim=256, num_layers=2, num_heads=2, ff_hidden_dim=512, max_seq_len=256)
+    _compare_step(c, 2, 192)
+
+
 def test_full_context_step_properties():
     """26M model at batch 16 x seq 2048 (the timed configuration): the oracle is too slow here, so the
     step is checked through size-independent properties: initial loss ~ ln(V) for N(0,0.02)

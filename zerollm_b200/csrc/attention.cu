@@ -30,13 +30,20 @@ namespace zl {
 namespace fa {
 
 constexpr int TILE = 64;      // rows per tile (queries or keys)
-constexpr int DH = 64;        // head dim supported by the bf16 kernels
 constexpr int THREADS = 128;  // 4 warps
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr int BWD_SMEM = TILE * 128 * 7 + 4 * TILE * 4;
 
-__device__ __forceinline__ uint32_t swz(int row, int col) {  // byte offset in a [64][64] bf16 tile
-  return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1));
+// Shared memory of the kernels for head dim DH (bytes): rows of DH bf16.
+template <int DH> __host__ __device__ constexpr int tile_bytes() { return TILE * DH * 2; }
+template <int DH> __host__ __device__ constexpr int fwd_smem() { return 5 * tile_bytes<DH>(); }  // Q, K[2], V[2]
+// K, V, Q[2], dO[2], dS^T [64][64], lse2[2][64], D[2][64]
+template <int DH> __host__ __device__ constexpr int bwd_smem() { return 6 * tile_bytes<DH>() + TILE * 128 + 4 * TILE * 4; }
+
+// Byte offset of element (row, col) in a swizzled tile with RW bf16 per row: 16-byte chunks are
+// XOR-ed with (row & 7), so the 8 rows an ldmatrix phase reads hit 8 different bank groups.
+template <int RW>
+__device__ __forceinline__ uint32_t swz(int row, int col) {
+  return (uint32_t)(row * (RW * 2) + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1));
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -46,12 +53,14 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Loads a 64-row x 64-col bf16 tile whose row r starts at base + r*ld (elements) into swizzled smem.
+// Loads a 64-row x DH-col bf16 tile whose row r starts at base + r*ld (elements) into swizzled smem.
 // Rows >= valid_rows are zero-filled.
+template <int DH>
 __device__ __forceinline__ void load_tile(uint32_t smem, const __nv_bfloat16* base, int64_t ld, int valid_rows) {
-  for (int i = threadIdx.x; i < TILE * 8; i += THREADS) {
-    const int r = i >> 3, c = (i & 7) * 8;
-    const uint32_t dst = smem + swz(r, c);
+  constexpr int CPR = DH / 8;  // 16-byte chunks per row
+  for (int i = threadIdx.x; i < TILE * CPR; i += THREADS) {
+    const int r = i / CPR, c = (i % CPR) * 8;
+    const uint32_t dst = smem + swz<DH>(r, c);
     if (r < valid_rows) {
       cp_async16(dst, base + (int64_t)r * ld + c);
     } else {
@@ -79,33 +88,41 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 }
 
 // A fragment (16 x 16) at rows [r0, r0+16), cols [c0, c0+16) of a row-major swizzled tile.
+template <int RW>
 __device__ __forceinline__ void load_a(uint32_t tile, int r0, int c0, uint32_t (&a)[4]) {
   const int l = threadIdx.x & 31;
-  ldsm_x4(tile + swz(r0 + (l & 15), c0 + (l >> 4) * 8), a[0], a[1], a[2], a[3]);
+  ldsm_x4(tile + swz<RW>(r0 + (l & 15), c0 + (l >> 4) * 8), a[0], a[1], a[2], a[3]);
 }
 // A fragment from a tile stored transposed: element (m, k) lives at [k][m].
+template <int RW>
 __device__ __forceinline__ void load_a_t(uint32_t tile, int m0, int k0, uint32_t (&a)[4]) {
   const int l = threadIdx.x & 31, i = l >> 3;
   const int k = k0 + (l & 7) + ((i >> 1) << 3), m = m0 + ((i & 1) << 3);
-  ldsm_x4_t(tile + swz(k, m), a[0], a[1], a[2], a[3]);
+  ldsm_x4_t(tile + swz<RW>(k, m), a[0], a[1], a[2], a[3]);
 }
 // B fragments for two n-tiles [n0, n0+16) x k [k0, k0+16) from a tile stored [n][k].
+template <int RW>
 __device__ __forceinline__ void load_b_nk(uint32_t tile, int n0, int k0, uint32_t (&b)[4]) {
   const int l = threadIdx.x & 31;
-  ldsm_x4(tile + swz(n0 + (l & 7) + ((l >> 4) << 3), k0 + ((l >> 3) & 1) * 8), b[0], b[1], b[2], b[3]);
+  ldsm_x4(tile + swz<RW>(n0 + (l & 7) + ((l >> 4) << 3), k0 + ((l >> 3) & 1) * 8), b[0], b[1], b[2], b[3]);
 }
 // B fragments for two n-tiles from a tile stored [k][n] (transposed load).
+template <int RW>
 __device__ __forceinline__ void load_b_kn(uint32_t tile, int k0, int n0, uint32_t (&b)[4]) {
   const int l = threadIdx.x & 31;
-  ldsm_x4_t(tile + swz(k0 + (l & 7) + (((l >> 3) & 1) << 3), n0 + ((l >> 4) << 3)), b[0], b[1], b[2], b[3]);
+  ldsm_x4_t(tile + swz<RW>(k0 + (l & 7) + (((l >> 3) & 1) << 3), n0 + ((l >> 4) << 3)), b[0], b[1], b[2], b[3]);
 }
 
 // ----------------------------------------------------------------- forward
+template <int DH>
 __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                          __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
                                                          int B, int S, int H, float scale_log2) {
-  __shared__ __align__(128) uint8_t sm[TILE * 128 * 5];  // Q, K[2], V[2]
-  const uint32_t sQ = smem_u32(sm), sK0 = sQ + TILE * 128, sV0 = sK0 + 2 * TILE * 128;
+  constexpr int TB = tile_bytes<DH>();
+  constexpr int KD = DH / 16;  // k-steps over the head dim
+  constexpr int ND = DH / 8;   // n-tiles of 8 over the head dim
+  extern __shared__ __align__(128) uint8_t sm[];  // Q, K[2], V[2]
+  const uint32_t sQ = smem_u32(sm), sK0 = sQ + TB, sV0 = sK0 + 2 * TB;
   const int E = H * DH;
   const int64_t ld = 3 * (int64_t)E;
   const int nq = (S + TILE - 1) / TILE;
@@ -115,24 +132,24 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
   const __nv_bfloat16* base = qkv + (int64_t)b * S * ld;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  load_tile(sQ, base + (int64_t)q0 * ld + h * DH, ld, S - q0);
-  load_tile(sK0, base + E + h * DH, ld, S);
-  load_tile(sV0, base + 2 * E + h * DH, ld, S);
+  load_tile<DH>(sQ, base + (int64_t)q0 * ld + h * DH, ld, S - q0);
+  load_tile<DH>(sK0, base + E + h * DH, ld, S);
+  load_tile<DH>(sV0, base + 2 * E + h * DH, ld, S);
   cp_async_commit();
 
-  float o[8][4];
+  float o[ND][4];
 #pragma unroll
-  for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  for (int n = 0; n < ND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-  uint32_t qa[4][4];
+  uint32_t qa[KD][4];
 
   const int nkv = qb + 1;
   for (int j = 0; j < nkv; ++j) {
     const int cur = j & 1;
     if (j + 1 < nkv) {
       const int k1 = (j + 1) * TILE;
-      load_tile(sK0 + (cur ^ 1) * TILE * 128, base + (int64_t)k1 * ld + E + h * DH, ld, S - k1);
-      load_tile(sV0 + (cur ^ 1) * TILE * 128, base + (int64_t)k1 * ld + 2 * E + h * DH, ld, S - k1);
+      load_tile<DH>(sK0 + (cur ^ 1) * TB, base + (int64_t)k1 * ld + E + h * DH, ld, S - k1);
+      load_tile<DH>(sV0 + (cur ^ 1) * TB, base + (int64_t)k1 * ld + 2 * E + h * DH, ld, S - k1);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -141,19 +158,19 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
     __syncthreads();
     if (j == 0) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) load_a(sQ, warp * 16, kk * 16, qa[kk]);
+      for (int kk = 0; kk < KD; ++kk) load_a<DH>(sQ, warp * 16, kk * 16, qa[kk]);
     }
-    const uint32_t sK = sK0 + cur * TILE * 128, sV = sV0 + cur * TILE * 128;
+    const uint32_t sK = sK0 + cur * TB, sV = sV0 + cur * TB;
     // S = Q K^T  (16 x 64 per warp)
     float s[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
+    for (int kk = 0; kk < KD; ++kk)
 #pragma unroll
       for (int n2 = 0; n2 < 4; ++n2) {
         uint32_t bf[4];
-        load_b_nk(sK, n2 * 16, kk * 16, bf);
+        load_b_nk<DH>(sK, n2 * 16, kk * 16, bf);
         mma16816(s[2 * n2], qa[kk], bf[0], bf[1]);
         mma16816(s[2 * n2 + 1], qa[kk], bf[2], bf[3]);
       }
@@ -194,7 +211,7 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
       lrow[hr] = lrow[hr] * corr + sum;
       mrow[hr] = mnew;
 #pragma unroll
-      for (int n = 0; n < 8; ++n) { o[n][2 * hr] *= corr; o[n][2 * hr + 1] *= corr; }
+      for (int n = 0; n < ND; ++n) { o[n][2 * hr] *= corr; o[n][2 * hr + 1] *= corr; }
     }
     // O += P V
 #pragma unroll
@@ -205,9 +222,9 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
       pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
       pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
-      for (int n2 = 0; n2 < 4; ++n2) {
+      for (int n2 = 0; n2 < ND / 2; ++n2) {
         uint32_t bf[4];
-        load_b_kn(sV, kk * 16, n2 * 16, bf);
+        load_b_kn<DH>(sV, kk * 16, n2 * 16, bf);
         mma16816(o[2 * n2], pa, bf[0], bf[1]);
         mma16816(o[2 * n2 + 1], pa, bf[2], bf[3]);
       }
@@ -223,7 +240,7 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
     const float inv = lrow[hr] > 0.f ? 1.f / lrow[hr] : 0.f;
     __nv_bfloat16* orow = out + ((int64_t)b * S + row) * E + h * DH;
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < ND; ++n) {
       const int c = n * 8 + 2 * (lane & 3);
       *reinterpret_cast<uint32_t*>(orow + c) = pack_bf16(o[n][2 * hr] * inv, o[n][2 * hr + 1] * inv);
     }
@@ -235,18 +252,23 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
 // ----------------------------------------------------------------- backward
 // D[b,h,i] = sum_d dO[i,d] * O[i,d]; also zeroes the fp32 dq accumulator and, when `nl` is
 // given, writes nl[b,h,i] = -lse[b,h,i] * log2(e) (the exponent offset the tcgen05 kernel reads).
+// One warp per (token, head); each lane covers Dh/32 consecutive elements.
 __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
                                   const float* __restrict__ lse, float* __restrict__ Dsum, float* __restrict__ nl,
-                                  float* __restrict__ dq_acc, int B, int S, int H) {
+                                  float* __restrict__ dq_acc, int B, int S, int H, int DH) {
   const int E = H * DH;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);  // one warp per (token, head)
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= (int64_t)B * S * H) return;
   const int lane = threadIdx.x & 31;
   const int64_t t = row / H;
   const int h = (int)(row % H);
-  const float2 a = unpack_bf16(*reinterpret_cast<const uint32_t*>(o + t * E + h * DH + 2 * lane));
-  const float2 g = unpack_bf16(*reinterpret_cast<const uint32_t*>(d_o + t * E + h * DH + 2 * lane));
-  float s = a.x * g.x + a.y * g.y;
+  float s = 0.f;
+  for (int c = 2 * lane; c < DH; c += 64) {
+    const float2 a = unpack_bf16(*reinterpret_cast<const uint32_t*>(o + t * E + h * DH + c));
+    const float2 g = unpack_bf16(*reinterpret_cast<const uint32_t*>(d_o + t * E + h * DH + c));
+    s += a.x * g.x + a.y * g.y;
+    *reinterpret_cast<float2*>(dq_acc + t * E + h * DH + c) = make_float2(0.f, 0.f);
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   const int64_t b = t / S, i = t % S;
@@ -254,17 +276,20 @@ __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __n
     Dsum[(b * H + h) * S + i] = s;
     if (nl) nl[(b * H + h) * S + i] = -lse[(b * H + h) * S + i] * LOG2E;
   }
-  *reinterpret_cast<float2*>(dq_acc + t * E + h * DH + 2 * lane) = make_float2(0.f, 0.f);
 }
 
 __device__ __forceinline__ void rope_inv_pair(float& x0, float& x1, const float* ct, const float* st, int pos,
-                                              int pair) {
-  const float c = __ldg(ct + (int64_t)pos * (DH / 2) + pair), s = __ldg(st + (int64_t)pos * (DH / 2) + pair);
+                                              int pair, int half) {
+  const float c = __ldg(ct + (int64_t)pos * half + pair), s = __ldg(st + (int64_t)pos * half + pair);
   const float a = x0, b = x1;
   x0 = a * c + b * s;
   x1 = -a * s + b * c;
 }
 
+// One CTA per (batch, head, 64-key block), four warps of 16 keys; dK / dV accumulate in registers
+// over the query blocks, dQ goes through fp32 atomics.  At head dim 128 the K / V fragments are
+// re-read from shared memory instead of kept in registers.
+template <int DH>
 __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                          const __nv_bfloat16* __restrict__ d_o,
                                                          const float* __restrict__ lse,
@@ -273,12 +298,14 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
                                                          __nv_bfloat16* __restrict__ d_qkv, const float* rope_cos,
                                                          const float* rope_sin, int B, int S, int H, float scale,
                                                          float scale_log2) {
-  // K, V (this key block), Q[2], dO[2], dS^T, lse2[2][64], D[2][64]  (dynamic: > 48 KB)
+  constexpr int TB = tile_bytes<DH>();
+  constexpr int KD = DH / 16;
+  constexpr int ND = DH / 8;
+  constexpr bool CACHE_KV = (DH == 64);
   extern __shared__ __align__(128) uint8_t sm[];
-  const uint32_t sK = smem_u32(sm), sV = sK + TILE * 128, sQ0 = sV + TILE * 128, sD0 = sQ0 + 2 * TILE * 128,
-                 sS = sD0 + 2 * TILE * 128;
-  float* sL = reinterpret_cast<float*>(sm + TILE * 128 * 7);  // [2][64] lse*log2e
-  float* sDs = sL + 2 * TILE;                                   // [2][64] D
+  const uint32_t sK = smem_u32(sm), sV = sK + TB, sQ0 = sV + TB, sD0 = sQ0 + 2 * TB, sS = sD0 + 2 * TB;
+  float* sL = reinterpret_cast<float*>(sm + 6 * TB + TILE * 128);  // [2][64] lse*log2e
+  float* sDs = sL + 2 * TILE;                                        // [2][64] D
   const int E = H * DH;
   const int64_t ld = 3 * (int64_t)E;
   const int nk = (S + TILE - 1) / TILE;
@@ -291,8 +318,8 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
 
   auto load_q_block = [&](int qb, int buf) {
     const int q0 = qb * TILE;
-    load_tile(sQ0 + buf * TILE * 128, base + (int64_t)q0 * ld + h * DH, ld, S - q0);
-    load_tile(sD0 + buf * TILE * 128, dob + (int64_t)q0 * E + h * DH, E, S - q0);
+    load_tile<DH>(sQ0 + buf * TB, base + (int64_t)q0 * ld + h * DH, ld, S - q0);
+    load_tile<DH>(sD0 + buf * TB, dob + (int64_t)q0 * E + h * DH, E, S - q0);
     for (int i = threadIdx.x; i < TILE; i += THREADS) {
       const int q = q0 + i;
       sL[buf * TILE + i] = q < S ? lse[((int64_t)b * H + h) * S + q] * LOG2E : 0.f;
@@ -300,17 +327,17 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
     }
   };
 
-  load_tile(sK, base + (int64_t)k0 * ld + E + h * DH, ld, S - k0);
-  load_tile(sV, base + (int64_t)k0 * ld + 2 * E + h * DH, ld, S - k0);
+  load_tile<DH>(sK, base + (int64_t)k0 * ld + E + h * DH, ld, S - k0);
+  load_tile<DH>(sV, base + (int64_t)k0 * ld + 2 * E + h * DH, ld, S - k0);
   load_q_block(kb, 0);
   cp_async_commit();
 
-  float dk[8][4], dv[8][4];
+  float dk[ND][4], dv[ND][4];
 #pragma unroll
-  for (int n = 0; n < 8; ++n)
+  for (int n = 0; n < ND; ++n)
 #pragma unroll
     for (int e = 0; e < 4; ++e) dk[n][e] = dv[n][e] = 0.f;
-  uint32_t ka[4][4], va[4][4];
+  uint32_t ka[CACHE_KV ? KD : 1][4], va[CACHE_KV ? KD : 1][4];
 
   const int nq = nk;
   for (int qb = kb; qb < nq; ++qb) {
@@ -323,14 +350,14 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
       cp_async_wait<0>();
     }
     __syncthreads();
-    if (qb == kb) {
+    if (CACHE_KV && qb == kb) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        load_a(sK, warp * 16, kk * 16, ka[kk]);
-        load_a(sV, warp * 16, kk * 16, va[kk]);
+      for (int kk = 0; kk < KD; ++kk) {
+        load_a<DH>(sK, warp * 16, kk * 16, ka[CACHE_KV ? kk : 0]);
+        load_a<DH>(sV, warp * 16, kk * 16, va[CACHE_KV ? kk : 0]);
       }
     }
-    const uint32_t sQ = sQ0 + cur * TILE * 128, sDO = sD0 + cur * TILE * 128;
+    const uint32_t sQ = sQ0 + cur * TB, sDO = sD0 + cur * TB;
     const float* Lq = sL + cur * TILE;
     const float* Dq = sDs + cur * TILE;
     const int q0 = qb * TILE;
@@ -341,17 +368,26 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
 #pragma unroll
       for (int e = 0; e < 4; ++e) st[n][e] = dpt[n][e] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
+    for (int kk = 0; kk < KD; ++kk) {
+      uint32_t kf[4], vf[4];
+      if constexpr (CACHE_KV) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) { kf[e] = ka[kk][e]; vf[e] = va[kk][e]; }
+      } else {
+        load_a<DH>(sK, warp * 16, kk * 16, kf);
+        load_a<DH>(sV, warp * 16, kk * 16, vf);
+      }
 #pragma unroll
       for (int n2 = 0; n2 < 4; ++n2) {
         uint32_t bq[4], bd[4];
-        load_b_nk(sQ, n2 * 16, kk * 16, bq);
-        load_b_nk(sDO, n2 * 16, kk * 16, bd);
-        mma16816(st[2 * n2], ka[kk], bq[0], bq[1]);
-        mma16816(st[2 * n2 + 1], ka[kk], bq[2], bq[3]);
-        mma16816(dpt[2 * n2], va[kk], bd[0], bd[1]);
-        mma16816(dpt[2 * n2 + 1], va[kk], bd[2], bd[3]);
+        load_b_nk<DH>(sQ, n2 * 16, kk * 16, bq);
+        load_b_nk<DH>(sDO, n2 * 16, kk * 16, bd);
+        mma16816(st[2 * n2], kf, bq[0], bq[1]);
+        mma16816(st[2 * n2 + 1], kf, bq[2], bq[3]);
+        mma16816(dpt[2 * n2], vf, bd[0], bd[1]);
+        mma16816(dpt[2 * n2 + 1], vf, bd[2], bd[3]);
       }
+    }
     // P^T and dS^T
     const int key_lo = k0 + warp * 16 + (lane >> 2);
 #pragma unroll
@@ -379,10 +415,10 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
       sa[2] = pack_bf16(dpt[2 * kk + 1][0], dpt[2 * kk + 1][1]);
       sa[3] = pack_bf16(dpt[2 * kk + 1][2], dpt[2 * kk + 1][3]);
 #pragma unroll
-      for (int n2 = 0; n2 < 4; ++n2) {
+      for (int n2 = 0; n2 < ND / 2; ++n2) {
         uint32_t bd[4], bq[4];
-        load_b_kn(sDO, kk * 16, n2 * 16, bd);
-        load_b_kn(sQ, kk * 16, n2 * 16, bq);
+        load_b_kn<DH>(sDO, kk * 16, n2 * 16, bd);
+        load_b_kn<DH>(sQ, kk * 16, n2 * 16, bq);
         mma16816(dv[2 * n2], pa, bd[0], bd[1]);
         mma16816(dv[2 * n2 + 1], pa, bd[2], bd[3]);
         mma16816(dk[2 * n2], sa, bq[0], bq[1]);
@@ -394,22 +430,22 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
     for (int n = 0; n < 8; ++n) {
       const int ql = n * 8 + 2 * (lane & 3);
       const int kl = warp * 16 + (lane >> 2);
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sS + swz(kl, ql)), "r"(pack_bf16(dpt[n][0], dpt[n][1])));
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sS + swz(kl + 8, ql)), "r"(pack_bf16(dpt[n][2], dpt[n][3])));
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sS + swz<64>(kl, ql)), "r"(pack_bf16(dpt[n][0], dpt[n][1])));
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(sS + swz<64>(kl + 8, ql)), "r"(pack_bf16(dpt[n][2], dpt[n][3])));
     }
     __syncthreads();
-    // dQ(64 q x 64 d) += dS (q x key) K (key x d): warp w owns queries [16w, 16w+16)
-    float dq[8][4];
+    // dQ(64 q x DH) += dS (q x key) K (key x d): warp w owns queries [16w, 16w+16)
+    float dq[ND][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.f;
+    for (int n = 0; n < ND; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t a[4];
-      load_a_t(sS, warp * 16, kk * 16, a);
+      load_a_t<64>(sS, warp * 16, kk * 16, a);
 #pragma unroll
-      for (int n2 = 0; n2 < 4; ++n2) {
+      for (int n2 = 0; n2 < ND / 2; ++n2) {
         uint32_t bk[4];
-        load_b_kn(sK, kk * 16, n2 * 16, bk);
+        load_b_kn<DH>(sK, kk * 16, n2 * 16, bk);
         mma16816(dq[2 * n2], a, bk[0], bk[1]);
         mma16816(dq[2 * n2 + 1], a, bk[2], bk[3]);
       }
@@ -421,7 +457,7 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
       if (q >= S) continue;
       float* dst = dq_acc + ((int64_t)b * S + q) * E + h * DH;
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < ND; ++n) {
         const int c = n * 8 + 2 * (lane & 3);
         atomicAdd(reinterpret_cast<float2*>(dst + c), make_float2(dq[n][2 * hr], dq[n][2 * hr + 1]));
       }
@@ -437,22 +473,21 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
     __nv_bfloat16* dkrow = d_qkv + ((int64_t)b * S + key) * ld + E + h * DH;
     __nv_bfloat16* dvrow = d_qkv + ((int64_t)b * S + key) * ld + 2 * E + h * DH;
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+    for (int n = 0; n < ND; ++n) {
       const int c = n * 8 + 2 * (lane & 3);
       float x0 = dk[n][2 * hr] * scale, x1 = dk[n][2 * hr + 1] * scale;
-      if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, key, c >> 1);
+      if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, key, c >> 1, DH / 2);
       *reinterpret_cast<uint32_t*>(dkrow + c) = pack_bf16(x0, x1);
       *reinterpret_cast<uint32_t*>(dvrow + c) = pack_bf16(dv[n][2 * hr], dv[n][2 * hr + 1]);
     }
   }
 }
 
-// dq (fp32 accumulator) -> scaled bf16 into the q part of d_qkv (optional inverse RoPE)
 // dQ = scale * dq_acc, rotated back by RoPE, into the Q columns of d_qkv.  dq_acc is [T, E]
 // (token-major, the mma.sync kernel) or [B, H, S, Dh] (head-major, the tcgen05 kernel).
 __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ d_qkv,
                                    const float* rope_cos, const float* rope_sin, int64_t T, int S, int H,
-                                   float scale, int head_major) {
+                                   int DH, float scale, int head_major) {
   const int E = H * DH;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per pair
   if (idx >= T * E / 2) return;
@@ -461,7 +496,7 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat
   const int64_t src = head_major ? (((t / S) * H + c / DH) * S + t % S) * DH + c % DH : t * E + c;
   const float2 v = *reinterpret_cast<const float2*>(dq_acc + src);
   float x0 = v.x * scale, x1 = v.y * scale;
-  if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, (int)(t % S), (c % DH) >> 1);
+  if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, (int)(t % S), (c % DH) >> 1, DH / 2);
   *reinterpret_cast<uint32_t*>(d_qkv + t * 3 * E + c) = pack_bf16(x0, x1);
 }
 
@@ -622,7 +657,8 @@ bool force_mma_sync() {
 extern "C" zl_status zl_attention_forward_bf16(const zl_bf16* qkv, zl_bf16* o, float* lse, int batch, int seq_len,
                                                int num_heads, int head_dim, zl_stream stream) {
   if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return set_error(ZL_EINVAL, "attention: invalid sizes");
-  if (head_dim != fa::DH) return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64)", head_dim);
+  if (head_dim != 64 && head_dim != 128)
+    return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64, 128)", head_dim);
   if (!qkv || !o || !lse) return set_error(ZL_EINVAL, "attention: null pointer");
   if (!force_mma_sync()) {
     zl_status st = ZL_OK;
@@ -632,9 +668,15 @@ extern "C" zl_status zl_attention_forward_bf16(const zl_bf16* qkv, zl_bf16* o, f
   }
   const int nq = (seq_len + fa::TILE - 1) / fa::TILE;
   const float scale_log2 = (1.0f / sqrtf((float)head_dim)) * fa::LOG2E;
-  fa::fa_fwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nq), fa::THREADS, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(o), lse, batch, seq_len,
-      num_heads, scale_log2);
+  const unsigned grid = (unsigned)((int64_t)batch * num_heads * nq);
+  auto launch = [&](auto kern, int smem) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kern<<<grid, fa::THREADS, smem, (cudaStream_t)stream>>>(reinterpret_cast<const __nv_bfloat16*>(qkv),
+                                                            reinterpret_cast<__nv_bfloat16*>(o), lse, batch, seq_len,
+                                                            num_heads, scale_log2);
+  };
+  if (head_dim == 64) launch(fa::fa_fwd_kernel<64>, fa::fwd_smem<64>());
+  else launch(fa::fa_fwd_kernel<128>, fa::fwd_smem<128>());
   return check_launch("fa_fwd_kernel");
 }
 
@@ -647,7 +689,8 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
                                                 int seq_len, int num_heads, int head_dim, const float* rope_cos,
                                                 const float* rope_sin, zl_stream stream) {
   if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return set_error(ZL_EINVAL, "attention: invalid sizes");
-  if (head_dim != fa::DH) return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64)", head_dim);
+  if (head_dim != 64 && head_dim != 128)
+    return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64, 128)", head_dim);
   if (!qkv || !o || !d_o || !lse || !d_qkv || !workspace) return set_error(ZL_EINVAL, "attention bwd: null pointer");
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(ZL_EINVAL, "attention bwd: rope tables");
   cudaStream_t st = (cudaStream_t)stream;
@@ -660,7 +703,7 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
   const int64_t rows = T * num_heads;
   fa::fa_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum,
-      tc ? nl : nullptr, dq_acc, batch, seq_len, num_heads);
+      tc ? nl : nullptr, dq_acc, batch, seq_len, num_heads, head_dim);
   zl_status s = check_launch("fa_bwd_pre_kernel");
   if (s != ZL_OK) return s;
   const float scale = 1.0f / sqrtf((float)head_dim);
@@ -671,17 +714,23 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
     if (s != ZL_OK) return s;
   } else {
     const int nk = (seq_len + fa::TILE - 1) / fa::TILE;
-    cudaFuncSetAttribute(fa::fa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::BWD_SMEM);
-    fa::fa_bwd_kernel<<<(unsigned)((int64_t)batch * num_heads * nk), fa::THREADS, fa::BWD_SMEM, st>>>(
-        reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum, dq_acc,
-        reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch, seq_len, num_heads, scale,
-        scale * fa::LOG2E);
+    const unsigned grid = (unsigned)((int64_t)batch * num_heads * nk);
+    auto launch = [&](auto kern, int smem) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      kern<<<grid, fa::THREADS, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(qkv),
+                                            reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum, dq_acc,
+                                            reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch,
+                                            seq_len, num_heads, scale, scale * fa::LOG2E);
+    };
+    if (head_dim == 64) launch(fa::fa_bwd_kernel<64>, fa::bwd_smem<64>());
+    else launch(fa::fa_bwd_kernel<128>, fa::bwd_smem<128>());
     s = check_launch("fa_bwd_kernel");
     if (s != ZL_OK) return s;
   }
   const int64_t pairs = T * E / 2;
   fa::fa_bwd_post_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
-      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, scale, tc ? 1 : 0);
+      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, head_dim, scale,
+      tc ? 1 : 0);
   return check_launch("fa_bwd_post_kernel");
 }
 

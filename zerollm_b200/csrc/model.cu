@@ -108,7 +108,9 @@ zl_status validate(const zl_model_config& c) {
       c.max_seq_len <= 0)
     return zl::set_error(ZL_EINVAL, "model config: sizes must be positive");
   if (c.embed_dim % c.num_heads) return zl::set_error(ZL_EINVAL, "model config: embed_dim %% num_heads != 0");
-  if (c.embed_dim / c.num_heads != 64) return zl::set_error(ZL_EUNSUPPORTED, "model: head_dim must be 64");
+  if (c.num_heads <= 0 || c.embed_dim % c.num_heads ||
+      (c.embed_dim / c.num_heads != 64 && c.embed_dim / c.num_heads != 128))
+    return zl::set_error(ZL_EUNSUPPORTED, "model: head_dim must be 64 or 128");
   if (c.embed_dim % 64 || c.ff_hidden_dim % 64 || c.vocab_size % 64)
     return zl::set_error(ZL_EUNSUPPORTED, "model: embed_dim, ff_hidden_dim and vocab_size must be multiples of 64");
   if (c.num_layers > 256) return zl::set_error(ZL_EUNSUPPORTED, "model: at most 256 layers");
