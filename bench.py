@@ -33,8 +33,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "train tokens/sec (26M model, seq 2048)"
+# The scaled configuration (vocab 32000, d_model 2048, 24 layers, 16 heads of 128, FFN 8192, ~1.3 B
+# parameters): `--model scaled`, per-GPU batch 8 x 2048, ids seeded 5 (+ rank).
+SCALED = dict(vocab=32000, dim=2048, layers=24, heads=16, ffn=8192)
+METRIC_SCALED = "train tokens/sec (1.3B scaled model, seq 2048)"
+
+
+def flop_per_token(vocab, dim, layers, ffn, seq):
+    """6 * N_gemm + 6 * L * S * d (causal attention, fwd + bwd)."""
+    return 6 * (layers * (4 * dim * dim + 2 * dim * ffn) + vocab * dim) + 6 * layers * seq * dim
 VOCAB, DIM, LAYERS, HEADS, FFN = 6400, 512, 6, 8, 2048
-FLOP_PER_TOKEN = 6 * (LAYERS * (4 * DIM * DIM + 2 * DIM * FFN) + VOCAB * DIM) + 6 * LAYERS * 2048 * DIM
 
 
 def peaks():
@@ -297,14 +305,19 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         uid = [nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-    cfg = Config.baseline_26m()
+    scaled = args.model == "scaled"
+    if scaled:
+        cfg = Config(vocab_size=SCALED["vocab"], embed_dim=SCALED["dim"], num_layers=SCALED["layers"],
+                     num_heads=SCALED["heads"], ff_hidden_dim=SCALED["ffn"], max_seq_len=S)
+    else:
+        cfg = Config.baseline_26m()
     model = ZeroLLM(cfg, T, seed=0, init_std=0.02)
     model.set_optimizer(0.9, 0.95, 1e-8, 0.1)
     if world > 1:
         model.attach_nccl(uid[0], rank, world, 25 * 1024 * 1024)
-    seed = 3 if world == 1 else 4 + rank
+    seed = (5 + rank) if scaled else (3 if world == 1 else 4 + rank)
     rng = np.random.default_rng(seed)
-    ids = rng.integers(0, VOCAB, size=(B, S + 1), dtype=np.int32)
+    ids = rng.integers(0, cfg.vocab_size, size=(B, S + 1), dtype=np.int32)
     h_inp = torch.from_numpy(np.ascontiguousarray(ids[:, :S])).reshape(-1).pin_memory()
     h_tgt = torch.from_numpy(np.ascontiguousarray(ids[:, 1:])).reshape(-1).pin_memory()
     d_inp, d_tgt = h_inp.cuda(), h_tgt.cuda()
@@ -369,26 +382,30 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.empty_cache()
 
     bd, roof = None, None
-    if rank == 0 and not args.no_breakdown:
+    if rank == 0 and not args.no_breakdown and not scaled:
         bd = kernel_breakdown(B, S)
         roof = roofline_of(bd, peaks())
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and not scaled:
         cpu = cpu_sample(1, 2048, 1)
     if rank != 0:
         return
     tokens = T * world
     value = tokens / (ms * 1e-3)
     pk = peaks()
+    fpt = flop_per_token(cfg.vocab_size, cfg.embed_dim, cfg.num_layers, cfg.ff_hidden_dim, S)
+    name = "1.3B scaled ZeroLLM" if scaled else "26M ZeroLLM"
     line = {
-        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform ids in [0,6400), N(0,0.02) weights)",
-        "config": {"workload": f"26M ZeroLLM training step (RMSNorm, RoPE, untied head), batch {B} x seq {S} per GPU",
-                   "model": "zerollm-26m", "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
-                   "l2": "inputs larger than L2 (per-step working set ~3 GB)"},
-        "mfu": round(value * FLOP_PER_TOKEN / world / (pk["bf16_tflops"] * 1e12), 4),
-        "flop_per_token": FLOP_PER_TOKEN,
+        "metric": METRIC_SCALED if scaled else METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic (uniform ids in [0,{cfg.vocab_size}), N(0,0.02) weights)",
+        "config": {"workload": f"{name} training step (RMSNorm, RoPE, untied head), batch {B} x seq {S} per GPU",
+                   "model": "zerollm-1.3b-scaled" if scaled else "zerollm-26m", "global_batch": B * world,
+                   "seq_len": S, "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (per-step working set of several GB)"},
+        "mfu": round(value * fpt / world / (pk["bf16_tflops"] * 1e12), 4),
+        "flop_per_token": fpt,
         "e2e": {"value": round(tokens / (ms_e2e * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(2 * T * 4), "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
@@ -410,12 +427,15 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--model", default="26m", choices=["26m", "scaled"])
+    ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (default 16; 8 for --model scaled)")
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--no-breakdown", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.batch is None:
+        args.batch = 8 if args.model == "scaled" else 16
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -402,7 +402,8 @@ def test_sgd_adam_api_vs_oracle(K):
 
 
 def test_colsum_bf16(L):
-    for M, N in [(32768, 512), (1000, 1536), (4096, 2048)]:
+    # widths above 2048 run in 2048-column slices (FF1 of the scaled shape: 8192; its QKV: 6144)
+    for M, N in [(32768, 512), (1000, 1536), (4096, 2048), (2048, 8192), (777, 6144), (300, 2056)]:
         x = torch.randn(M, N).bfloat16()
         ref = x.float().sum(0)
         db = torch.ones(N, device="cuda")

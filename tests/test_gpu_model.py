@@ -189,6 +189,31 @@ def test_full_context_step_properties():
     m.close()
 
 
+def test_scaled_config_step_properties():
+    """The scaled shape (vocab 32000, d_model 2048, 24 layers, 16 heads of 128, FFN 8192, ~1.3 B
+    parameters) on one sequence of 2048: initial loss ~ ln(V) + s^2/2 for N(0, 0.02) weights,
+    finite gradients, and repeated steps on the batch reduce the loss."""
+    from zerollm_b200 import Config, ZeroLLM
+    c = Config(vocab_size=32000, embed_dim=2048, num_layers=24, num_heads=16, ff_hidden_dim=8192, max_seq_len=2048)
+    B, S = 1, 2048
+    m = ZeroLLM(c, B * S, seed=5)
+    assert 1.2e9 < m.num_params < 1.5e9, m.num_params
+    m.set_optimizer()
+    inp, tgt = _batch(B, S, c.vocab_size, 5)
+    ids, tg = torch.from_numpy(inp).cuda(), torch.from_numpy(tgt).cuda()
+    l0 = m.train_step(ids, tg, B, S, lr=1e-4).item()
+    s2 = (0.02 ** 2) * c.embed_dim
+    assert abs(l0 - (np.log(c.vocab_size) + s2 / 2)) < 0.1, l0
+    g = m.grads()
+    assert np.isfinite(g).all() and np.abs(g).max() > 0
+    del g
+    losses = [l0]
+    for _ in range(3):
+        losses.append(m.train_step(ids, tg, B, S, lr=1e-4).item())
+    assert losses[-1] < losses[0] - 0.1, losses
+    m.close()
+
+
 def test_graph_replay_matches_eager():
     """Steps replayed from the captured CUDA graph equal eagerly launched steps (up to the
     summation-order freedom of the fp32 atomics in the embedding and dQ accumulation)."""

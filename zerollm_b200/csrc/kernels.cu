@@ -685,15 +685,19 @@ __global__ void norm_bwd_f32_kernel(const float* __restrict__ x, const float* __
 // A block covers `rows_per_block` rows; its threads are laid out as
 // (N/8 column groups) x (256 / (N/8) row lanes) so every row is read with
 // coalesced 16-byte loads, eight rows in flight per thread.
+// blockIdx.y selects a slice of up to 2048 columns (rows longer than 2048 use several slices).
 __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* __restrict__ dy,
                                                           float* __restrict__ part, int64_t M, int N,
                                                           int64_t rows_per_block) {
-  const int groups = N / 8;
+  const int col0 = blockIdx.y * 2048;
+  const int W = min(2048, N - col0);  // this slice's columns
+  const int groups = W / 8;
   const int rpar = blockDim.x / groups;
   const int grp = threadIdx.x % groups, rl = threadIdx.x / groups;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per_block;
   const int64_t r1 = r0 + rows_per_block < M ? r0 + rows_per_block : M;
-  extern __shared__ float sc[];  // [rpar][N]
+  extern __shared__ float sc[];  // [rpar][W]
+  dy += col0;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (rl < rpar) {
     int64_t r = r0 + rl;
@@ -715,13 +719,13 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
       for (int j = 0; j < 8; ++j) acc[j] += v[j];
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sc[rl * N + grp * 8 + j] = acc[j];
+    for (int j = 0; j < 8; ++j) sc[rl * W + grp * 8 + j] = acc[j];
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < N; c += blockDim.x) {
+  for (int c = threadIdx.x; c < W; c += blockDim.x) {
     float s = 0.f;
-    for (int k = 0; k < rpar; ++k) s += sc[k * N + c];
-    part[(int64_t)blockIdx.x * N + c] = s;
+    for (int k = 0; k < rpar; ++k) s += sc[k * W + c];
+    part[(int64_t)blockIdx.x * N + col0 + c] = s;
   }
 }
 
@@ -845,13 +849,15 @@ extern "C" int64_t zl_colsum_workspace_floats(int64_t M, int N) {
 }
 extern "C" zl_status zl_colsum_bf16(const zl_bf16* dy, float* db, float* workspace, int64_t M, int N, zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;
-  if (N % 8 || N / 8 > 256) return set_error(ZL_EUNSUPPORTED, "colsum: N=%d (multiple of 8, <= 2048)", N);
+  if (N % 8) return set_error(ZL_EUNSUPPORTED, "colsum: N=%d must be a multiple of 8", N);
   const int64_t rpb = colsum_rows_per_block(M);
   const int nb = (int)((M + rpb - 1) / rpb);
-  const int groups = N / 8;
-  const int rpar = 256 / groups;
-  const int threads = rpar * groups;
-  colsum_bf16_kernel<<<nb, threads, (size_t)rpar * N * sizeof(float), ST(s)>>>(
+  const int slices = (N + 2047) / 2048;
+  const int W = N < 2048 ? N : 2048;  // widest slice
+  const int rpar = 256 / (W / 8);     // row lanes of the widest slice (narrower slices use more)
+  const int smem_rows = 256 / ((N - (slices - 1) * 2048) / 8);
+  const size_t smem = (size_t)std::max(rpar * W, smem_rows * (N - (slices - 1) * 2048)) * sizeof(float);
+  colsum_bf16_kernel<<<dim3(nb, slices), 256, smem, ST(s)>>>(
       reinterpret_cast<const __nv_bfloat16*>(dy), workspace, M, N, rpb);
   zl_status st = check_launch("colsum_bf16");
   if (st != ZL_OK) return st;

@@ -23,6 +23,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include <nccl.h>
@@ -45,16 +46,32 @@ uint64_t splitmix64(uint64_t* s) {
   z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
   return z ^ (z >> 31);
 }
-void fill_normal(float* out, int64_t n, uint64_t seed, float mean, float stdv) {
-  uint64_t s = seed;
+// Normals by Box-Muller, one pair per two draws.  splitmix64 advances its state by a fixed step
+// per draw, so the pair range [p0, p1) starts from seed + 2 * p0 * step and large tensors are filled
+// by several host threads with exactly the serial sequence.
+void fill_normal_range(float* out, int64_t n, uint64_t seed, float mean, float stdv, int64_t p0, int64_t p1) {
+  uint64_t s = seed + 2ull * (uint64_t)p0 * 0x9E3779B97F4A7C15ull;
   const double two_pi = 6.283185307179586476925286766559;
-  for (int64_t i = 0; i < n; i += 2) {
+  for (int64_t p = p0; p < p1; ++p) {
+    const int64_t i = 2 * p;
     const double u1 = ((double)(splitmix64(&s) >> 11) + 1.0) * (1.0 / 9007199254740992.0);
     const double u2 = (double)(splitmix64(&s) >> 11) * (1.0 / 9007199254740992.0);
     const double r = sqrt(-2.0 * log(u1));
     out[i] = (float)(mean + stdv * r * cos(two_pi * u2));
     if (i + 1 < n) out[i + 1] = (float)(mean + stdv * r * sin(two_pi * u2));
   }
+}
+void fill_normal(float* out, int64_t n, uint64_t seed, float mean, float stdv) {
+  const int64_t pairs = (n + 1) / 2;
+  const int64_t nt = std::min<int64_t>(std::max(1u, std::thread::hardware_concurrency()), 32);
+  if (pairs < (1 << 18) || nt == 1) {
+    fill_normal_range(out, n, seed, mean, stdv, 0, pairs);
+    return;
+  }
+  std::vector<std::thread> th;
+  for (int64_t t = 0; t < nt; ++t)
+    th.emplace_back(fill_normal_range, out, n, seed, mean, stdv, pairs * t / nt, pairs * (t + 1) / nt);
+  for (auto& x : th) x.join();
 }
 
 enum Kind { K_MAT = 0, K_BIAS = 1, K_GAMMA = 2, K_BETA = 3, K_EMB = 4 };
