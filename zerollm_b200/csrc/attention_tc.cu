@@ -34,14 +34,23 @@ namespace fatc {
 constexpr int BQ = 128, BKV = 128, D = 64;
 constexpr int THREADS = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 softmax / epilogue
 constexpr int TILE_BYTES = 128 * 128; // 128 rows x 64 bf16
-constexpr int KVST = 4;               // K / V stages (loads run three blocks ahead)
-constexpr int SMEM_Q = 0, SMEM_K = TILE_BYTES, SMEM_V = SMEM_K + KVST * TILE_BYTES;
-constexpr int SMEM_BAR = SMEM_V + KVST * TILE_BYTES;
-constexpr int SMEM_TOTAL = SMEM_BAR + 128 + 1024;
-constexpr uint32_t TMEM_COLS = 512;   // S/P buffer b at [128 b, 128 b + 128), O at [256, 320)
+constexpr uint32_t TMEM_COLS = 512;   // forward: S/P buffer b at [128 b, 128 b + 128), O at [256, 256 + Dh)
 constexpr uint32_t O_COL = 256;
 constexpr uint32_t IDESC_S = make_idesc(1, 128, 128, 0, 0);  // bf16, M=128, N=128, A/B K-major
-constexpr uint32_t IDESC_O = make_idesc(1, 128, 64, 0, 1);   // bf16, M=128, N=64, A (TMEM) K-major, B MN-major
+
+// Forward shapes by head dim: a 128-row tile of Q, K or V is Dh/64 swizzle atoms of [128][64] bf16
+// side by side (16 KB each); K / V stages fill the rest of shared memory.
+template <int DH>
+struct Fwd {
+  static constexpr int ATOMS = DH / 64;
+  static constexpr int T_BYTES = ATOMS * TILE_BYTES;
+  static constexpr int KVST = DH == 64 ? 4 : 3;  // loads run KVST-1 blocks ahead
+  static constexpr int SMEM_Q = 0, SMEM_K = T_BYTES, SMEM_V = SMEM_K + KVST * T_BYTES;
+  static constexpr int SMEM_BAR = SMEM_V + KVST * T_BYTES;
+  static constexpr int SMEM_TOTAL = SMEM_BAR + 128 + 1024;
+  static constexpr uint32_t IDESC_O = make_idesc(1, 128, DH, 0, 1);  // M=128, N=Dh, A (TMEM), B MN-major
+  static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
+};
 
 enum : int { DEV_TIMEOUT_ATTN = 11 };
 
@@ -51,9 +60,13 @@ __device__ __forceinline__ float fast_exp2(float x) {  // MUFU ex2 (inputs <= 0 
   return y;
 }
 
+template <int DH>
 __global__ void __launch_bounds__(THREADS, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out,
                      float* __restrict__ lse, int S, int H, float scale_log2) {
+  using C = Fwd<DH>;
+  constexpr int KVST = C::KVST, SMEM_Q = C::SMEM_Q, SMEM_K = C::SMEM_K, SMEM_V = C::SMEM_V, SMEM_BAR = C::SMEM_BAR;
+  constexpr int T_BYTES = C::T_BYTES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -67,7 +80,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* drain = s_full + 4;             // final commit: every MMA of this CTA has retired
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 5);
 
-  const int E = H * D;
+  const int E = H * DH;
   const int nq = S / BQ;
   const int qb = nq - 1 - (int)(blockIdx.x % nq);  // heavy blocks first
   const int bh = blockIdx.x / nq, b = bh / H, h = bh % H;
@@ -100,17 +113,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_2d(smem + SMEM_Q, &tm, q_full, h * D, row0);
+      mbar_arrive_expect_tx(q_full, T_BYTES);
+#pragma unroll
+      for (int a = 0; a < C::ATOMS; ++a)
+        tma_load_2d(smem + SMEM_Q + a * TILE_BYTES, &tm, q_full, h * DH + a * 64, row0);
       int issued = 0;
       for (int j = 0; j < nkv; ++j) {
         const int st = j % KVST;
         const uint32_t ph = (j / KVST) & 1;
         if (!bounded_wait(&kv_empty[st], ph ^ 1u, DEV_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * T_BYTES);
         const int krow = b * S + j * BKV;
-        tma_load_2d(smem + SMEM_K + st * TILE_BYTES, &tm, &kv_full[st], E + h * D, krow);
-        tma_load_2d(smem + SMEM_V + st * TILE_BYTES, &tm, &kv_full[st], 2 * E + h * D, krow);
+#pragma unroll
+        for (int a = 0; a < C::ATOMS; ++a) {
+          tma_load_2d(smem + SMEM_K + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st], E + h * DH + a * 64, krow);
+          tma_load_2d(smem + SMEM_V + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st], 2 * E + h * DH + a * 64,
+                      krow);
+        }
         issued = j + 1;
       }
       // no copy may still be landing in shared memory when the CTA exits
@@ -123,12 +142,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t sq = smem_u32(smem + SMEM_Q);
     auto issue_s = [&](int j) {  // S_j = Q K_j^T into TMEM buffer j & 1 (K from stage j % KVST)
       const int sb = j & 1;
-      const uint32_t sk = smem_u32(smem + SMEM_K + (j % KVST) * TILE_BYTES);
+      const uint32_t sk = smem_u32(smem + SMEM_K + (j % KVST) * T_BYTES);
       if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k)
-          umma_f16(tmem + (uint32_t)(sb * BKV), smem_desc_sw128(sq + k * 32, 16, 1024),
-                   smem_desc_sw128(sk + k * 32, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
+        for (int k = 0; k < DH / 16; ++k) {  // 16 head dims per MMA: atom k / 4, 32 bytes per step inside it
+          const uint32_t off = (uint32_t)((k >> 2) * TILE_BYTES + (k & 3) * 32);
+          umma_f16(tmem + (uint32_t)(sb * BKV), smem_desc_sw128(sq + off, 16, 1024),
+                   smem_desc_sw128(sk + off, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
+        }
         umma_commit(&s_full[sb]);
       }
       __syncwarp();
@@ -149,12 +170,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!bounded_wait_warp(p_full, j & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t sv = smem_u32(smem + SMEM_V + st * TILE_BYTES);
+      const uint32_t sv = smem_u32(smem + SMEM_V + st * T_BYTES);
       if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA: P columns k*8.., V rows k*16..
+        for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA: P columns k*8.., V rows k*16.. (atoms TILE_BYTES apart)
           umma_f16_ts(tmem + O_COL, tmem + (uint32_t)(sb * BKV + k * 8),
-                      smem_desc_sw128(sv + k * 16 * 128, TILE_BYTES, 1024), IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
+                      smem_desc_sw128(sv + k * 16 * 128, TILE_BYTES, 1024), C::IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(o_full);
         umma_commit(&kv_empty[st]);
       }
@@ -237,16 +258,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (raise && j > 0) {  // O *= corr once the previous P.V has landed
         if (!bounded_wait_warp(o_full, (j - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
         tc_fence_after();
-        uint32_t o[2][32];
-        tmem_ld32(t_lane + O_COL, o[0]);
-        tmem_ld32(t_lane + O_COL + 32, o[1]);
-        tmem_ld_wait();
+#pragma unroll 1
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_lane + O_COL + (uint32_t)(c * 32), o);
+          tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * corr);
-        tmem_st32(t_lane + O_COL, o[0]);
-        tmem_st32(t_lane + O_COL + 32, o[1]);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+          tmem_st32(t_lane + O_COL + (uint32_t)(c * 32), o);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
@@ -256,22 +276,22 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (ok && bounded_wait_warp(o_full, (nkv - 1) & 1, DEV_TIMEOUT_ATTN)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = out + (size_t)(row0 + r_local) * E + h * D;
-      uint32_t o[2][32];
-      tmem_ld32(t_lane + O_COL, o[0]);
-      tmem_ld32(t_lane + O_COL + 32, o[1]);
-      tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
+      __nv_bfloat16* orow = out + (size_t)(row0 + r_local) * E + h * DH;
+#pragma unroll 1
+      for (int c = 0; c < DH / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + O_COL + (uint32_t)(c * 32), o);
+        tmem_ld_wait();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 u;
-          u.x = pack_bf16(__uint_as_float(o[c][q * 8 + 0]) * inv, __uint_as_float(o[c][q * 8 + 1]) * inv);
-          u.y = pack_bf16(__uint_as_float(o[c][q * 8 + 2]) * inv, __uint_as_float(o[c][q * 8 + 3]) * inv);
-          u.z = pack_bf16(__uint_as_float(o[c][q * 8 + 4]) * inv, __uint_as_float(o[c][q * 8 + 5]) * inv);
-          u.w = pack_bf16(__uint_as_float(o[c][q * 8 + 6]) * inv, __uint_as_float(o[c][q * 8 + 7]) * inv);
+          u.x = pack_bf16(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
+          u.y = pack_bf16(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
+          u.z = pack_bf16(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
+          u.w = pack_bf16(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
           *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) = u;
         }
+      }
       lse[((size_t)b * H + h) * S + qb * BQ + r_local] = (m + log2f(l)) * 0.6931471805599453f;
     }
   }
@@ -686,20 +706,24 @@ __global__ void __launch_bounds__(THREADS_B, 1)
 }  // namespace bwd
 }  // namespace fatc
 
-// Returns true if the tcgen05 kernel handled the call.
+// Returns true if the tcgen05 kernel handled the call (head dim 64 or 128, S a multiple of 128).
 bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh,
                       cudaStream_t st, zl_status* status) {
-  if (Dh != fatc::D || S % fatc::BQ != 0 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return false;
+  if ((Dh != 64 && Dh != 128) || S % fatc::BQ != 0 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return false;
   CUtensorMap tm;
   const int E = H * Dh;
   if (!make_tma_map(&tm, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128)) {
     *status = set_error(ZL_ECUDA, "attention: cuTensorMapEncodeTiled failed");
     return true;
   }
-  cudaFuncSetAttribute(fatc::fa_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM_TOTAL);
   const float scale_log2 = (1.0f / sqrtf((float)Dh)) * 1.4426950408889634f;
   const int grid = B * H * (S / fatc::BQ);
-  fatc::fa_fwd_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM_TOTAL, st>>>(tm, out, lse, S, H, scale_log2);
+  auto launch = [&](auto kern, int smem) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kern<<<grid, fatc::THREADS, smem, st>>>(tm, out, lse, S, H, scale_log2);
+  };
+  if (Dh == 64) launch(fatc::fa_fwd_tc_kernel<64>, fatc::Fwd<64>::SMEM_TOTAL);
+  else launch(fatc::fa_fwd_tc_kernel<128>, fatc::Fwd<128>::SMEM_TOTAL);
   *status = check_launch("fa_fwd_tc_kernel");
   return true;
 }
