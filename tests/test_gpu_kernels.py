@@ -67,9 +67,18 @@ def _gemm(L, A, B, M, N, K_, layout, flags=0, epi=None, out=None, ws=None):
     return out
 
 
+@pytest.fixture(params=["pair", "single"])
+def gemm_kind(request, monkeypatch):
+    """bf16 GEMMs of at least 256 rows can run on the CTA-pair kernel (cta_group::2) or the
+    one-SM kernel; ZL_GEMM_PAIR=1 / 0 forces one of them, so every GEMM test runs both."""
+    monkeypatch.setenv("ZL_GEMM_PAIR", "1" if request.param == "pair" else "0")
+    return request.param
+
+
 @pytest.mark.parametrize("a_k,b_k", [(True, True), (True, False), (False, True), (False, False)])
-@pytest.mark.parametrize("M,N,K_", [(128, 256, 64), (304, 200, 136), (1024, 512, 512), (512, 1536, 512)])
-def test_gemm_bf16_layouts(L, a_k, b_k, M, N, K_):
+@pytest.mark.parametrize("M,N,K_", [(128, 256, 64), (304, 200, 136), (1024, 512, 512), (512, 1536, 512),
+                                    (640, 392, 200), (2304, 128, 512)])
+def test_gemm_bf16_layouts(L, a_k, b_k, M, N, K_, gemm_kind):
     g = torch.Generator().manual_seed(M * 7 + N)
     A = torch.randn(M, K_, generator=g)
     B = torch.randn(N, K_, generator=g)
@@ -85,7 +94,7 @@ def test_gemm_bf16_layouts(L, a_k, b_k, M, N, K_):
 
 
 @pytest.mark.parametrize("T,N,K_", [(32768, 512, 2048), (2048, 2048, 512), (2048, 512, 2048), (2048, 1536, 512)])
-def test_gemm_bf16_weight_grad_splitk(L, T, N, K_):
+def test_gemm_bf16_weight_grad_splitk(L, T, N, K_, gemm_kind):
     """dW-shaped products dW[N,K] = dY[T,N]^T X[T,K]: reduction over T, both operands MN-major
     (split-K path), in both orientations of the FFN weights."""
     g = torch.Generator().manual_seed(1)
@@ -99,7 +108,7 @@ def test_gemm_bf16_weight_grad_splitk(L, T, N, K_):
     assert rel(acc.cpu().view(N, K_), ref + 1.0) < 1e-4
 
 
-def test_gemm_bf16_epilogues(L):
+def test_gemm_bf16_epilogues(L, gemm_kind):
     import ctypes as C
     M, N, K_ = 512, 1536, 512
     S, Dh = 256, 64

@@ -17,6 +17,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -455,6 +456,209 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ two-SM GEMM (bf16)
+// A cluster of two CTAs on two SMs computes 256 x BN output tiles with tcgen05.mma.cta_group::2:
+// each CTA loads its own 128 rows of A and half of the BN columns of B (so every SM streams half
+// of B per tile instead of all of it), the even CTA issues the MMAs for both, and each CTA keeps
+// its 128 x BN half of the accumulator in its own TMEM and drains it with its own epilogue warps.
+//   * full[s]      (even CTA) counts the bytes both CTAs' TMA loads bring into stage s
+//   * empty[s]     (both CTAs) arrived by the MMA's multicast commit when stage s is consumed
+//   * acc_full[b]  (both CTAs) arrived by the multicast commit when accumulator b is complete
+//   * acc_empty[b] (even CTA) arrived by the epilogue threads of both CTAs
+// No TMA load uses multicast.
+template <int BN, int STAGES>
+struct Smem2 {
+  static constexpr int A_BYTES = BM * 128;         // this CTA's 128 rows of A (or BK x 128)
+  static constexpr int B_BYTES = (BN / 2) * 128;   // this CTA's half of B
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kStgBytes;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmArgs args) {
+  using L = Smem2<BN, STAGES>;
+  constexpr int BK = 64, UMMA_K = 16, ATOM = 64;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = make_idesc(1, 2 * BM, BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = (int)blockIdx.x >> 1, npairs = (int)gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 2 * kEpiWarps * 32); }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = pair; u < args.units && ok; u += npairs) {
+        const int tile = u / args.splits, split = u % args.splits;
+        const int m0 = (tile / args.n_tiles_n) * (2 * BM) + (int)rank * BM;  // this CTA's rows
+        const int n0 = (tile % args.n_tiles_n) * BN + (int)rank * (BN / 2);  // this CTA's half of B
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!bounded_wait(&empty[stage], phase ^ 1u, DEV_TIMEOUT_EMPTY)) { ok = false; break; }
+          uint8_t* sA = smem + stage * L::STAGE_BYTES;
+          uint8_t* sB = sA + L::A_BYTES;
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);  // the even CTA's barrier
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d_pair(sA, &tmA, bar, k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / ATOM; ++c) tma_load_2d_pair(sA + c * BK * 128, &tmA, bar, m0 + c * ATOM, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(sB, &tmB, bar, k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < (BN / 2) / ATOM; ++c)
+              tma_load_2d_pair(sB + c * BK * 128, &tmB, bar, n0 + c * ATOM, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (even CTA only)
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = pair; u < args.units && ok; u += npairs) {
+        const int split = u % args.splits;
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
+        // both CTAs' epilogues have drained accumulator `acc`
+        if (!__all_sync(0xffffffffu, bounded_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, DEV_TIMEOUT_ACC))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!bounded_wait_warp(&full[stage], phase, DEV_TIMEOUT_FULL)) { ok = false; break; }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a_base = smem_u32(smem + stage * L::STAGE_BYTES);
+            const uint32_t b_base = a_base + L::A_BYTES;
+#pragma unroll
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+              uint64_t ad, bd;
+              if (!A_MN) ad = smem_desc_sw128(a_base + k * UMMA_K * 2, 16, 1024);
+              else       ad = smem_desc_sw128(a_base + k * UMMA_K * 128, BK * 128, 1024);
+              if (!B_MN) bd = smem_desc_sw128(b_base + k * UMMA_K * 2, 16, 1024);
+              else       bd = smem_desc_sw128(b_base + k * UMMA_K * 128, BK * 128, 1024);
+              umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit_pair(&empty[stage], 0x3);
+          }
+          __syncwarp();
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        if (lane == 0) umma_commit_pair(&acc_full[acc], 0x3);
+        __syncwarp();
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (both CTAs, own TMEM half)
+    const int ew = warp - 2;
+    const int quarter = warp & 3;
+    const int col_half = ew >> 2;
+    const uint32_t stg = smem_u32(smem + L::EPI_OFF + ew * kStgBytes);
+    const bool fast_ok = ((args.flags & ZL_EPI_OUT_F32) ? (args.N % 4 == 0) : (args.N % 8 == 0)) &&
+                         (!(args.flags & ZL_EPI_ROPE) || args.epi.head_dim % 32 == 0);
+    const uint32_t acc_empty_leader[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0),
+                                          mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = pair; u < args.units; u += npairs) {
+      const int tile = u / args.splits, split = u % args.splits;
+      const int m0 = (tile / args.n_tiles_n) * (2 * BM) + (int)rank * BM;
+      const int n0 = (tile % args.n_tiles_n) * BN;
+      if (!bounded_wait_warp(&acc_full[acc], acc_phase, DEV_TIMEOUT_ACC)) break;
+      tc_fence_after();
+      const int r0 = m0 + quarter * 32;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = col_half * (BN / 2); c < (col_half + 1) * (BN / 2); c += 32) {
+        uint32_t raw[32];
+        tmem_ld32(t_row + (uint32_t)c, raw);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+        const int c0 = n0 + c;
+        if (c0 >= args.N || r0 >= args.M) continue;
+        const bool full_chunk = fast_ok && (c0 + 32 <= args.N);
+        if (args.splits > 1) {
+          if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v);
+          else if (r0 + lane < args.M) {
+            float* out = args.ws + ((size_t)split * args.M + r0 + lane) * args.N + c0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (c0 + j < args.N) out[j] = v[j];
+          }
+        } else if (full_chunk) {
+          epilogue_chunk(args, stg, lane, r0, c0, v);
+        } else {
+          epilogue_store32(args, r0 + lane, c0, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acc_empty_leader[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  // The even CTA's MMAs read both CTAs' shared memory and write both TMEMs: neither CTA may
+  // leave (or free its TMEM) before both are done.
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // Sums split-K partials and applies the epilogue: one thread per 32 columns of a row.
 __global__ void splitk_reduce_kernel(const GemmArgs args) {
   const int chunks = (args.N + 31) / 32;
@@ -654,6 +858,87 @@ cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CU
   return launch_tc<T, BN, STAGES, true, true>(ma, mb, a, grid, st);
 }
 
+// Two-SM variant: tiles of 256 rows (a CTA pair), grid = 2 x pairs, cluster of 2.
+Plan make_plan_pair(int M, int N, int K) {
+  Plan p;
+  p.bn = (N <= 128) ? 128 : 256;
+  p.n_tiles_n = (N + p.bn - 1) / p.bn;
+  p.tiles = ((M + 2 * BM - 1) / (2 * BM)) * p.n_tiles_n;
+  p.k_blocks = (K + 63) / 64;
+  const int pairs = sm_count() / 2;
+  int best = 1;
+  if (p.tiles < pairs && p.k_blocks >= 8) {
+    double best_t = 1e30;
+    const int smax = std::min(16, p.k_blocks / 4);
+    for (int s = 1; s <= smax; ++s) {
+      const int units = p.tiles * s;
+      const int waves = (units + pairs - 1) / pairs;
+      const double t = (double)waves * ((p.k_blocks + s - 1) / s) + 0.5 * s;
+      if (t < best_t) { best_t = t; best = s; }
+    }
+  }
+  p.kb_per_split = (p.k_blocks + best - 1) / best;
+  p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.units = p.tiles * p.splits;
+  return p;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+cudaError_t launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, int pairs, cudaStream_t st) {
+  using L = Smem2<BN, STAGES>;
+  auto kern = gemm_tc2_kernel<BN, STAGES, A_MN, B_MN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // persistent pairs: no more than can be resident at once (one CTA per SM)
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64) {
+    if (max_clusters[dev] == 0) {
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = pairs;
+      }
+      max_clusters[dev] = n;
+    }
+    if (pairs > max_clusters[dev]) cfg.gridDim = dim3(2 * max_clusters[dev], 1, 1);
+  }
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, a);
+}
+
+template <int BN, int STAGES>
+cudaError_t dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+                          int pairs, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_tc2<BN, STAGES, false, false>(ma, mb, a, pairs, st);
+  if (!a_mn && b_mn) return launch_tc2<BN, STAGES, false, true>(ma, mb, a, pairs, st);
+  if (a_mn && !b_mn) return launch_tc2<BN, STAGES, true, false>(ma, mb, a, pairs, st);
+  return launch_tc2<BN, STAGES, true, true>(ma, mb, a, pairs, st);
+}
+
+// Which bf16 GEMMs run on the CTA-pair kernel.  Measured on B200: the pair wins once the reduction
+// is long (K >= 1536: +3 to +10 %, long-K dW products and the scaled model's GEMMs reach 94-97 % of
+// the measured peak) and loses a little at K = 512, where the per-tile work is short.
+// ZL_GEMM_PAIR=0 / =1 forces the one-SM / pair kernel (read on every call).
+bool use_pair(int M, int K) {
+  if (M < 2 * BM) return false;
+  const char* e = getenv("ZL_GEMM_PAIR");
+  if (e && e[0] == '0') return false;
+  if (e && e[0] == '1') return true;
+  return K >= 1024;
+}
 }  // namespace
 
 bool make_tma_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
@@ -664,10 +949,15 @@ int sm_count_current() { return sm_count(); }
 
 int64_t gemm_workspace_floats(int M, int N, int K, int layout, int flags, bool f32_inputs) {
   (void)layout;
+  (void)flags;
   const int BK = f32_inputs ? Elem<float>::BK : Elem<__nv_bfloat16>::BK;
   Plan p = make_plan(M, N, K, BK, true);
-  (void)flags;
-  return p.splits > 1 ? (int64_t)p.splits * M * N : 0;
+  int64_t w = p.splits > 1 ? (int64_t)p.splits * M * N : 0;
+  if (!f32_inputs && M >= 2 * BM) {  // the two-SM plan may split differently
+    Plan q = make_plan_pair(M, N, K);
+    if (q.splits > 1) w = std::max(w, (int64_t)q.splits * M * N);
+  }
+  return w;
 }
 
 // Generic tcgen05 GEMM launcher (T = __nv_bfloat16 or float/tf32).
@@ -695,7 +985,9 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   a.M = M; a.N = N; a.K = K;
   a.D = D; a.flags = flags;
   if (epi) a.epi = *epi; else memset(&a.epi, 0, sizeof(a.epi));
-  Plan p = make_plan(M, N, K, E::BK, true);
+  // bf16 products of at least one 256-row tile go to the CTA-pair kernel
+  const bool pair = !is_f32 && sm_count() >= 2 && use_pair(M, K);
+  Plan p = pair ? make_plan_pair(M, N, K) : make_plan(M, N, K, E::BK, true);
   if (p.splits > 1 && !ws) {
     // no workspace supplied: fall back to a single split
     p.splits = 1; p.kb_per_split = p.k_blocks; p.units = p.tiles;
@@ -705,12 +997,19 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   constexpr int ATOM = 128 / E::bytes;
   CUtensorMap ma, mb;
   bool ok = a_mn ? make_map(&ma, A, is_f32, M, K, ATOM, E::BK) : make_map(&ma, A, is_f32, K, M, E::BK, BM);
-  ok = ok && (b_mn ? make_map(&mb, B, is_f32, N, K, ATOM, E::BK) : make_map(&mb, B, is_f32, K, N, E::BK, p.bn));
+  const int b_box_rows = pair ? p.bn / 2 : p.bn;  // a CTA of a pair loads half of B's columns
+  ok = ok && (b_mn ? make_map(&mb, B, is_f32, N, K, ATOM, E::BK) : make_map(&mb, B, is_f32, K, N, E::BK, b_box_rows));
   if (!ok) return set_error(ZL_ECUDA, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
-  const int grid = std::min(p.units, sm_count());
   cudaError_t e;
-  if (p.bn == 128) e = dispatch_major<T, 128, 6>(a_mn, b_mn, ma, mb, a, grid, st);
-  else e = dispatch_major<T, 256, 4>(a_mn, b_mn, ma, mb, a, grid, st);
+  if (pair) {
+    const int pairs = std::min(p.units, sm_count() / 2);
+    if (p.bn == 128) e = dispatch_pair<128, 8>(a_mn, b_mn, ma, mb, a, pairs, st);
+    else e = dispatch_pair<256, 6>(a_mn, b_mn, ma, mb, a, pairs, st);
+  } else {
+    const int grid = std::min(p.units, sm_count());
+    if (p.bn == 128) e = dispatch_major<T, 128, 6>(a_mn, b_mn, ma, mb, a, grid, st);
+    else e = dispatch_major<T, 256, 4>(a_mn, b_mn, ma, mb, a, grid, st);
+  }
   if (e != cudaSuccess) return set_error(ZL_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
   if (p.splits > 1) {
     const bool plain_f32 = (flags & ~(ZL_EPI_OUT_F32 | ZL_EPI_ACCUM)) == 0 && (flags & ZL_EPI_OUT_F32) && N % 4 == 0 &&
