@@ -250,29 +250,34 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
 }
 
 // ----------------------------------------------------------------- backward
-// D[b,h,i] = sum_d dO[i,d] * O[i,d]; also zeroes the fp32 dq accumulator and, when `nl` is
-// given, writes nl[b,h,i] = -lse[b,h,i] * log2(e) (the exponent offset the tcgen05 kernel reads).
-// One warp per (token, head); each lane covers Dh/32 consecutive elements.
+// D[b,h,i] = sum_d dO[i,d] * O[i,d] and, when `nl` is given, nl[b,h,i] = -lse[b,h,i] * log2(e) (the
+// exponent offset the tcgen05 kernel reads).  One thread per 8 consecutive elements of a token's
+// row (16-byte loads of O and dO); the Dh/8 threads of a head reduce with shuffles.
 __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
                                   const float* __restrict__ lse, float* __restrict__ Dsum, float* __restrict__ nl,
-                                  float* __restrict__ dq_acc, int B, int S, int H, int DH) {
+                                  int B, int S, int H, int DH) {
   const int E = H * DH;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (row >= (int64_t)B * S * H) return;
-  const int lane = threadIdx.x & 31;
-  const int64_t t = row / H;
-  const int h = (int)(row % H);
+  const int cpt = E / 8;  // chunks per token
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = idx < (int64_t)B * S * cpt;
+  const int64_t t = live ? idx / cpt : 0;
+  const int c = live ? (int)(idx % cpt) : 0;
   float s = 0.f;
-  for (int c = 2 * lane; c < DH; c += 64) {
-    const float2 a = unpack_bf16(*reinterpret_cast<const uint32_t*>(o + t * E + h * DH + c));
-    const float2 g = unpack_bf16(*reinterpret_cast<const uint32_t*>(d_o + t * E + h * DH + c));
-    s += a.x * g.x + a.y * g.y;
-    *reinterpret_cast<float2*>(dq_acc + t * E + h * DH + c) = make_float2(0.f, 0.f);
-  }
+  if (live) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + t * E) + c);
+    const uint4 g = __ldg(reinterpret_cast<const uint4*>(d_o + t * E) + c);
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  const int64_t b = t / S, i = t % S;
-  if (lane == 0) {
+    for (int k = 0; k < 4; ++k) {
+      const float2 x = unpack_bf16(av[k]), y = unpack_bf16(gv[k]);
+      s += x.x * y.x + x.y * y.y;
+    }
+  }
+  // Dh/8 (8 or 16) consecutive lanes hold one head; E/8 is a multiple of 8, so groups never straddle warps
+  for (int off = (DH / 8) >> 1; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (live && (c % (DH / 8)) == 0) {
+    const int h = c / (DH / 8);
+    const int64_t b = t / S, i = t % S;
     Dsum[(b * H + h) * S + i] = s;
     if (nl) nl[(b * H + h) * S + i] = -lse[(b * H + h) * S + i] * LOG2E;
   }
@@ -484,20 +489,28 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
 }
 
 // dQ = scale * dq_acc, rotated back by RoPE, into the Q columns of d_qkv.  dq_acc is [T, E]
-// (token-major, the mma.sync kernel) or [B, H, S, Dh] (head-major, the tcgen05 kernel).
+// (token-major, the mma.sync kernel) or [B, H, S, Dh] (head-major, the tcgen05 kernel).  One thread
+// per 8 consecutive elements (two 16-byte loads, one 16-byte store).
 __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ d_qkv,
                                    const float* rope_cos, const float* rope_sin, int64_t T, int S, int H,
                                    int DH, float scale, int head_major) {
   const int E = H * DH;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per pair
-  if (idx >= T * E / 2) return;
-  const int64_t t = idx / (E / 2);
-  const int c = (int)(idx % (E / 2)) * 2;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * (E / 8)) return;
+  const int64_t t = idx / (E / 8);
+  const int c = (int)(idx % (E / 8)) * 8;
   const int64_t src = head_major ? (((t / S) * H + c / DH) * S + t % S) * DH + c % DH : t * E + c;
-  const float2 v = *reinterpret_cast<const float2*>(dq_acc + src);
-  float x0 = v.x * scale, x1 = v.y * scale;
-  if (rope_cos) rope_inv_pair(x0, x1, rope_cos, rope_sin, (int)(t % S), (c % DH) >> 1, DH / 2);
-  *reinterpret_cast<uint32_t*>(d_qkv + t * 3 * E + c) = pack_bf16(x0, x1);
+  const float4 v0 = __ldg(reinterpret_cast<const float4*>(dq_acc + src));
+  const float4 v1 = __ldg(reinterpret_cast<const float4*>(dq_acc + src) + 1);
+  float x[8] = {v0.x * scale, v0.y * scale, v0.z * scale, v0.w * scale,
+                v1.x * scale, v1.y * scale, v1.z * scale, v1.w * scale};
+  if (rope_cos) {
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) rope_inv_pair(x[k], x[k + 1], rope_cos, rope_sin, (int)(t % S), ((c % DH) + k) >> 1, DH / 2);
+  }
+  uint4 u;
+  u.x = pack_bf16(x[0], x[1]); u.y = pack_bf16(x[2], x[3]); u.z = pack_bf16(x[4], x[5]); u.w = pack_bf16(x[6], x[7]);
+  *reinterpret_cast<uint4*>(d_qkv + t * 3 * E + c) = u;
 }
 
 }  // namespace fa
@@ -700,10 +713,13 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
   float* Dsum = workspace + T * E;
   float* nl = Dsum + (int64_t)batch * num_heads * seq_len;
   const bool tc = !force_mma_sync() && fa_bwd_tc_supported(qkv, d_o, dq_acc, d_qkv, seq_len, head_dim);
-  const int64_t rows = T * num_heads;
-  fa::fa_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+  // the dq accumulator starts at zero (both backward kernels add into it)
+  cudaError_t ce = cudaMemsetAsync(dq_acc, 0, (size_t)T * E * sizeof(float), st);
+  if (ce != cudaSuccess) return set_error(ZL_ECUDA, "attention bwd: memset: %s", cudaGetErrorString(ce));
+  const int64_t chunks = T * (E / 8);
+  fa::fa_bwd_pre_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum,
-      tc ? nl : nullptr, dq_acc, batch, seq_len, num_heads, head_dim);
+      tc ? nl : nullptr, batch, seq_len, num_heads, head_dim);
   zl_status s = check_launch("fa_bwd_pre_kernel");
   if (s != ZL_OK) return s;
   const float scale = 1.0f / sqrtf((float)head_dim);
@@ -727,8 +743,7 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
     s = check_launch("fa_bwd_kernel");
     if (s != ZL_OK) return s;
   }
-  const int64_t pairs = T * E / 2;
-  fa::fa_bwd_post_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
+  fa::fa_bwd_post_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
       dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, head_dim, scale,
       tc ? 1 : 0);
   return check_launch("fa_bwd_post_kernel");
