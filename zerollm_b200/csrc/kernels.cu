@@ -184,31 +184,30 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
   if (PREFETCH && row < M) fetch(row);
   for (; row < M; row += nwarps) {
     const float mu = KIND == 0 ? mean[row] : 0.f, rs = rstd[row];
-    float xh[kMaxChunks][8], a[kMaxChunks][8];
-    float s1 = 0.f, s2 = 0.f;
-    float dv[kMaxChunks][8];
     if (!PREFETCH) fetch(row);
+    // keep only the packed row; both passes unpack it again (registers, not arithmetic, limit
+    // the resident warps here)
+    uint4 cx[kMaxChunks], cd[kMaxChunks];
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c)
-      if ((c * 32 + lane) * 8 < N) {
-        unpack8(nx[c], xh[c]);
-        unpack8(nd[c], dv[c]);
-      }
+    for (int c = 0; c < kMaxChunks; ++c) { cx[c] = nx[c]; cd[c] = nd[c]; }
     if (PREFETCH && row + nwarps < M) fetch(row + nwarps);
+    float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < N) {
-        float gv[8];
+        float gv[8], xv[8], dv[8];
         load8f(g + col, gv);
+        unpack8(cx[c], xv);
+        unpack8(cd[c], dv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          xh[c][j] = (xh[c][j] - mu) * rs;
-          a[c][j] = dv[c][j] * gv[j];
-          s1 += a[c][j];
-          s2 += a[c][j] * xh[c][j];
-          pg[c][j] += dv[c][j] * xh[c][j];
-          pb[c][j] += dv[c][j];
+          const float xh = (xv[j] - mu) * rs;
+          const float a = dv[j] * gv[j];
+          s1 += a;
+          s2 += a * xh;
+          pg[c][j] += dv[j] * xh;
+          if (KIND == 0) pb[c][j] += dv[j];
         }
       }
     }
@@ -219,10 +218,15 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
     for (int c = 0; c < kMaxChunks; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < N) {
-        float o[8];
+        float gv[8], xv[8], dv[8], o[8];
+        load8f(g + col, gv);
+        unpack8(cx[c], xv);
+        unpack8(cd[c], dv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          o[j] = KIND == 0 ? rs * (a[c][j] - s1 * invN - xh[c][j] * s2 * invN) : rs * (a[c][j] - xh[c][j] * s2 * invN);
+          const float xh = (xv[j] - mu) * rs;
+          const float a = dv[j] * gv[j];
+          o[j] = KIND == 0 ? rs * (a - s1 * invN - xh * s2 * invN) : rs * (a - xh * s2 * invN);
           if (COL) pc[c][j] += o[j];
         }
         store8(dx + row * N + col, o);
