@@ -29,7 +29,8 @@ constexpr int BM = 128;
 constexpr int kEpiWarps = 8;                       // two warps per TMEM lane quarter
 constexpr int kThreads = 64 + kEpiWarps * 32;      // producer warp + MMA warp + epilogue
 constexpr int kStgStride = 80;                     // bytes per staged row: 64 B of data + 16 B pad
-constexpr int kStgBytes = 32 * kStgStride;         // per epilogue warp
+constexpr int kStgBytes = 4096;                    // per epilogue warp: a 32 x 32 fp32 tile for the TMA store
+static_assert(32 * kStgStride <= kStgBytes, "staging");
 
 template <typename T>
 struct Elem;
@@ -45,6 +46,7 @@ struct Elem<float> {
 struct GemmArgs {
   int M, N, K;
   int n_tiles_n, tiles, k_blocks, splits, kb_per_split, units;
+  int tma_out;  // full chunks leave through TMA stores (tensor maps of D and of the split-K workspace)
   void* D;
   int flags;
   zl_epilogue epi;
@@ -160,9 +162,48 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* v) {
 // Fused epilogue for one 32 x 32 chunk: rows [r0, r0+32) (this lane: r0+lane), columns [c0, c0+32).
 // Requires N % 8 == 0 (bf16 out) / N % 4 == 0 (fp32 out) and c0 + 32 <= N; other chunks use
 // epilogue_store32 (per-thread path).
+// The warp's 32 x 32 chunk (this lane: row `lane`) as a swizzled tile in its staging buffer, then one
+// TMA store (or element-wise add for an accumulating fp32 output) of the box at (c0, r0).
+// bf16: rows of 64 bytes, 64-byte swizzle; fp32: rows of 128 bytes, 128-byte swizzle.  The
+// buffer is 1024-byte aligned and its previous bulk copy has finished reading it.
+__device__ __forceinline__ void chunk_tma_out(const CUtensorMap* tm, uint32_t stg, int lane, int r0, int c0,
+                                              const float (&v)[32], bool f32, bool add) {
+  if (f32) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t dst = stg + lane * 128 + ((q ^ (lane & 7)) << 4);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(__float_as_uint(v[q * 4])),
+                   "r"(__float_as_uint(v[q * 4 + 1])), "r"(__float_as_uint(v[q * 4 + 2])),
+                   "r"(__float_as_uint(v[q * 4 + 3])));
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t dst = stg + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(pack_bf16(v[q * 8 + 0], v[q * 8 + 1])),
+                   "r"(pack_bf16(v[q * 8 + 2], v[q * 8 + 3])), "r"(pack_bf16(v[q * 8 + 4], v[q * 8 + 5])),
+                   "r"(pack_bf16(v[q * 8 + 6], v[q * 8 + 7])));
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (add) tma_reduce_add_2d_bulk(tm, stg, c0, r0);
+    else tma_store_2d_bulk(tm, stg, c0, r0);
+    bulk_commit();
+  }
+}
+
+// Before the staging buffer is written again: the lane that issued the last bulk copy waits until
+// that copy has read it.
+__device__ __forceinline__ void stg_reclaim(int lane) {
+  if (lane == 0) bulk_wait_read0();
+  __syncwarp();
+}
+
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, uint32_t stg, int lane, int r0, int c0,
-                                               float (&v)[32]) {
-  const int f = a.flags;
+                                               float (&v)[32], const CUtensorMap* tm_out = nullptr) {
+  int f = a.flags;
   const int r = r0 + lane;
   const int nrows = min(32, a.M - r0);
   if (f & ZL_EPI_BIAS) {
@@ -185,6 +226,34 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, uint32_t stg, 
       v[j] = x0 * c - x1 * s;
       v[j + 1] = x0 * s + x1 * c;
     }
+  }
+  if (tm_out) {
+    // TMA-store path: the staging buffer belongs to the output tile, so residual and mask row
+    // segments (64 contiguous bytes per lane) are read straight into registers; residual first,
+    // then the mask, as below
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      const int flag = pass == 0 ? ZL_EPI_RESIDUAL : ZL_EPI_RELU_MASK;
+      if (!(f & flag)) continue;
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(pass == 0 ? a.epi.residual : a.epi.aux);
+      uint4 u[4] = {};
+      if (r < a.M) {
+        const uint4* p = reinterpret_cast<const uint4*>(src + (size_t)r * a.N + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) u[q] = __ldg(p + q);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float t[8];
+        unpack8(u[q], t);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (pass == 0) v[q * 8 + k] += t[k];
+          else v[q * 8 + k] = t[k] > 0.f ? v[q * 8 + k] : 0.f;
+        }
+      }
+    }
+    f &= ~(ZL_EPI_RESIDUAL | ZL_EPI_RELU_MASK);
   }
   if (f & ZL_EPI_RESIDUAL) {
     __syncwarp();
@@ -221,6 +290,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, uint32_t stg, 
   if (f & ZL_EPI_RELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+  }
+  if (tm_out) {
+    __syncwarp();  // the residual / mask rows in the buffer have been read
+    const bool f32 = (f & ZL_EPI_OUT_F32) != 0;
+    chunk_tma_out(tm_out, stg, lane, r0, c0, v, f32, f32 && (f & ZL_EPI_ACCUM) != 0);
+    return;
   }
   if (f & ZL_EPI_OUT_F32) {
     float* out = reinterpret_cast<float*>(a.D) + (size_t)r0 * a.N + c0;
@@ -270,7 +345,11 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, uint32_t stg, 
 
 // Split-K partial chunk: raw fp32 accumulators to ws[split] (coalesced through staging).
 __device__ __forceinline__ void partial_chunk(const GemmArgs& a, uint32_t stg, int lane, int split, int r0, int c0,
-                                              const float (&v)[32]) {
+                                              const float (&v)[32], const CUtensorMap* tm_ws = nullptr) {
+  if (tm_ws) {  // ws viewed as [splits * M, N]
+    chunk_tma_out(tm_ws, stg, lane, split * a.M + r0, c0, v, true, false);
+    return;
+  }
   const int nrows = min(32, a.M - r0);
   float* out = a.ws + ((size_t)split * a.M + r0) * a.N + c0;
 #pragma unroll
@@ -291,6 +370,7 @@ __device__ __forceinline__ void partial_chunk(const GemmArgs& a, uint32_t stg, i
 template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmW,
                    const GemmArgs args) {
   using E = Elem<T>;
   using L = Smem<BN, STAGES, E::bytes>;
@@ -408,6 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stg = smem_u32(smem + L::EPI_OFF + ew * kStgBytes);
     const bool fast_ok = ((args.flags & ZL_EPI_OUT_F32) ? (args.N % 4 == 0) : (args.N % 8 == 0)) &&
                          (!(args.flags & ZL_EPI_ROPE) || args.epi.head_dim % 32 == 0);
+    const bool use_tma = fast_ok && args.tma_out;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
@@ -428,8 +509,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c0 = n0 + c;
         if (c0 >= args.N || r0 >= args.M) continue;
         const bool full_chunk = fast_ok && (c0 + 32 <= args.N);
+        if (use_tma) stg_reclaim(lane);
         if (args.splits > 1) {
-          if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v);
+          // a box must not run past row M: the workspace map would carry it into the next split
+          if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v, (use_tma && r0 + 32 <= args.M) ? &tmW : nullptr);
           else if (r0 + lane < args.M) {
             float* out = args.ws + ((size_t)split * args.M + r0 + lane) * args.N + c0;
 #pragma unroll
@@ -437,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (c0 + j < args.N) out[j] = v[j];
           }
         } else if (full_chunk) {
-          epilogue_chunk(args, stg, lane, r0, c0, v);
+          epilogue_chunk(args, stg, lane, r0, c0, v, use_tma ? &tmD : nullptr);
         } else {
           epilogue_store32(args, r0 + lane, c0, v);
         }
@@ -446,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
+    if (use_tma && lane == 0) bulk_wait0();  // this warp's output copies are complete
   }
 
   tc_fence_before();
@@ -479,6 +563,7 @@ struct Smem2 {
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmW,
                     const GemmArgs args) {
   using L = Smem2<BN, STAGES>;
   constexpr int BK = 64, UMMA_K = 16, ATOM = 64;
@@ -605,6 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stg = smem_u32(smem + L::EPI_OFF + ew * kStgBytes);
     const bool fast_ok = ((args.flags & ZL_EPI_OUT_F32) ? (args.N % 4 == 0) : (args.N % 8 == 0)) &&
                          (!(args.flags & ZL_EPI_ROPE) || args.epi.head_dim % 32 == 0);
+    const bool use_tma = fast_ok && args.tma_out;
     const uint32_t acc_empty_leader[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0),
                                           mapa_shared(smem_u32(&acc_empty[1]), 0)};
     int acc = 0;
@@ -628,8 +714,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c0 = n0 + c;
         if (c0 >= args.N || r0 >= args.M) continue;
         const bool full_chunk = fast_ok && (c0 + 32 <= args.N);
+        if (use_tma) stg_reclaim(lane);
         if (args.splits > 1) {
-          if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v);
+          // a box must not run past row M: the workspace map would carry it into the next split
+          if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v, (use_tma && r0 + 32 <= args.M) ? &tmW : nullptr);
           else if (r0 + lane < args.M) {
             float* out = args.ws + ((size_t)split * args.M + r0 + lane) * args.N + c0;
 #pragma unroll
@@ -637,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (c0 + j < args.N) out[j] = v[j];
           }
         } else if (full_chunk) {
-          epilogue_chunk(args, stg, lane, r0, c0, v);
+          epilogue_chunk(args, stg, lane, r0, c0, v, use_tma ? &tmD : nullptr);
         } else {
           epilogue_store32(args, r0 + lane, c0, v);
         }
@@ -646,6 +734,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_cluster(acc_empty_leader[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
+    if (use_tma && lane == 0) bulk_wait0();  // this warp's output copies are complete
   }
 
   // The even CTA's MMAs read both CTAs' shared memory and write both TMEMs: neither CTA may
@@ -795,7 +884,7 @@ int sm_count() {
 
 // 2-D tiled map over a row-major [rows, inner] matrix with a box of [box_rows, box_inner].
 bool make_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
-              uint32_t box_rows) {
+              uint32_t box_rows, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
   const uint64_t esz = is_f32 ? 4 : 2;
@@ -805,7 +894,7 @@ bool make_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, ui
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, is_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                    const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -839,23 +928,24 @@ Plan make_plan(int M, int N, int K, int BK, bool out_allows_split) {
 }
 
 template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
-cudaError_t launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, int grid, cudaStream_t st) {
+cudaError_t launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& mw,
+                      const GemmArgs& a, int grid, cudaStream_t st) {
   using E = Elem<T>;
   using L = Smem<BN, STAGES, E::bytes>;
   auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, a);
+  kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, md, mw, a);
   return cudaGetLastError();
 }
 
 template <typename T, int BN, int STAGES>
-cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
-                           int grid, cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_tc<T, BN, STAGES, false, false>(ma, mb, a, grid, st);
-  if (!a_mn && b_mn) return launch_tc<T, BN, STAGES, false, true>(ma, mb, a, grid, st);
-  if (a_mn && !b_mn) return launch_tc<T, BN, STAGES, true, false>(ma, mb, a, grid, st);
-  return launch_tc<T, BN, STAGES, true, true>(ma, mb, a, grid, st);
+cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
+                           const CUtensorMap& mw, const GemmArgs& a, int grid, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_tc<T, BN, STAGES, false, false>(ma, mb, md, mw, a, grid, st);
+  if (!a_mn && b_mn) return launch_tc<T, BN, STAGES, false, true>(ma, mb, md, mw, a, grid, st);
+  if (a_mn && !b_mn) return launch_tc<T, BN, STAGES, true, false>(ma, mb, md, mw, a, grid, st);
+  return launch_tc<T, BN, STAGES, true, true>(ma, mb, md, mw, a, grid, st);
 }
 
 // Two-SM variant: tiles of 256 rows (a CTA pair), grid = 2 x pairs, cluster of 2.
@@ -884,7 +974,8 @@ Plan make_plan_pair(int M, int N, int K) {
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-cudaError_t launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, int pairs, cudaStream_t st) {
+cudaError_t launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& mw,
+                       const GemmArgs& a, int pairs, cudaStream_t st) {
   using L = Smem2<BN, STAGES>;
   auto kern = gemm_tc2_kernel<BN, STAGES, A_MN, B_MN>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
@@ -916,16 +1007,16 @@ cudaError_t launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
     }
     if (pairs > max_clusters[dev]) cfg.gridDim = dim3(2 * max_clusters[dev], 1, 1);
   }
-  return cudaLaunchKernelEx(&cfg, kern, ma, mb, a);
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, md, mw, a);
 }
 
 template <int BN, int STAGES>
-cudaError_t dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
-                          int pairs, cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_tc2<BN, STAGES, false, false>(ma, mb, a, pairs, st);
-  if (!a_mn && b_mn) return launch_tc2<BN, STAGES, false, true>(ma, mb, a, pairs, st);
-  if (a_mn && !b_mn) return launch_tc2<BN, STAGES, true, false>(ma, mb, a, pairs, st);
-  return launch_tc2<BN, STAGES, true, true>(ma, mb, a, pairs, st);
+cudaError_t dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
+                          const CUtensorMap& mw, const GemmArgs& a, int pairs, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_tc2<BN, STAGES, false, false>(ma, mb, md, mw, a, pairs, st);
+  if (!a_mn && b_mn) return launch_tc2<BN, STAGES, false, true>(ma, mb, md, mw, a, pairs, st);
+  if (a_mn && !b_mn) return launch_tc2<BN, STAGES, true, false>(ma, mb, md, mw, a, pairs, st);
+  return launch_tc2<BN, STAGES, true, true>(ma, mb, md, mw, a, pairs, st);
 }
 
 // Which bf16 GEMMs run on the CTA-pair kernel.  Measured on B200: the pair wins once the reduction
@@ -1000,15 +1091,28 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   const int b_box_rows = pair ? p.bn / 2 : p.bn;  // a CTA of a pair loads half of B's columns
   ok = ok && (b_mn ? make_map(&mb, B, is_f32, N, K, ATOM, E::BK) : make_map(&mb, B, is_f32, K, N, E::BK, b_box_rows));
   if (!ok) return set_error(ZL_ECUDA, "gemm: cuTensorMapEncodeTiled failed (M=%d N=%d K=%d)", M, N, K);
+  // Output tensor maps for the TMA-store epilogue: D ([M, N], bf16 with 64-byte or fp32 with
+  // 128-byte swizzle, 32 x 32 boxes) and the split-K workspace ([splits * M, N] fp32).  They need
+  // 16-byte aligned bases and row pitches; otherwise the epilogue stores from registers.
+  const bool out_f32 = is_f32 || (flags & ZL_EPI_OUT_F32);
+  CUtensorMap md = ma, mw = ma;
+  a.tma_out = 0;
+  if (((reinterpret_cast<uintptr_t>(D) & 15) == 0) && (out_f32 ? N % 4 == 0 : N % 8 == 0) &&
+      (p.splits == 1 || (ws && (reinterpret_cast<uintptr_t>(ws) & 15) == 0))) {
+    bool mok = make_map(&md, D, out_f32, N, M, 32, 32,
+                        out_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (mok && p.splits > 1) mok = make_map(&mw, ws, true, N, (uint64_t)p.splits * M, 32, 32);
+    a.tma_out = mok ? 1 : 0;
+  }
   cudaError_t e;
   if (pair) {
     const int pairs = std::min(p.units, sm_count() / 2);
-    if (p.bn == 128) e = dispatch_pair<128, 8>(a_mn, b_mn, ma, mb, a, pairs, st);
-    else e = dispatch_pair<256, 6>(a_mn, b_mn, ma, mb, a, pairs, st);
+    if (p.bn == 128) e = dispatch_pair<128, 8>(a_mn, b_mn, ma, mb, md, mw, a, pairs, st);
+    else e = dispatch_pair<256, 6>(a_mn, b_mn, ma, mb, md, mw, a, pairs, st);
   } else {
     const int grid = std::min(p.units, sm_count());
-    if (p.bn == 128) e = dispatch_major<T, 128, 6>(a_mn, b_mn, ma, mb, a, grid, st);
-    else e = dispatch_major<T, 256, 4>(a_mn, b_mn, ma, mb, a, grid, st);
+    if (p.bn == 128) e = dispatch_major<T, 128, 6>(a_mn, b_mn, ma, mb, md, mw, a, grid, st);
+    else e = dispatch_major<T, 256, 4>(a_mn, b_mn, ma, mb, md, mw, a, grid, st);
   }
   if (e != cudaSuccess) return set_error(ZL_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
   if (p.splits > 1) {

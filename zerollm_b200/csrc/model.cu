@@ -252,13 +252,6 @@ zl_status grads_ready(zl_model* M, int64_t prefix, cudaStream_t st) {
   return ZL_OK;
 }
 
-int64_t layer_grad_end(zl_model* M, int l, int which) {  // end offset of tensor `which` of layer l
-  const auto& t = M->L.lay[l];
-  // find the tensor starting at t[which] and return off+size
-  for (size_t i = 0; i < M->L.off.size(); ++i)
-    if (M->L.off[i] == t[which]) return M->L.off[i] + M->L.size[i];
-  return -1;
-}
 int64_t end_of(zl_model* M, int64_t off) {
   for (size_t i = 0; i < M->L.off.size(); ++i)
     if (M->L.off[i] == off) return M->L.off[i] + M->L.size[i];
