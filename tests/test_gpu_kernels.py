@@ -168,17 +168,18 @@ def test_linear_api(K):
 
 
 # ------------------------------------------------------------------ attention
-@pytest.mark.parametrize("kernel", ["default", "mma"])
+@pytest.mark.parametrize("kernel", ["tc", "tc_pp", "mma"])
 @pytest.mark.parametrize("B,S,H,Dh", [(2, 128, 2, 64), (1, 200, 3, 64), (2, 512, 4, 64), (1, 1024, 2, 64),
-                                      (2, 256, 2, 128), (1, 200, 1, 128)])
+                                      (2, 384, 2, 64), (2, 256, 2, 128), (1, 1024, 2, 128), (1, 200, 1, 128)])
 def test_attention_bf16_vs_oracle(L, B, S, H, Dh, kernel, monkeypatch):
-    """Flash attention fwd+bwd against the oracle.  "default" runs the tcgen05
-    kernels where the shape allows (S % 128 == 0, head dim 64) and mma.sync otherwise;
-    "mma" forces the mma.sync kernels."""
+    """Flash attention fwd+bwd against the oracle.  "tc" runs the one-tile tcgen05
+    forward where the shape allows (S % 128 == 0) and mma.sync otherwise; "tc_pp" the
+    persistent two-tile forward where S % 256 == 0; "mma" forces the mma.sync kernels."""
     if kernel == "mma":
         monkeypatch.setenv("ZL_ATTENTION_KERNEL", "mma")
     else:
         monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
+        monkeypatch.setenv("ZL_ATTN_FWD_PP", "1" if kernel == "tc_pp" else "0")
     E = H * Dh
     T = B * S
     qkv = O.normal(T * 3 * E, 21) * 0.5
@@ -209,6 +210,28 @@ def test_attention_bf16_vs_oracle(L, B, S, H, Dh, kernel, monkeypatch):
     assert rel(g[:, :E], dq.reshape(T, E)) < BF16_TOL
     assert rel(g[:, E:2 * E], dk.reshape(T, E)) < BF16_TOL
     assert rel(g[:, 2 * E:], dv.reshape(T, E)) < BF16_TOL
+
+
+@pytest.mark.parametrize("B,S,H,Dh", [(16, 2048, 8, 64), (2, 2048, 16, 128), (3, 1536, 5, 64)])
+def test_attention_fwd_persistent_matches_one_tile(L, B, S, H, Dh, monkeypatch):
+    """The persistent two-tile forward walks several work units per CTA (more pairs
+    than SMs at these shapes) and must reproduce the one-tile kernel bit for bit:
+    both take the same row maxima, rescaling decisions and P.V block order."""
+    monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
+    E, T = H * Dh, B * S
+    qkv_d = (torch.randn(T * 3 * E, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5)) * 0.5
+             ).bfloat16()
+    outs = []
+    for pp in ("0", "1"):
+        monkeypatch.setenv("ZL_ATTN_FWD_PP", pp)
+        o = torch.full((T * E,), float("nan"), device="cuda", dtype=torch.bfloat16)
+        lse = torch.full((B * H * S,), float("nan"), device="cuda")
+        L.call("zl_attention_forward_bf16", qkv_d.data_ptr(), o.data_ptr(), lse.data_ptr(), B, S, H, Dh, None)
+        torch.cuda.synchronize()
+        outs.append((o, lse))
+    assert torch.isfinite(outs[1][0].float()).all() and torch.isfinite(outs[1][1]).all()
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
 
 
 def _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d):

@@ -15,6 +15,7 @@
 // probabilities rounded to bf16 before P.V, row sums from the unrounded
 // values, lse = natural log-sum-exp of the scaled scores.
 #include <cmath>
+#include <cstdlib>
 
 #include <type_traits>
 
@@ -304,8 +305,335 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ============================================ forward, persistent, two query tiles per work unit
+// One CTA per SM walks work units (batch, head, query tiles 2p and 2p+1), heaviest first, in a
+// snake order over the CTAs.  The two tiles share every K/V block load.  Each tile has its own MMA
+// warp and softmax warpgroup, so two independent softmax streams run on every SM sub-partition.
+// Buffers drain unit to unit: the producer loads the next unit's Q and K/V as soon as their slots
+// free up, and a tile's first S of the next unit is computed while its softmax warps still write
+// the previous unit's O.
+//
+// TMEM (512 columns): S_t at [128 t, 128 t + 128).  Head dim 64: P_t at 256 + 64 t and O_t at
+// 384 + 64 t, so S of block j+1 is computed as soon as the softmax holds S_j in registers.  Head dim
+// 128: O_t at 256 + 128 t, and P_t is written over the first 64 columns of S_t; S of block j+1 is
+// then issued only after the P.V of block j has retired, since tcgen05 products on different
+// accumulators are not ordered with respect to each other.
+template <int DH>
+struct FwdPP {
+  static constexpr int ATOMS = DH / 64;
+  static constexpr int T_BYTES = ATOMS * TILE_BYTES;
+  static constexpr int KVST = DH == 64 ? 5 : 2;
+  static constexpr bool SEP_P = DH == 64;
+  static constexpr int SMEM_Q = 0, SMEM_K = 2 * T_BYTES, SMEM_V = SMEM_K + KVST * T_BYTES;
+  static constexpr int SMEM_BAR = SMEM_V + KVST * T_BYTES;
+  static constexpr int SMEM_TOTAL = SMEM_BAR + 256 + 1024;
+  static constexpr uint32_t IDESC_O = make_idesc(1, 128, DH, 0, 1);  // M=128, N=Dh, A (TMEM), B MN-major
+  __host__ __device__ static constexpr uint32_t s_col(int t) { return (uint32_t)(t * 128); }
+  __host__ __device__ static constexpr uint32_t p_col(int t) { return SEP_P ? 256u + 64u * t : (uint32_t)(t * 128); }
+  __host__ __device__ static constexpr uint32_t o_col(int t) { return SEP_P ? 384u + 64u * t : 256u + 128u * t; }
+  static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
+};
+constexpr int THREADS_PP = 384;  // warp 0 TMA, warps 1-2 MMA of tiles 0-1, warp 3 idle, 4-7 / 8-11 softmax
+
+// Work unit k of a CTA (k = 0, 1, ...): snake order over the CTAs, so that a CTA that draws a heavy
+// unit in one round draws a light one in the next.
+__device__ __forceinline__ int pp_unit(int k, int cta, int G) { return k * G + ((k & 1) ? G - 1 - cta : cta); }
+
+template <int DH>
+__global__ void __launch_bounds__(THREADS_PP, 1)
+    fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out,
+                     float* __restrict__ lse, int S, int H, int nunits, float scale_log2) {
+  using C = FwdPP<DH>;
+  constexpr int KVST = C::KVST, T_BYTES = C::T_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::SMEM_BAR);
+  uint64_t* q_full = bar + 0;
+  uint64_t* q_empty = bar + 1;            // both tiles' last S product of the unit has retired
+  uint64_t* kv_full = bar + 2;            // [KVST]
+  uint64_t* kv_empty = bar + 2 + KVST;    // [KVST]: both tiles are done with the block
+  uint64_t* s_full = bar + 2 + 2 * KVST;  // [2] per tile
+  uint64_t* s_used = s_full + 2;          // [2] the tile's softmax warps hold S in registers
+  uint64_t* p_full = s_full + 4;          // [2]
+  uint64_t* pv_done = s_full + 6;         // [2]
+  uint64_t* drain = s_full + 8;           // both MMA warps' last products have retired
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(s_full + 9);
+
+  const int E = H * DH;
+  const int npair = S / (2 * BQ);
+  const int nbh = nunits / npair;
+  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // unit u: query tiles 2p, 2p+1 of (batch, head) bh; the heaviest pairs have the lowest u
+  auto unit_pair = [&](int u) { return npair - 1 - u / nbh; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 2);
+    for (int i = 0; i < KVST; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 2);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_used[t], 128);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&pv_done[t], 1);
+    }
+    mbar_init(drain, 2);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t g = 0, nq_loads = 0;  // K/V blocks and Q pairs issued
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int u = pp_unit(k, cta, G);
+        if (u >= nunits) break;
+        const int p = unit_pair(u), bh = u % nbh, b = bh / H, h = bh % H;
+        if (!bounded_wait(q_empty, (nq_loads & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(q_full, 2 * T_BYTES);
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int a = 0; a < C::ATOMS; ++a)
+            tma_load_2d(smem + C::SMEM_Q + t * T_BYTES + a * TILE_BYTES, &tm, q_full, h * DH + a * 64,
+                        b * S + (2 * p + t) * BQ);
+        ++nq_loads;
+        const int nkv = 2 * p + 2;
+        for (int j = 0; j < nkv; ++j) {
+          const uint32_t st = g % KVST;
+          if (!bounded_wait(&kv_empty[st], ((g / KVST) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * T_BYTES);
+          const int krow = b * S + j * BKV;
+#pragma unroll
+          for (int a = 0; a < C::ATOMS; ++a) {
+            tma_load_2d(smem + C::SMEM_K + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st], E + h * DH + a * 64,
+                        krow);
+            tma_load_2d(smem + C::SMEM_V + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st],
+                        2 * E + h * DH + a * 64, krow);
+          }
+          ++g;
+        }
+      }
+      // no copy may still be landing in shared memory when the CTA exits
+      if (nq_loads > 0) bounded_wait(q_full, (nq_loads - 1) & 1, DEV_TIMEOUT_ATTN);
+      for (uint32_t j = g > (uint32_t)KVST ? g - KVST : 0; j < g; ++j)
+        bounded_wait(&kv_full[j % KVST], (j / KVST) & 1, DEV_TIMEOUT_ATTN);
+    }
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuer of tile t
+    const int t = warp - 1;
+    const uint32_t sq = smem_u32(smem + C::SMEM_Q + t * T_BYTES);
+    const uint32_t t_s = tmem + C::s_col(t), t_p = tmem + C::p_col(t), t_o = tmem + C::o_col(t);
+    uint32_t c = 0, g = 0;  // this tile's blocks so far, K/V blocks so far
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int u = pp_unit(k, cta, G);
+      if (u >= nunits) break;
+      const int p = unit_pair(u);
+      const int n = 2 * p + 1 + t, nkv = 2 * p + 2;
+      if (!bounded_wait_warp(q_full, (uint32_t)k & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      // S_t of block j: K/V block g + j, tile block c + j.  Its S columns must be free: read by the
+      // softmax (separate P) or released by the previous P.V (P over S).
+      auto issue_s = [&](int j) -> bool {
+        const uint32_t use = g + (uint32_t)j, st = use % KVST;
+        if (!bounded_wait_warp(&kv_full[st], (use / KVST) & 1, DEV_TIMEOUT_ATTN)) return false;
+        const uint32_t prev = c + (uint32_t)j;
+        if (prev > 0 && !bounded_wait_warp(C::SEP_P ? &s_used[t] : &pv_done[t], (prev - 1) & 1, DEV_TIMEOUT_ATTN))
+          return false;
+        tc_fence_after();
+        const uint32_t sk = smem_u32(smem + C::SMEM_K + st * T_BYTES);
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < DH / 16; ++kk) {
+            const uint32_t off = (uint32_t)((kk >> 2) * TILE_BYTES + (kk & 3) * 32);
+            umma_f16(t_s, smem_desc_sw128(sq + off, 16, 1024), smem_desc_sw128(sk + off, 16, 1024), IDESC_S,
+                     kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+          if (j == n - 1) umma_commit(q_empty);  // the tile's Q is no longer read once this retires
+        }
+        __syncwarp();
+        return true;
+      };
+      ok = issue_s(0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (C::SEP_P && j + 1 < n && !issue_s(j + 1)) { ok = false; break; }
+        if (!bounded_wait_warp(&p_full[t], (c + (uint32_t)j) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = (g + (uint32_t)j) % KVST;
+        const uint32_t sv = smem_u32(smem + C::SMEM_V + st * T_BYTES);
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
+            umma_f16_ts(t_o, t_p + (uint32_t)(kk * 8), smem_desc_sw128(sv + kk * 16 * 128, TILE_BYTES, 1024),
+                        C::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&pv_done[t]);
+          umma_commit(&kv_empty[st]);
+        }
+        __syncwarp();
+        if (!C::SEP_P && j + 1 < n && !issue_s(j + 1)) { ok = false; break; }
+      }
+      if (!ok) break;
+      if (t == 0) {  // tile 0 (one block fewer) releases the unit's last K/V block once it has landed
+        const uint32_t use = g + (uint32_t)nkv - 1, st = use % KVST;
+        if (!bounded_wait_warp(&kv_full[st], (use / KVST) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        if (lane == 0) mbar_arrive(&kv_empty[st]);
+        __syncwarp();
+      }
+      c += (uint32_t)n;
+      g += (uint32_t)nkv;
+    }
+    // TMEM is freed below only after every MMA issued here has retired
+    if (lane == 0) umma_commit(drain);
+    __syncwarp();
+    bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax + epilogue of tile t
+    const int t = (warp - 4) >> 2;
+    const int quarter = warp & 3;
+    const int r_local = quarter * 32 + lane;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t t_s = t_lane + C::s_col(t), t_p = t_lane + C::p_col(t), t_o = t_lane + C::o_col(t);
+    uint32_t c = 0;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int u = pp_unit(k, cta, G);
+      if (u >= nunits) break;
+      const int p = unit_pair(u), bh = u % nbh, b = bh / H, h = bh % H;
+      const int qb = 2 * p + t, n = qb + 1;
+      const int q_pos = qb * BQ + r_local;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j, ++c) {
+        if (!bounded_wait_warp(&s_full[t], c & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t r[4][32];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) tmem_ld32(t_s + (uint32_t)(cc * 32), r[cc]);
+        tmem_ld_wait();
+        if (C::SEP_P) {  // S may now be overwritten by the next block's product
+          tc_fence_before();
+          mbar_arrive(&s_used[t]);
+        }
+        const int key0 = j * BKV;
+        float corr = 1.f;
+        bool raise = false;
+        // The diagonal block (the only one with masked keys) is a separate instance, so the others
+        // carry no per-element mask.
+        auto block = [&](auto diag_tag) -> bool {
+          constexpr bool DIAG = decltype(diag_tag)::value;
+          auto val = [&](int cc, int i) {
+            const float v = __uint_as_float(r[cc][i]);
+            return (DIAG && key0 + cc * 32 + i > q_pos) ? -INFINITY : v;
+          };
+          float mxp[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mxp[i] = val(0, i);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (cc > 0 || i >= 8) mxp[i & 7] = fmaxf(mxp[i & 7], val(cc, i));
+          const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                 fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+          // lazy rescaling, as in the one-tile kernel: m only rises by more than 8 (log2 units)
+          const float m_cand = fmaxf(m, mx * scale_log2);
+          raise = __any_sync(0xffffffffu, m_cand > m + 8.f);
+          if (raise) {
+            corr = fast_exp2(m - m_cand);
+            m = m_cand;
+          }
+          // separate P columns: the previous block's P.V must have read them (and O is then current)
+          if (C::SEP_P && c > 0 && !bounded_wait_warp(&pv_done[t], (c - 1) & 1, DEV_TIMEOUT_ATTN)) return false;
+          const float neg_m = -m;
+          float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float p0 = fast_exp2(fmaf(val(cc, i), scale_log2, neg_m));
+              const float p1 = fast_exp2(fmaf(val(cc, i + 1), scale_log2, neg_m));
+              sp[i & 7] += p0;
+              sp[(i + 1) & 7] += p1;
+              pk[i >> 1] = pack_bf16(p0, p1);
+            }
+            tmem_st16(t_p + (uint32_t)(cc * 16), pk);
+          }
+          const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+          l = l * corr + sum;
+          return true;
+        };
+        const bool fine = (j == n - 1) ? block(std::integral_constant<bool, true>{})
+                                       : block(std::integral_constant<bool, false>{});
+        if (!fine) { ok = false; break; }
+        if (raise && j > 0) {  // O *= corr once the previous P.V has landed
+          if (!C::SEP_P && !bounded_wait_warp(&pv_done[t], (c - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int cc = 0; cc < DH / 32; ++cc) {
+            uint32_t o[32];
+            tmem_ld32(t_o + (uint32_t)(cc * 32), o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+            tmem_st32(t_o + (uint32_t)(cc * 32), o);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
+      }
+      if (!ok) break;
+      // epilogue: O / l -> bf16 and lse.  The next unit's first P.V, which overwrites O, waits for
+      // the p_full arrival that follows these reads.
+      if (!bounded_wait_warp(&pv_done[t], (c - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = out + (size_t)(b * S + q_pos) * E + h * DH;
+#pragma unroll 1
+      for (int cc = 0; cc < DH / 32; ++cc) {
+        uint32_t o[32];
+        tmem_ld32(t_o + (uint32_t)(cc * 32), o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
+          w.y = pack_bf16(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
+          w.z = pack_bf16(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
+          w.w = pack_bf16(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + cc * 32 + q * 8) = w;
+        }
+      }
+      lse[(size_t)bh * S + q_pos] = (m + log2f(l)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 
 // ============================================================== backward
+
 // One CTA per (batch, head, 128-key block); it walks the query blocks from the diagonal to the end
 // of the sequence.  Per query block i:
 //   MMA:     S^T = K Q_i^T, dP^T = V dO_i^T                                      (TMEM, fp32)
@@ -717,6 +1045,23 @@ bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, 
     return true;
   }
   const float scale_log2 = (1.0f / sqrtf((float)Dh)) * 1.4426950408889634f;
+  // Persistent two-tile kernel when the sequence holds whole tile pairs and there are enough pairs
+  // to give every SM one; ZL_ATTN_FWD_PP=0/1 forces either kernel (pairs permitting).
+  const int nunits = S % (2 * fatc::BQ) == 0 ? B * H * (S / (2 * fatc::BQ)) : 0;
+  const int sms = sm_count_current();
+  const char* force = getenv("ZL_ATTN_FWD_PP");
+  const bool pp = nunits > 0 && (force ? force[0] == '1' : nunits >= sms);
+  if (pp) {
+    const int grid = nunits < sms ? nunits : sms;
+    auto launch_pp = [&](auto kern, int smem) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      kern<<<grid, fatc::THREADS_PP, smem, st>>>(tm, out, lse, S, H, nunits, scale_log2);
+    };
+    if (Dh == 64) launch_pp(fatc::fa_fwd_pp_kernel<64>, fatc::FwdPP<64>::SMEM_TOTAL);
+    else launch_pp(fatc::fa_fwd_pp_kernel<128>, fatc::FwdPP<128>::SMEM_TOTAL);
+    *status = check_launch("fa_fwd_pp_kernel");
+    return true;
+  }
   const int grid = B * H * (S / fatc::BQ);
   auto launch = [&](auto kern, int smem) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
