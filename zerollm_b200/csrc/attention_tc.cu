@@ -27,7 +27,7 @@
 
 namespace zl {
 bool make_tma_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
-                  uint32_t box_rows);
+                  uint32_t box_rows, int swizzle_bytes = 128);
 int sm_count_current();
 
 namespace fatc {
@@ -634,8 +634,11 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
 
 // ============================================================== backward
 
-// One CTA per (batch, head, 128-key block); it walks the query blocks from the diagonal to the end
-// of the sequence.  Per query block i:
+// Persistent: one CTA per SM walks work units (batch, head, 128-key block), the units with the most
+// query blocks first, in snake order over the CTAs.  A unit walks its query blocks from the diagonal
+// to the end of the sequence, and the CTA's blocks form one pipeline across units: the next unit's
+// K / V and first Q / dO stages load, and its first S^T / dP^T are computed, while the softmax warps
+// finish the previous unit (last dQ, then dK / dV out of TMEM).  Per query block i:
 //   MMA:     S^T = K Q_i^T, dP^T = V dO_i^T                                      (TMEM, fp32)
 //   softmax: P^T = exp2(S^T * scale_log2 - lse2[q]) with the causal mask, dS^T = P^T (dP^T - D[q]);
 //            P^T goes back to TMEM as bf16 (A operand of dV), dS^T to shared memory
@@ -658,20 +661,25 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
 // applied by the caller's post pass.
 namespace bwd {
 constexpr int NSOFT = ZL_ATTN_BWD_SOFTMAX_WARPS;
-constexpr int THREADS_B = 64 + 32 * NSOFT;  // warp 0 TMA, warp 1 MMA, warps 2.. softmax
+// Warpgroup 0: warp 0 TMA, warp 1 MMA, warps 2-3 idle; warps 4.. softmax.  (Registers are granted
+// per warpgroup, so the two idle warps cost none; moving registers from warpgroup 0 to the softmax
+// warps with setmaxnreg measured slower.)
+constexpr int THREADS_B = 128 + 32 * NSOFT;
 constexpr int WPQ = NSOFT / 4;              // softmax warps per TMEM lane quadrant
 constexpr int QCOLS = BQ / WPQ;             // query columns (of S^T / dP^T) per softmax warp
 constexpr int DCOLS = D / WPQ;              // head-dim columns (of dQ / dK / dV) per softmax warp
 static_assert(NSOFT == 8 || NSOFT == 16, "softmax warps");
 constexpr int QST = 3;                               // Q / dO / row-vector stages (loads run two blocks ahead)
-constexpr int SM_K = 0, SM_V = TILE_BYTES, SM_Q = 2 * TILE_BYTES, SM_DO = SM_Q + QST * TILE_BYTES;
+// K is double buffered (the next unit's key block loads while this one finishes); V has one buffer,
+// which its last reader (the unit's last dP^T) releases early in the unit's last block.
+constexpr int SM_K = 0, SM_V = 2 * TILE_BYTES, SM_Q = 3 * TILE_BYTES, SM_DO = SM_Q + QST * TILE_BYTES;
 constexpr int SM_DS = SM_DO + QST * TILE_BYTES;
 constexpr int DQ_BYTES = BQ * D * 4;                 // the fp32 dQ tile: two [128][32] boxes, 128-byte swizzle
 constexpr int SM_DQ = SM_DS + 2 * TILE_BYTES;
 constexpr int VEC_BYTES = 2 * BQ * 4;                // nl[128], D[128] of one query block
 constexpr int SM_VEC = SM_DQ + DQ_BYTES;             // [QST] stages
 constexpr int SM_BAR = SM_VEC + QST * VEC_BYTES;
-constexpr int SMEM_TOTAL = SM_BAR + 128 + 1024;
+constexpr int SMEM_TOTAL = SM_BAR + 256 + 1024;
 static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
 constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384, C_P = 448;
 constexpr uint32_t IDESC_SD = make_idesc(1, 128, 128, 0, 0);  // K Q^T / V dO^T: both K-major
@@ -705,38 +713,51 @@ template <int N> __device__ __forceinline__ void tmem_st_n(uint32_t taddr, const
 
 __global__ void __launch_bounds__(THREADS_B, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                     const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ nl_g,
+                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
+                     const float* __restrict__ nl_g,
                      const float* __restrict__ Dsum,
                      __nv_bfloat16* __restrict__ d_qkv, const float* __restrict__ rope_cos,
-                     const float* __restrict__ rope_sin, int S, int H, float scale, float scale_log2) {
+                     const float* __restrict__ rope_sin, int S, int H, int nunits, float scale, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM_BAR);
-  uint64_t* kv_full = bar + 0;
-  uint64_t* q_full = bar + 1;         // [QST]
-  uint64_t* q_empty = bar + 1 + QST;  // [QST]
-  uint64_t* sd_full = bar + 1 + 2 * QST;
+  uint64_t* k_full = bar + 0;          // [2] K buffers (alternate work units)
+  uint64_t* k_empty = bar + 2;         // [2] the unit's last dQ product has retired
+  uint64_t* v_full = bar + 4;
+  uint64_t* v_empty = bar + 5;         // the unit's last dP^T product has retired
+  uint64_t* q_full = bar + 6;          // [QST]
+  uint64_t* q_empty = bar + 6 + QST;   // [QST]
+  uint64_t* sd_full = bar + 6 + 2 * QST;
   uint64_t* ds_ready = sd_full + 1;
   uint64_t* mm_done = sd_full + 2;
   uint64_t* dq_free = sd_full + 3;
-  uint64_t* drain = sd_full + 4;      // final commit: every MMA of this CTA has retired
-  uint64_t* sd_used = sd_full + 5;    // the softmax warps have loaded S^T / dP^T into registers
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sd_full + 6);
+  uint64_t* drain = sd_full + 4;       // final commit: every MMA of this CTA has retired
+  uint64_t* sd_used = sd_full + 5;     // the softmax warps have loaded S^T / dP^T into registers
+  uint64_t* dkv_free = sd_full + 6;    // the softmax warps have read dK / dV of the unit out of TMEM
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sd_full + 7);
 
   const int E = H * D;
   const int nk = S / BKV;
-  // key-block-major order: the CTAs of key block 0 (most query blocks) are launched first
-  const int nbh = (int)gridDim.x / nk;
-  const int kb = (int)blockIdx.x / nbh;
-  const int bh = (int)blockIdx.x % nbh, b = bh / H, h = bh % H;
-  const int krow0 = b * S + kb * BKV;
-  const int niter = nk - kb;  // query blocks kb .. nk-1
+  const int nbh = nunits / nk;
+  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t row_base = (size_t)bh * S;  // (b, h) rows of nl, D and the dQ accumulator
+  // Work unit u = (key block kb, batch-head bh), key-block-major so the units with the most query
+  // blocks come first; CTAs draw units in snake order.  The CTA's blocks form one flat sequence:
+  // unit k of this CTA contributes query blocks kb .. nk-1.
+  struct Unit {
+    int kb, bh, niter;
+  };
+  auto unit_of = [&](int k) -> Unit {
+    const int u = pp_unit(k, cta, G);
+    if (u >= nunits) return Unit{0, 0, 0};
+    return Unit{u / nbh, u % nbh, nk - u / nbh};
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
     for (int i = 0; i < QST; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
     mbar_init(sd_full, 1);
     mbar_init(ds_ready, 32 * NSOFT);
@@ -744,10 +765,12 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     mbar_init(dq_free, 32 * NSOFT);
     mbar_init(drain, 1);
     mbar_init(sd_used, 32 * NSOFT);
+    mbar_init(dkv_free, 32 * NSOFT);
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_dq);
+    tma_prefetch_desc(&tm_dkv);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -759,35 +782,81 @@ __global__ void __launch_bounds__(THREADS_B, 1)
   const uint32_t tmem = *tmem_holder;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    // Per unit: K into buffer k & 1 (once the unit two back has finished with it), then the unit's
+    // first Q / dO / row-vector stage, then V (once the previous unit's last dP^T has read the single
+    // V buffer), then the remaining stages.  This is the order in which the slots drain.
     if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
-      tma_load_2d(smem + SM_K, &tm_qkv, kv_full, E + h * D, krow0);
-      tma_load_2d(smem + SM_V, &tm_qkv, kv_full, 2 * E + h * D, krow0);
-      int issued = 0;
-      for (int i = 0; i < niter; ++i) {
-        const int st = i % QST;
-        if (!bounded_wait(&q_empty[st], ((i / QST) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES + VEC_BYTES);
-        const int qb = kb + i;
-        const int qrow = b * S + qb * BQ;
-        tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_qkv, &q_full[st], h * D, qrow);
-        tma_load_2d(smem + SM_DO + st * TILE_BYTES, &tm_do, &q_full[st], h * D, qrow);
-        float* vec = reinterpret_cast<float*>(smem + SM_VEC + st * VEC_BYTES);
-        bulk_load(vec, nl_g + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
-        bulk_load(vec + BQ, Dsum + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
-        issued = i + 1;
+      uint32_t n = 0, nkl = 0, nvl = 0;  // Q stages, K and V tiles issued
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const Unit un = unit_of(k);
+        if (un.niter == 0) break;
+        const int b = un.bh / H, h = un.bh % H;
+        const int krow = b * S + un.kb * BKV;
+        const size_t row_base = (size_t)un.bh * S;
+        const int kbuf = k & 1;
+        if (!bounded_wait(&k_empty[kbuf], ((k >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&k_full[kbuf], TILE_BYTES);
+        tma_load_2d(smem + SM_K + kbuf * TILE_BYTES, &tm_qkv, &k_full[kbuf], E + h * D, krow);
+        ++nkl;
+        for (int i = 0; i < un.niter; ++i, ++n) {
+          const uint32_t st = n % QST;
+          if (!bounded_wait(&q_empty[st], ((n / QST) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES + VEC_BYTES);
+          const int qb = un.kb + i;
+          const int qrow = b * S + qb * BQ;
+          tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_qkv, &q_full[st], h * D, qrow);
+          tma_load_2d(smem + SM_DO + st * TILE_BYTES, &tm_do, &q_full[st], h * D, qrow);
+          float* vec = reinterpret_cast<float*>(smem + SM_VEC + st * VEC_BYTES);
+          bulk_load(vec, nl_g + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
+          bulk_load(vec + BQ, Dsum + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
+          if (i == 0) {
+            if (!bounded_wait(v_empty, (k & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; ++n; break; }
+            mbar_arrive_expect_tx(v_full, TILE_BYTES);
+            tma_load_2d(smem + SM_V, &tm_qkv, v_full, 2 * E + h * D, krow);
+            ++nvl;
+          }
+        }
       }
-      // no copy may still be landing in shared memory when the CTA exits
-      bounded_wait(kv_full, 0, DEV_TIMEOUT_ATTN);
-      for (int i = issued - QST < 0 ? 0 : issued - QST; i < issued; ++i)
-        bounded_wait(&q_full[i % QST], (i / QST) & 1, DEV_TIMEOUT_ATTN);
+      // no copy may still be landing in shared memory when the CTA exits: the last load of every
+      // slot has completed (the consumers waited for all of them on the normal path)
+      for (uint32_t k = nkl > 2u ? nkl - 2 : 0; k < nkl; ++k)
+        bounded_wait(&k_full[k & 1], (k >> 1) & 1, DEV_TIMEOUT_ATTN);
+      if (nvl > 0) bounded_wait(v_full, (nvl - 1) & 1, DEV_TIMEOUT_ATTN);
+      for (uint32_t j = n > (uint32_t)QST ? n - QST : 0; j < n; ++j)
+        bounded_wait(&q_full[j % QST], (j / QST) & 1, DEV_TIMEOUT_ATTN);
     }
   } else if (warp == 1) {
-    const uint32_t sk = smem_u32(smem + SM_K), sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
-    // S^T / dP^T of query block j (stage j % QST) -> sd_full
-    auto issue_sd = [&](int j) {
-      const uint32_t sq = smem_u32(smem + SM_Q + (j % QST) * TILE_BYTES);
-      const uint32_t sdo = smem_u32(smem + SM_DO + (j % QST) * TILE_BYTES);
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
+    struct Cur {
+      int k;      // unit of this CTA
+      Unit un;
+      int i;      // query block inside the unit (query block kb + i)
+      uint32_t n; // block of the CTA's flat sequence
+    };
+    auto advance = [&](Cur c) -> Cur {
+      if (++c.i == c.un.niter) {
+        ++c.k;
+        c.un = unit_of(c.k);
+        c.i = 0;
+      }
+      ++c.n;
+      return c;
+    };
+    // S^T / dP^T of block c -> sd_full; the unit's last one also releases V
+    auto issue_sd = [&](const Cur& c) -> bool {
+      const uint32_t st = c.n % QST;
+      if (!bounded_wait_warp(&q_full[st], (c.n / QST) & 1, DEV_TIMEOUT_ATTN)) return false;
+      if (c.i == 0) {
+        if (!bounded_wait_warp(&k_full[c.k & 1], (c.k >> 1) & 1, DEV_TIMEOUT_ATTN)) return false;
+        if (!bounded_wait_warp(v_full, c.k & 1, DEV_TIMEOUT_ATTN)) return false;
+      }
+      tc_fence_after();
+      const uint32_t sk = smem_u32(smem + SM_K + (c.k & 1) * TILE_BYTES);
+      const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES);
+      const uint32_t sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -797,32 +866,35 @@ __global__ void __launch_bounds__(THREADS_B, 1)
                    IDESC_SD, k > 0 ? 1u : 0u);
         }
         umma_commit(sd_full);
+        if (c.i == c.un.niter - 1) umma_commit(v_empty);
       }
       __syncwarp();
+      return true;
     };
-    bool ok = bounded_wait_warp(kv_full, 0, DEV_TIMEOUT_ATTN) && bounded_wait_warp(&q_full[0], 0, DEV_TIMEOUT_ATTN);
-    if (ok) {
-      tc_fence_after();
-      issue_sd(0);
-    }
-    for (int i = 0; i < niter && ok; ++i) {
-      const int st = i % QST;
-      if (i + 1 < niter) {
-        // the softmax warps hold S^T / dP^T of block i in registers: block i+1 can overwrite them
-        if (!bounded_wait_warp(sd_used, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-        const int sn = (i + 1) % QST;
-        if (!bounded_wait_warp(&q_full[sn], ((i + 1) / QST) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-        tc_fence_after();
-        issue_sd(i + 1);
+    Cur cur{0, unit_of(0), 0, 0};
+    bool ok = cur.un.niter > 0 && issue_sd(cur);
+    while (ok && cur.un.niter > 0) {
+      const Cur nxt = advance(cur);
+      if (nxt.un.niter > 0) {
+        // the softmax warps hold S^T / dP^T of this block in registers: the next block (of this
+        // unit or the next) can overwrite them
+        if (!bounded_wait_warp(sd_used, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        if (!issue_sd(nxt)) { ok = false; break; }
       }
-      // softmax of block i is done: P^T (TMEM) and dS^T (smem) are ready
-      if (!bounded_wait_warp(ds_ready, i & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      // softmax of this block is done: P^T (TMEM) and dS^T (smem) are ready
+      if (!bounded_wait_warp(ds_ready, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      // a unit's first dV / dK products overwrite the accumulators: the previous unit's must be read
+      if (cur.i == 0 && cur.k > 0 && !bounded_wait_warp(dkv_free, (cur.k - 1) & 1, DEV_TIMEOUT_ATTN)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
+      const uint32_t st = cur.n % QST;
       const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < BQ / 16; ++k) {  // 16 queries per MMA
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          const uint32_t acc = (cur.i > 0 || k > 0) ? 1u : 0u;
           umma_f16_ts(tmem + C_DV, tmem + C_P + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
                       IDESC_VK, acc);
           umma_f16(tmem + C_DK, smem_desc_sw128(sds + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
@@ -830,9 +902,10 @@ __global__ void __launch_bounds__(THREADS_B, 1)
         }
       }
       __syncwarp();
-      // dQ of block i-1 has been read out of TMEM
-      if (i > 0 && !bounded_wait_warp(dq_free, (i - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      // dQ of the previous block has been read out of TMEM
+      if (cur.n > 0 && !bounded_wait_warp(dq_free, (cur.n - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
       tc_fence_after();
+      const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * TILE_BYTES);
       if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA
@@ -840,26 +913,27 @@ __global__ void __launch_bounds__(THREADS_B, 1)
                    smem_desc_sw128(sk + k * 2048, TILE_BYTES, 1024), IDESC_Q, k > 0 ? 1u : 0u);
         umma_commit(mm_done);
         umma_commit(&q_empty[st]);
+        if (cur.i == cur.un.niter - 1) umma_commit(&k_empty[cur.k & 1]);
       }
       __syncwarp();
+      cur = nxt;
     }
     // TMEM is freed below only after every MMA issued here has retired
     if (lane == 0) umma_commit(drain);
     __syncwarp();
     bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
-  } else {
+  } else if (warp >= 4) {
     const int quarter = warp & 3;
-    const int cs = (warp - 2) >> 2;               // column slice: queries [QCOLS*cs, +QCOLS), head dims [DCOLS*cs, +DCOLS)
+    const int cs = (warp - 4) >> 2;               // column slice: queries [QCOLS*cs, +QCOLS), head dims [DCOLS*cs, +DCOLS)
     const int r_local = quarter * 32 + lane;      // key row (S^T / dP^T / dV / dK) and query row (dQ)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-    const int key = kb * BKV + r_local;           // position of this thread's key
-    const bool elected = (threadIdx.x == 64);     // issues the dQ reductions
+    const bool elected = (threadIdx.x == 128);    // issues the dQ reductions
     uint8_t* sds = smem + SM_DS;
     bool ok = true;
-    // dQ of block j: TMEM -> shared boxes.  The reduction of the previous tile must have finished
+    // dQ of a block: TMEM -> shared boxes.  The reduction of the previous tile must have finished
     // reading the buffer first: the elected thread waits for it, and a named barrier passes that on.
-    auto dq_readout = [&](int j, bool have) {
-      if (elected) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    auto dq_readout = [&](bool have) {
+      if (elected) bulk_wait_read0();
       named_sync_softmax();
       if (have) {
         uint32_t dq[DCOLS];
@@ -877,151 +951,182 @@ __global__ void __launch_bounds__(THREADS_B, 1)
               make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
       }
     };
-    // every softmax thread runs dq_readout and dq_reduce once per block (also after a timeout), so
-    // the named barriers always complete
-    auto dq_reduce = [&](int j, bool have) {
+    // y: the block's first row in the dQ accumulator.  Every softmax thread runs dq_readout and
+    // dq_reduce for the same blocks (also after a timeout), so the named barriers always complete.
+    auto dq_reduce = [&](int y, bool have) {
       fence_async_smem();
       named_sync_softmax();
       if (elected && have) {
         const uint8_t* tile = smem + SM_DQ;
-        const int y = (int)(row_base + (size_t)(kb + j) * BQ);
         tma_reduce_add_2d(&tm_dq, tile, 0, y);
         tma_reduce_add_2d(&tm_dq, tile + DQ_BYTES / 2, 32, y);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        bulk_commit();
       }
     };
-    for (int i = 0; i < niter; ++i) {
-      const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + (i % QST) * VEC_BYTES);
-      const bool diag = (i == 0);
-      ok = ok && bounded_wait_warp(sd_full, i & 1, DEV_TIMEOUT_ATTN);
-      bool have_dq = false;
-      if (ok) {
-        tc_fence_after();
-        // P^T / dS^T of this thread's 64 queries are computed into registers first (4 sub-chunks of 16;
-        // the TMEM loads of sub-chunk g+1 are in flight while g is computed), and only then does the
-        // thread wait for block i-1's MMAs to release the P^T columns and the dS^T buffer.
-        auto chunks = [&](auto diag_tag) {
-          constexpr bool DIAG = decltype(diag_tag)::value;
-          constexpr int NG = QCOLS / 16;          // sub-chunks of 16 queries
-          // with two softmax warps per sub-partition the TMEM loads of sub-chunk g+1 are issued
-          // before g is computed; with four, the other warps hide the load latency instead
-          constexpr bool PREFETCH = (WPQ == 2);
-          constexpr int NB = PREFETCH ? 2 : 1;
-          uint32_t rs[NB][16], rd[NB][16];
-          uint32_t pp[QCOLS / 2], dd[QCOLS / 2];
-          const uint32_t c0 = (uint32_t)(cs * QCOLS);
-          if constexpr (PREFETCH) {
-            tmem_ld16(t_lane + C_S + c0, rs[0]);
-            tmem_ld16(t_lane + C_DP + c0, rd[0]);
-            tmem_ld_wait();
-          }
-#pragma unroll
-          for (int g = 0; g < NG; ++g) {
-            const int b = PREFETCH ? (g & 1) : 0;
+    uint32_t n = 0;   // block of the CTA's flat sequence
+    int prev_y = 0;   // dQ accumulator row of block n-1
+    for (int ku = 0;; ++ku) {
+      const Unit un = unit_of(ku);
+      if (un.niter == 0) break;
+      for (int i = 0; i < un.niter; ++i, ++n) {
+        const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + (n % QST) * VEC_BYTES);
+        const bool diag = (i == 0);
+        ok = ok && bounded_wait_warp(sd_full, n & 1, DEV_TIMEOUT_ATTN);
+        bool have_dq = false;
+        if (ok) {
+          tc_fence_after();
+          // P^T / dS^T of this thread's queries are computed into registers first (sub-chunks of 16;
+          // the TMEM loads of sub-chunk g+1 are in flight while g is computed), and only then does
+          // the thread wait for the previous block's MMAs to release the P^T columns and dS^T buffer.
+          auto chunks = [&](auto diag_tag) {
+            constexpr bool DIAG = decltype(diag_tag)::value;
+            constexpr int NG = QCOLS / 16;          // sub-chunks of 16 queries
+            // with two softmax warps per sub-partition the TMEM loads of sub-chunk g+1 are issued
+            // before g is computed; with four, the other warps hide the load latency instead
+            constexpr bool PREFETCH = (WPQ == 2);
+            constexpr int NB = PREFETCH ? 2 : 1;
+            uint32_t rs[NB][16], rd[NB][16];
+            uint32_t pp[QCOLS / 2], dd[QCOLS / 2];
+            const uint32_t c0 = (uint32_t)(cs * QCOLS);
             if constexpr (PREFETCH) {
-              if (g + 1 < NG) {
-                tmem_ld16(t_lane + C_S + c0 + (uint32_t)((g + 1) * 16), rs[(g + 1) & 1]);
-                tmem_ld16(t_lane + C_DP + c0 + (uint32_t)((g + 1) * 16), rd[(g + 1) & 1]);
-              }
-            } else {
-              tmem_ld16(t_lane + C_S + c0 + (uint32_t)(g * 16), rs[0]);
-              tmem_ld16(t_lane + C_DP + c0 + (uint32_t)(g * 16), rd[0]);
+              tmem_ld16(t_lane + C_S + c0, rs[0]);
+              tmem_ld16(t_lane + C_DP + c0, rd[0]);
               tmem_ld_wait();
             }
-            const int q0 = cs * QCOLS + g * 16;  // first query of the sub-chunk
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const float4 nl4 = *reinterpret_cast<const float4*>(vec + q0 + j);
-              const float4 d4 = *reinterpret_cast<const float4*>(vec + BQ + q0 + j);
-              const float nlv[4] = {nl4.x, nl4.y, nl4.z, nl4.w};
-              const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
-              float p[4], d[4];
+            for (int g = 0; g < NG; ++g) {
+              const int bb = PREFETCH ? (g & 1) : 0;
+              if constexpr (PREFETCH) {
+                if (g + 1 < NG) {
+                  tmem_ld16(t_lane + C_S + c0 + (uint32_t)((g + 1) * 16), rs[(g + 1) & 1]);
+                  tmem_ld16(t_lane + C_DP + c0 + (uint32_t)((g + 1) * 16), rd[(g + 1) & 1]);
+                }
+              } else {
+                tmem_ld16(t_lane + C_S + c0 + (uint32_t)(g * 16), rs[0]);
+                tmem_ld16(t_lane + C_DP + c0 + (uint32_t)(g * 16), rd[0]);
+                tmem_ld_wait();
+              }
+              const int q0 = cs * QCOLS + g * 16;  // first query of the sub-chunk
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 nl4 = *reinterpret_cast<const float4*>(vec + q0 + j);
+                const float4 d4 = *reinterpret_cast<const float4*>(vec + BQ + q0 + j);
+                const float nlv[4] = {nl4.x, nl4.y, nl4.z, nl4.w};
+                const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+                float p[4], d[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  p[t] = fast_exp2(fmaf(__uint_as_float(rs[bb][j + t]), scale_log2, nlv[t]));
+                  if (DIAG && r_local > q0 + j + t) p[t] = 0.f;
+                  d[t] = p[t] * (__uint_as_float(rd[bb][j + t]) - dv[t]);
+                }
+                pp[g * 8 + (j >> 1)] = pack_bf16(p[0], p[1]);
+                pp[g * 8 + (j >> 1) + 1] = pack_bf16(p[2], p[3]);
+                dd[g * 8 + (j >> 1)] = pack_bf16(d[0], d[1]);
+                dd[g * 8 + (j >> 1) + 1] = pack_bf16(d[2], d[3]);
+              }
+              if constexpr (PREFETCH) {
+                if (g + 1 < NG) tmem_ld_wait();
+              }
+            }
+            tc_fence_before();
+            mbar_arrive(sd_used);
+            if (n > 0) {
+              // the previous block's dV / dK / dQ MMAs have finished reading P^T and dS^T (at a
+              // unit's first block this was already waited for at the end of the previous unit)
+              ok = bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN);
+              if (!ok) return;
+              tc_fence_after();
+              have_dq = (i > 0);
+            }
+            tmem_st_n<QCOLS / 2>(t_lane + C_P + (uint32_t)(cs * (QCOLS / 2)), pp);
+            if (i == 0 && n > 0) {  // the previous unit's dK / dV stores have read this warp's dS^T rows
+              if (lane == 0) bulk_wait_read0();
+              __syncwarp();
+            }
+            // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout
+            uint8_t* rowp = sds + ((cs * QCOLS) >> 6) * TILE_BYTES + r_local * 128;
+            const int t0 = ((cs * QCOLS) & 63) >> 3;
+#pragma unroll
+            for (int t = 0; t < QCOLS / 8; ++t)
+              *reinterpret_cast<uint4*>(rowp + (((t0 + t) ^ (r_local & 7)) * 16)) =
+                  make_uint4(dd[t * 4], dd[t * 4 + 1], dd[t * 4 + 2], dd[t * 4 + 3]);
+          };
+          if (diag) chunks(std::integral_constant<bool, true>{});
+          else chunks(std::integral_constant<bool, false>{});
+          if (ok) {
+            tmem_st_wait();
+            tc_fence_before();
+            fence_async_smem();
+            mbar_arrive(ds_ready);
+          }
+        }
+        if (i > 0) {  // dQ of the previous block of this unit
+          have_dq = have_dq && ok;
+          dq_readout(have_dq);
+          dq_reduce(prev_y, have_dq);
+        }
+        prev_y = (int)((size_t)un.bh * S + (size_t)(un.kb + i) * BQ);
+      }
+      // end of the unit: dQ of its last block, then dK (scaled, inverse RoPE) and dV, head-dim
+      // columns [DCOLS*cs, +DCOLS)
+      ok = ok && bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN);
+      dq_readout(ok);
+      dq_reduce(prev_y, ok);
+      if (ok) {
+        const int b = un.bh / H, h = un.bh % H;
+        const int key = un.kb * BKV + r_local;  // position of this thread's key
+        // The warp's [32 keys][DCOLS] boxes of dK and dV are staged (64-byte swizzle) in the part of
+        // the dS^T buffer that this warp writes, which the unit's last MMAs have finished reading,
+        // and leave by TMA store: one store per box instead of one 16-byte store per lane and row.
+        const uint32_t box_k = smem_u32(sds) + (uint32_t)(cs * TILE_BYTES + quarter * 4096);
+        const uint32_t box_v = box_k + 2048;
+        tc_fence_after();
+#pragma unroll 1
+        for (int part = 0; part < 2; ++part) {  // dK (scaled, inverse RoPE), then dV
+          uint32_t acc[DCOLS];
+          tmem_ld_n<DCOLS>(t_lane + (part == 0 ? C_DK : C_DV) + (uint32_t)(cs * DCOLS), acc);
+          tmem_ld_wait();
+          if (part == 1) {
+            tc_fence_before();
+            mbar_arrive(dkv_free);
+          }
+#pragma unroll
+          for (int q = 0; q < DCOLS / 8; ++q) {
+            float x[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) x[t] = __uint_as_float(acc[q * 8 + t]) * (part == 0 ? scale : 1.f);
+            if (part == 0 && rope_cos) {  // the 4 rotation pairs of these 8 columns: one 16-byte load each
+              const size_t pr = (size_t)key * (D / 2) + ((cs * DCOLS + q * 8) >> 1);
+              const float4 c4 = __ldg(reinterpret_cast<const float4*>(rope_cos + pr));
+              const float4 s4 = __ldg(reinterpret_cast<const float4*>(rope_sin + pr));
+              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
               for (int t = 0; t < 4; ++t) {
-                p[t] = fast_exp2(fmaf(__uint_as_float(rs[b][j + t]), scale_log2, nlv[t]));
-                if (DIAG && r_local > q0 + j + t) p[t] = 0.f;
-                d[t] = p[t] * (__uint_as_float(rd[b][j + t]) - dv[t]);
+                const float a0 = x[2 * t], a1 = x[2 * t + 1];
+                x[2 * t] = a0 * cc[t] + a1 * ss[t];
+                x[2 * t + 1] = -a0 * ss[t] + a1 * cc[t];
               }
-              pp[g * 8 + (j >> 1)] = pack_bf16(p[0], p[1]);
-              pp[g * 8 + (j >> 1) + 1] = pack_bf16(p[2], p[3]);
-              dd[g * 8 + (j >> 1)] = pack_bf16(d[0], d[1]);
-              dd[g * 8 + (j >> 1) + 1] = pack_bf16(d[2], d[3]);
             }
-            if constexpr (PREFETCH) {
-              if (g + 1 < NG) tmem_ld_wait();
-            }
+            const uint32_t off = (uint32_t)(lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"((part == 0 ? box_k : box_v) + off),
+                         "r"(pack_bf16(x[0], x[1])), "r"(pack_bf16(x[2], x[3])), "r"(pack_bf16(x[4], x[5])),
+                         "r"(pack_bf16(x[6], x[7])));
           }
-          tc_fence_before();
-          mbar_arrive(sd_used);
-          if (i > 0) {
-            // block i-1's dV / dK / dQ MMAs have finished reading P^T and dS^T
-            ok = bounded_wait_warp(mm_done, (i - 1) & 1, DEV_TIMEOUT_ATTN);
-            if (!ok) return;
-            tc_fence_after();
-            have_dq = true;
-          }
-          tmem_st_n<QCOLS / 2>(t_lane + C_P + (uint32_t)(cs * (QCOLS / 2)), pp);
-          // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout
-          uint8_t* rowp = sds + ((cs * QCOLS) >> 6) * TILE_BYTES + r_local * 128;
-          const int t0 = ((cs * QCOLS) & 63) >> 3;
-#pragma unroll
-          for (int t = 0; t < QCOLS / 8; ++t)
-            *reinterpret_cast<uint4*>(rowp + (((t0 + t) ^ (r_local & 7)) * 16)) =
-                make_uint4(dd[t * 4], dd[t * 4 + 1], dd[t * 4 + 2], dd[t * 4 + 3]);
-        };
-        if (diag) chunks(std::integral_constant<bool, true>{});
-        else chunks(std::integral_constant<bool, false>{});
-        if (ok) {
-          tmem_st_wait();
-          tc_fence_before();
-          fence_async_smem();
-          mbar_arrive(ds_ready);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int y0 = b * S + un.kb * BKV + quarter * 32;
+          tma_store_2d_bulk(&tm_dkv, box_k, E + h * D + cs * DCOLS, y0);
+          tma_store_2d_bulk(&tm_dkv, box_v, 2 * E + h * D + cs * DCOLS, y0);
+          bulk_commit();
         }
       }
-      have_dq = have_dq && ok;
-      dq_readout(i - 1, have_dq);
-      dq_reduce(i - 1, have_dq);
+      // after a timeout the warp keeps walking the units without waiting, so that every softmax
+      // warp meets the same named barriers
     }
-    ok = ok && bounded_wait_warp(mm_done, (niter - 1) & 1, DEV_TIMEOUT_ATTN);
-    dq_readout(niter - 1, ok);
-    dq_reduce(niter - 1, ok);
-    if (elected) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    // dK (scaled, inverse RoPE) and dV for this key block: head-dim columns [DCOLS*cs, +DCOLS)
-    if (ok) {
-      tc_fence_after();
-      uint32_t dk[DCOLS], dv[DCOLS];
-      tmem_ld_n<DCOLS>(t_lane + C_DK + (uint32_t)(cs * DCOLS), dk);
-      tmem_ld_n<DCOLS>(t_lane + C_DV + (uint32_t)(cs * DCOLS), dv);
-      tmem_ld_wait();
-      const size_t row = (size_t)b * S + key;
-      __nv_bfloat16* dkrow = d_qkv + row * 3 * E + E + h * D + cs * DCOLS;
-      __nv_bfloat16* dvrow = d_qkv + row * 3 * E + 2 * E + h * D + cs * DCOLS;
-#pragma unroll
-      for (int q = 0; q < DCOLS / 8; ++q) {
-        float x[8], y[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          x[t] = __uint_as_float(dk[q * 8 + t]) * scale;
-          y[t] = __uint_as_float(dv[q * 8 + t]);
-        }
-        if (rope_cos) {
-#pragma unroll
-          for (int t = 0; t < 8; t += 2) {
-            const int pair = (cs * DCOLS + q * 8 + t) >> 1;
-            const float cs = __ldg(rope_cos + (size_t)key * (D / 2) + pair);
-            const float sn = __ldg(rope_sin + (size_t)key * (D / 2) + pair);
-            const float a0 = x[t], a1 = x[t + 1];
-            x[t] = a0 * cs + a1 * sn;
-            x[t + 1] = -a0 * sn + a1 * cs;
-          }
-        }
-        uint4 uk, uv;
-        uk.x = pack_bf16(x[0], x[1]); uk.y = pack_bf16(x[2], x[3]); uk.z = pack_bf16(x[4], x[5]); uk.w = pack_bf16(x[6], x[7]);
-        uv.x = pack_bf16(y[0], y[1]); uv.y = pack_bf16(y[2], y[3]); uv.z = pack_bf16(y[4], y[5]); uv.w = pack_bf16(y[6], y[7]);
-        *reinterpret_cast<uint4*>(dkrow + q * 8) = uk;
-        *reinterpret_cast<uint4*>(dvrow + q * 8) = uv;
-      }
-    }
+    if (lane == 0) bulk_wait0();  // every dQ reduction and dK / dV store of this warp has landed
   }
 
   tc_fence_before();
@@ -1086,18 +1191,21 @@ bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, c
 zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
                            float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
                            int S, int H, int Dh, cudaStream_t st) {
-  CUtensorMap tq, tdo, tdq;
+  CUtensorMap tq, tdo, tdq, tdkv;
   const int E = H * Dh;
   if (!make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128) ||
       !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, 128) ||
-      !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 128))
+      !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 128) ||
+      !make_tma_map(&tdkv, d_qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 32, 32, 64))
     return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
   cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        fatc::bwd::SMEM_TOTAL);
   const float scale = 1.0f / sqrtf((float)Dh);
-  const int grid = B * H * (S / fatc::BKV);
+  const int nunits = B * H * (S / fatc::BKV);
+  const int sms = sm_count_current();
+  const int grid = nunits < sms ? nunits : sms;
   fatc::bwd::fa_bwd_tc_kernel<<<grid, fatc::bwd::THREADS_B, fatc::bwd::SMEM_TOTAL, st>>>(
-      tq, tdo, tdq, nl, Dsum, d_qkv, rope_cos, rope_sin, S, H, scale, scale * 1.4426950408889634f);
+      tq, tdo, tdq, tdkv, nl, Dsum, d_qkv, rope_cos, rope_sin, S, H, nunits, scale, scale * 1.4426950408889634f);
   return check_launch("fa_bwd_tc_kernel");
 }
 

@@ -1033,8 +1033,9 @@ bool use_pair(int M, int K) {
 }  // namespace
 
 bool make_tma_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
-                  uint32_t box_rows) {
-  return make_map(map, ptr, is_f32, inner, rows, box_inner, box_rows);
+                  uint32_t box_rows, int swizzle_bytes) {
+  return make_map(map, ptr, is_f32, inner, rows, box_inner, box_rows,
+                  swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 int sm_count_current() { return sm_count(); }
 
