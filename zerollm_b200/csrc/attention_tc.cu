@@ -637,16 +637,18 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
 // Persistent: one CTA per SM walks work units (batch, head, 128-key block), the units with the most
 // query blocks first, in snake order over the CTAs.  A unit walks its query blocks from the diagonal
 // to the end of the sequence, and the CTA's blocks form one pipeline across units: the next unit's
-// K / V and first Q / dO stages load, and its first S^T / dP^T are computed, while the softmax warps
-// finish the previous unit (last dQ, then dK / dV out of TMEM).  Per query block i:
+// K / V and first Q / dO stages load, and its first S^T / dP^T are computed, while the last block of
+// the previous unit is still in flight.  The softmax warps write a finished unit's last dQ and its
+// dK / dV right after the next unit's first block (releasing TMEM before storing), so they never
+// wait for a unit's last products.  Per query block i:
 //   MMA:     S^T = K Q_i^T, dP^T = V dO_i^T                                      (TMEM, fp32)
 //   softmax: P^T = exp2(S^T * scale_log2 - lse2[q]) with the causal mask, dS^T = P^T (dP^T - D[q]);
 //            P^T goes back to TMEM as bf16 (A operand of dV), dS^T to shared memory
 //   MMA:     dV += P^T dO_i   (A from TMEM)
 //            dK += dS^T Q_i   (A = dS^T in shared memory, K-major)
 //            dQ_i = dS K      (A = the same dS^T read MN-major, B = K MN-major)
-//   dQ_i:    TMEM -> two swizzled [128][32] shared boxes -> TMA reduce-add into the fp32 accumulator
-//            ([B, H, S, Dh]), done by the softmax warps one block later
+//   dQ_i:    TMEM -> one swizzled [32][32] shared box per softmax warp -> TMA reduce-add into the
+//            fp32 accumulator ([B, H, S, Dh]), done by each softmax warp on its own one block later
 // The tensor core and the softmax warps overlap across blocks: as soon as the softmax warps hold
 // S^T / dP^T of block i in registers (sd_used), the MMA warp issues S^T / dP^T of block i+1; once
 // P^T / dS^T of block i are written (ds_ready) it issues dV / dK / dQ of block i, while the softmax
@@ -656,9 +658,9 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
 // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ [384,448), P^T [448,512).
 // Eight softmax warps: warps w and w+4 share the TMEM lanes of quadrant w % 4 and split the 128
 // query columns into halves.  The per-query rows nl = -lse*log2(e) and D = rowsum(dO*O) arrive by
-// bulk copy with Q_i / dO_i.  At the end dK (times the softmax scale, rotated back by RoPE when
-// tables are given) and dV go to the packed gradient buffer; dQ's scale and inverse RoPE are
-// applied by the caller's post pass.
+// bulk copy with Q_i / dO_i.  A unit's dK (times the softmax scale, rotated back by RoPE when tables
+// are given) and dV leave by TMA store to the packed gradient buffer; dQ's scale and inverse RoPE
+// are applied by the caller's post pass.
 namespace bwd {
 constexpr int NSOFT = ZL_ATTN_BWD_SOFTMAX_WARPS;
 // Warpgroup 0: warp 0 TMA, warp 1 MMA, warps 2-3 idle; warps 4.. softmax.  (Registers are granted
@@ -686,17 +688,10 @@ constexpr uint32_t IDESC_SD = make_idesc(1, 128, 128, 0, 0);  // K Q^T / V dO^T:
 constexpr uint32_t IDESC_VK = make_idesc(1, 128, 64, 0, 1);   // dV / dK: A (TMEM or K-major), B MN-major
 constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);    // dQ: A MN-major (dS^T), B MN-major (K)
 
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, %0;" ::"n"(32 * NSOFT) : "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-// Element-wise add of a shared-memory box into global memory through the tensor map (fp32).
-__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
-  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
-               ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
 
@@ -927,44 +922,89 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     const int cs = (warp - 4) >> 2;               // column slice: queries [QCOLS*cs, +QCOLS), head dims [DCOLS*cs, +DCOLS)
     const int r_local = quarter * 32 + lane;      // key row (S^T / dP^T / dV / dK) and query row (dQ)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-    const bool elected = (threadIdx.x == 128);    // issues the dQ reductions
     uint8_t* sds = smem + SM_DS;
+    // This warp's 4 KB staging area: one [32][32] fp32 dQ box (128-byte swizzle), or the [32][32] bf16
+    // dK and dV boxes (64-byte swizzle) of a finished unit.  The warps stage and store independently.
+    const uint32_t stg = smem_u32(smem + SM_DQ) + (uint32_t)((cs * 4 + quarter) * 4096);
     bool ok = true;
-    // dQ of a block: TMEM -> shared boxes.  The reduction of the previous tile must have finished
-    // reading the buffer first: the elected thread waits for it, and a named barrier passes that on.
-    auto dq_readout = [&](bool have) {
-      if (elected) bulk_wait_read0();
-      named_sync_softmax();
-      if (have) {
-        uint32_t dq[DCOLS];
-        tc_fence_after();
-        tmem_ld_n<DCOLS>(t_lane + C_DQ + (uint32_t)(cs * DCOLS), dq);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(dq_free);
-        // box (cs*DCOLS)/32, 16-byte chunks from ((cs*DCOLS) % 32) / 4
-        uint8_t* rowp = smem + SM_DQ + ((cs * DCOLS) >> 5) * (DQ_BYTES / 2) + r_local * 128;
-        const int k0 = ((cs * DCOLS) & 31) >> 2;
-#pragma unroll
-        for (int k = 0; k < DCOLS / 4; ++k)  // 128-byte swizzle: the 8 rows of a store phase hit 8 bank groups
-          *reinterpret_cast<uint4*>(rowp + (((k0 + k) ^ (r_local & 7)) * 16)) =
-              make_uint4(dq[k * 4], dq[k * 4 + 1], dq[k * 4 + 2], dq[k * 4 + 3]);
-      }
+    auto stage_free = [&]() {  // the warp's last bulk copy has read the staging area
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
     };
-    // y: the block's first row in the dQ accumulator.  Every softmax thread runs dq_readout and
-    // dq_reduce for the same blocks (also after a timeout), so the named barriers always complete.
-    auto dq_reduce = [&](int y, bool have) {
-      fence_async_smem();
-      named_sync_softmax();
-      if (elected && have) {
-        const uint8_t* tile = smem + SM_DQ;
-        tma_reduce_add_2d(&tm_dq, tile, 0, y);
-        tma_reduce_add_2d(&tm_dq, tile + DQ_BYTES / 2, 32, y);
+    // dQ rows [quarter*32, +32), columns [cs*DCOLS, +DCOLS) of a block, out of TMEM (dq_free)
+    auto dq_load = [&](uint32_t (&dq)[DCOLS]) {
+      tc_fence_after();
+      tmem_ld_n<DCOLS>(t_lane + C_DQ + (uint32_t)(cs * DCOLS), dq);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    };
+    // ... then staged and added into the fp32 accumulator; y = the block's first accumulator row
+    auto dq_store = [&](const uint32_t (&dq)[DCOLS], int y) {
+      stage_free();
+#pragma unroll
+      for (int k = 0; k < DCOLS / 4; ++k)
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stg + lane * 128 + ((k ^ (lane & 7)) << 4)),
+                     "r"(dq[k * 4]), "r"(dq[k * 4 + 1]), "r"(dq[k * 4 + 2]), "r"(dq[k * 4 + 3]));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_2d_bulk(&tm_dq, stg, cs * DCOLS, y + quarter * 32);
         bulk_commit();
       }
     };
-    uint32_t n = 0;   // block of the CTA's flat sequence
-    int prev_y = 0;   // dQ accumulator row of block n-1
+    // A finished unit: dQ of its last block, then dK (times the softmax scale, rotated back by RoPE
+    // when tables are given) and dV.  Both TMEM regions are released before anything is stored.
+    auto unit_out = [&](const Unit& pu, int y) {
+      uint32_t dq[DCOLS], dk[DCOLS], dv[DCOLS];
+      dq_load(dq);
+      tmem_ld_n<DCOLS>(t_lane + C_DK + (uint32_t)(cs * DCOLS), dk);
+      tmem_ld_n<DCOLS>(t_lane + C_DV + (uint32_t)(cs * DCOLS), dv);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(dkv_free);
+      dq_store(dq, y);
+      const int b = pu.bh / H, h = pu.bh % H;
+      const int key = pu.kb * BKV + r_local;  // position of this thread's key
+      stage_free();
+#pragma unroll
+      for (int q = 0; q < DCOLS / 8; ++q) {
+        float x[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) x[t] = __uint_as_float(dk[q * 8 + t]) * scale;
+        if (rope_cos) {  // the 4 rotation pairs of these 8 columns: one 16-byte load each
+          const size_t pr = (size_t)key * (D / 2) + ((cs * DCOLS + q * 8) >> 1);
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(rope_cos + pr));
+          const float4 s4 = __ldg(reinterpret_cast<const float4*>(rope_sin + pr));
+          const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float a0 = x[2 * t], a1 = x[2 * t + 1];
+            x[2 * t] = a0 * cc[t] + a1 * ss[t];
+            x[2 * t + 1] = -a0 * ss[t] + a1 * cc[t];
+          }
+        }
+        const uint32_t off = (uint32_t)(lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stg + off), "r"(pack_bf16(x[0], x[1])),
+                     "r"(pack_bf16(x[2], x[3])), "r"(pack_bf16(x[4], x[5])), "r"(pack_bf16(x[6], x[7])));
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stg + 2048 + off),
+                     "r"(pack_bf16(__uint_as_float(dv[q * 8 + 0]), __uint_as_float(dv[q * 8 + 1]))),
+                     "r"(pack_bf16(__uint_as_float(dv[q * 8 + 2]), __uint_as_float(dv[q * 8 + 3]))),
+                     "r"(pack_bf16(__uint_as_float(dv[q * 8 + 4]), __uint_as_float(dv[q * 8 + 5]))),
+                     "r"(pack_bf16(__uint_as_float(dv[q * 8 + 6]), __uint_as_float(dv[q * 8 + 7]))));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int y0 = b * S + pu.kb * BKV + quarter * 32;
+        tma_store_2d_bulk(&tm_dkv, stg, E + h * D + cs * DCOLS, y0);
+        tma_store_2d_bulk(&tm_dkv, stg + 2048, 2 * E + h * D + cs * DCOLS, y0);
+        bulk_commit();
+      }
+    };
+    uint32_t n = 0;        // block of the CTA's flat sequence
+    int prev_y = 0;        // dQ accumulator row of block n-1
+    Unit pu{0, 0, 0};      // the previous unit (its dK / dV stay in TMEM until its first successor block)
     for (int ku = 0;; ++ku) {
       const Unit un = unit_of(ku);
       if (un.niter == 0) break;
@@ -972,7 +1012,6 @@ __global__ void __launch_bounds__(THREADS_B, 1)
         const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + (n % QST) * VEC_BYTES);
         const bool diag = (i == 0);
         ok = ok && bounded_wait_warp(sd_full, n & 1, DEV_TIMEOUT_ATTN);
-        bool have_dq = false;
         if (ok) {
           tc_fence_after();
           // P^T / dS^T of this thread's queries are computed into registers first (sub-chunks of 16;
@@ -1032,18 +1071,12 @@ __global__ void __launch_bounds__(THREADS_B, 1)
             tc_fence_before();
             mbar_arrive(sd_used);
             if (n > 0) {
-              // the previous block's dV / dK / dQ MMAs have finished reading P^T and dS^T (at a
-              // unit's first block this was already waited for at the end of the previous unit)
+              // the previous block's dV / dK / dQ MMAs have finished reading P^T and dS^T
               ok = bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN);
               if (!ok) return;
               tc_fence_after();
-              have_dq = (i > 0);
             }
             tmem_st_n<QCOLS / 2>(t_lane + C_P + (uint32_t)(cs * (QCOLS / 2)), pp);
-            if (i == 0 && n > 0) {  // the previous unit's dK / dV stores have read this warp's dS^T rows
-              if (lane == 0) bulk_wait_read0();
-              __syncwarp();
-            }
             // dS^T row segment -> shared memory in the swizzled [q-half][key][64] layout
             uint8_t* rowp = sds + ((cs * QCOLS) >> 6) * TILE_BYTES + r_local * 128;
             const int t0 = ((cs * QCOLS) & 63) >> 3;
@@ -1061,71 +1094,23 @@ __global__ void __launch_bounds__(THREADS_B, 1)
             mbar_arrive(ds_ready);
           }
         }
-        if (i > 0) {  // dQ of the previous block of this unit
-          have_dq = have_dq && ok;
-          dq_readout(have_dq);
-          dq_reduce(prev_y, have_dq);
+        if (ok && n > 0) {
+          // the previous block's dQ; at a unit's first block, also the previous unit's dK / dV (the
+          // MMA warp waits for both before this block's products)
+          if (i > 0) {
+            uint32_t dq[DCOLS];
+            dq_load(dq);
+            dq_store(dq, prev_y);
+          } else {
+            unit_out(pu, prev_y);
+          }
         }
         prev_y = (int)((size_t)un.bh * S + (size_t)(un.kb + i) * BQ);
       }
-      // end of the unit: dQ of its last block, then dK (scaled, inverse RoPE) and dV, head-dim
-      // columns [DCOLS*cs, +DCOLS)
-      ok = ok && bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN);
-      dq_readout(ok);
-      dq_reduce(prev_y, ok);
-      if (ok) {
-        const int b = un.bh / H, h = un.bh % H;
-        const int key = un.kb * BKV + r_local;  // position of this thread's key
-        // The warp's [32 keys][DCOLS] boxes of dK and dV are staged (64-byte swizzle) in the part of
-        // the dS^T buffer that this warp writes, which the unit's last MMAs have finished reading,
-        // and leave by TMA store: one store per box instead of one 16-byte store per lane and row.
-        const uint32_t box_k = smem_u32(sds) + (uint32_t)(cs * TILE_BYTES + quarter * 4096);
-        const uint32_t box_v = box_k + 2048;
-        tc_fence_after();
-#pragma unroll 1
-        for (int part = 0; part < 2; ++part) {  // dK (scaled, inverse RoPE), then dV
-          uint32_t acc[DCOLS];
-          tmem_ld_n<DCOLS>(t_lane + (part == 0 ? C_DK : C_DV) + (uint32_t)(cs * DCOLS), acc);
-          tmem_ld_wait();
-          if (part == 1) {
-            tc_fence_before();
-            mbar_arrive(dkv_free);
-          }
-#pragma unroll
-          for (int q = 0; q < DCOLS / 8; ++q) {
-            float x[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) x[t] = __uint_as_float(acc[q * 8 + t]) * (part == 0 ? scale : 1.f);
-            if (part == 0 && rope_cos) {  // the 4 rotation pairs of these 8 columns: one 16-byte load each
-              const size_t pr = (size_t)key * (D / 2) + ((cs * DCOLS + q * 8) >> 1);
-              const float4 c4 = __ldg(reinterpret_cast<const float4*>(rope_cos + pr));
-              const float4 s4 = __ldg(reinterpret_cast<const float4*>(rope_sin + pr));
-              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const float a0 = x[2 * t], a1 = x[2 * t + 1];
-                x[2 * t] = a0 * cc[t] + a1 * ss[t];
-                x[2 * t + 1] = -a0 * ss[t] + a1 * cc[t];
-              }
-            }
-            const uint32_t off = (uint32_t)(lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"((part == 0 ? box_k : box_v) + off),
-                         "r"(pack_bf16(x[0], x[1])), "r"(pack_bf16(x[2], x[3])), "r"(pack_bf16(x[4], x[5])),
-                         "r"(pack_bf16(x[6], x[7])));
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          const int y0 = b * S + un.kb * BKV + quarter * 32;
-          tma_store_2d_bulk(&tm_dkv, box_k, E + h * D + cs * DCOLS, y0);
-          tma_store_2d_bulk(&tm_dkv, box_v, 2 * E + h * D + cs * DCOLS, y0);
-          bulk_commit();
-        }
-      }
-      // after a timeout the warp keeps walking the units without waiting, so that every softmax
-      // warp meets the same named barriers
+      pu = un;
+      if (!ok) break;
     }
+    if (n > 0 && ok && bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN)) unit_out(pu, prev_y);
     if (lane == 0) bulk_wait0();  // every dQ reduction and dK / dV store of this warp has landed
   }
 
@@ -1195,7 +1180,7 @@ zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, c
   const int E = H * Dh;
   if (!make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128) ||
       !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, 128) ||
-      !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 128) ||
+      !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 32) ||
       !make_tma_map(&tdkv, d_qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 32, 32, 64))
     return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
   cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
