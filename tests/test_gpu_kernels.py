@@ -108,9 +108,11 @@ def test_gemm_bf16_weight_grad_splitk(L, T, N, K_, gemm_kind):
     assert rel(acc.cpu().view(N, K_), ref + 1.0) < 1e-4
 
 
-def test_gemm_bf16_epilogues(L, gemm_kind):
-    import ctypes as C
-    M, N, K_ = 512, 1536, 512
+@pytest.mark.parametrize("b_k,M", [(True, 512), (False, 500)])
+def test_gemm_bf16_epilogues(L, gemm_kind, b_k, M):
+    """Every fused epilogue on the forward layout (A, B K-major) and on the dX layout (B MN-major),
+    the latter with a row count that leaves a partial last tile."""
+    N, K_ = 1536, 512
     S, Dh = 256, 64
     g = torch.Generator().manual_seed(3)
     A = torch.randn(M, K_, generator=g).bfloat16()
@@ -122,18 +124,19 @@ def test_gemm_bf16_epilogues(L, gemm_kind):
     bias_d, res_d, aux_d = bias.cuda(), _bf(res), _bf(aux)
     e = L.Epilogue()
     e.bias, e.residual, e.aux = bias_d.data_ptr(), res_d.data_ptr(), aux_d.data_ptr()
-    kk = L.A_KMAJOR | L.B_KMAJOR
-    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_BIAS | L.EPI_RELU, e)
+    kk = L.A_KMAJOR | (L.B_KMAJOR if b_k else 0)
+    Bd = _bf(B) if b_k else _bf(B.T.contiguous())
+    o = _gemm(L, _bf(A), Bd, M, N, K_, kk, L.EPI_BIAS | L.EPI_RELU, e)
     assert rel(o.float().cpu().view(M, N), torch.relu(base + bias)) < BF16_TOL
-    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_BIAS | L.EPI_RESIDUAL, e)
+    o = _gemm(L, _bf(A), Bd, M, N, K_, kk, L.EPI_BIAS | L.EPI_RESIDUAL, e)
     assert rel(o.float().cpu().view(M, N), base + bias + res.float()) < BF16_TOL
-    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_RELU_MASK, e)
+    o = _gemm(L, _bf(A), Bd, M, N, K_, kk, L.EPI_RELU_MASK, e)
     assert rel(o.float().cpu().view(M, N), torch.where(aux.float() > 0, base, torch.zeros(()))) < BF16_TOL
     # RoPE on the first 2*512 columns (q | k) with positions m % S
     c, s = O.rope_table(S, Dh)
     cd, sd = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
     e.rope_cos, e.rope_sin, e.rope_cols, e.rope_seq, e.head_dim = cd.data_ptr(), sd.data_ptr(), 1024, S, Dh
-    o = _gemm(L, _bf(A), _bf(B), M, N, K_, kk, L.EPI_BIAS | L.EPI_ROPE, e)
+    o = _gemm(L, _bf(A), Bd, M, N, K_, kk, L.EPI_BIAS | L.EPI_ROPE, e)
     want = (base + bias).numpy().copy()
     qk = np.ascontiguousarray(want[:, :1024])
     rot = O.rope_apply(qk, M, S, 16, Dh, 1024, c, s).reshape(M, 1024)

@@ -366,8 +366,138 @@ __device__ __forceinline__ void partial_chunk(const GemmArgs& a, uint32_t stg, i
   }
 }
 
+// ------------------------------------------------------------------ pipelined bf16 epilogue
+// One epilogue warp's share of an accumulator tile with a bf16 output leaving by TMA store: rows
+// [r0, r0+32) (this lane: r0+lane), columns n0 + [cbase, cbase + BN/2) in 32-column chunks.  The
+// global inputs of chunk k+1 (bias column, residual or mask rows, RoPE table entries) are loaded
+// while chunk k is finished, and two 2 KB staging boxes alternate, so a chunk never waits for the
+// previous chunk's store to read its box.  KIND fixes which row-wise input the chunk reads, so
+// that only its prefetch registers exist; bias and ReLU are runtime flags.
+enum EpiKind : int { EK_PLAIN = 0, EK_RESIDUAL = 1, EK_MASK = 2, EK_ROPE = 3 };
+
+template <int KIND>
+struct EpiPrefetch {
+  float bias = 0.f;  // lane j: bias of column c0 + j
+  uint4 row[KIND == EK_PLAIN ? 1 : 4];      // residual / mask row segment (64 bytes)
+  float4 rc[KIND == EK_ROPE ? 4 : 1], rs[KIND == EK_ROPE ? 4 : 1];  // cos / sin of 16 pairs
+};
+
+template <int KIND>
+__device__ __forceinline__ void epi_fetch(const GemmArgs& a, int r, int lane, int c0, EpiPrefetch<KIND>& p) {
+  if (a.flags & ZL_EPI_BIAS) p.bias = __ldg(a.epi.bias + c0 + lane);
+  if constexpr (KIND == EK_RESIDUAL || KIND == EK_MASK) {
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(KIND == EK_RESIDUAL ? a.epi.residual : a.epi.aux);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p.row[q] = make_uint4(0, 0, 0, 0);
+    if (r < a.M) {
+      const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)r * a.N + c0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) p.row[q] = __ldg(s + q);
+    }
+  }
+  if constexpr (KIND == EK_ROPE) {
+    if (c0 < a.epi.rope_cols) {
+      const int half = a.epi.head_dim >> 1;
+      const size_t base = (size_t)(r % a.epi.rope_seq) * half + ((c0 % a.epi.head_dim) >> 1);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        p.rc[q] = __ldg(reinterpret_cast<const float4*>(a.epi.rope_cos + base) + q);
+        p.rs[q] = __ldg(reinterpret_cast<const float4*>(a.epi.rope_sin + base) + q);
+      }
+    }
+  }
+}
+
+template <int BN, int KIND>
+__device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensorMap* tmD, uint32_t t_row,
+                                               uint32_t stg, int lane, int r0, int n0, int cbase) {
+  constexpr int NCH = BN / 64;
+  const int f = a.flags;
+  const int r = r0 + lane;
+  EpiPrefetch<KIND> cur, nxt;
+  epi_fetch<KIND>(a, r, lane, n0 + cbase, cur);
+#pragma unroll 1
+  for (int k = 0; k < NCH; ++k) {
+    const int c = cbase + k * 32, c0 = n0 + c;
+    if (c0 >= a.N) break;
+    uint32_t raw[32];
+    tmem_ld32(t_row + (uint32_t)c, raw);
+    if (k + 1 < NCH && c0 + 32 < a.N) epi_fetch<KIND>(a, r, lane, c0 + 32, nxt);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+    if (f & ZL_EPI_BIAS) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, cur.bias, j);
+    }
+    if constexpr (KIND == EK_ROPE) {
+      if (c0 < a.epi.rope_cols) {
+        const float cc[16] = {cur.rc[0].x, cur.rc[0].y, cur.rc[0].z, cur.rc[0].w, cur.rc[1].x, cur.rc[1].y,
+                              cur.rc[1].z, cur.rc[1].w, cur.rc[2].x, cur.rc[2].y, cur.rc[2].z, cur.rc[2].w,
+                              cur.rc[3].x, cur.rc[3].y, cur.rc[3].z, cur.rc[3].w};
+        const float ss[16] = {cur.rs[0].x, cur.rs[0].y, cur.rs[0].z, cur.rs[0].w, cur.rs[1].x, cur.rs[1].y,
+                              cur.rs[1].z, cur.rs[1].w, cur.rs[2].x, cur.rs[2].y, cur.rs[2].z, cur.rs[2].w,
+                              cur.rs[3].x, cur.rs[3].y, cur.rs[3].z, cur.rs[3].w};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float x0 = v[2 * j], x1 = v[2 * j + 1];
+          v[2 * j] = x0 * cc[j] - x1 * ss[j];
+          v[2 * j + 1] = x0 * ss[j] + x1 * cc[j];
+        }
+      }
+    }
+    if constexpr (KIND == EK_RESIDUAL || KIND == EK_MASK) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float t[8];
+        unpack8(cur.row[q], t);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (KIND == EK_RESIDUAL) v[q * 8 + j] += t[j];
+          else v[q * 8 + j] = t[j] > 0.f ? v[q * 8 + j] : 0.f;
+        }
+      }
+    }
+    if (f & ZL_EPI_RELU) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+    }
+    // stage [32][32] bf16 (64-byte swizzle) in box k & 1, whose store from chunk k-2 has read it
+    const uint32_t box = stg + (uint32_t)((k & 1) * 2048);
+    if (lane == 0) bulk_wait_read1();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t dst = box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(pack_bf16(v[q * 8 + 0], v[q * 8 + 1])),
+                   "r"(pack_bf16(v[q * 8 + 2], v[q * 8 + 3])), "r"(pack_bf16(v[q * 8 + 4], v[q * 8 + 5])),
+                   "r"(pack_bf16(v[q * 8 + 6], v[q * 8 + 7])));
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d_bulk(tmD, box, c0, r0);
+      bulk_commit();
+    }
+    cur = nxt;
+  }
+}
+
+// The kind of the pipelined bf16 epilogue for these flags, or -1 when the general path is needed
+// (fp32 output, split-K partials, two row-wise inputs at once, or chunks that are not whole).
+__host__ __device__ inline int bf16_epi_kind(int flags, int N, int splits) {
+  if ((flags & (ZL_EPI_OUT_F32 | ZL_EPI_ACCUM)) || splits > 1 || N % 32 != 0) return -1;
+  const int rows = (flags & ZL_EPI_RESIDUAL ? 1 : 0) + (flags & ZL_EPI_RELU_MASK ? 1 : 0) + (flags & ZL_EPI_ROPE ? 1 : 0);
+  if (rows > 1) return -1;
+  if (flags & ZL_EPI_RESIDUAL) return EK_RESIDUAL;
+  if (flags & ZL_EPI_RELU_MASK) return EK_MASK;
+  if (flags & ZL_EPI_ROPE) return EK_ROPE;
+  return EK_PLAIN;
+}
+
 // ------------------------------------------------------------------ kernel
-template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
+template <typename T, int BN, int STAGES, bool A_MN, bool B_MN, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmW,
@@ -498,6 +628,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int r0 = m0 + quarter * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (KIND >= 0) {  // bf16 output by TMA store, pipelined (the host chose KIND)
+        if (r0 < args.M) drain_bf16_tma<BN, KIND>(args, &tmD, t_row, stg, lane, r0, n0, col_half * (BN / 2));
+      } else
 #pragma unroll 1
       for (int c = col_half * (BN / 2); c < (col_half + 1) * (BN / 2); c += 32) {
         uint32_t raw[32];
@@ -560,7 +693,7 @@ struct Smem2 {
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmW,
@@ -703,6 +836,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int r0 = m0 + quarter * 32;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (KIND >= 0) {  // bf16 output by TMA store, pipelined (the host chose KIND)
+        if (r0 < args.M) drain_bf16_tma<BN, KIND>(args, &tmD, t_row, stg, lane, r0, n0, col_half * (BN / 2));
+      } else
 #pragma unroll 1
       for (int c = col_half * (BN / 2); c < (col_half + 1) * (BN / 2); c += 32) {
         uint32_t raw[32];
@@ -927,25 +1063,42 @@ Plan make_plan(int M, int N, int K, int BK, bool out_allows_split) {
   return p;
 }
 
-template <typename T, int BN, int STAGES, bool A_MN, bool B_MN>
+template <typename T, int BN, int STAGES, bool A_MN, bool B_MN, int KIND>
 cudaError_t launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& mw,
                       const GemmArgs& a, int grid, cudaStream_t st) {
   using E = Elem<T>;
   using L = Smem<BN, STAGES, E::bytes>;
-  auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN>;
+  auto kern = gemm_tc_kernel<T, BN, STAGES, A_MN, B_MN, KIND>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, L::TOTAL, st>>>(ma, mb, md, mw, a);
   return cudaGetLastError();
 }
 
+// Kernel instances: the pipelined bf16 epilogue kinds exist for A K-major products (forward and
+// dX), whose outputs are bf16; dW products (A MN-major) write fp32 through the general path.
+template <typename T, int BN, int STAGES, bool B_MN>
+cudaError_t launch_kind(int kind, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
+                        const CUtensorMap& mw, const GemmArgs& a, int grid, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    switch (kind) {
+      case EK_PLAIN: return launch_tc<T, BN, STAGES, false, B_MN, EK_PLAIN>(ma, mb, md, mw, a, grid, st);
+      case EK_RESIDUAL: return launch_tc<T, BN, STAGES, false, B_MN, EK_RESIDUAL>(ma, mb, md, mw, a, grid, st);
+      case EK_MASK: return launch_tc<T, BN, STAGES, false, B_MN, EK_MASK>(ma, mb, md, mw, a, grid, st);
+      case EK_ROPE: return launch_tc<T, BN, STAGES, false, B_MN, EK_ROPE>(ma, mb, md, mw, a, grid, st);
+      default: break;
+    }
+  }
+  return launch_tc<T, BN, STAGES, false, B_MN, -1>(ma, mb, md, mw, a, grid, st);
+}
+
 template <typename T, int BN, int STAGES>
-cudaError_t dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
-                           const CUtensorMap& mw, const GemmArgs& a, int grid, cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_tc<T, BN, STAGES, false, false>(ma, mb, md, mw, a, grid, st);
-  if (!a_mn && b_mn) return launch_tc<T, BN, STAGES, false, true>(ma, mb, md, mw, a, grid, st);
-  if (a_mn && !b_mn) return launch_tc<T, BN, STAGES, true, false>(ma, mb, md, mw, a, grid, st);
-  return launch_tc<T, BN, STAGES, true, true>(ma, mb, md, mw, a, grid, st);
+cudaError_t dispatch_major(bool a_mn, bool b_mn, int kind, const CUtensorMap& ma, const CUtensorMap& mb,
+                           const CUtensorMap& md, const CUtensorMap& mw, const GemmArgs& a, int grid, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_kind<T, BN, STAGES, false>(kind, ma, mb, md, mw, a, grid, st);
+  if (!a_mn && b_mn) return launch_kind<T, BN, STAGES, true>(kind, ma, mb, md, mw, a, grid, st);
+  if (a_mn && !b_mn) return launch_tc<T, BN, STAGES, true, false, -1>(ma, mb, md, mw, a, grid, st);
+  return launch_tc<T, BN, STAGES, true, true, -1>(ma, mb, md, mw, a, grid, st);
 }
 
 // Two-SM variant: tiles of 256 rows (a CTA pair), grid = 2 x pairs, cluster of 2.
@@ -973,11 +1126,11 @@ Plan make_plan_pair(int M, int N, int K) {
   return p;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int KIND>
 cudaError_t launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md, const CUtensorMap& mw,
                        const GemmArgs& a, int pairs, cudaStream_t st) {
   using L = Smem2<BN, STAGES>;
-  auto kern = gemm_tc2_kernel<BN, STAGES, A_MN, B_MN>;
+  auto kern = gemm_tc2_kernel<BN, STAGES, A_MN, B_MN, KIND>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -1010,13 +1163,25 @@ cudaError_t launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   return cudaLaunchKernelEx(&cfg, kern, ma, mb, md, mw, a);
 }
 
+template <int BN, int STAGES, bool B_MN>
+cudaError_t launch_kind2(int kind, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
+                         const CUtensorMap& mw, const GemmArgs& a, int pairs, cudaStream_t st) {
+  switch (kind) {
+    case EK_PLAIN: return launch_tc2<BN, STAGES, false, B_MN, EK_PLAIN>(ma, mb, md, mw, a, pairs, st);
+    case EK_RESIDUAL: return launch_tc2<BN, STAGES, false, B_MN, EK_RESIDUAL>(ma, mb, md, mw, a, pairs, st);
+    case EK_MASK: return launch_tc2<BN, STAGES, false, B_MN, EK_MASK>(ma, mb, md, mw, a, pairs, st);
+    case EK_ROPE: return launch_tc2<BN, STAGES, false, B_MN, EK_ROPE>(ma, mb, md, mw, a, pairs, st);
+    default: return launch_tc2<BN, STAGES, false, B_MN, -1>(ma, mb, md, mw, a, pairs, st);
+  }
+}
+
 template <int BN, int STAGES>
-cudaError_t dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
-                          const CUtensorMap& mw, const GemmArgs& a, int pairs, cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_tc2<BN, STAGES, false, false>(ma, mb, md, mw, a, pairs, st);
-  if (!a_mn && b_mn) return launch_tc2<BN, STAGES, false, true>(ma, mb, md, mw, a, pairs, st);
-  if (a_mn && !b_mn) return launch_tc2<BN, STAGES, true, false>(ma, mb, md, mw, a, pairs, st);
-  return launch_tc2<BN, STAGES, true, true>(ma, mb, md, mw, a, pairs, st);
+cudaError_t dispatch_pair(bool a_mn, bool b_mn, int kind, const CUtensorMap& ma, const CUtensorMap& mb,
+                          const CUtensorMap& md, const CUtensorMap& mw, const GemmArgs& a, int pairs, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_kind2<BN, STAGES, false>(kind, ma, mb, md, mw, a, pairs, st);
+  if (!a_mn && b_mn) return launch_kind2<BN, STAGES, true>(kind, ma, mb, md, mw, a, pairs, st);
+  if (a_mn && !b_mn) return launch_tc2<BN, STAGES, true, false, -1>(ma, mb, md, mw, a, pairs, st);
+  return launch_tc2<BN, STAGES, true, true, -1>(ma, mb, md, mw, a, pairs, st);
 }
 
 // Which bf16 GEMMs run on the CTA-pair kernel.  Measured on B200: the pair wins once the reduction
@@ -1105,15 +1270,24 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
     if (mok && p.splits > 1) mok = make_map(&mw, ws, true, N, (uint64_t)p.splits * M, 32, 32);
     a.tma_out = mok ? 1 : 0;
   }
+  // the pipelined bf16 epilogue kind (or -1): TMA output, whole 32-column chunks, and for RoPE whole
+  // 32-column head slices and 16-byte aligned tables
+  int kind = -1;
+  if (!is_f32 && !a_mn && a.tma_out) {
+    kind = bf16_epi_kind(flags, N, p.splits);
+    if (kind == EK_ROPE && (a.epi.head_dim % 32 != 0 || a.epi.rope_cols % 32 != 0 ||
+                            ((reinterpret_cast<uintptr_t>(a.epi.rope_cos) | reinterpret_cast<uintptr_t>(a.epi.rope_sin)) & 15)))
+      kind = -1;
+  }
   cudaError_t e;
   if (pair) {
     const int pairs = std::min(p.units, sm_count() / 2);
-    if (p.bn == 128) e = dispatch_pair<128, 8>(a_mn, b_mn, ma, mb, md, mw, a, pairs, st);
-    else e = dispatch_pair<256, 6>(a_mn, b_mn, ma, mb, md, mw, a, pairs, st);
+    if (p.bn == 128) e = dispatch_pair<128, 8>(a_mn, b_mn, kind, ma, mb, md, mw, a, pairs, st);
+    else e = dispatch_pair<256, 6>(a_mn, b_mn, kind, ma, mb, md, mw, a, pairs, st);
   } else {
     const int grid = std::min(p.units, sm_count());
-    if (p.bn == 128) e = dispatch_major<T, 128, 6>(a_mn, b_mn, ma, mb, md, mw, a, grid, st);
-    else e = dispatch_major<T, 256, 4>(a_mn, b_mn, ma, mb, md, mw, a, grid, st);
+    if (p.bn == 128) e = dispatch_major<T, 128, 6>(a_mn, b_mn, kind, ma, mb, md, mw, a, grid, st);
+    else e = dispatch_major<T, 256, 4>(a_mn, b_mn, kind, ma, mb, md, mw, a, grid, st);
   }
   if (e != cudaSuccess) return set_error(ZL_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
   if (p.splits > 1) {
