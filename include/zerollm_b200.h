@@ -143,11 +143,13 @@ typedef struct {
   const float *bias;        /* [N] */
   const zl_bf16 *residual;  /* [M, N] */
   const zl_bf16 *aux;       /* [M, N] relu mask source */
-  const float *rope_cos;    /* [seq, head_dim/2] */
+  const float *rope_cos;    /* [seq, head_dim/2], or [head_dim/2, seq] when rope_pair_major */
   const float *rope_sin;
   int rope_cols;            /* columns [0, rope_cols) are rotated (2*d for q|k of a qkv row) */
   int rope_seq;             /* position of row m is m % rope_seq */
   int head_dim;
+  int rope_pair_major;      /* 1: tables stored pair-major, which the epilogue reads with coalesced
+                               loads (32 consecutive rows = 32 consecutive positions per load) */
 } zl_epilogue;
 /* D[M,N] = sum_k A(m,k) B(n,k), bf16 operands, fp32 accumulate in TMEM, fused epilogue.
  * `workspace` (fp32, >= zl_gemm_workspace_floats(...) elements, may be NULL when that is 0)

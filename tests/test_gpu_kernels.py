@@ -142,6 +142,11 @@ def test_gemm_bf16_epilogues(L, gemm_kind, b_k, M):
     rot = O.rope_apply(qk, M, S, 16, Dh, 1024, c, s).reshape(M, 1024)
     want[:, :1024] = rot
     assert rel(o.float().cpu().view(M, N), want) < BF16_TOL
+    # the same rotation from pair-major tables ([Dh/2, S]), which the epilogue reads coalesced
+    cdt, sdt = torch.from_numpy(c.reshape(S, Dh // 2).T.copy()).cuda(), torch.from_numpy(s.reshape(S, Dh // 2).T.copy()).cuda()
+    e.rope_cos, e.rope_sin, e.rope_pair_major = cdt.data_ptr(), sdt.data_ptr(), 1
+    o2 = _gemm(L, _bf(A), Bd, M, N, K_, kk, L.EPI_BIAS | L.EPI_ROPE, e)
+    assert torch.equal(o2, o)
 
 
 # ------------------------------------------------------------------ fp32 API GEMMs (tf32 / SIMT)

@@ -87,7 +87,8 @@ __device__ __forceinline__ void epilogue_store32(const GemmArgs& a, int r, int c
     for (int j = 0; j < 32; j += 2) {
       if (j + 1 < nvalid && c0 + j < a.epi.rope_cols) {
         const int i = ((c0 + j) % hd) >> 1;
-        const float c = __ldg(a.epi.rope_cos + (size_t)pos * half + i), s = __ldg(a.epi.rope_sin + (size_t)pos * half + i);
+        const size_t ti = a.epi.rope_pair_major ? (size_t)i * a.epi.rope_seq + pos : (size_t)pos * half + i;
+        const float c = __ldg(a.epi.rope_cos + ti), s = __ldg(a.epi.rope_sin + ti);
         const float x0 = v[j], x1 = v[j + 1];
         v[j] = x0 * c - x1 * s;
         v[j + 1] = x0 * s + x1 * c;
@@ -216,12 +217,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, uint32_t stg, 
   if ((f & ZL_EPI_ROPE) && c0 < a.epi.rope_cols) {
     const int half = a.epi.head_dim >> 1;
     const int pos = r % a.epi.rope_seq;
-    const float* ct = a.epi.rope_cos + (size_t)pos * half;
-    const float* st = a.epi.rope_sin + (size_t)pos * half;
+    // element i of this row's table slice: pair-major tables are [half, seq]
+    const size_t t0 = a.epi.rope_pair_major ? (size_t)pos : (size_t)pos * half;
+    const size_t ts = a.epi.rope_pair_major ? (size_t)a.epi.rope_seq : 1;
     const int i0 = (c0 % a.epi.head_dim) >> 1;
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
-      const float c = __ldg(ct + i0 + (j >> 1)), s = __ldg(st + i0 + (j >> 1));
+      const size_t ti = t0 + (size_t)(i0 + (j >> 1)) * ts;
+      const float c = __ldg(a.epi.rope_cos + ti), s = __ldg(a.epi.rope_sin + ti);
       const float x0 = v[j], x1 = v[j + 1];
       v[j] = x0 * c - x1 * s;
       v[j + 1] = x0 * s + x1 * c;
@@ -379,7 +382,7 @@ template <int KIND>
 struct EpiPrefetch {
   float bias = 0.f;  // lane j: bias of column c0 + j
   uint4 row[KIND == EK_PLAIN ? 1 : 4];      // residual / mask row segment (64 bytes)
-  float4 rc[KIND == EK_ROPE ? 4 : 1], rs[KIND == EK_ROPE ? 4 : 1];  // cos / sin of 16 pairs
+  float rc[KIND == EK_ROPE ? 16 : 1], rs[KIND == EK_ROPE ? 16 : 1];  // cos / sin of 16 pairs
 };
 
 template <int KIND>
@@ -397,14 +400,39 @@ __device__ __forceinline__ void epi_fetch(const GemmArgs& a, int r, int lane, in
   }
   if constexpr (KIND == EK_ROPE) {
     if (c0 < a.epi.rope_cols) {
-      const int half = a.epi.head_dim >> 1;
-      const size_t base = (size_t)(r % a.epi.rope_seq) * half + ((c0 % a.epi.head_dim) >> 1);
+      const int half = a.epi.head_dim >> 1, i0 = (c0 % a.epi.head_dim) >> 1, pos = r % a.epi.rope_seq;
+      if (a.epi.rope_pair_major) {  // [half, seq]: the warp's 32 positions are one 128-byte line per pair
+        const size_t base = (size_t)i0 * a.epi.rope_seq + pos;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        p.rc[q] = __ldg(reinterpret_cast<const float4*>(a.epi.rope_cos + base) + q);
-        p.rs[q] = __ldg(reinterpret_cast<const float4*>(a.epi.rope_sin + base) + q);
+        for (int j = 0; j < 16; ++j) {
+          p.rc[j] = __ldg(a.epi.rope_cos + base + (size_t)j * a.epi.rope_seq);
+          p.rs[j] = __ldg(a.epi.rope_sin + base + (size_t)j * a.epi.rope_seq);
+        }
+      } else {  // [seq, half]: 64 contiguous bytes of this lane's row
+        const size_t base = (size_t)pos * half + i0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.epi.rope_cos + base) + q);
+          const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.epi.rope_sin + base) + q);
+          p.rc[4 * q] = c4.x; p.rc[4 * q + 1] = c4.y; p.rc[4 * q + 2] = c4.z; p.rc[4 * q + 3] = c4.w;
+          p.rs[4 * q] = s4.x; p.rs[4 * q + 1] = s4.y; p.rs[4 * q + 2] = s4.z; p.rs[4 * q + 3] = s4.w;
+        }
       }
     }
+  }
+}
+
+// Before a tile's accumulator is ready: pull this lane's row segment of the residual or mask
+// input for the warp's BN/2 columns into L2, so that the per-chunk loads (issued one chunk ahead)
+// find it there instead of waiting on HBM.
+template <int BN, int KIND>
+__device__ __forceinline__ void epi_prefetch_l2(const GemmArgs& a, int r, int c0) {
+  if constexpr (KIND == EK_RESIDUAL || KIND == EK_MASK) {
+    if (r >= a.M || c0 >= a.N) return;
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(KIND == EK_RESIDUAL ? a.epi.residual : a.epi.aux);
+    const char* p = reinterpret_cast<const char*>(src + (size_t)r * a.N + c0);
+    const int bytes = min(BN / 2, a.N - c0) * 2;
+    for (int o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + o));
   }
 }
 
@@ -433,17 +461,11 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
     }
     if constexpr (KIND == EK_ROPE) {
       if (c0 < a.epi.rope_cols) {
-        const float cc[16] = {cur.rc[0].x, cur.rc[0].y, cur.rc[0].z, cur.rc[0].w, cur.rc[1].x, cur.rc[1].y,
-                              cur.rc[1].z, cur.rc[1].w, cur.rc[2].x, cur.rc[2].y, cur.rc[2].z, cur.rc[2].w,
-                              cur.rc[3].x, cur.rc[3].y, cur.rc[3].z, cur.rc[3].w};
-        const float ss[16] = {cur.rs[0].x, cur.rs[0].y, cur.rs[0].z, cur.rs[0].w, cur.rs[1].x, cur.rs[1].y,
-                              cur.rs[1].z, cur.rs[1].w, cur.rs[2].x, cur.rs[2].y, cur.rs[2].z, cur.rs[2].w,
-                              cur.rs[3].x, cur.rs[3].y, cur.rs[3].z, cur.rs[3].w};
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const float x0 = v[2 * j], x1 = v[2 * j + 1];
-          v[2 * j] = x0 * cc[j] - x1 * ss[j];
-          v[2 * j + 1] = x0 * ss[j] + x1 * cc[j];
+          v[2 * j] = x0 * cur.rc[j] - x1 * cur.rs[j];
+          v[2 * j + 1] = x0 * cur.rs[j] + x1 * cur.rc[j];
         }
       }
     }
@@ -624,6 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
       const int tile = u / args.splits, split = u % args.splits;
       const int m0 = (tile / args.n_tiles_n) * BM, n0 = (tile % args.n_tiles_n) * BN;
+      if constexpr (KIND >= 0) epi_prefetch_l2<BN, KIND>(args, m0 + quarter * 32 + lane, n0 + col_half * (BN / 2));
       if (!bounded_wait(&acc_full[acc], acc_phase, DEV_TIMEOUT_ACC)) break;
       tc_fence_after();
       const int r0 = m0 + quarter * 32;
@@ -832,6 +855,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tile = u / args.splits, split = u % args.splits;
       const int m0 = (tile / args.n_tiles_n) * (2 * BM) + (int)rank * BM;
       const int n0 = (tile % args.n_tiles_n) * BN;
+      if constexpr (KIND >= 0) epi_prefetch_l2<BN, KIND>(args, m0 + quarter * 32 + lane, n0 + col_half * (BN / 2));
       if (!bounded_wait_warp(&acc_full[acc], acc_phase, DEV_TIMEOUT_ACC)) break;
       tc_fence_after();
       const int r0 = m0 + quarter * 32;
@@ -1276,7 +1300,8 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   if (!is_f32 && !a_mn && a.tma_out) {
     kind = bf16_epi_kind(flags, N, p.splits);
     if (kind == EK_ROPE && (a.epi.head_dim % 32 != 0 || a.epi.rope_cols % 32 != 0 ||
-                            ((reinterpret_cast<uintptr_t>(a.epi.rope_cos) | reinterpret_cast<uintptr_t>(a.epi.rope_sin)) & 15)))
+                            (!a.epi.rope_pair_major &&
+                             ((reinterpret_cast<uintptr_t>(a.epi.rope_cos) | reinterpret_cast<uintptr_t>(a.epi.rope_sin)) & 15))))
       kind = -1;
   }
   cudaError_t e;

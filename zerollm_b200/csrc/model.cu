@@ -159,6 +159,7 @@ struct zl_model {
   float *params = nullptr, *grads = nullptr, *m = nullptr, *v = nullptr;
   bf16* pbf = nullptr;
   float *pos_table = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+  float *rope_cos_pm = nullptr, *rope_sin_pm = nullptr;  // the same tables pair-major ([Dh/2, S]) for the QKV epilogue
   // activations
   std::vector<bf16*> x, qkv, attn, r1, h1, f, r2;
   std::vector<float*> lse, mean1, rstd1, mean2, rstd2;
@@ -283,8 +284,11 @@ zl_status forward(zl_model* M, const int32_t* ids, int B, int S, float* logits_f
     int fl = c.bias ? ZL_EPI_BIAS : 0;
     if (c.pos == 1) {
       fl |= ZL_EPI_ROPE;
-      e.rope_cos = M->rope_cos;
-      e.rope_sin = M->rope_sin;
+      // pair-major tables ([Dh/2, max_seq_len]) serve when the step's sequence fills the table rows
+      const bool pm = S == c.max_seq_len;
+      e.rope_cos = pm ? M->rope_cos_pm : M->rope_cos;
+      e.rope_sin = pm ? M->rope_sin_pm : M->rope_sin;
+      e.rope_pair_major = pm ? 1 : 0;
       e.rope_cols = 2 * d;
       e.rope_seq = S;
       e.head_dim = d / H;
@@ -496,6 +500,16 @@ extern "C" zl_status zl_model_create(const zl_model_config* cfg, int64_t max_tok
     A(M->rope_sin, (int64_t)sn.size());
     cudaMemcpy(M->rope_cos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice);
     cudaMemcpy(M->rope_sin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice);
+    std::vector<float> cst(cs.size()), snt(cs.size());
+    for (int p = 0; p < c.max_seq_len; ++p)
+      for (int i = 0; i < half; ++i) {
+        cst[(size_t)i * c.max_seq_len + p] = cs[(size_t)p * half + i];
+        snt[(size_t)i * c.max_seq_len + p] = sn[(size_t)p * half + i];
+      }
+    A(M->rope_cos_pm, (int64_t)cst.size());
+    A(M->rope_sin_pm, (int64_t)snt.size());
+    cudaMemcpy(M->rope_cos_pm, cst.data(), cst.size() * sizeof(float), cudaMemcpyHostToDevice);
+    cudaMemcpy(M->rope_sin_pm, snt.data(), snt.size() * sizeof(float), cudaMemcpyHostToDevice);
   }
 #undef A
   // weights

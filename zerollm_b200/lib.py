@@ -28,7 +28,7 @@ class ZLError(RuntimeError):
 
 class Epilogue(C.Structure):
     _fields_ = [("bias", vp), ("residual", vp), ("aux", vp), ("rope_cos", vp), ("rope_sin", vp),
-                ("rope_cols", i32), ("rope_seq", i32), ("head_dim", i32)]
+                ("rope_cols", i32), ("rope_seq", i32), ("head_dim", i32), ("rope_pair_major", i32)]
 
 
 class ModelConfig(C.Structure):
