@@ -883,29 +883,24 @@ __global__ void __launch_bounds__(THREADS_B, 1)
         ok = false;
         break;
       }
+      // dQ of the previous block has been read out of TMEM
+      if (cur.n > 0 && !bounded_wait_warp(dq_free, (cur.n - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
       tc_fence_after();
       const uint32_t st = cur.n % QST;
       const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
+      const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * TILE_BYTES);
       if (lane == 0) {
+        // dV, dK and dQ are three independent accumulation chains, issued interleaved
 #pragma unroll
-        for (int k = 0; k < BQ / 16; ++k) {  // 16 queries per MMA
+        for (int k = 0; k < BQ / 16; ++k) {  // 16 queries (dV, dK) / 16 keys (dQ) per MMA
           const uint32_t acc = (cur.i > 0 || k > 0) ? 1u : 0u;
           umma_f16_ts(tmem + C_DV, tmem + C_P + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
                       IDESC_VK, acc);
           umma_f16(tmem + C_DK, smem_desc_sw128(sds + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
                    smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024), IDESC_VK, acc);
-        }
-      }
-      __syncwarp();
-      // dQ of the previous block has been read out of TMEM
-      if (cur.n > 0 && !bounded_wait_warp(dq_free, (cur.n - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * TILE_BYTES);
-      if (lane == 0) {
-#pragma unroll
-        for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA
           umma_f16(tmem + C_DQ, smem_desc_sw128(sds + k * 2048, TILE_BYTES, 1024),
                    smem_desc_sw128(sk + k * 2048, TILE_BYTES, 1024), IDESC_Q, k > 0 ? 1u : 0u);
+        }
         umma_commit(mm_done);
         umma_commit(&q_empty[st]);
         if (cur.i == cur.un.niter - 1) umma_commit(&k_empty[cur.k & 1]);
