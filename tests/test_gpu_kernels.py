@@ -354,8 +354,10 @@ def test_softmax_and_ce_f32_api(K):
     assert rel(K.ce_backward(p_r, t, rows, C_), O.ce_backward(p_r, t, rows, C_)) < 1e-6
 
 
-def test_ce_fused_bf16_vs_oracle(L):
-    rows, V = 512, 6400
+@pytest.mark.parametrize("V", [6400, 1000, 4096, 9008])
+def test_ce_fused_bf16_vs_oracle(L, V):
+    """Row held in registers (V <= 8192) and in shared memory (larger V)."""
+    rows = 512
     x = O.normal(rows * V, 7) * 2
     t = O.uniform_ids(rows, 8, V)
     t[5] = -1

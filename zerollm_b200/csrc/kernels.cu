@@ -430,6 +430,73 @@ __global__ void ce_fused_bf16_kernel(__nv_bfloat16* __restrict__ logits, const i
     x[i] = __float2bfloat16_rn((__expf(srow[i] - lse) - (i == t ? 1.f : 0.f)) * grad_scale);
 }
 
+// The same loss and gradient with the row held in registers (vocab <= 8 * 256 * MAXV): one exponential
+// per logit, reused for the row sum and the gradient, and no shared-memory copy of the row.  Every
+// thread keeps up to MAXV vectors of 8 logits (vector i of the row goes to thread i % 256).
+template <int MAXV>
+__global__ void __launch_bounds__(256) ce_fused_reg_bf16_kernel(__nv_bfloat16* __restrict__ logits,
+                                                               const int32_t* __restrict__ targets, int V, float cap,
+                                                               float grad_scale, float* __restrict__ loss_rows) {
+  __shared__ float red[8];
+  const int64_t r = blockIdx.x;
+  __nv_bfloat16* x = logits + r * V;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int nv = V / 8;
+  const int t = targets[r];
+  const bool valid = t >= 0 && t < V;
+  // the target logit, read before any thread overwrites the row with its gradient
+  const float xt = (tid == 0 && valid) ? __bfloat162float(x[t]) : 0.f;
+  float e[MAXV][8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = tid + k * 256;
+    if (i < nv) {
+      load8(x + i * 8, e[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, e[k][j]);
+    }
+  }
+  mx = warp_max(mx);
+  if (lane == 0) red[w] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) mx = fmaxf(mx, red[k]);
+  __syncthreads();
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = tid + k * 256;
+    if (i < nv) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        e[k][j] = __expf(e[k][j] - mx);
+        sum += e[k][j];
+      }
+    }
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[w] = sum;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) tot += red[k];  // fixed order
+  const float lse = mx + logf(tot);
+  if (tid == 0) loss_rows[r] = valid ? fminf(lse - xt, cap) : 0.f;
+  const float inv = 1.f / tot;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = tid + k * 256;
+    if (i < nv) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (e[k][j] * inv - (i * 8 + j == t ? 1.f : 0.f)) * grad_scale;
+      store8(x + i * 8, o);
+    }
+  }
+}
+
 // Deterministic mean of `n` values (single CTA, fixed order tree).
 __global__ void mean_kernel(const float* __restrict__ v, int64_t n, float* __restrict__ out, float denom) {
   __shared__ double red[1024];
@@ -830,10 +897,16 @@ extern "C" zl_status zl_cross_entropy_fused_bf16(zl_bf16* logits, const int32_t*
   if (rows <= 0 || vocab <= 0) return set_error(ZL_EINVAL, "cross_entropy: sizes must be positive");
   if (vocab % 8) return set_error(ZL_EUNSUPPORTED, "cross_entropy: vocab %% 8 != 0");
   const size_t sm = (size_t)vocab * sizeof(float);
-  if (sm > 200 * 1024) return set_error(ZL_EUNSUPPORTED, "cross_entropy: vocab too large");
-  cudaFuncSetAttribute(ce_fused_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  ce_fused_bf16_kernel<<<rows, 256, sm, ST(s)>>>(reinterpret_cast<__nv_bfloat16*>(logits), targets, vocab, -logf(eps),
-                                                 grad_scale, loss_rows);
+  auto lg = reinterpret_cast<__nv_bfloat16*>(logits);
+  if (vocab <= 8 * 256 * 2) {
+    ce_fused_reg_bf16_kernel<2><<<rows, 256, 0, ST(s)>>>(lg, targets, vocab, -logf(eps), grad_scale, loss_rows);
+  } else if (vocab <= 8 * 256 * 4) {
+    ce_fused_reg_bf16_kernel<4><<<rows, 256, 0, ST(s)>>>(lg, targets, vocab, -logf(eps), grad_scale, loss_rows);
+  } else {
+    if (sm > 200 * 1024) return set_error(ZL_EUNSUPPORTED, "cross_entropy: vocab too large");
+    cudaFuncSetAttribute(ce_fused_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    ce_fused_bf16_kernel<<<rows, 256, sm, ST(s)>>>(lg, targets, vocab, -logf(eps), grad_scale, loss_rows);
+  }
   zl_status st = check_launch("ce_fused_bf16");
   if (st != ZL_OK || !loss_out) return st;
   mean_kernel<<<1, 1024, 0, ST(s)>>>(loss_rows, rows, loss_out, (float)rows);
