@@ -291,8 +291,8 @@ def test_mha_f32_api_vs_oracle(K, ref_sem):
 
 # ------------------------------------------------------------------ norms, CE, embedding, optimizers
 @pytest.mark.parametrize("kind", [0, 1])
-def test_norm_bf16_vs_oracle(L, kind):
-    M, N = 1000, 512
+@pytest.mark.parametrize("M,N", [(1000, 512), (777, 264), (300, 1024), (200, 2048)])
+def test_norm_bf16_vs_oracle(L, kind, M, N):
     x = O.normal(M * N, 41)
     g = 1 + 0.1 * O.normal(N, 42)
     b = 0.1 * O.normal(N, 43)

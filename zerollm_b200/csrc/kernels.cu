@@ -146,15 +146,23 @@ __global__ void __launch_bounds__(256) norm_fwd_bf16_kernel(const __nv_bfloat16*
 // column sums of dx (COL: the bias gradient of the layer whose output this norm consumed).
 // Rows of up to 512 columns combine their eight warps' partials in shared memory; wider rows use
 // shared-memory atomics.
-template <int KIND, int kMaxChunks, bool COL>
+// STAGES > 0: each warp streams its rows through a ring of STAGES shared-memory slots filled by
+// 1-D bulk copies (x row and dy row per slot), so that STAGES rows per warp are in flight instead of
+// the one prefetched row of the register path (STAGES == 0).  Dynamic shared memory: the rings
+// [8][STAGES][2][N] bf16, their barriers [8][STAGES], then the partial accumulators.
+template <int KIND, int kMaxChunks, bool COL, int STAGES>
 __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ dy,
                                                           const float* __restrict__ g, const float* __restrict__ mean,
                                                           const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
                                                           float* __restrict__ part, int64_t M, int N) {
   constexpr int NK = 1 + (KIND == 0 ? 1 : 0) + (COL ? 1 : 0);  // partial sets
-  extern __shared__ float sacc[];                               // [8][NK*N] (tree) or [NK*N] (atomics)
+  extern __shared__ __align__(16) uint8_t nb_smem[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  const size_t ring_bytes = STAGES > 0 ? (size_t)8 * STAGES * 4 * N : 0;
+  uint8_t* ring = nb_smem + (size_t)w * STAGES * 4 * N;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(nb_smem + ring_bytes) + w * (STAGES > 0 ? STAGES : 1);
+  float* sacc = reinterpret_cast<float*>(nb_smem + ring_bytes + (STAGES > 0 ? 8 * STAGES * 8 : 0));  // [8][NK*N] or [NK*N]
   const bool tree = N <= 512;
   const int NP = NK * N;
   if (!tree) {
@@ -168,8 +176,8 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
     for (int j = 0; j < 8; ++j) pg[c][j] = pb[c][j] = pc[c][j] = 0.f;
   const int64_t nwarps = (int64_t)gridDim.x * warps;
   int64_t row = (int64_t)blockIdx.x * warps + w;
-  // rows of up to 512 columns prefetch the next row; wider rows would run out of registers
-  constexpr bool PREFETCH = kMaxChunks <= 2;
+  // register path: rows of up to 512 columns prefetch the next row; wider rows would run out of registers
+  constexpr bool PREFETCH = STAGES == 0 && kMaxChunks <= 2;
   uint4 nx[kMaxChunks], nd[kMaxChunks];
   auto fetch = [&](int64_t r) {
 #pragma unroll
@@ -181,16 +189,52 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
       }
     }
   };
+  // staged path: row k of this warp (row + k * nwarps) goes to slot k % STAGES
+  auto issue = [&](int64_t k) {
+    const int64_t r = row + k * nwarps;
+    if (r >= M) return;
+    const int sl = (int)(k % STAGES);
+    uint8_t* dst = ring + (size_t)sl * 4 * N;
+    mbar_arrive_expect_tx(&bars[sl], (uint32_t)(4 * N));
+    bulk_copy_g2s(dst, x + r * N, (uint32_t)(2 * N), &bars[sl]);
+    bulk_copy_g2s(dst + 2 * N, dy + r * N, (uint32_t)(2 * N), &bars[sl]);
+  };
+  if constexpr (STAGES > 0) {
+    if (lane == 0) {
+      for (int i = 0; i < STAGES; ++i) mbar_init(&bars[i], 1);
+      fence_mbar_init();
+      for (int i = 0; i < STAGES; ++i) issue(i);
+    }
+    __syncwarp();
+  }
   if (PREFETCH && row < M) fetch(row);
-  for (; row < M; row += nwarps) {
-    const float mu = KIND == 0 ? mean[row] : 0.f, rs = rstd[row];
-    if (!PREFETCH) fetch(row);
+  int64_t k = 0;
+  for (; row + k * nwarps < M; ++k) {
+    const int64_t r = row + k * nwarps;
+    const float mu = KIND == 0 ? mean[r] : 0.f, rs = rstd[r];
     // keep only the packed row; both passes unpack it again (registers, not arithmetic, limit
     // the resident warps here)
     uint4 cx[kMaxChunks], cd[kMaxChunks];
+    if constexpr (STAGES > 0) {
+      const int sl = (int)(k % STAGES);
+      if (!bounded_wait_warp(&bars[sl], (uint32_t)((k / STAGES) & 1), DEV_TIMEOUT_FULL)) break;
+      const uint8_t* src = ring + (size_t)sl * 4 * N;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) { cx[c] = nx[c]; cd[c] = nd[c]; }
-    if (PREFETCH && row + nwarps < M) fetch(row + nwarps);
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < N) {
+          cx[c] = *reinterpret_cast<const uint4*>(src + col * 2);
+          cd[c] = *reinterpret_cast<const uint4*>(src + 2 * N + col * 2);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) issue(k + STAGES);  // the slot has been read by every lane
+    } else {
+      if (!PREFETCH) fetch(r);
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) { cx[c] = nx[c]; cd[c] = nd[c]; }
+      if (PREFETCH && r + nwarps < M) fetch(r + nwarps);
+    }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
@@ -229,9 +273,15 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
           o[j] = KIND == 0 ? rs * (a - s1 * invN - xh * s2 * invN) : rs * (a - xh * s2 * invN);
           if (COL) pc[c][j] += o[j];
         }
-        store8(dx + row * N + col, o);
+        store8(dx + r * N + col, o);
       }
     }
+  }
+  if constexpr (STAGES > 0) {  // after a timeout: no copy may still be landing when the block exits
+    if (lane == 0)
+      for (int64_t j = k; j < k + STAGES; ++j)
+        if (row + j * nwarps < M) bounded_wait(&bars[j % STAGES], (uint32_t)((j / STAGES) & 1), DEV_TIMEOUT_FULL);
+    __syncwarp();
   }
   // block partials: [dgamma | dbeta | column sums]
   auto put = [&](float* base, bool atomic) {
@@ -270,10 +320,11 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
 constexpr int kReduceWarps = 32;
 __global__ void __launch_bounds__(kReduceWarps * 32) reduce_partials_kernel(const float* __restrict__ part, int nb, int N,
                                                                          int stride, float* __restrict__ out0,
-                                                                         float* __restrict__ out1) {
+                                                                         float* __restrict__ out1,
+                                                                         float* __restrict__ out2) {
   __shared__ float red[kReduceWarps][33];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int ncols = out1 ? 2 * N : N;
+  const int ncols = (out2 ? 3 : out1 ? 2 : 1) * N;
   const int c = blockIdx.x * 32 + lane;
   float s = 0.f;
   if (c < ncols) {
@@ -295,12 +346,16 @@ __global__ void __launch_bounds__(kReduceWarps * 32) reduce_partials_kernel(cons
 #pragma unroll 8
     for (int j = 0; j < kReduceWarps; ++j) t += red[j][lane];
     if (c < N) out0[c] += t;
-    else out1[c - N] += t;
+    else if (c < 2 * N) out1[c - N] += t;
+    else out2[c - 2 * N] += t;
   }
 }
-void launch_reduce_partials(const float* part, int nb, int N, int stride, float* out0, float* out1, cudaStream_t st) {
-  const int ncols = out1 ? 2 * N : N;
-  reduce_partials_kernel<<<(ncols + 31) / 32, kReduceWarps * 32, 0, st>>>(part, nb, N, stride, out0, out1);
+// Partial columns [0, N) -> out0, [N, 2N) -> out1, [2N, 3N) -> out2 (out1 / out2 may be null, in
+// which case the later ones are too).
+void launch_reduce_partials(const float* part, int nb, int N, int stride, float* out0, float* out1, cudaStream_t st,
+                            float* out2 = nullptr) {
+  const int ncols = (out2 ? 3 : out1 ? 2 : 1) * N;
+  reduce_partials_kernel<<<(ncols + 31) / 32, kReduceWarps * 32, 0, st>>>(part, nb, N, stride, out0, out1, out2);
 }
 
 int norm_bwd_blocks(int64_t M) {
@@ -849,23 +904,41 @@ zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, cons
   if (M <= 0 || N <= 0) return ZL_OK;
   if (N % 8 || N > 256 * kMaxRowChunks) return set_error(ZL_EUNSUPPORTED, "norm: N=%d must be a multiple of 8, <= 2048", N);
   if (!workspace || !dgamma || (kind == 0 && (!dbeta || !mean))) return set_error(ZL_EINVAL, "norm bwd: null pointer");
-  const int nb = norm_bwd_blocks(M);
+  int nb = norm_bwd_blocks(M);
   const auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   const auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
   auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
   const int NK = 1 + (kind == 0 ? 1 : 0) + (dcol ? 1 : 0);
-  const size_t sm = (size_t)(N <= 512 ? 8 : 1) * NK * N * sizeof(float);
+  const size_t acc = (size_t)(N <= 512 ? 8 : 1) * NK * N * sizeof(float);
   const int ch = N <= 256 ? 1 : N <= 512 ? 2 : N <= 1024 ? 4 : 8;
-#define NB(K, C, COL) norm_bwd_bf16_kernel<K, C, COL><<<nb, 256, sm, s>>>(X, DY, gamma, K == 0 ? mean : nullptr, rstd, DX, workspace, M, N)
-#define NBC(K, COL) { if (ch == 1) NB(K, 1, COL); else if (ch == 2) NB(K, 2, COL); else if (ch == 4) NB(K, 4, COL); else NB(K, 8, COL); }
+  // rows stream through shared memory by bulk copy when x and dy are 16-byte aligned
+  const bool staged = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy)) & 15) == 0;
+  const int stages = !staged ? 0 : ch <= 2 ? 3 : 2;
+  // the staged kernel keeps two blocks resident per SM (one block for 2048 columns); one wave of
+  // them, each warp with its rows in flight, beats more blocks
+  if (stages > 0) nb = std::min(nb, sm_count_current() * (ch == 8 ? 1 : 2));
+  const size_t sm = (size_t)8 * stages * 4 * N + (size_t)8 * stages * 8 + acc;
+#define NB(K, C, COL, ST)                                                                                        \
+  {                                                                                                              \
+    auto kern = norm_bwd_bf16_kernel<K, C, COL, ST>;                                                             \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                            \
+    kern<<<nb, 256, sm, s>>>(X, DY, gamma, K == 0 ? mean : nullptr, rstd, DX, workspace, M, N);                  \
+  }
+#define NBS(K, C, COL) { if (stages == 3) NB(K, C, COL, 3) else if (stages == 2) NB(K, C, COL, 2) else NB(K, C, COL, 0) }
+#define NBC(K, COL) { if (ch == 1) NBS(K, 1, COL) else if (ch == 2) NBS(K, 2, COL) else if (ch == 4) NBS(K, 4, COL) else NBS(K, 8, COL) }
   if (kind == 0) { if (dcol) NBC(0, true) else NBC(0, false) }
   else { if (dcol) NBC(1, true) else NBC(1, false) }
 #undef NBC
+#undef NBS
 #undef NB
   zl_status st = check_launch("norm_bwd_bf16");
   if (st != ZL_OK) return st;
-  launch_reduce_partials(workspace, nb, N, NK * N, dgamma, kind == 0 ? dbeta : nullptr, s);
-  if (dcol) launch_reduce_partials(workspace + (NK - 1) * N, nb, N, NK * N, dcol, nullptr, s);
+  // one reduction over the partial sets dgamma | dbeta (LayerNorm) | column sums
+  float* outs[3] = {dgamma, nullptr, nullptr};
+  int no = 1;
+  if (kind == 0) outs[no++] = dbeta;
+  if (dcol) outs[no++] = dcol;
+  launch_reduce_partials(workspace, nb, N, NK * N, outs[0], outs[1], s, outs[2]);
   return check_launch("norm_bwd_reduce");
 }
 }  // namespace zl
