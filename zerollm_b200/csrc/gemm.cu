@@ -47,6 +47,7 @@ struct GemmArgs {
   int M, N, K;
   int n_tiles_n, tiles, k_blocks, splits, kb_per_split, units;
   int tma_out;  // full chunks leave through TMA stores (tensor maps of D and of the split-K workspace)
+  int split_direct;  // accumulating fp32 output: every split adds its partial into D (TMA reduce-add)
   void* D;
   int flags;
   zl_epilogue epi;
@@ -666,7 +667,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c0 >= args.N || r0 >= args.M) continue;
         const bool full_chunk = fast_ok && (c0 + 32 <= args.N);
         if (use_tma) stg_reclaim(lane);
-        if (args.splits > 1) {
+        if (args.split_direct) {
+          // every split adds its partial into D; the adds of different splits land in any order
+          chunk_tma_out(&tmD, stg, lane, r0, c0, v, true, true);
+        } else if (args.splits > 1) {
           // a box must not run past row M: the workspace map would carry it into the next split
           if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v, (use_tma && r0 + 32 <= args.M) ? &tmW : nullptr);
           else if (r0 + lane < args.M) {
@@ -875,7 +879,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c0 >= args.N || r0 >= args.M) continue;
         const bool full_chunk = fast_ok && (c0 + 32 <= args.N);
         if (use_tma) stg_reclaim(lane);
-        if (args.splits > 1) {
+        if (args.split_direct) {
+          // every split adds its partial into D; the adds of different splits land in any order
+          chunk_tma_out(&tmD, stg, lane, r0, c0, v, true, true);
+        } else if (args.splits > 1) {
           // a box must not run past row M: the workspace map would carry it into the next split
           if (full_chunk) partial_chunk(args, stg, lane, split, r0, c0, v, (use_tma && r0 + 32 <= args.M) ? &tmW : nullptr);
           else if (r0 + lane < args.M) {
@@ -1269,7 +1276,9 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   // bf16 products of at least one 256-row tile go to the CTA-pair kernel
   const bool pair = !is_f32 && sm_count() >= 2 && use_pair(M, K);
   Plan p = pair ? make_plan_pair(M, N, K) : make_plan(M, N, K, E::BK, true);
-  if (p.splits > 1 && !ws) {
+  const bool direct_ok = (is_f32 || (flags & ZL_EPI_OUT_F32)) && flags == (ZL_EPI_OUT_F32 | ZL_EPI_ACCUM) &&
+                         N % 32 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
+  if (p.splits > 1 && !ws && !direct_ok) {
     // no workspace supplied: fall back to a single split
     p.splits = 1; p.kb_per_split = p.k_blocks; p.units = p.tiles;
   }
@@ -1287,12 +1296,17 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   const bool out_f32 = is_f32 || (flags & ZL_EPI_OUT_F32);
   CUtensorMap md = ma, mw = ma;
   a.tma_out = 0;
+  a.split_direct = 0;
+  // An accumulating fp32 output with nothing else in the epilogue takes the splits' partials
+  // directly (TMA reduce-add into D): no workspace pass and no reduction launch.
+  const bool direct = p.splits > 1 && out_f32 && flags == (ZL_EPI_OUT_F32 | ZL_EPI_ACCUM) && N % 32 == 0;
   if (((reinterpret_cast<uintptr_t>(D) & 15) == 0) && (out_f32 ? N % 4 == 0 : N % 8 == 0) &&
-      (p.splits == 1 || (ws && (reinterpret_cast<uintptr_t>(ws) & 15) == 0))) {
+      (p.splits == 1 || direct || (ws && (reinterpret_cast<uintptr_t>(ws) & 15) == 0))) {
     bool mok = make_map(&md, D, out_f32, N, M, 32, 32,
                         out_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
-    if (mok && p.splits > 1) mok = make_map(&mw, ws, true, N, (uint64_t)p.splits * M, 32, 32);
+    if (mok && p.splits > 1 && !direct) mok = make_map(&mw, ws, true, N, (uint64_t)p.splits * M, 32, 32);
     a.tma_out = mok ? 1 : 0;
+    a.split_direct = (mok && direct) ? 1 : 0;
   }
   // the pipelined bf16 epilogue kind (or -1): TMA output, whole 32-column chunks, and for RoPE whole
   // 32-column head slices and 16-byte aligned tables
@@ -1315,7 +1329,7 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
     else e = dispatch_major<T, 256, 4>(a_mn, b_mn, kind, ma, mb, md, mw, a, grid, st);
   }
   if (e != cudaSuccess) return set_error(ZL_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
-  if (p.splits > 1) {
+  if (p.splits > 1 && !a.split_direct) {
     const bool plain_f32 = (flags & ~(ZL_EPI_OUT_F32 | ZL_EPI_ACCUM)) == 0 && (flags & ZL_EPI_OUT_F32) && N % 4 == 0 &&
                            ((reinterpret_cast<uintptr_t>(D) | reinterpret_cast<uintptr_t>(ws)) & 15) == 0;
     if (plain_f32) {

@@ -360,12 +360,12 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     M->launches += c.bias ? 3 : 2;
     TRY(grads_ready(M, end_of_any(M, {t[L_N2G], t[L_N2B]}), st));
     // r2 = h1 + f W2^T + b2
-    TRY(gemm(M, M->dr, M->f[l], G(M, t[L_W2]), d, F, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    TRY(gemm(M, M->dr, M->f[l], G(M, t[L_W2]), d, F, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     TRY(grads_ready(M, end_of_any(M, {t[L_W2], t[L_B2]}), st));
     zl_epilogue e{};
     e.aux = reinterpret_cast<zl_bf16*>(M->f[l]);
     TRY(gemm(M, M->dr, W(M, t[L_W2]), M->dF, Ti, F, d, ZL_A_KMAJOR, ZL_EPI_RELU_MASK, &e, st));
-    TRY(gemm(M, M->dF, M->h1[l], G(M, t[L_W1]), F, d, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    TRY(gemm(M, M->dF, M->h1[l], G(M, t[L_W1]), F, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dF), G(M, t[L_B1]), M->ws, T, F, st)); M->launches += 2; }
     TRY(grads_ready(M, end_of_any(M, {t[L_W1], t[L_B1]}), st));
     e = zl_epilogue{};
@@ -379,7 +379,7 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     M->launches += c.bias ? 3 : 2;
     TRY(grads_ready(M, end_of_any(M, {t[L_N1G], t[L_N1B]}), st));
     // r1 = x + attn Wo^T + bo
-    TRY(gemm(M, M->dr, M->attn[l], G(M, t[L_WO]), d, d, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    TRY(gemm(M, M->dr, M->attn[l], G(M, t[L_WO]), d, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     TRY(grads_ready(M, end_of_any(M, {t[L_WO], t[L_BO]}), st));
     TRY(gemm(M, M->dr, W(M, t[L_WO]), M->dattn, Ti, d, d, ZL_A_KMAJOR, 0, nullptr, st));
     TRY(zl_attention_backward_bf16(reinterpret_cast<zl_bf16*>(M->qkv[l]), reinterpret_cast<zl_bf16*>(M->attn[l]),
@@ -387,7 +387,7 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
                                    reinterpret_cast<zl_bf16*>(M->dqkv), M->ws, B, S, H, d / H,
                                    c.pos == 1 ? M->rope_cos : nullptr, c.pos == 1 ? M->rope_sin : nullptr, st));
     M->launches += 3;
-    TRY(gemm(M, M->dqkv, M->x[l], G(M, t[L_WQKV]), 3 * d, d, Ti, 0, ZL_EPI_OUT_F32, nullptr, st));
+    TRY(gemm(M, M->dqkv, M->x[l], G(M, t[L_WQKV]), 3 * d, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dqkv), G(M, t[L_BQKV]), M->ws, T, 3 * d, st)); M->launches += 2; }
     TRY(grads_ready(M, end_of_any(M, {t[L_WQKV], t[L_BQKV]}), st));
     e = zl_epilogue{};
