@@ -32,7 +32,8 @@ typedef enum {
   ZL_ENCCL = 4,       /* NCCL error */
   ZL_ENOMEM = 5,      /* arena allocation failed */
   ZL_EUNSUPPORTED = 6,/* shape/layout outside what the kernel supports */
-  ZL_ESTATE = 7       /* call order violated (e.g. backward before forward) */
+  ZL_ESTATE = 7,      /* call order violated (e.g. backward before forward) */
+  ZL_EIO = 8          /* checkpoint file missing, short or unwritable (reference: runtime_error) */
 } zl_status;
 
 typedef void *zl_stream;
@@ -251,6 +252,27 @@ zl_status zl_model_num_params(zl_model *m, int64_t *n);
 zl_status zl_model_buffers(zl_model *m, float **params, float **grads, float **adam_m, float **adam_v);
 /* After the caller writes params directly: refresh the bf16 shadow. */
 zl_status zl_model_params_updated(zl_model *m, zl_stream stream);
+/* Checkpoints in the reference's directory layout (src/utils/serializer.hpp:24-56,
+ * src/model/zerollm.cpp:334-425 and the layers' save/load, e.g. src/layer/linear.cpp:215-250):
+ *   dir/config.bin   the reference's ZeroLLMConfig (six int32, bool with_grad, three zero bytes)
+ *   dir/embedding/weights/table.bin
+ *   dir/decoder/layer_<i>/self_attn/{q,k,v,out}_proj/weights/{weight,bias}.bin
+ *   dir/decoder/layer_<i>/{ln1,ln2}/weights/{gamma,beta}.bin
+ *   dir/decoder/layer_<i>/ff/{ff1,ff2}/weights/{weight,bias}.bin
+ *   dir/output_ln/weights/{gamma,beta}.bin
+ * each a raw fp32 array (Linear weights [out, in] row-major).  Topologies the reference does not
+ * have add: RMSNorm writes gamma.bin only, an untied head writes head/weights/weight.bin, a model
+ * without biases writes no bias.bin, and dir/zerollm_b200.txt records norm / pos / tied / bias.
+ * with_optimizer also writes optimizer/adamw_m.bin and optimizer/adamw_v.bin (the flat parameter
+ * arena order of zl_model_param_layout) and optimizer/state.bin (int32 step count); the reference
+ * saves no optimizer state.  Load checks config.bin (embed_dim, num_layers and vocab_size must
+ * match, as the reference does) and every file's size, then refreshes the bf16 shadow. */
+zl_status zl_model_save(zl_model *m, const char *dir, int with_optimizer);
+zl_status zl_model_load(zl_model *m, const char *dir, int with_optimizer);
+/* The tensor files of a configuration's checkpoint, one line per file:
+ * "<relative path> <arena offset> <float count>\n", into buf (NUL-terminated when it fits);
+ * *len receives the bytes needed (excluding the NUL). */
+zl_status zl_checkpoint_manifest(const zl_model_config *cfg, char *buf, int64_t cap, int64_t *len);
 zl_status zl_model_set_optimizer(zl_model *m, const zl_adamw_config *opt);
 /* One training step: zero_grad -> forward -> fused CE -> backward -> [bucketed all-reduce] -> AdamW.
  * ids/targets are device int32 [batch*seq]; *loss_out (device fp32) receives the mean loss of this

@@ -750,6 +750,15 @@ class ZeroLLM : public Module {
     ZLB_CALL(zl_model_set_optimizer(m_, &o), "ZeroLLM::set_optimizer");
   }
   void step(float learning_rate, cudaStream_t s = 0) { ZLB_CALL(zl_model_step(m_, learning_rate, s), "ZeroLLM::step"); }
+  // zerollm.cpp:334-425: the reference's checkpoint directory (config.bin and one raw fp32 file per
+  // tensor); a configuration mismatch throws std::runtime_error as there.  with_optimizer adds the
+  // AdamW moments and step count, which the reference does not save.
+  void save(const std::string& path, bool with_optimizer = false) {
+    ZLB_CALL(zl_model_save(m_, path.c_str(), with_optimizer ? 1 : 0), "ZeroLLM::save");
+  }
+  void load(const std::string& path, bool with_optimizer = false) {
+    ZLB_CALL(zl_model_load(m_, path.c_str(), with_optimizer ? 1 : 0), "ZeroLLM::load");
+  }
   // Fused step; the mean loss is written to loss_dev (device float).
   void train_step(const int* ids, const int* targets, int batch_size, int seq_len, float lr, float* loss_dev,
                   cudaStream_t s = 0) {

@@ -22,6 +22,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <filesystem>
 #include <string>
 #include <thread>
 #include <vector>
@@ -813,4 +814,188 @@ extern "C" zl_status zl_model_param_checksum(zl_model* M, uint64_t* out, zl_stre
   if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "checksum: %s", cudaGetErrorString(e));
   *out = h;
   return ZL_OK;
+}
+
+// ===================================================================== checkpoints
+// The reference's directory layout (serializer.hpp:24-56; zerollm.cpp:334-425; the layers' save /
+// load: embedding.cpp:255-285, transformer_decoder.cpp:148-160, transformer_block.cpp:218-232,
+// mha.cpp:261-275, feedward.cpp:148-160, linear.cpp:215-250, layernorm.cpp:172-190): one raw fp32
+// file per tensor under <dir>/<module path>/weights/, and <dir>/config.bin, the raw ZeroLLMConfig
+// struct (zerollm_config.hpp:10-17).  The fused q|k|v matrix of this library is split into the
+// reference's q_proj / k_proj / v_proj files.
+namespace {
+struct CkptEntry {
+  std::string rel;
+  int64_t off, count;
+};
+
+std::vector<CkptEntry> checkpoint_entries(const zl_model_config& c, const Layout& L) {
+  std::vector<CkptEntry> e;
+  const int64_t d = c.embed_dim, F = c.ff_hidden_dim, V = c.vocab_size;
+  e.push_back({"embedding/weights/table.bin", L.emb, V * d});
+  for (int l = 0; l < c.num_layers; ++l) {
+    const auto& t = L.lay[l];
+    const std::string b = "decoder/layer_" + std::to_string(l) + "/";
+    const char* proj[3] = {"q_proj", "k_proj", "v_proj"};
+    for (int j = 0; j < 3; ++j) {
+      e.push_back({b + "self_attn/" + proj[j] + "/weights/weight.bin", t[L_WQKV] + j * d * d, d * d});
+      if (c.bias) e.push_back({b + "self_attn/" + proj[j] + "/weights/bias.bin", t[L_BQKV] + j * d, d});
+    }
+    e.push_back({b + "self_attn/out_proj/weights/weight.bin", t[L_WO], d * d});
+    if (c.bias) e.push_back({b + "self_attn/out_proj/weights/bias.bin", t[L_BO], d});
+    e.push_back({b + "ln1/weights/gamma.bin", t[L_N1G], d});
+    if (c.norm == 0) e.push_back({b + "ln1/weights/beta.bin", t[L_N1B], d});
+    e.push_back({b + "ff/ff1/weights/weight.bin", t[L_W1], F * d});
+    if (c.bias) e.push_back({b + "ff/ff1/weights/bias.bin", t[L_B1], F});
+    e.push_back({b + "ff/ff2/weights/weight.bin", t[L_W2], d * F});
+    if (c.bias) e.push_back({b + "ff/ff2/weights/bias.bin", t[L_B2], d});
+    e.push_back({b + "ln2/weights/gamma.bin", t[L_N2G], d});
+    if (c.norm == 0) e.push_back({b + "ln2/weights/beta.bin", t[L_N2B], d});
+  }
+  e.push_back({"output_ln/weights/gamma.bin", L.nog, d});
+  if (c.norm == 0) e.push_back({"output_ln/weights/beta.bin", L.nob, d});
+  if (!c.tied) e.push_back({"head/weights/weight.bin", L.head, V * d});  // no reference counterpart
+  return e;
+}
+
+// config.bin: six int32 and a bool, padded to 28 bytes as the reference's compiler lays it out
+struct RefConfigFile {
+  int32_t vocab_size, embed_dim, num_layers, num_heads, ff_hidden_dim, max_seq_len;
+  uint8_t with_grad, pad[3];
+};
+static_assert(sizeof(RefConfigFile) == 28, "config.bin layout");
+
+bool write_file(const std::string& path, const void* data, size_t bytes) {
+  FILE* f = fopen(path.c_str(), "wb");
+  if (!f) return false;
+  const bool ok = bytes == 0 || fwrite(data, 1, bytes, f) == bytes;
+  return fclose(f) == 0 && ok;
+}
+
+// Reads exactly `bytes` bytes; false when the file is missing or has another size.
+bool read_file(const std::string& path, void* data, size_t bytes) {
+  FILE* f = fopen(path.c_str(), "rb");
+  if (!f) return false;
+  bool ok = fseek(f, 0, SEEK_END) == 0 && (size_t)ftell(f) == bytes && fseek(f, 0, SEEK_SET) == 0;
+  ok = ok && (bytes == 0 || fread(data, 1, bytes, f) == bytes);
+  fclose(f);
+  return ok;
+}
+
+std::string topology_line(const zl_model_config& c) {
+  char buf[160];
+  snprintf(buf, sizeof buf, "norm=%d pos=%d tied=%d bias=%d eps=%.9g rope_base=%.9g\n", c.norm, c.pos, c.tied, c.bias,
+           (double)c.eps, (double)c.rope_base);
+  return buf;
+}
+}  // namespace
+
+extern "C" zl_status zl_checkpoint_manifest(const zl_model_config* cfg, char* buf, int64_t cap, int64_t* len) {
+  if (!cfg || !len) return zl::set_error(ZL_EINVAL, "checkpoint manifest: null argument");
+  TRY(validate(*cfg));
+  const Layout L = build_layout(*cfg);
+  std::string s;
+  for (const auto& e : checkpoint_entries(*cfg, L))
+    s += e.rel + " " + std::to_string(e.off) + " " + std::to_string(e.count) + "\n";
+  *len = (int64_t)s.size();
+  if (buf && cap > 0) {
+    const size_t n = std::min<size_t>((size_t)cap - 1, s.size());
+    memcpy(buf, s.data(), n);
+    buf[n] = 0;
+  }
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_save(zl_model* M, const char* dir, int with_optimizer) {
+  if (!M || !dir) return zl::set_error(ZL_EINVAL, "save: null argument");
+  namespace fs = std::filesystem;
+  const std::string root(dir);
+  const zl_model_config& c = M->cfg;
+  std::vector<float> host((size_t)M->L.total);
+  cudaError_t ce = cudaMemcpy(host.data(), M->params, host.size() * sizeof(float), cudaMemcpyDeviceToHost);
+  if (ce != cudaSuccess) return zl::set_error(ZL_ECUDA, "save: %s", cudaGetErrorString(ce));
+  std::error_code ec;
+  fs::create_directories(root, ec);
+  if (ec) return zl::set_error(ZL_EIO, "save: cannot create %s: %s", root.c_str(), ec.message().c_str());
+  const RefConfigFile rc{c.vocab_size, c.embed_dim, c.num_layers, c.num_heads, c.ff_hidden_dim, c.max_seq_len, 1, {0, 0, 0}};
+  if (!write_file(root + "/config.bin", &rc, sizeof rc))
+    return zl::set_error(ZL_EIO, "Failed to open file for writing: %s/config.bin", root.c_str());
+  const std::string topo = topology_line(c);
+  if (!write_file(root + "/zerollm_b200.txt", topo.data(), topo.size()))
+    return zl::set_error(ZL_EIO, "Failed to open file for writing: %s/zerollm_b200.txt", root.c_str());
+  for (const auto& e : checkpoint_entries(c, M->L)) {
+    const std::string path = root + "/" + e.rel;
+    fs::create_directories(fs::path(path).parent_path(), ec);
+    if (ec || !write_file(path, host.data() + e.off, (size_t)e.count * sizeof(float)))
+      return zl::set_error(ZL_EIO, "Failed to open file for writing: %s", path.c_str());
+  }
+  if (with_optimizer) {
+    fs::create_directories(root + "/optimizer", ec);
+    if (ec) return zl::set_error(ZL_EIO, "save: cannot create %s/optimizer", root.c_str());
+    const char* names[2] = {"adamw_m.bin", "adamw_v.bin"};
+    float* src[2] = {M->m, M->v};
+    for (int i = 0; i < 2; ++i) {
+      ce = cudaMemcpy(host.data(), src[i], host.size() * sizeof(float), cudaMemcpyDeviceToHost);
+      if (ce != cudaSuccess) return zl::set_error(ZL_ECUDA, "save: %s", cudaGetErrorString(ce));
+      if (!write_file(root + "/optimizer/" + names[i], host.data(), host.size() * sizeof(float)))
+        return zl::set_error(ZL_EIO, "Failed to open file for writing: %s/optimizer/%s", root.c_str(), names[i]);
+    }
+    const int32_t t = M->t;
+    if (!write_file(root + "/optimizer/state.bin", &t, sizeof t))
+      return zl::set_error(ZL_EIO, "Failed to open file for writing: %s/optimizer/state.bin", root.c_str());
+  }
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_load(zl_model* M, const char* dir, int with_optimizer) {
+  if (!M || !dir) return zl::set_error(ZL_EINVAL, "load: null argument");
+  const std::string root(dir);
+  const zl_model_config& c = M->cfg;
+  // config check as in zerollm.cpp:378-396: a missing config.bin is not an error
+  RefConfigFile rc{};
+  if (read_file(root + "/config.bin", &rc, sizeof rc)) {
+    if (rc.embed_dim != c.embed_dim || rc.num_layers != c.num_layers || rc.vocab_size != c.vocab_size)
+      return zl::set_error(ZL_EINVAL, "Model configuration mismatch detected during load (file: embed_dim=%d "
+                                       "num_layers=%d vocab_size=%d)", rc.embed_dim, rc.num_layers, rc.vocab_size);
+  }
+  // this library's topology record, when present, must match too
+  std::string topo(160, '\0');
+  FILE* tf = fopen((root + "/zerollm_b200.txt").c_str(), "rb");
+  if (tf) {
+    const size_t n = fread(&topo[0], 1, topo.size() - 1, tf);
+    fclose(tf);
+    topo.resize(n);
+    int nm = -1, ps = -1, td = -1, bs = -1;
+    if (sscanf(topo.c_str(), "norm=%d pos=%d tied=%d bias=%d", &nm, &ps, &td, &bs) == 4 &&
+        (nm != c.norm || ps != c.pos || td != c.tied || bs != c.bias))
+      return zl::set_error(ZL_EINVAL, "load: checkpoint topology (norm=%d pos=%d tied=%d bias=%d) differs from the model",
+                           nm, ps, td, bs);
+  }
+  std::vector<float> host((size_t)M->L.total);
+  cudaError_t ce = cudaMemcpy(host.data(), M->params, host.size() * sizeof(float), cudaMemcpyDeviceToHost);
+  if (ce != cudaSuccess) return zl::set_error(ZL_ECUDA, "load: %s", cudaGetErrorString(ce));
+  for (const auto& e : checkpoint_entries(c, M->L)) {
+    const std::string path = root + "/" + e.rel;
+    if (!read_file(path, host.data() + e.off, (size_t)e.count * sizeof(float)))
+      return zl::set_error(ZL_EIO, "Failed to read %lld floats from %s", (long long)e.count, path.c_str());
+  }
+  std::vector<float> mh, vh;
+  int32_t t = 0;
+  if (with_optimizer) {
+    mh.resize(host.size());
+    vh.resize(host.size());
+    if (!read_file(root + "/optimizer/adamw_m.bin", mh.data(), mh.size() * sizeof(float)) ||
+        !read_file(root + "/optimizer/adamw_v.bin", vh.data(), vh.size() * sizeof(float)) ||
+        !read_file(root + "/optimizer/state.bin", &t, sizeof t))
+      return zl::set_error(ZL_EIO, "load: optimizer state missing or of the wrong size under %s/optimizer", root.c_str());
+  }
+  // every file read: only now does the model change
+  ce = cudaMemcpy(M->params, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess && with_optimizer) {
+    ce = cudaMemcpy(M->m, mh.data(), mh.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(M->v, vh.data(), vh.size() * sizeof(float), cudaMemcpyHostToDevice);
+    M->t = t;
+  }
+  if (ce != cudaSuccess) return zl::set_error(ZL_ECUDA, "load: %s", cudaGetErrorString(ce));
+  return zl_model_params_updated(M, nullptr);
 }

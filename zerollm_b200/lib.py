@@ -11,7 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libzerollm_b200.so")
 
-ZL_OK, ZL_EINVAL, ZL_ECUDA, ZL_ETIMEOUT, ZL_ENCCL, ZL_ENOMEM, ZL_EUNSUPPORTED, ZL_ESTATE = range(8)
+ZL_OK, ZL_EINVAL, ZL_ECUDA, ZL_ETIMEOUT, ZL_ENCCL, ZL_ENOMEM, ZL_EUNSUPPORTED, ZL_ESTATE, ZL_EIO = range(9)
 EPI_BIAS, EPI_RELU, EPI_RESIDUAL, EPI_RELU_MASK, EPI_ROPE = 1, 2, 4, 8, 16
 EPI_ACCUM, EPI_OUT_F32 = 64, 128
 A_KMAJOR, B_KMAJOR = 1, 2
@@ -105,6 +105,9 @@ SIGNATURES = {
     "zl_model_attach_nccl": (i32, [vp, vp, i32, i32, i64]),
     "zl_bucket_plan": (i32, [vp, vp, i32, i64, vp, vp, i32, C.POINTER(i32)]),
     "zl_model_param_checksum": (i32, [vp, C.POINTER(u64), vp]),
+    "zl_model_save": (i32, [vp, C.c_char_p, i32]),
+    "zl_model_load": (i32, [vp, C.c_char_p, i32]),
+    "zl_checkpoint_manifest": (i32, [C.POINTER(ModelConfig), C.c_char_p, i64, C.POINTER(i64)]),
     "zl_comm_create": (i32, [vp, i32, i32, C.c_double, C.POINTER(vp)]),
     "zl_comm_create_from_file": (i32, [C.c_char_p, i32, i32, C.c_double, C.POINTER(vp)]),
     "zl_comm_destroy": (i32, [vp]),

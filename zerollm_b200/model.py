@@ -8,6 +8,7 @@ arena (parameters, gradients, AdamW moments, activations).
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -56,6 +57,20 @@ def param_layout(cfg: Config):
            C.byref(n), C.byref(total))
     k = n.value
     return offs[:k].copy(), sizes[:k].copy(), kinds[:k].copy(), int(total.value)
+
+
+def checkpoint_manifest(cfg: Config):
+    """The tensor files of a checkpoint in the reference's directory layout:
+    [(relative path, arena offset, float count)] (zerollm.cpp:334-425 and the layers' save)."""
+    n = C.c_int64(0)
+    L.call("zl_checkpoint_manifest", C.byref(cfg.c()), None, 0, C.byref(n))
+    buf = C.create_string_buffer(int(n.value) + 1)
+    L.call("zl_checkpoint_manifest", C.byref(cfg.c()), buf, int(n.value) + 1, C.byref(n))
+    out = []
+    for line in buf.value.decode().splitlines():
+        rel, off, cnt = line.split()
+        out.append((rel, int(off), int(cnt)))
+    return out
 
 
 def _stream(stream):
@@ -152,6 +167,15 @@ class ZeroLLM:
         out = C.c_uint64(0)
         L.call("zl_model_param_checksum", self.h, C.byref(out), _stream(None))
         return int(out.value)
+
+    # ------------------------------------------------------------ checkpoints
+    def save(self, path: str, with_optimizer: bool = False):
+        """Writes the reference's checkpoint directory layout (ZeroLLM::save, zerollm.cpp:334-366)."""
+        L.call("zl_model_save", self.h, os.fsencode(path), int(with_optimizer))
+
+    def load(self, path: str, with_optimizer: bool = False):
+        """Reads a checkpoint directory (ZeroLLM::load, zerollm.cpp:375-425)."""
+        L.call("zl_model_load", self.h, os.fsencode(path), int(with_optimizer))
 
 
 def nccl_unique_id() -> bytes:
