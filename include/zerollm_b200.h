@@ -310,6 +310,32 @@ zl_status zl_bucket_plan(const int64_t *tensor_offsets, const int64_t *tensor_si
 /* ---- communicator behind the reference's distributed backend (abstract_backend.hpp:13-27,
  *      gpu_backend.cpp:66-130), MPI-free.  dtype follows dist_types.hpp DataType order
  *      (0 f32, 1 f16, 2 bf16, 3 i32, 4 i64); op follows ReduceOp (0 sum, 1 prod, 2 min, 3 max, 4 avg). */
+/* ===================================================================== */
+/* Token data pipeline: LLMDataLoader (src/runtime/dataloader.cpp:35-149) */
+/* ===================================================================== */
+/* Stories are one int32 token array with offsets: story i = tokens[offsets[i], offsets[i+1]).
+ * Samples: for every non-empty story, start positions 0, S, 2S, ... below len + 1
+ * (dataloader.cpp:57-66).  token(story, p) = story[p] for p < len, eos_id at p == len, pad_id after
+ * (:109-119); a sample's inputs are tokens [start, start + S) and its targets [start + 1, start + S + 1)
+ * (:138-142).  shuffle != 0 reorders the samples with a generator seeded by `seed`, again at every
+ * reset (the reference seeds it from std::random_device); 0 keeps story order.  The loader keeps its
+ * own copy of the tokens. */
+typedef struct zl_loader zl_loader;
+zl_status zl_loader_create(const int32_t *tokens, const int64_t *offsets, int64_t n_stories, int batch, int seq_len,
+                           int32_t eos_id, int32_t pad_id, int shuffle, uint64_t seed, zl_loader **out);
+zl_status zl_loader_destroy(zl_loader *l);
+/* New epoch: stops the device feed, rewinds, reshuffles (dataloader.cpp:17-21). */
+zl_status zl_loader_reset(zl_loader *l);
+zl_status zl_loader_info(zl_loader *l, int64_t *samples, int64_t *batches);
+/* Next batch into host buffers of batch * seq_len int32 each; *count = samples in it (the last batch
+ * of an epoch may be short, 0 once the epoch is over). */
+zl_status zl_loader_next(zl_loader *l, int32_t *ids, int32_t *targets, int *count);
+/* Device feed: a host thread assembles the following batches into `depth` pinned buffers;
+ * zl_loader_next_device enqueues the copy of the next one into device ids / targets on `stream`
+ * (count as above) and recycles the pinned buffer once that copy has completed. */
+zl_status zl_loader_start(zl_loader *l, int depth);
+zl_status zl_loader_next_device(zl_loader *l, int32_t *d_ids, int32_t *d_targets, int *count, zl_stream stream);
+
 typedef struct zl_comm zl_comm;
 /* Non-blocking NCCL init from a 128-byte id with a host deadline (ZL_ETIMEOUT, communicator aborted). */
 zl_status zl_comm_create(const void *id, int rank, int world, double timeout_s, zl_comm **out);

@@ -18,7 +18,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-ccbin", "g++",
          "-I", os.path.join(ROOT, "include"), "-I", CSRC, "--expt-relaxed-constexpr"]
-SOURCES = ["kernels.cu", "gemm.cu", "attention.cu", "attention_tc.cu", "model.cu", "dist.cu"]
+SOURCES = ["kernels.cu", "gemm.cu", "attention.cu", "attention_tc.cu", "model.cu", "dist.cu", "loader.cu"]
 
 
 def _compile(src: str, verbose: bool) -> str:

@@ -108,6 +108,13 @@ SIGNATURES = {
     "zl_model_save": (i32, [vp, C.c_char_p, i32]),
     "zl_model_load": (i32, [vp, C.c_char_p, i32]),
     "zl_checkpoint_manifest": (i32, [C.POINTER(ModelConfig), C.c_char_p, i64, C.POINTER(i64)]),
+    "zl_loader_create": (i32, [vp, vp, i64, i32, i32, i32, i32, i32, u64, C.POINTER(vp)]),
+    "zl_loader_destroy": (i32, [vp]),
+    "zl_loader_reset": (i32, [vp]),
+    "zl_loader_info": (i32, [vp, C.POINTER(i64), C.POINTER(i64)]),
+    "zl_loader_next": (i32, [vp, vp, vp, C.POINTER(i32)]),
+    "zl_loader_start": (i32, [vp, i32]),
+    "zl_loader_next_device": (i32, [vp, vp, vp, C.POINTER(i32), vp]),
     "zl_comm_create": (i32, [vp, i32, i32, C.c_double, C.POINTER(vp)]),
     "zl_comm_create_from_file": (i32, [C.c_char_p, i32, i32, C.c_double, C.POINTER(vp)]),
     "zl_comm_destroy": (i32, [vp]),
