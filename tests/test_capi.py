@@ -93,6 +93,18 @@ def test_kernel_entry_points_validate_before_touching_the_device():
     assert b"invalid" in L.zl_last_error() or b"size" in L.zl_last_error()
 
 
+def test_attention_backward_rejects_misaligned_rope_tables():
+    """The backward reads the rotation tables 16 bytes at a time: a misaligned table is refused on
+    the host, before any device work (the data pointers here are never dereferenced)."""
+    from zerollm_b200 import lib
+    L = lib.load()
+    fake = [256 * (i + 1) for i in range(6)]  # qkv, o, d_o, lse, d_qkv, workspace
+    st = L.zl_attention_backward_bf16(*fake, 1, 128, 2, 64, 4100, 8192, None)
+    assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
+    st = L.zl_attention_backward_bf16(*fake, 1, 128, 2, 64, 4096, None, None)
+    assert st == lib.ZL_EINVAL and b"rope tables" in L.zl_last_error()
+
+
 def test_cpp_api_program_builds():
     """The C++ drop-in headers compile against the C ABI (nvcc cross-compiles without a GPU)."""
     from zerollm_b200 import build

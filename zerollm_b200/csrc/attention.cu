@@ -505,8 +505,17 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat
   float x[8] = {v0.x * scale, v0.y * scale, v0.z * scale, v0.w * scale,
                 v1.x * scale, v1.y * scale, v1.z * scale, v1.w * scale};
   if (rope_cos) {
+    // the chunk's four rotation pairs are consecutive in the [S, Dh/2] tables: one float4 of each
+    const int64_t r = (t % S) * (DH / 2) + ((c % DH) >> 1);
+    const float4 cv = __ldg(reinterpret_cast<const float4*>(rope_cos + r));
+    const float4 sv = __ldg(reinterpret_cast<const float4*>(rope_sin + r));
+    const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) rope_inv_pair(x[k], x[k + 1], rope_cos, rope_sin, (int)(t % S), ((c % DH) + k) >> 1, DH / 2);
+    for (int k = 0; k < 4; ++k) {
+      const float a = x[2 * k], b = x[2 * k + 1];
+      x[2 * k] = a * cs[k] + b * sn[k];
+      x[2 * k + 1] = -a * sn[k] + b * cs[k];
+    }
   }
   uint4 u;
   u.x = pack_bf16(x[0], x[1]); u.y = pack_bf16(x[2], x[3]); u.z = pack_bf16(x[4], x[5]); u.w = pack_bf16(x[6], x[7]);
@@ -706,6 +715,9 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
     return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64, 128)", head_dim);
   if (!qkv || !o || !d_o || !lse || !d_qkv || !workspace) return set_error(ZL_EINVAL, "attention bwd: null pointer");
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return set_error(ZL_EINVAL, "attention bwd: rope tables");
+  // the backward kernels read the rotation tables four pairs at a time (16-byte loads)
+  if (((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15) != 0)
+    return set_error(ZL_EINVAL, "attention bwd: rope tables must be 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t T = (int64_t)batch * seq_len;
   const int E = num_heads * head_dim;
