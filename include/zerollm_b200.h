@@ -283,6 +283,13 @@ zl_status zl_model_train_step(zl_model *m, const int32_t *ids, const int32_t *ta
  * pointers and shape captures zero_grad -> forward -> CE -> backward into a graph that later calls replay
  * (AdamW stays a separate launch so lr may change).  0 disables. */
 zl_status zl_model_set_graph(zl_model *m, int enabled);
+/* In-step kernel timing (no reference counterpart; a measurement aid).  When enabled, the step
+ * records timing events just before and after each layer's attention forward kernel and the
+ * attention backward's main kernel (event nodes of the captured step graph).
+ * zl_model_kernel_times returns their mean duration per launch over the layers, in ms, for the most
+ * recent step (it waits for that step's events); ZL_ESTATE when timing is off or no step ran. */
+zl_status zl_model_set_kernel_timing(zl_model *m, int enabled);
+zl_status zl_model_kernel_times(zl_model *m, float *attn_fwd_ms, float *attn_bwd_ms);
 /* Reference-API pieces: forward to fp32 logits [batch*seq, V] (zerollm.cpp:101-195) ... */
 zl_status zl_model_forward(zl_model *m, const int32_t *ids, int batch, int seq_len, float *logits,
                            zl_stream stream);

@@ -233,3 +233,35 @@ def test_graph_replay_matches_eager():
     (l0, p0), (l1, p1) = out
     assert np.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
     assert rel(p1, p0) < 1e-5
+
+
+def test_in_step_kernel_timing():
+    """With kernel timing on, the captured step carries event nodes around the attention kernels:
+    the step's results are unchanged, and the per-launch times are positive and below the step's."""
+    from zerollm_b200 import ZeroLLM, ZLError
+    c = _cfgs(True)[0]
+    B, S = 4, 128
+    inp, tgt = _batch(B, S, c.vocab_size, 9)
+    ids, tg = torch.from_numpy(inp).cuda(), torch.from_numpy(tgt).cuda()
+    out = []
+    for timing in (False, True):
+        m = ZeroLLM(c, B * S, seed=0)
+        m.set_optimizer()
+        m.set_kernel_timing(timing)
+        if timing:
+            with pytest.raises(ZLError):
+                m.kernel_times()  # no step recorded yet
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        losses = [m.train_step(ids, tg, B, S, lr=1e-3).item() for _ in range(2)]
+        e0.record()
+        losses.append(m.train_step(ids, tg, B, S, lr=1e-3).item())
+        e1.record()
+        torch.cuda.synchronize()
+        if timing:
+            f, b = m.kernel_times()
+            assert 0 < f < e0.elapsed_time(e1) and 0 < b < e0.elapsed_time(e1), (f, b, e0.elapsed_time(e1))
+        out.append((losses, m.params()))
+        m.close()
+    (l0, p0), (l1, p1) = out
+    assert np.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
+    assert rel(p1, p0) < 1e-5

@@ -706,10 +706,27 @@ extern "C" int64_t zl_attention_workspace_floats(int batch, int seq_len, int num
   return (int64_t)batch * seq_len * num_heads * head_dim + 2 * (int64_t)batch * num_heads * seq_len;
 }
 
+namespace zl {
+// The backward of zl_attention_backward_bf16; ev0 / ev1 (may be null) are recorded just before and
+// after its main kernel, as graph event nodes when the stream is being captured.
+zl_status attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o, const float* lse,
+                                  zl_bf16* d_qkv, float* workspace, int batch, int seq_len, int num_heads,
+                                  int head_dim, const float* rope_cos, const float* rope_sin, zl_stream stream,
+                                  cudaEvent_t ev0, cudaEvent_t ev1);
+}  // namespace zl
+
 extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o,
                                                 const float* lse, zl_bf16* d_qkv, float* workspace, int batch,
                                                 int seq_len, int num_heads, int head_dim, const float* rope_cos,
                                                 const float* rope_sin, zl_stream stream) {
+  return zl::attention_backward_bf16(qkv, o, d_o, lse, d_qkv, workspace, batch, seq_len, num_heads, head_dim, rope_cos,
+                                     rope_sin, stream, nullptr, nullptr);
+}
+
+zl_status zl::attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o, const float* lse,
+                                      zl_bf16* d_qkv, float* workspace, int batch, int seq_len, int num_heads,
+                                      int head_dim, const float* rope_cos, const float* rope_sin, zl_stream stream,
+                                      cudaEvent_t ev0, cudaEvent_t ev1) {
   if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return set_error(ZL_EINVAL, "attention: invalid sizes");
   if (head_dim != 64 && head_dim != 128)
     return set_error(ZL_EUNSUPPORTED, "attention: head_dim %d (supported: 64, 128)", head_dim);
@@ -735,6 +752,7 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
   zl_status s = check_launch("fa_bwd_pre_kernel");
   if (s != ZL_OK) return s;
   const float scale = 1.0f / sqrtf((float)head_dim);
+  if (ev0) record_timing_event(ev0, st);
   if (tc) {
     s = fa_bwd_tc_launch(reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), nl,
                          Dsum, dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch, seq_len,
@@ -755,6 +773,7 @@ extern "C" zl_status zl_attention_backward_bf16(const zl_bf16* qkv, const zl_bf1
     s = check_launch("fa_bwd_kernel");
     if (s != ZL_OK) return s;
   }
+  if (ev1) record_timing_event(ev1, st);
   fa::fa_bwd_post_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
       dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, head_dim, scale,
       tc ? 1 : 0);

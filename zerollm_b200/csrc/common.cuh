@@ -351,4 +351,12 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
 namespace zl {
 zl_status set_error(zl_status code, const char* fmt, ...);
 zl_status check_launch(const char* what);
+// Records a timing event: as an event node of the graph when `st` is being captured, else directly.
+inline void record_timing_event(cudaEvent_t ev, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, st);
+}
 }  // namespace zl

@@ -36,6 +36,11 @@ namespace zl {
 zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma, const float* mean,
                              const float* rstd, zl_bf16* dx, float* dgamma, float* dbeta, float* dcol,
                              float* workspace, int64_t M, int N, cudaStream_t s);
+// attention.cu: the attention backward with events recorded around its main kernel
+zl_status attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o, const float* lse,
+                                  zl_bf16* d_qkv, float* workspace, int batch, int seq_len, int num_heads,
+                                  int head_dim, const float* rope_cos, const float* rope_sin, zl_stream stream,
+                                  cudaEvent_t ev0, cudaEvent_t ev1);
 }  // namespace zl
 
 
@@ -188,6 +193,10 @@ struct zl_model {
   cudaGraphExec_t graph_exec = nullptr;
   const void *g_ids = nullptr, *g_tgt = nullptr, *g_loss = nullptr;
   int g_B = 0, g_S = 0, g_seen = 0, g_launches = 0;
+  // In-step kernel timing: per layer, events just before and after the attention forward kernel
+  // and the attention backward's main kernel (graph event nodes in the captured step).
+  std::vector<cudaEvent_t> kt_ev;  // [layer][fwd start, fwd end, bwd start, bwd end]
+  bool kt_valid = false;           // a step has recorded them
 };
 
 namespace {
@@ -295,8 +304,10 @@ zl_status forward(zl_model* M, const int32_t* ids, int B, int S, float* logits_f
       e.head_dim = d / H;
     }
     TRY(gemm(M, M->x[l], W(M, t[L_WQKV]), M->qkv[l], (int)T, 3 * d, d, KK, fl, &e, st));
+    if (!M->kt_ev.empty()) zl::record_timing_event(M->kt_ev[4 * l], st);
     TRY(zl_attention_forward_bf16(reinterpret_cast<zl_bf16*>(M->qkv[l]), reinterpret_cast<zl_bf16*>(M->attn[l]),
                                   M->lse[l], B, S, H, d / H, st));
+    if (!M->kt_ev.empty()) zl::record_timing_event(M->kt_ev[4 * l + 1], st);
     M->launches++;
     e = zl_epilogue{};
     e.bias = P(M, t[L_BO]);
@@ -383,10 +394,12 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     TRY(gemm(M, M->dr, M->attn[l], G(M, t[L_WO]), d, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     TRY(grads_ready(M, end_of_any(M, {t[L_WO], t[L_BO]}), st));
     TRY(gemm(M, M->dr, W(M, t[L_WO]), M->dattn, Ti, d, d, ZL_A_KMAJOR, 0, nullptr, st));
-    TRY(zl_attention_backward_bf16(reinterpret_cast<zl_bf16*>(M->qkv[l]), reinterpret_cast<zl_bf16*>(M->attn[l]),
-                                   reinterpret_cast<zl_bf16*>(M->dattn), M->lse[l],
-                                   reinterpret_cast<zl_bf16*>(M->dqkv), M->ws, B, S, H, d / H,
-                                   c.pos == 1 ? M->rope_cos : nullptr, c.pos == 1 ? M->rope_sin : nullptr, st));
+    TRY(zl::attention_backward_bf16(reinterpret_cast<zl_bf16*>(M->qkv[l]), reinterpret_cast<zl_bf16*>(M->attn[l]),
+                                    reinterpret_cast<zl_bf16*>(M->dattn), M->lse[l],
+                                    reinterpret_cast<zl_bf16*>(M->dqkv), M->ws, B, S, H, d / H,
+                                    c.pos == 1 ? M->rope_cos : nullptr, c.pos == 1 ? M->rope_sin : nullptr, st,
+                                    M->kt_ev.empty() ? nullptr : M->kt_ev[4 * l + 2],
+                                    M->kt_ev.empty() ? nullptr : M->kt_ev[4 * l + 3]));
     M->launches += 3;
     TRY(gemm(M, M->dqkv, M->x[l], G(M, t[L_WQKV]), 3 * d, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dqkv), G(M, t[L_BQKV]), M->ws, T, 3 * d, st)); M->launches += 2; }
@@ -539,6 +552,7 @@ extern "C" zl_status zl_model_destroy(zl_model* M) {
   if (!M) return ZL_OK;
   if (M->graph_exec) cudaGraphExecDestroy(M->graph_exec);
   if (M->cap_stream) cudaStreamDestroy(M->cap_stream);
+  for (cudaEvent_t ev : M->kt_ev) cudaEventDestroy(ev);
   if (M->dist.comm) {
     cudaStreamSynchronize(M->dist.comm_stream);
     ncclCommDestroy(M->dist.comm);
@@ -661,6 +675,49 @@ extern "C" zl_status zl_model_set_graph(zl_model* M, int enabled) {
   return ZL_OK;
 }
 
+extern "C" zl_status zl_model_set_kernel_timing(zl_model* M, int enabled) {
+  if (!M) return zl::set_error(ZL_EINVAL, "null model");
+  if ((enabled != 0) == !M->kt_ev.empty()) return ZL_OK;
+  cudaDeviceSynchronize();  // no recorded event may be pending when it is destroyed
+  for (cudaEvent_t ev : M->kt_ev) cudaEventDestroy(ev);
+  M->kt_ev.clear();
+  M->kt_valid = false;
+  if (enabled) {
+    M->kt_ev.resize(4 * (size_t)M->cfg.num_layers);
+    for (auto& ev : M->kt_ev) {
+      cudaError_t e = cudaEventCreate(&ev);
+      if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "kernel timing: cudaEventCreate: %s", cudaGetErrorString(e));
+    }
+  }
+  if (M->graph_exec) {  // the captured step must gain (or lose) its event nodes
+    cudaGraphExecDestroy(M->graph_exec);
+    M->graph_exec = nullptr;
+  }
+  return ZL_OK;
+}
+
+extern "C" zl_status zl_model_kernel_times(zl_model* M, float* attn_fwd_ms, float* attn_bwd_ms) {
+  if (!M || !attn_fwd_ms || !attn_bwd_ms) return zl::set_error(ZL_EINVAL, "null argument");
+  if (M->kt_ev.empty()) return zl::set_error(ZL_ESTATE, "kernel timing is off");
+  if (!M->kt_valid) return zl::set_error(ZL_ESTATE, "kernel timing: no step has run since timing was enabled");
+  const int L = M->cfg.num_layers;
+  cudaError_t e = cudaEventSynchronize(M->kt_ev[4 * (L - 1) + 1]);  // forward of the last layer
+  if (e == cudaSuccess) e = cudaEventSynchronize(M->kt_ev[3]);      // backward of layer 0 (last)
+  if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "kernel timing: %s", cudaGetErrorString(e));
+  double f = 0, b = 0;
+  for (int l = 0; l < L; ++l) {
+    float x = 0, y = 0;
+    e = cudaEventElapsedTime(&x, M->kt_ev[4 * l], M->kt_ev[4 * l + 1]);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&y, M->kt_ev[4 * l + 2], M->kt_ev[4 * l + 3]);
+    if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "kernel timing: %s", cudaGetErrorString(e));
+    f += x;
+    b += y;
+  }
+  *attn_fwd_ms = (float)(f / L);
+  *attn_bwd_ms = (float)(b / L);
+  return ZL_OK;
+}
+
 extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const int32_t* targets, int B, int S, float lr,
                                          int update, float* loss_out, zl_stream stream) {
   if (!M || !ids || !targets) return zl::set_error(ZL_EINVAL, "null argument");
@@ -669,6 +726,7 @@ extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const 
   M->dist.joined = false;
   if (M->use_graph) TRY(step_graph(M, ids, targets, B, S, loss_out, st));
   else TRY(step_body(M, ids, targets, B, S, loss_out, st));
+  if (!M->kt_ev.empty()) M->kt_valid = true;
   if (update) TRY(adamw(M, lr, st));
   else if (M->dist.comm && !M->dist.joined) {
     cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);

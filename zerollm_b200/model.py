@@ -153,6 +153,17 @@ class ZeroLLM:
     def set_graph(self, enabled: bool):
         L.call("zl_model_set_graph", self.h, int(enabled))
 
+    def set_kernel_timing(self, enabled: bool):
+        """Records events around each layer's attention kernels inside the step (graph event nodes)."""
+        L.call("zl_model_set_kernel_timing", self.h, int(enabled))
+
+    def kernel_times(self) -> tuple:
+        """(attention forward ms, attention backward main-kernel ms) per launch, mean over the layers
+        of the most recent step."""
+        f, b = C.c_float(0), C.c_float(0)
+        L.call("zl_model_kernel_times", self.h, C.byref(f), C.byref(b))
+        return float(f.value), float(b.value)
+
     def last_launches(self) -> int:
         n = C.c_int(0)
         L.call("zl_model_last_launches", self.h, C.byref(n))
