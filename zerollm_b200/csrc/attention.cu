@@ -252,20 +252,18 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
 // ----------------------------------------------------------------- backward
 // D[b,h,i] = sum_d dO[i,d] * O[i,d] and, when `nl` is given, nl[b,h,i] = -lse[b,h,i] * log2(e) (the
 // exponent offset the tcgen05 kernel reads).  One thread per 8 consecutive elements of a token's
-// row (16-byte loads of O and dO); the Dh/8 threads of a head reduce with shuffles.
+// row (16-byte loads of O and dO, at element offset 8 * thread index); the Dh/8 threads of a head
+// reduce with shuffles.  Index arithmetic is 32-bit (the host checks B * S * H * Dh < 2^31).
 __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
                                   const float* __restrict__ lse, float* __restrict__ Dsum, float* __restrict__ nl,
                                   int B, int S, int H, int DH) {
-  const int E = H * DH;
-  const int cpt = E / 8;  // chunks per token
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const bool live = idx < (int64_t)B * S * cpt;
-  const int64_t t = live ? idx / cpt : 0;
-  const int c = live ? (int)(idx % cpt) : 0;
+  const uint32_t cpt = (uint32_t)(H * DH) / 8u;  // chunks per token
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = idx < (uint32_t)B * (uint32_t)S * cpt;
   float s = 0.f;
   if (live) {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + t * E) + c);
-    const uint4 g = __ldg(reinterpret_cast<const uint4*>(d_o + t * E) + c);
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(o) + idx);
+    const uint4 g = __ldg(reinterpret_cast<const uint4*>(d_o) + idx);
     const uint32_t av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -275,11 +273,13 @@ __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __n
   }
   // Dh/8 (8 or 16) consecutive lanes hold one head; E/8 is a multiple of 8, so groups never straddle warps
   for (int off = (DH / 8) >> 1; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (live && (c % (DH / 8)) == 0) {
-    const int h = c / (DH / 8);
-    const int64_t b = t / S, i = t % S;
-    Dsum[(b * H + h) * S + i] = s;
-    if (nl) nl[(b * H + h) * S + i] = -lse[(b * H + h) * S + i] * LOG2E;
+  const uint32_t per_head = (uint32_t)DH / 8u;
+  if (live && (idx % per_head) == 0) {
+    const uint32_t t = idx / cpt, c = idx - t * cpt;
+    const uint32_t b = t / (uint32_t)S, i = t - b * (uint32_t)S;
+    const uint32_t at = (b * (uint32_t)H + c / per_head) * (uint32_t)S + i;
+    Dsum[at] = s;
+    if (nl) nl[at] = -lse[at] * LOG2E;
   }
 }
 
@@ -494,19 +494,23 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
 __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ d_qkv,
                                    const float* rope_cos, const float* rope_sin, int64_t T, int S, int H,
                                    int DH, float scale, int head_major) {
-  const int E = H * DH;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= T * (E / 8)) return;
-  const int64_t t = idx / (E / 8);
-  const int c = (int)(idx % (E / 8)) * 8;
-  const int64_t src = head_major ? (((t / S) * H + c / DH) * S + t % S) * DH + c % DH : t * E + c;
+  // 32-bit index arithmetic (the host checks T * E < 2^31): 64-bit divisions by runtime values
+  // cost more issue slots than the thread's 48 bytes of traffic
+  const uint32_t E = (uint32_t)(H * DH);
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint32_t)T * (E / 8u)) return;
+  const uint32_t t = idx / (E / 8u);
+  const uint32_t c = (idx - t * (E / 8u)) * 8u;
+  const uint32_t bb = t / (uint32_t)S, pos = t - bb * (uint32_t)S;
+  const uint32_t hh = c / (uint32_t)DH, cd = c - hh * (uint32_t)DH;
+  const uint32_t src = head_major ? ((bb * (uint32_t)H + hh) * (uint32_t)S + pos) * (uint32_t)DH + cd : idx * 8u;
   const float4 v0 = __ldg(reinterpret_cast<const float4*>(dq_acc + src));
   const float4 v1 = __ldg(reinterpret_cast<const float4*>(dq_acc + src) + 1);
   float x[8] = {v0.x * scale, v0.y * scale, v0.z * scale, v0.w * scale,
                 v1.x * scale, v1.y * scale, v1.z * scale, v1.w * scale};
   if (rope_cos) {
     // the chunk's four rotation pairs are consecutive in the [S, Dh/2] tables: one float4 of each
-    const int64_t r = (t % S) * (DH / 2) + ((c % DH) >> 1);
+    const uint32_t r = pos * (uint32_t)(DH / 2) + (cd >> 1);
     const float4 cv = __ldg(reinterpret_cast<const float4*>(rope_cos + r));
     const float4 sv = __ldg(reinterpret_cast<const float4*>(rope_sin + r));
     const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
@@ -519,7 +523,7 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat
   }
   uint4 u;
   u.x = pack_bf16(x[0], x[1]); u.y = pack_bf16(x[2], x[3]); u.z = pack_bf16(x[4], x[5]); u.w = pack_bf16(x[6], x[7]);
-  *reinterpret_cast<uint4*>(d_qkv + t * 3 * E + c) = u;
+  *reinterpret_cast<uint4*>(d_qkv + (size_t)t * 3 * E + c) = u;
 }
 
 }  // namespace fa
@@ -738,6 +742,7 @@ zl_status zl::attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, cons
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t T = (int64_t)batch * seq_len;
   const int E = num_heads * head_dim;
+  if (T * E >= ((int64_t)1 << 31)) return set_error(ZL_EUNSUPPORTED, "attention bwd: batch*seq*embed must be < 2^31");
   float* dq_acc = workspace;
   float* Dsum = workspace + T * E;
   float* nl = Dsum + (int64_t)batch * num_heads * seq_len;
