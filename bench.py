@@ -345,7 +345,8 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    model.set_kernel_timing(True)  # event nodes around the attention kernels of every captured step
+    if world == 1:  # event nodes around the attention kernels of every captured step (the roofline's timing)
+        model.set_kernel_timing(True)
     for _ in range(args.warmup):
         model.train_step(d_inp, d_tgt, B, S, lr)
     barrier()
@@ -360,7 +361,7 @@ def run_ours(args, rank, world, local_rank):
     e1.record(st)
     barrier()
     ck = clocks.stop()
-    in_step = model.kernel_times()  # attention kernels of the last timed step, ms per launch
+    in_step = model.kernel_times() if world == 1 else None  # attention kernels of the last timed step, ms/launch
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     launches = model.last_launches() * args.steps
     loss_now = model.loss_dev.item()
@@ -395,7 +396,7 @@ def run_ours(args, rank, world, local_rank):
     bd, roof = None, None
     if rank == 0 and not args.no_breakdown and not scaled:
         bd = kernel_breakdown(B, S)
-        roof = roofline_of(bd, peaks(), {"attention_fwd": in_step[0], "attention_bwd": in_step[1]})
+        roof = roofline_of(bd, peaks(), {"attention_fwd": in_step[0], "attention_bwd": in_step[1]} if in_step else None)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and not scaled:
         cpu = cpu_sample(1, 2048, 1)
@@ -421,10 +422,11 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": int(2 * T * 4), "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
         "clocks": ck,
-        "attention_ms_in_step": {"fwd": round(in_step[0], 4), "bwd": round(in_step[1], 4)},
         "loss": round(loss_now, 4),
         "weights_identical_across_ranks": consistent,
     }
+    if in_step:
+        line["attention_ms_in_step"] = {"fwd": round(in_step[0], 4), "bwd": round(in_step[1], 4)}
     if roof:
         line["roofline"] = roof
         line["kernels_ms"] = {k: round(v["ms"], 4) for k, v in bd.items()}
