@@ -103,6 +103,10 @@ def test_attention_backward_rejects_misaligned_rope_tables():
     assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
     st = L.zl_attention_backward_bf16(*fake, 1, 128, 2, 64, 4096, None, None)
     assert st == lib.ZL_EINVAL and b"rope tables" in L.zl_last_error()
+    odd = list(fake)
+    odd[5] += 4  # workspace off a 16-byte boundary
+    st = L.zl_attention_backward_bf16(*odd, 1, 128, 2, 64, None, None, None)
+    assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
 
 
 def test_cpp_api_program_builds():

@@ -254,9 +254,11 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
 // exponent offset the tcgen05 kernel reads).  One thread per 8 consecutive elements of a token's
 // row (16-byte loads of O and dO, at element offset 8 * thread index); the Dh/8 threads of a head
 // reduce with shuffles.  Index arithmetic is 32-bit (the host checks B * S * H * Dh < 2^31).
+// The same threads zero the fp32 dQ accumulator (T * E floats, 8 per thread) that the main pass then
+// adds into, in place of a separate memset.
 __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
                                   const float* __restrict__ lse, float* __restrict__ Dsum, float* __restrict__ nl,
-                                  int B, int S, int H, int DH) {
+                                  float* __restrict__ dq_zero, int B, int S, int H, int DH) {
   const uint32_t cpt = (uint32_t)(H * DH) / 8u;  // chunks per token
   const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
   const bool live = idx < (uint32_t)B * (uint32_t)S * cpt;
@@ -264,6 +266,9 @@ __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __n
   if (live) {
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(o) + idx);
     const uint4 g = __ldg(reinterpret_cast<const uint4*>(d_o) + idx);
+    float4* z = reinterpret_cast<float4*>(dq_zero) + (size_t)idx * 2;
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
     const uint32_t av[4] = {a.x, a.y, a.z, a.w}, gv[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -739,6 +744,10 @@ zl_status zl::attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, cons
   // the backward kernels read the rotation tables four pairs at a time (16-byte loads)
   if (((reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin)) & 15) != 0)
     return set_error(ZL_EINVAL, "attention bwd: rope tables must be 16-byte aligned");
+  // the D pass reads o and d_o, and zeroes the workspace's dQ accumulator, 16 bytes at a time
+  if (((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(d_o) | reinterpret_cast<uintptr_t>(workspace)) &
+       15) != 0)
+    return set_error(ZL_EINVAL, "attention bwd: o, d_o and workspace must be 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t T = (int64_t)batch * seq_len;
   const int E = num_heads * head_dim;
@@ -747,13 +756,11 @@ zl_status zl::attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, cons
   float* Dsum = workspace + T * E;
   float* nl = Dsum + (int64_t)batch * num_heads * seq_len;
   const bool tc = !force_mma_sync() && fa_bwd_tc_supported(qkv, d_o, dq_acc, d_qkv, seq_len, head_dim);
-  // the dq accumulator starts at zero (both backward kernels add into it)
-  cudaError_t ce = cudaMemsetAsync(dq_acc, 0, (size_t)T * E * sizeof(float), st);
-  if (ce != cudaSuccess) return set_error(ZL_ECUDA, "attention bwd: memset: %s", cudaGetErrorString(ce));
+  // the dq accumulator starts at zero (both backward kernels add into it): the pre pass zeroes it
   const int64_t chunks = T * (E / 8);
   fa::fa_bwd_pre_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum,
-      tc ? nl : nullptr, batch, seq_len, num_heads, head_dim);
+      tc ? nl : nullptr, dq_acc, batch, seq_len, num_heads, head_dim);
   zl_status s = check_launch("fa_bwd_pre_kernel");
   if (s != ZL_OK) return s;
   const float scale = 1.0f / sqrtf((float)head_dim);
