@@ -258,11 +258,19 @@ def roofline_of(bd, pk, live=None):
 
 
 # ---------------------------------------------------------------------------- CPU baseline (oracle)
-def cpu_sample(B=1, S=2048, steps=1):
-    """One fp32 training step of the 26M model (BASELINE topology) on the CPU restatement."""
+def host_cores():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def cpu_sample(B=1, S=2048, steps=1, threads=None):
+    """fp32 training step(s) of the 26M model (baseline topology) on the CPU restatement, with an
+    explicit OpenMP team size (default: every core this process may run on).  The size is set
+    through the oracle itself, because a multi-process launcher exports OMP_NUM_THREADS=1."""
     from oracle import oracle as O
     import numpy as np
-    m = O.Model()
+    want = threads or host_cores()
+    used = O.set_threads(want)
+    m = O.Model(max_seq=max(S, 2048))
     p = O.init_params(m, seed=0)
     mm, vv = np.zeros_like(p), np.zeros_like(p)
     ids = O.uniform_ids(B * (S + 1), 3, VOCAB).reshape(B, S + 1)
@@ -271,10 +279,18 @@ def cpu_sample(B=1, S=2048, steps=1):
     for i in range(steps):
         O.train_step(m, p, mm, vv, inp, tgt, B, S, step=i + 1)
     dt = time.perf_counter() - t0
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    return {"value": round(B * S * steps / dt, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{steps} fp32 step(s) of {B}x{S} tokens, 26M model, oracle/liboracle.so (OpenMP)",
+    return {"value": round(B * S * steps / dt, 2), "unit": "tokens/s", "cores": used, "kind": "port",
+            "sample": f"{steps} fp32 step(s) of {B}x{S} tokens, 26M model, oracle/liboracle.so (OpenMP, "
+                      f"{used} threads)",
             "seconds": round(dt, 2)}
+
+
+def cpu_single_thread():
+    """The single-core figure beside the all-core one: one fp32 step of one 256-token sequence
+    (a few seconds on one core; the seq-2048 step would take about a minute)."""
+    r = cpu_sample(1, 256, 1, threads=1)
+    r["seq_len"] = 256
+    return r
 
 
 def run_reference(args, rank, world):
@@ -291,13 +307,15 @@ def run_reference(args, rank, world):
     dt = time.perf_counter() - t0
     tok = 2048 * K
     v = round(tok / dt, 2)
+    one = cpu_single_thread()
     line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": K, "warmup": W,
             "ms_per_step": round(1e3 * dt / K, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": "26M ZeroLLM train step, seq 2048, CPU sample of 1x2048 tokens per step",
                        "global_batch": 1, "seq_len": 2048, "parallelism": "cpu"},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": samples[0]["cores"], "kind": "port",
-                             "sample": "1x2048 tokens per step, fp32 fwd+bwd+AdamW, oracle/liboracle.so"},
+                             "sample": "1x2048 tokens per step, fp32 fwd+bwd+AdamW, oracle/liboracle.so",
+                             "single_thread": one},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -409,6 +427,7 @@ def run_ours(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and not scaled:
         cpu = cpu_sample(1, 2048, 1)
+        cpu["single_thread"] = cpu_single_thread()
     if rank != 0:
         return
     tokens = T * world

@@ -172,7 +172,8 @@ zl_status zl_attention_backward_bf16(const zl_bf16 *qkv, const zl_bf16 *o, const
                                      int seq_len, int num_heads, int head_dim, const float *rope_cos,
                                      const float *rope_sin, zl_stream stream);
 int64_t zl_attention_workspace_floats(int batch, int seq_len, int num_heads, int head_dim);
-/* Norms on bf16 rows with fp32 statistics.  kind: 0 LayerNorm (mean/rstd), 1 RMSNorm (rstd only). */
+/* Norms on bf16 rows with fp32 statistics.  kind: 0 LayerNorm (mean/rstd), 1 RMSNorm (rstd only).
+ * x and y must be 16-byte aligned (ZL_EINVAL otherwise). */
 zl_status zl_norm_forward_bf16(int kind, const zl_bf16 *x, const float *gamma, const float *beta, zl_bf16 *y,
                                float *mean, float *rstd, int64_t M, int N, float eps, zl_stream stream);
 /* dx = norm backward (bf16) of the full upstream gradient dy; dgamma/dbeta accumulated (fp32).
@@ -181,10 +182,11 @@ zl_status zl_norm_backward_bf16(int kind, const zl_bf16 *x, const zl_bf16 *dy, c
                                 const float *mean, const float *rstd, zl_bf16 *dx, float *dgamma,
                                 float *dbeta, float *workspace, int64_t M, int N, zl_stream stream);
 int zl_norm_bwd_blocks(int64_t M);
-/* Token embedding for the model: x[t] = bf16(table[id] (+ pos[t % S])); invalid ids give a zero row. */
+/* Token embedding for the model: x[t] = bf16(table[id] (+ pos[t % S])); invalid ids give a zero row.
+ * table, pos and out must be 16-byte aligned (ZL_EINVAL otherwise). */
 zl_status zl_embedding_forward_bf16(const int32_t *ids, const float *table, const float *pos, zl_bf16 *out,
                                     int64_t T, int seq_len, int dim, int vocab, zl_stream stream);
-/* dtable[id] += dx[t] (fp32 atomics; invalid ids skipped) */
+/* dtable[id] += dx[t] (fp32 atomics; invalid ids skipped); dx and dtable 16-byte aligned. */
 zl_status zl_embedding_backward_bf16(const int32_t *ids, const zl_bf16 *dx, float *dtable, int64_t T, int dim,
                                      int vocab, zl_stream stream);
 /* Fused cross-entropy on bf16 logits [rows, V]: loss_rows[r] = min(lse - x_t, -log(eps)) (0 for invalid
@@ -193,7 +195,8 @@ zl_status zl_embedding_backward_bf16(const int32_t *ids, const zl_bf16 *dx, floa
 zl_status zl_cross_entropy_fused_bf16(zl_bf16 *logits, const int32_t *targets, int rows, int vocab,
                                       float eps, float grad_scale, float *loss_rows, float *loss_out,
                                       zl_stream stream);
-/* Column sums of a bf16 [M, N] matrix accumulated into db (fp32): bias gradients. */
+/* Column sums of a bf16 [M, N] matrix accumulated into db (fp32): bias gradients.  N a multiple of 8
+ * (ZL_EUNSUPPORTED otherwise); dy 16-byte aligned (ZL_EINVAL otherwise). */
 zl_status zl_colsum_bf16(const zl_bf16 *dy, float *db, float *workspace, int64_t M, int N, zl_stream stream);
 int64_t zl_colsum_workspace_floats(int64_t M, int N);
 /* zl_colsum_bf16 without a workspace argument (no counterpart in the reference, whose bias
@@ -203,10 +206,13 @@ int64_t zl_colsum_workspace_floats(int64_t M, int N);
  * allocation.  The partial sums go to a fixed 4 MiB device array inside the library
  * (zl_colsum_noalloc_max_floats() floats); the call allocates nothing.  Sizes whose
  * zl_colsum_workspace_floats(M, N) exceeds that maximum return ZL_EINVAL with a message
- * (e.g. M <= 32768 fits at N = 2048).  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress) and keeps it; make that first call before any stream
- * capture.  Calls on one device share the array: calls that overlap on the GPU (two streams,
- * or two host threads) race and give wrong sums, so order them on one stream. */
+ * (e.g. M <= 32768 fits at N = 2048; at N <= 880 every M fits).  N must be a multiple of 8
+ * (ZL_EUNSUPPORTED otherwise), like zl_colsum_bf16.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) and keeps it for the life of the process;
+ * make that first call before any stream capture.  A device reset (cudaDeviceReset) after the
+ * first call is not supported: the kept address would no longer name the array.  Calls on one
+ * device share the array: calls that overlap on the GPU (two streams, or two host threads)
+ * race and give wrong sums, so order them on one stream. */
 zl_status zl_colsum_bf16_noalloc(const zl_bf16 *dy, float *db, int64_t M, int N, zl_stream stream);
 int64_t zl_colsum_noalloc_max_floats(void);
 /* Flat AdamW over the whole parameter arena (adamw.cu:26-73 per element) with the gradient

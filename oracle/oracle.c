@@ -29,6 +29,19 @@
 static int g_bf16 = 0;
 void orc_set_bf16_emulation(int on) { g_bf16 = on; }
 
+/* OpenMP team size for every later parallel region of this library (callers set it explicitly:
+ * a launcher such as torchrun exports OMP_NUM_THREADS=1 to each rank).  Returns the size now in
+ * force; n <= 0 only queries it. */
+int orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
+
 static inline float bf16r(float x) {
     uint32_t u;
     memcpy(&u, &x, 4);

@@ -137,6 +137,8 @@ typedef struct {
  * [norm2.g, norm2.b?, w2, b2?, w1, b1?, norm1.g, norm1.b?, wo, bo?, wqkv, bqkv?],
  * then tok_emb.  Fills up to max_n offsets/sizes; returns the tensor count
  * and writes the total element count. */
+/* OpenMP team size for later calls (n <= 0: query only); returns the size in force. */
+int orc_set_threads(int n);
 int orc_param_layout(const orc_model_cfg *cfg, int64_t *offsets, int64_t *sizes,
                      int *kinds, int max_n, int64_t *total);
 /* N(0, init_std) for matrices and the embedding (tensor i seeded with

@@ -39,6 +39,7 @@ def lib():
             raise RuntimeError(f"oracle library missing: {path} (run `make -C oracle`)")
         L = C.CDLL(path)
         sig = {
+            "orc_set_threads": (C.c_int, [C.c_int]),
             "orc_fill_normal": (None, [f32p, C.c_int64, C.c_uint64, C.c_float, C.c_float]),
             "orc_fill_uniform_ids": (None, [i32p, C.c_int64, C.c_uint64, C.c_int32]),
             "orc_matmul": (None, [f32p, f32p, f32p, C.c_int, C.c_int, C.c_int]),
@@ -89,6 +90,11 @@ def lib():
             fn.argtypes = args
         _LIB = L
     return _LIB
+
+
+def set_threads(n: int) -> int:
+    """Sets the OpenMP team size of the oracle's parallel loops; returns the size in force."""
+    return int(lib().orc_set_threads(int(n)))
 
 
 def _vp(a):

@@ -109,6 +109,24 @@ def test_attention_backward_rejects_misaligned_rope_tables():
     assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
 
 
+def test_bf16_entry_points_reject_misaligned_rows():
+    """The bf16 norm, embedding and column-sum kernels move rows 16 bytes at a time: pointers off a
+    16-byte boundary are refused on the host with ZL_EINVAL (never dereferenced here)."""
+    from zerollm_b200 import lib
+    L = lib.load()
+    a, odd = 1 << 20, (1 << 20) + 8
+    st = L.zl_norm_forward_bf16(1, odd, a, None, a, None, a, 4, 512, 1e-5, None)
+    assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
+    st = L.zl_embedding_forward_bf16(a, a, odd, a, 4, 4, 512, 100, None)
+    assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
+    st = L.zl_embedding_backward_bf16(a, odd, a, 4, 512, 100, None)
+    assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
+    st = L.zl_colsum_bf16(odd, a, a, 4, 512, None)
+    assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
+    st = L.zl_colsum_bf16_noalloc(odd, a, 4, 512, None)
+    assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
+
+
 def test_cpp_api_program_builds():
     """The C++ drop-in headers compile against the C ABI (nvcc cross-compiles without a GPU)."""
     from zerollm_b200 import build

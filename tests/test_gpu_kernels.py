@@ -149,6 +149,25 @@ def test_gemm_bf16_epilogues(L, gemm_kind, b_k, M):
     assert torch.equal(o2, o)
 
 
+def test_gemm_bf16_kernel_bench_shape(L, gemm_kind):
+    """The kernel-microbenchmark GEMM (M = 16384, K = 512, N = 2048, inputs N(0,1)) in its three
+    forms -- forward Y = X W^T, input gradient dX = dY W, weight gradient dW = dY^T X -- against a
+    fp32 product of the same bf16 operands."""
+    M, K_, N = 16384, 512, 2048
+    g = torch.Generator(device="cuda").manual_seed(2)
+    X = torch.randn(M, K_, device="cuda", generator=g).bfloat16()
+    W = torch.randn(N, K_, device="cuda", generator=g).bfloat16()
+    dY = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    cases = [("fwd", X, W, M, N, K_, L.A_KMAJOR | L.B_KMAJOR, X.float() @ W.float().T),
+             ("dx", dY, W, M, K_, N, L.A_KMAJOR, dY.float() @ W.float()),
+             ("dw", dY, X, N, K_, M, 0, dY.float().T @ X.float())]
+    for name, A, Bm, Mm, Nn, Kk, layout, ref in cases:
+        out = _gemm(L, A.reshape(-1), Bm.reshape(-1), Mm, Nn, Kk, layout, L.EPI_OUT_F32)
+        assert rel(out.view(Mm, Nn).cpu(), ref.cpu()) < 1e-4, name
+        out16 = _gemm(L, A.reshape(-1), Bm.reshape(-1), Mm, Nn, Kk, layout, 0)
+        assert rel(out16.float().view(Mm, Nn).cpu(), ref.cpu()) < BF16_TOL, name
+
+
 # ------------------------------------------------------------------ fp32 API GEMMs (tf32 / SIMT)
 @pytest.mark.parametrize("M,N,K_", [(64, 128, 96), (33, 17, 5), (256, 512, 512)])
 def test_matmul_f32_api(K, M, N, K_):
@@ -188,6 +207,23 @@ def test_attention_bf16_vs_oracle(L, B, S, H, Dh, kernel, monkeypatch):
     else:
         monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
         monkeypatch.setenv("ZL_ATTN_FWD_PP", "1" if kernel == "tc_pp" else "0")
+    _attention_vs_oracle(L, B, S, H, Dh)
+
+
+@pytest.mark.parametrize("B,S,H,Dh", [(16, 2048, 8, 64), (2, 2048, 8, 64), (3, 1536, 5, 64), (8, 2048, 16, 128),
+                                      (3, 2048, 8, 128)])
+def test_attention_many_units_per_cta_vs_oracle(L, B, S, H, Dh, monkeypatch):
+    """The persistent kernels at shapes with more work units than SMs, so every CTA walks several
+    units and the cross-unit pipeline (a unit's first blocks issued while the previous unit's
+    dQ / dK / dV leave, the next unit's Q and K/V loaded while the softmax warps write O) runs as
+    it does in the timed step.  (16, 2048, 8, 64) is the 26M model's attention at batch 16 (2048
+    backward units, 1024 forward pairs); (8, 2048, 16, 128) the scaled model's at batch 8."""
+    monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
+    monkeypatch.delenv("ZL_ATTN_FWD_PP", raising=False)
+    _attention_vs_oracle(L, B, S, H, Dh)
+
+
+def _attention_vs_oracle(L, B, S, H, Dh):
     E = H * Dh
     T = B * S
     qkv = O.normal(T * 3 * E, 21) * 0.5

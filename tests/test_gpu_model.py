@@ -156,6 +156,15 @@ def test_step_matches_oracle_26m_seq256(idx):
     _compare_step(c, 8, 256)
 
 
+@pytest.mark.parametrize("idx", [0, 1])
+def test_step_matches_oracle_26m_seq2048(idx):
+    """26M model (both topologies) at the timed sequence length, batch 2 x seq 2048: the attention
+    backward walks 256 units (more than one per SM) and every kernel runs at its seq-2048 shape,
+    under the same bars as the seq-256 test."""
+    c = _cfgs(False)[idx]
+    _compare_step(c, 2, 2048)
+
+
 def test_step_matches_oracle_head_dim_128():
     """Head dim 128, the attention shape of the scaled configuration (d_model 2048, 16 heads):
     a small model with 2 heads of 128 and the baseline topology (RMSNorm, RoPE, untied head)."""

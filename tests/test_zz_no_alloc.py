@@ -1,8 +1,9 @@
 """zl_colsum_bf16_noalloc: the column sum with its partials in the library's
 fixed device array, against zl_colsum_bf16 with a caller workspace, through
 the C ABI.  Two calls in a row on different inputs (the second must not see
-the first call's partials), at the largest size the array admits and at a
-ragged one, plus the size check.  Collected last on purpose: it must pass
+the first call's partials), at the largest size the array admits at N = 2048,
+at a ragged one, at a tall narrow one (every M fits at N <= 880) and at a width
+past 2048 (two column slices), plus the size, width and alignment checks.  Collected last on purpose: it must pass
 both in a fresh process (where its first call sets up the device address)
 and after every other test.
 """
@@ -35,7 +36,7 @@ def _colsum_with_workspace(L, dy, db0, M, N):
     return db
 
 
-@pytest.mark.parametrize("M,N", [(32768, 2048), (1000, 520)])
+@pytest.mark.parametrize("M,N", [(32768, 2048), (1000, 520), (131072, 512), (300, 2056)])
 def test_noalloc_matches_workspace_entry(L, M, N):
     assert L.load().zl_colsum_workspace_floats(M, N) <= L.load().zl_colsum_noalloc_max_floats()
     g = torch.Generator(device="cuda").manual_seed(M + N)
@@ -59,3 +60,14 @@ def test_noalloc_rejects_sizes_over_the_maximum(L):
     with pytest.raises(L.ZLError) as e:
         L.call("zl_colsum_bf16_noalloc", dy.data_ptr(), db.data_ptr(), M, N, None)
     assert e.value.code == L.ZL_EINVAL and "static maximum" in str(e.value)
+
+
+def test_noalloc_rejects_unsupported_width_and_misaligned_rows(L):
+    dy = torch.zeros(4096, device="cuda", dtype=torch.bfloat16)
+    db = torch.zeros(2056, device="cuda")
+    with pytest.raises(L.ZLError) as e:
+        L.call("zl_colsum_bf16_noalloc", dy.data_ptr(), db.data_ptr(), 1, 2052, None)  # N % 8 != 0
+    assert e.value.code == L.ZL_EUNSUPPORTED
+    with pytest.raises(L.ZLError) as e:
+        L.call("zl_colsum_bf16_noalloc", dy.data_ptr() + 2, db.data_ptr(), 1, 8, None)  # dy off 16 bytes
+    assert e.value.code == L.ZL_EINVAL and "16-byte aligned" in str(e.value)

@@ -8,10 +8,11 @@
 // products are all the same kernel with different operand majorness -- no
 // transposes through HBM.
 //
-// CTA = 6 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory
+// CTA = 10 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory
 // ring (128-byte swizzle), warp 1 owns TMEM and issues tcgen05.mma from one
-// thread into one of two 128 x BN fp32 accumulators, warps 2-5 drain the
-// other accumulator (tcgen05.ld) through the fused epilogue and store.
+// thread into one of two 128 x BN fp32 accumulators, warps 2-9 (two per TMEM
+// lane quarter) drain the other accumulator (tcgen05.ld) through the fused
+// epilogue and store it by TMA.
 // Every wait is bounded (common.cuh); a timeout records an error and the CTA
 // unwinds, freeing TMEM.
 #include <algorithm>

@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 
 #include "common.cuh"
@@ -861,6 +862,13 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
 using namespace zl;
 #define ST(s) static_cast<cudaStream_t>(s)
 static inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+// True when any of the pointers is off a 16-byte boundary (the bf16 kernels move rows 16 bytes at a
+// time; a misaligned vector access would fault the context, so the entry points refuse it instead).
+static inline bool misaligned16(std::initializer_list<const void*> ps) {
+  uintptr_t a = 0;
+  for (const void* p : ps) a |= reinterpret_cast<uintptr_t>(p);
+  return (a & 15) != 0;
+}
 
 extern "C" const char* zl_last_error(void) { return zl::g_err; }
 extern "C" const char* zl_version(void) { return "zerollm_b200 0.1 (sm_100a)"; }
@@ -882,6 +890,7 @@ extern "C" zl_status zl_norm_forward_bf16(int kind, const zl_bf16* x, const floa
   if (M <= 0 || N <= 0) return ZL_OK;
   if (N % 8 || N > 256 * kMaxRowChunks) return set_error(ZL_EUNSUPPORTED, "norm: N=%d must be a multiple of 8, <= 2048", N);
   if (kind == 0 && !beta) return set_error(ZL_EINVAL, "layernorm: beta is null");
+  if (misaligned16({x, y})) return set_error(ZL_EINVAL, "norm: x and y must be 16-byte aligned");
   const auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   auto Y = reinterpret_cast<__nv_bfloat16*>(y);
   const int ch = N <= 256 ? 1 : N <= 512 ? 2 : N <= 1024 ? 4 : 8;
@@ -952,6 +961,7 @@ extern "C" zl_status zl_embedding_forward_bf16(const int32_t* ids, const float* 
                                                int64_t T, int seq_len, int dim, int vocab, zl_stream s) {
   if (T <= 0) return ZL_OK;
   if (dim % 8) return set_error(ZL_EUNSUPPORTED, "embedding: dim %% 8 != 0");
+  if (misaligned16({table, pos, out})) return set_error(ZL_EINVAL, "embedding: table, pos and out must be 16-byte aligned");
   embed_fwd_bf16_kernel<<<nblk(T, 8), 256, 0, ST(s)>>>(ids, table, pos, reinterpret_cast<__nv_bfloat16*>(out), T,
                                                        seq_len, dim, vocab);
   return check_launch("embed_fwd_bf16");
@@ -960,6 +970,7 @@ extern "C" zl_status zl_embedding_backward_bf16(const int32_t* ids, const zl_bf1
                                                 int vocab, zl_stream s) {
   if (T <= 0) return ZL_OK;
   if (dim % 8) return set_error(ZL_EUNSUPPORTED, "embedding: dim %% 8 != 0");
+  if (misaligned16({dx, dtable})) return set_error(ZL_EINVAL, "embedding: dx and dtable must be 16-byte aligned");
   embed_bwd_bf16_kernel<<<nblk(T, 8), 256, 0, ST(s)>>>(ids, reinterpret_cast<const __nv_bfloat16*>(dx), dtable, T,
                                                        dim, vocab);
   return check_launch("embed_bwd_bf16");
@@ -1000,6 +1011,7 @@ extern "C" int64_t zl_colsum_workspace_floats(int64_t M, int N) {
 extern "C" zl_status zl_colsum_bf16(const zl_bf16* dy, float* db, float* workspace, int64_t M, int N, zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;
   if (N % 8) return set_error(ZL_EUNSUPPORTED, "colsum: N=%d must be a multiple of 8", N);
+  if (misaligned16({dy})) return set_error(ZL_EINVAL, "colsum: dy must be 16-byte aligned");
   const int64_t rpb = colsum_rows_per_block(M);
   const int nb = (int)((M + rpb - 1) / rpb);
   const int slices = (N + 2047) / 2048;
@@ -1048,8 +1060,9 @@ extern "C" int64_t zl_colsum_noalloc_max_floats(void) { return kColsumScratchFlo
 
 extern "C" zl_status zl_colsum_bf16_noalloc(const zl_bf16* dy, float* db, int64_t M, int N, zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;
-  if (N % 8 || N / 8 > 256) return set_error(ZL_EUNSUPPORTED, "colsum_noalloc: N=%d (multiple of 8, <= 2048)", N);
+  if (N % 8) return set_error(ZL_EUNSUPPORTED, "colsum_noalloc: N=%d must be a multiple of 8", N);
   if (!dy || !db) return set_error(ZL_EINVAL, "colsum_noalloc: null pointer");
+  if (misaligned16({dy})) return set_error(ZL_EINVAL, "colsum_noalloc: dy must be 16-byte aligned");
   const int64_t need = zl_colsum_workspace_floats(M, N);
   if (need > kColsumScratchFloats)
     return set_error(ZL_EINVAL,
