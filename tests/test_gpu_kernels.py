@@ -278,8 +278,8 @@ def test_attention_fwd_persistent_matches_one_tile(L, B, S, H, Dh, monkeypatch):
     assert torch.equal(outs[0][1], outs[1][1])
 
 
-def _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d):
-    Dh, E = 64, H * 64
+def _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d, Dh=64):
+    E = H * Dh
     dqkv = torch.empty(B * S * 3 * E, device="cuda", dtype=torch.bfloat16)
     ws = torch.empty(L.load().zl_attention_workspace_floats(B, S, H, Dh), device="cuda")
     L.call("zl_attention_backward_bf16", qkv_d.data_ptr(), o.data_ptr(), dO_d.data_ptr(), lse.data_ptr(),
@@ -288,12 +288,12 @@ def _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d):
     return dqkv.float().cpu().numpy().reshape(B * S, 3 * E)
 
 
-@pytest.mark.parametrize("B,S,H", [(2, 256, 4), (1, 2048, 1)])
-def test_attention_bwd_rope_tcgen05_vs_mma(L, B, S, H, monkeypatch):
+@pytest.mark.parametrize("B,S,H,Dh", [(2, 256, 4, 64), (1, 2048, 1, 64), (2, 256, 2, 128), (1, 2048, 2, 128)])
+def test_attention_bwd_rope_tcgen05_vs_mma(L, B, S, H, Dh, monkeypatch):
     """The two backward kernels fold the inverse RoPE of dQ/dK in different
     places (tcgen05: dK in the key-block epilogue; mma.sync: in its own
     epilogue); both must give the same gradient as the forward's rotation."""
-    Dh, E = 64, H * 64
+    E = H * Dh
     T = B * S
     qkv_d = (torch.from_numpy(O.normal(T * 3 * E, 31)) * 0.5).bfloat16().cuda()
     dO_d = torch.from_numpy(O.normal(T * E, 32)).bfloat16().cuda()
@@ -303,9 +303,9 @@ def test_attention_bwd_rope_tcgen05_vs_mma(L, B, S, H, monkeypatch):
     o = torch.empty(T * E, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B * H * S, device="cuda")
     L.call("zl_attention_forward_bf16", qkv_d.data_ptr(), o.data_ptr(), lse.data_ptr(), B, S, H, Dh, None)
-    g_tc = _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d)
+    g_tc = _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d, Dh)
     monkeypatch.setenv("ZL_ATTENTION_KERNEL", "mma")
-    g_mma = _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d)
+    g_mma = _attention_bwd_run(L, qkv_d, o, dO_d, lse, B, S, H, cos_d, sin_d, Dh)
     for part in range(3):
         sl = slice(part * E, (part + 1) * E)
         assert rel(g_tc[:, sl], g_mma[:, sl]) < BF16_TOL, part

@@ -19,10 +19,6 @@
 
 #include <type_traits>
 
-#ifndef ZL_ATTN_BWD_SOFTMAX_WARPS
-#define ZL_ATTN_BWD_SOFTMAX_WARPS 8
-#endif
-
 #include "common.cuh"
 
 namespace zl {
@@ -662,7 +658,7 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
 // are given) and dV leave by TMA store to the packed gradient buffer; dQ's scale and inverse RoPE
 // are applied by the caller's post pass.
 namespace bwd {
-constexpr int NSOFT = ZL_ATTN_BWD_SOFTMAX_WARPS;
+constexpr int NSOFT = 8;
 // Warpgroup 0: warp 0 TMA, warp 1 MMA, warps 2-3 idle; warps 4.. softmax.  (Registers are granted
 // per warpgroup, so the two idle warps cost none; moving registers from warpgroup 0 to the softmax
 // warps with setmaxnreg measured slower.)
@@ -670,7 +666,9 @@ constexpr int THREADS_B = 128 + 32 * NSOFT;
 constexpr int WPQ = NSOFT / 4;              // softmax warps per TMEM lane quadrant
 constexpr int QCOLS = BQ / WPQ;             // query columns (of S^T / dP^T) per softmax warp
 constexpr int DCOLS = D / WPQ;              // head-dim columns (of dQ / dK / dV) per softmax warp
-static_assert(NSOFT == 8 || NSOFT == 16, "softmax warps");
+// The dQ / dK / dV staging area (SM_DQ, DQ_BYTES) holds one 4 KB box per softmax warp, and the boxes
+// are 32 columns wide: both are laid out for exactly eight softmax warps (32 head-dim columns each).
+static_assert(NSOFT == 8 && DCOLS == 32 && NSOFT * 4096 == BQ * D * 4, "staging laid out for 8 softmax warps");
 constexpr int QST = 3;                               // Q / dO / row-vector stages (loads run two blocks ahead)
 // K is double buffered (the next unit's key block loads while this one finishes); V has one buffer,
 // which its last reader (the unit's last dP^T) releases early in the unit's last block.
@@ -1117,6 +1115,452 @@ __global__ void __launch_bounds__(THREADS_B, 1)
   }
 }
 }  // namespace bwd
+
+// ============================================================== backward, head dim 128
+// The same pipeline as the head-dim-64 backward (work units, barriers, warp roles), with the products
+// shaped for 128 head dims.  TMEM cannot hold 128-column S^T / dP^T next to 128-column dV / dK
+// accumulators, so a block is 128 keys x 64 queries and dQ is computed transposed:
+//   S^T = K Q_i^T, dP^T = V dO_i^T      M = 128 keys,      N = 64 queries, K = 128 head dims
+//   dV += P^T dO_i (A from TMEM)        M = 128 keys,      N = 128 dims,   K = 64 queries
+//   dK += dS^T Q_i (A = dS^T K-major)   M = 128 keys,      N = 128 dims,   K = 64 queries
+//   dQ_i^T = K^T dS^T                   M = 128 head dims, N = 64 queries, K = 128 keys
+//                                       (A = the K tile read MN-major, B = dS^T read MN-major)
+// TMEM columns: S^T [0,64), dP^T [64,128), P^T [128,160), dQ^T [192,256), dV [256,384), dK [384,512).
+// dQ^T comes out of TMEM with the head dims on the lanes; each softmax warp writes its [32 queries]
+// [32 dims] piece transposed into its swizzled staging box (one conflict-free 4-byte store per query),
+// so the fp32 accumulator keeps the [B, H, S, Dh] layout of the head-dim-64 kernel and the same post
+// pass finishes dQ.  A key block meets the diagonal in query blocks 2 kb and 2 kb + 1, so the first
+// two blocks of every unit are masked.  dK / dV of a finished unit leave as [32 keys][64 dims] bf16
+// boxes by TMA store, dK first, through the warp's staging box.
+namespace bwd128 {
+using bwd::bulk_load;
+using bwd::fence_async_smem;
+constexpr int D = 128, BQ = 64, BKV = 128, NSOFT = 8;
+constexpr int THREADS = 128 + 32 * NSOFT;  // warp 0 TMA, warp 1 MMA, warps 2-3 idle, warps 4-11 softmax
+constexpr int QCOLS = 32;                  // queries per softmax warp (two warps per TMEM lane quadrant)
+constexpr int DCOLS = 64;                  // head dims of dK / dV per softmax warp
+constexpr int QST = 2;                     // Q / dO / row-vector stages
+constexpr int KATOM = BKV * 128, QATOM = BQ * 128;  // one [rows][64] bf16 swizzle atom: 16 KB / 8 KB
+constexpr int K_BYTES = 2 * KATOM, Q_BYTES = 2 * QATOM;
+constexpr int SM_K = 0, SM_V = 2 * K_BYTES, SM_Q = SM_V + K_BYTES, SM_DO = SM_Q + QST * Q_BYTES;
+constexpr int SM_DS = SM_DO + QST * Q_BYTES;  // dS^T [128 keys][64 queries] bf16: one atom
+constexpr int SM_STG = SM_DS + KATOM;         // one 4 KB staging box per softmax warp
+constexpr int VEC_BYTES = 2 * BQ * 4;         // nl[64], D[64] of one query block
+constexpr int SM_VEC = SM_STG + NSOFT * 4096;
+constexpr int SM_BAR = SM_VEC + QST * VEC_BYTES;
+constexpr int SMEM_TOTAL = SM_BAR + 256 + 1024;
+static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
+static_assert(NSOFT * QCOLS == 4 * BQ && NSOFT * DCOLS == 4 * D, "softmax warps cover a block");
+constexpr uint32_t C_S = 0, C_DP = 64, C_P = 128, C_DQ = 192, C_DV = 256, C_DK = 384;
+constexpr uint32_t IDESC_SD = make_idesc(1, 128, 64, 0, 0);   // S^T / dP^T: A, B K-major
+constexpr uint32_t IDESC_VK = make_idesc(1, 128, 128, 0, 1);  // dV / dK: A TMEM or K-major, B MN-major
+constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);    // dQ^T: A, B MN-major
+
+__global__ void __launch_bounds__(THREADS, 1)
+    fa_bwd_tc128_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_dq,
+                        const __grid_constant__ CUtensorMap tm_dkv, const float* __restrict__ nl_g,
+                        const float* __restrict__ Dsum, const float* __restrict__ rope_cos,
+                        const float* __restrict__ rope_sin, int S, int H, int nunits, float scale, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+  uint64_t* k_full = bar + 0;          // [2] K buffers (alternate work units)
+  uint64_t* k_empty = bar + 2;         // [2] the unit's last dQ^T product has retired
+  uint64_t* v_full = bar + 4;
+  uint64_t* v_empty = bar + 5;         // the unit's last dP^T product has retired
+  uint64_t* q_full = bar + 6;          // [QST]
+  uint64_t* q_empty = bar + 6 + QST;   // [QST]
+  uint64_t* sd_full = bar + 6 + 2 * QST;
+  uint64_t* ds_ready = sd_full + 1;
+  uint64_t* mm_done = sd_full + 2;
+  uint64_t* dq_free = sd_full + 3;
+  uint64_t* drain = sd_full + 4;       // final commit: every MMA of this CTA has retired
+  uint64_t* sd_used = sd_full + 5;     // the softmax warps hold S^T / dP^T of the block in registers
+  uint64_t* dkv_free = sd_full + 6;    // the softmax warps have read dK / dV of the unit out of TMEM
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sd_full + 7);
+
+  const int E = H * D;
+  const int nk = S / BKV;
+  const int nbh = nunits / nk;
+  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // unit u = (key block kb, batch-head bh), key-block-major (most query blocks first), snake order
+  struct Unit {
+    int kb, bh, niter;
+  };
+  auto unit_of = [&](int k) -> Unit {
+    const int u = pp_unit(k, cta, G);
+    if (u >= nunits) return Unit{0, 0, 0};
+    return Unit{u / nbh, u % nbh, 2 * (nk - u / nbh)};
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    for (int i = 0; i < QST; ++i) { mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1); }
+    mbar_init(sd_full, 1);
+    mbar_init(ds_ready, 32 * NSOFT);
+    mbar_init(mm_done, 1);
+    mbar_init(dq_free, 32 * NSOFT);
+    mbar_init(drain, 1);
+    mbar_init(sd_used, 32 * NSOFT);
+    mbar_init(dkv_free, 32 * NSOFT);
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
+    tma_prefetch_desc(&tm_dkv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t n = 0, nkl = 0, nvl = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const Unit un = unit_of(k);
+        if (un.niter == 0) break;
+        const int b = un.bh / H, h = un.bh % H;
+        const int krow = b * S + un.kb * BKV;
+        const size_t row_base = (size_t)un.bh * S;
+        const int kbuf = k & 1;
+        if (!bounded_wait(&k_empty[kbuf], ((k >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(&k_full[kbuf], K_BYTES);
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(smem + SM_K + kbuf * K_BYTES + a * KATOM, &tm_k, &k_full[kbuf], E + h * D + a * 64, krow);
+        ++nkl;
+        for (int i = 0; i < un.niter; ++i, ++n) {
+          const uint32_t st = n % QST;
+          if (!bounded_wait(&q_empty[st], ((n / QST) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[st], 2 * Q_BYTES + VEC_BYTES);
+          const int qb = 2 * un.kb + i;
+          const int qrow = b * S + qb * BQ;
+          for (int a = 0; a < 2; ++a) {
+            tma_load_2d(smem + SM_Q + st * Q_BYTES + a * QATOM, &tm_q, &q_full[st], h * D + a * 64, qrow);
+            tma_load_2d(smem + SM_DO + st * Q_BYTES + a * QATOM, &tm_do, &q_full[st], h * D + a * 64, qrow);
+          }
+          float* vec = reinterpret_cast<float*>(smem + SM_VEC + st * VEC_BYTES);
+          bulk_load(vec, nl_g + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
+          bulk_load(vec + BQ, Dsum + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
+          if (i == 0) {
+            if (!bounded_wait(v_empty, (k & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; ++n; break; }
+            mbar_arrive_expect_tx(v_full, K_BYTES);
+            for (int a = 0; a < 2; ++a)
+              tma_load_2d(smem + SM_V + a * KATOM, &tm_k, v_full, 2 * E + h * D + a * 64, krow);
+            ++nvl;
+          }
+        }
+      }
+      // no copy may still be landing in shared memory when the CTA exits
+      for (uint32_t k = nkl > 2u ? nkl - 2 : 0; k < nkl; ++k)
+        bounded_wait(&k_full[k & 1], (k >> 1) & 1, DEV_TIMEOUT_ATTN);
+      if (nvl > 0) bounded_wait(v_full, (nvl - 1) & 1, DEV_TIMEOUT_ATTN);
+      for (uint32_t j = n > (uint32_t)QST ? n - QST : 0; j < n; ++j)
+        bounded_wait(&q_full[j % QST], (j / QST) & 1, DEV_TIMEOUT_ATTN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
+    struct Cur {
+      int k;
+      Unit un;
+      int i;
+      uint32_t n;
+    };
+    auto advance = [&](Cur c) -> Cur {
+      if (++c.i == c.un.niter) {
+        ++c.k;
+        c.un = unit_of(c.k);
+        c.i = 0;
+      }
+      ++c.n;
+      return c;
+    };
+    auto issue_sd = [&](const Cur& c) -> bool {
+      const uint32_t st = c.n % QST;
+      if (!bounded_wait_warp(&q_full[st], (c.n / QST) & 1, DEV_TIMEOUT_ATTN)) return false;
+      if (c.i == 0) {
+        if (!bounded_wait_warp(&k_full[c.k & 1], (c.k >> 1) & 1, DEV_TIMEOUT_ATTN)) return false;
+        if (!bounded_wait_warp(v_full, c.k & 1, DEV_TIMEOUT_ATTN)) return false;
+      }
+      tc_fence_after();
+      const uint32_t sk = smem_u32(smem + SM_K + (c.k & 1) * K_BYTES);
+      const uint32_t sq = smem_u32(smem + SM_Q + st * Q_BYTES);
+      const uint32_t sdo = smem_u32(smem + SM_DO + st * Q_BYTES);
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {  // 16 head dims per MMA; atoms of 64 dims
+          const uint32_t ka = (uint32_t)((k >> 2) * KATOM + (k & 3) * 32);
+          const uint32_t qa = (uint32_t)((k >> 2) * QATOM + (k & 3) * 32);
+          umma_f16(tmem + C_S, smem_desc_sw128(sk + ka, 16, 1024), smem_desc_sw128(sq + qa, 16, 1024), IDESC_SD,
+                   k > 0 ? 1u : 0u);
+          umma_f16(tmem + C_DP, smem_desc_sw128(sv + ka, 16, 1024), smem_desc_sw128(sdo + qa, 16, 1024), IDESC_SD,
+                   k > 0 ? 1u : 0u);
+        }
+        umma_commit(sd_full);
+        if (c.i == c.un.niter - 1) umma_commit(v_empty);
+      }
+      __syncwarp();
+      return true;
+    };
+    Cur cur{0, unit_of(0), 0, 0};
+    bool ok = cur.un.niter > 0 && issue_sd(cur);
+    while (ok && cur.un.niter > 0) {
+      const Cur nxt = advance(cur);
+      if (nxt.un.niter > 0) {
+        if (!bounded_wait_warp(sd_used, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        if (!issue_sd(nxt)) { ok = false; break; }
+      }
+      if (!bounded_wait_warp(ds_ready, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      if (cur.i == 0 && cur.k > 0 && !bounded_wait_warp(dkv_free, (cur.k - 1) & 1, DEV_TIMEOUT_ATTN)) {
+        ok = false;
+        break;
+      }
+      if (cur.n > 0 && !bounded_wait_warp(dq_free, (cur.n - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t st = cur.n % QST;
+      const uint32_t sq = smem_u32(smem + SM_Q + st * Q_BYTES), sdo = smem_u32(smem + SM_DO + st * Q_BYTES);
+      const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * K_BYTES);
+      if (lane == 0) {
+        // dQ^T (16 keys per MMA) interleaved with dV and dK (16 queries per MMA)
+#pragma unroll
+        for (int j = 0; j < BKV / 16; ++j) {
+          umma_f16(tmem + C_DQ, smem_desc_sw128(sk + j * 2048, KATOM, 1024), smem_desc_sw128(sds + j * 2048, KATOM, 1024),
+                   IDESC_Q, j > 0 ? 1u : 0u);
+          if (j < BQ / 16) {
+            const uint32_t acc = (cur.i > 0 || j > 0) ? 1u : 0u;
+            umma_f16_ts(tmem + C_DV, tmem + C_P + (uint32_t)(j * 8), smem_desc_sw128(sdo + j * 2048, QATOM, 1024),
+                        IDESC_VK, acc);
+            umma_f16(tmem + C_DK, smem_desc_sw128(sds + j * 32, 16, 1024), smem_desc_sw128(sq + j * 2048, QATOM, 1024),
+                     IDESC_VK, acc);
+          }
+        }
+        umma_commit(mm_done);
+        umma_commit(&q_empty[st]);
+        if (cur.i == cur.un.niter - 1) umma_commit(&k_empty[cur.k & 1]);
+      }
+      __syncwarp();
+      cur = nxt;
+    }
+    if (lane == 0) umma_commit(drain);
+    __syncwarp();
+    bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
+  } else if (warp >= 4) {
+    const int quarter = warp & 3;
+    const int cs = (warp - 4) >> 2;            // queries [32 cs, +32); head dims [64 cs, +64) of dK / dV
+    const int r_local = quarter * 32 + lane;   // key row (S^T, dP^T, dV, dK); head dim row of dQ^T
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* sds = smem + SM_DS;
+    const uint32_t stg = smem_u32(smem + SM_STG) + (uint32_t)((cs * 4 + quarter) * 4096);
+    bool ok = true;
+    auto stage_free = [&]() {
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
+    };
+    // dQ^T rows (head dims) [32 quarter, +32), columns (queries) [32 cs, +32) of a block (dq_free)
+    auto dq_load = [&](uint32_t (&dq)[32]) {
+      tc_fence_after();
+      tmem_ld32(t_lane + C_DQ + (uint32_t)(cs * 32), dq);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    };
+    // ... transposed into a [32 queries][32 dims] fp32 box (128-byte swizzle) and added into the
+    // accumulator; y = the block's first accumulator row
+    auto dq_store = [&](const uint32_t (&dq)[32], int y) {
+      stage_free();
+      const uint32_t col = (uint32_t)((lane & 3) * 4);
+#pragma unroll
+      for (int q = 0; q < 32; ++q)
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(stg + q * 128 + ((((uint32_t)lane >> 2) ^ (q & 7)) << 4) + col),
+                     "r"(dq[q]));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_2d_bulk(&tm_dq, stg, quarter * 32, y + cs * 32);
+        bulk_commit();
+      }
+    };
+    // 32 columns of dK (times the softmax scale, rotated back by RoPE when tables are given) or of dV,
+    // packed to bf16 pairs
+    auto pack_cols = [&](uint32_t col0, bool is_k, int key, uint32_t (&out)[16]) {
+      uint32_t r[32];
+      tmem_ld32(t_lane + (is_k ? C_DK : C_DV) + col0, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float x[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) x[t] = __uint_as_float(r[q * 8 + t]) * (is_k ? scale : 1.0f);
+        if (is_k && rope_cos) {
+          const size_t pr = (size_t)key * (D / 2) + ((col0 + q * 8) >> 1);
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(rope_cos + pr));
+          const float4 s4 = __ldg(reinterpret_cast<const float4*>(rope_sin + pr));
+          const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float a0 = x[2 * t], a1 = x[2 * t + 1];
+            x[2 * t] = a0 * cc[t] + a1 * ss[t];
+            x[2 * t + 1] = -a0 * ss[t] + a1 * cc[t];
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) out[q * 4 + t] = pack_bf16(x[2 * t], x[2 * t + 1]);
+      }
+    };
+    // a [32 keys][64 dims] bf16 box (128-byte rows, swizzled) by TMA store
+    auto store_box = [&](const uint32_t (&p)[32], int x, int y) {
+      stage_free();
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stg + lane * 128 + ((c ^ (lane & 7)) << 4)),
+                     "r"(p[c * 4]), "r"(p[c * 4 + 1]), "r"(p[c * 4 + 2]), "r"(p[c * 4 + 3]));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d_bulk(&tm_dkv, stg, x, y);
+        bulk_commit();
+      }
+    };
+    // A finished unit: dQ of its last block, then dK and dV; both TMEM regions are released before
+    // anything is stored.
+    auto unit_out = [&](const Unit& pu, int y) {
+      uint32_t dq[32];
+      dq_load(dq);
+      const int key = pu.kb * BKV + r_local;
+      uint32_t pk[32], pv[32];
+      {
+        uint32_t h0[16], h1[16];
+        pack_cols((uint32_t)(cs * DCOLS), true, key, h0);
+        pack_cols((uint32_t)(cs * DCOLS + 32), true, key, h1);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) { pk[j] = h0[j]; pk[16 + j] = h1[j]; }
+        pack_cols((uint32_t)(cs * DCOLS), false, key, h0);
+        pack_cols((uint32_t)(cs * DCOLS + 32), false, key, h1);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) { pv[j] = h0[j]; pv[16 + j] = h1[j]; }
+      }
+      tc_fence_before();
+      mbar_arrive(dkv_free);
+      dq_store(dq, y);
+      const int b = pu.bh / H, h = pu.bh % H;
+      const int y0 = b * S + pu.kb * BKV + quarter * 32;
+      store_box(pk, E + h * D + cs * DCOLS, y0);
+      store_box(pv, 2 * E + h * D + cs * DCOLS, y0);
+    };
+    uint32_t n = 0;
+    int prev_y = 0;
+    Unit pu{0, 0, 0};
+    for (int ku = 0;; ++ku) {
+      const Unit un = unit_of(ku);
+      if (un.niter == 0) break;
+      for (int i = 0; i < un.niter; ++i, ++n) {
+        const float* vec = reinterpret_cast<const float*>(smem + SM_VEC + (n % QST) * VEC_BYTES);
+        ok = ok && bounded_wait_warp(sd_full, n & 1, DEV_TIMEOUT_ATTN);
+        if (ok) {
+          tc_fence_after();
+          // keys above the diagonal: key r_local against query moff + q of the block (blocks 0 and 1)
+          const int moff = 64 * i;
+          auto chunks = [&](auto diag_tag) {
+            constexpr bool DIAG = decltype(diag_tag)::value;
+            constexpr int NG = QCOLS / 16;
+            uint32_t rs[2][16], rd[2][16];
+            uint32_t pp[QCOLS / 2], dd[QCOLS / 2];
+            const uint32_t c0 = (uint32_t)(cs * QCOLS);
+            tmem_ld16(t_lane + C_S + c0, rs[0]);
+            tmem_ld16(t_lane + C_DP + c0, rd[0]);
+            tmem_ld_wait();
+#pragma unroll
+            for (int g = 0; g < NG; ++g) {
+              const int bb = g & 1;
+              if (g + 1 < NG) {
+                tmem_ld16(t_lane + C_S + c0 + (uint32_t)((g + 1) * 16), rs[(g + 1) & 1]);
+                tmem_ld16(t_lane + C_DP + c0 + (uint32_t)((g + 1) * 16), rd[(g + 1) & 1]);
+              }
+              const int q0 = cs * QCOLS + g * 16;
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 nl4 = *reinterpret_cast<const float4*>(vec + q0 + j);
+                const float4 d4 = *reinterpret_cast<const float4*>(vec + BQ + q0 + j);
+                const float nlv[4] = {nl4.x, nl4.y, nl4.z, nl4.w};
+                const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+                float p[4], d[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  p[t] = fast_exp2(fmaf(__uint_as_float(rs[bb][j + t]), scale_log2, nlv[t]));
+                  if (DIAG && r_local > moff + q0 + j + t) p[t] = 0.f;
+                  d[t] = p[t] * (__uint_as_float(rd[bb][j + t]) - dv[t]);
+                }
+                pp[g * 8 + (j >> 1)] = pack_bf16(p[0], p[1]);
+                pp[g * 8 + (j >> 1) + 1] = pack_bf16(p[2], p[3]);
+                dd[g * 8 + (j >> 1)] = pack_bf16(d[0], d[1]);
+                dd[g * 8 + (j >> 1) + 1] = pack_bf16(d[2], d[3]);
+              }
+              if (g + 1 < NG) tmem_ld_wait();
+            }
+            tc_fence_before();
+            mbar_arrive(sd_used);
+            if (n > 0) {
+              ok = bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN);
+              if (!ok) return;
+              tc_fence_after();
+            }
+            tmem_st16(t_lane + C_P + (uint32_t)(cs * (QCOLS / 2)), pp);
+            // dS^T row segment -> shared memory ([key][64 queries], 128-byte swizzle)
+            uint8_t* rowp = sds + r_local * 128;
+            const int t0 = cs * (QCOLS / 8);
+#pragma unroll
+            for (int t = 0; t < QCOLS / 8; ++t)
+              *reinterpret_cast<uint4*>(rowp + (((t0 + t) ^ (r_local & 7)) * 16)) =
+                  make_uint4(dd[t * 4], dd[t * 4 + 1], dd[t * 4 + 2], dd[t * 4 + 3]);
+          };
+          if (i < 2) chunks(std::integral_constant<bool, true>{});
+          else chunks(std::integral_constant<bool, false>{});
+          if (ok) {
+            tmem_st_wait();
+            tc_fence_before();
+            fence_async_smem();
+            mbar_arrive(ds_ready);
+          }
+        }
+        if (ok && n > 0) {
+          if (i > 0) {
+            uint32_t dq[32];
+            dq_load(dq);
+            dq_store(dq, prev_y);
+          } else {
+            unit_out(pu, prev_y);
+          }
+        }
+        prev_y = (int)((size_t)un.bh * S + (size_t)(2 * un.kb + i) * BQ);
+      }
+      pu = un;
+      if (!ok) break;
+    }
+    if (n > 0 && ok && bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN)) unit_out(pu, prev_y);
+    if (lane == 0) bulk_wait0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+}  // namespace bwd128
 }  // namespace fatc
 
 // Returns true if the tcgen05 kernel handled the call (head dim 64 or 128, S a multiple of 128).
@@ -1158,10 +1602,10 @@ bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, 
   return true;
 }
 
-// Whether the tcgen05 backward takes this call: head_dim 64, S a multiple of 128, and 16-byte
+// Whether a tcgen05 backward takes this call: head_dim 64 or 128, S a multiple of 128, and 16-byte
 // aligned TMA sources, dQ accumulator and gradient rows.
 bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, const void* d_qkv, int S, int Dh) {
-  return Dh == fatc::D && S % fatc::BQ == 0 &&
+  return (Dh == 64 || Dh == 128) && S % fatc::BQ == 0 &&
          ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(d_o) | reinterpret_cast<uintptr_t>(dq_acc) |
            reinterpret_cast<uintptr_t>(d_qkv)) & 15) == 0;
 }
@@ -1173,6 +1617,25 @@ zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, c
                            int S, int H, int Dh, cudaStream_t st) {
   CUtensorMap tq, tdo, tdq, tdkv;
   const int E = H * Dh;
+  const float scale = 1.0f / sqrtf((float)Dh);
+  const int nunits = B * H * (S / fatc::BKV);
+  const int sms = sm_count_current();
+  const int grid = nunits < sms ? nunits : sms;
+  if (Dh == 128) {
+    namespace K = fatc::bwd128;
+    CUtensorMap tk;
+    // K / V: 128-row boxes; Q / dO: 64-row boxes (64 head dims per box); dK / dV out: [32][64] boxes
+    if (!make_tma_map(&tk, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, K::BKV) ||
+        !make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, K::BQ) ||
+        !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, K::BQ) ||
+        !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 32) ||
+        !make_tma_map(&tdkv, d_qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 32))
+      return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
+    cudaFuncSetAttribute(K::fa_bwd_tc128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM_TOTAL);
+    K::fa_bwd_tc128_kernel<<<grid, K::THREADS, K::SMEM_TOTAL, st>>>(
+        tk, tq, tdo, tdq, tdkv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, scale, scale * 1.4426950408889634f);
+    return check_launch("fa_bwd_tc128_kernel");
+  }
   if (!make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128) ||
       !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, 128) ||
       !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 32) ||
@@ -1180,10 +1643,6 @@ zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, c
     return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
   cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        fatc::bwd::SMEM_TOTAL);
-  const float scale = 1.0f / sqrtf((float)Dh);
-  const int nunits = B * H * (S / fatc::BKV);
-  const int sms = sm_count_current();
-  const int grid = nunits < sms ? nunits : sms;
   fatc::bwd::fa_bwd_tc_kernel<<<grid, fatc::bwd::THREADS_B, fatc::bwd::SMEM_TOTAL, st>>>(
       tq, tdo, tdq, tdkv, nl, Dsum, d_qkv, rope_cos, rope_sin, S, H, nunits, scale, scale * 1.4426950408889634f);
   return check_launch("fa_bwd_tc_kernel");
