@@ -172,6 +172,60 @@ zl_status zl_attention_backward_bf16(const zl_bf16 *qkv, const zl_bf16 *o, const
                                      int seq_len, int num_heads, int head_dim, const float *rope_cos,
                                      const float *rope_sin, zl_stream stream);
 int64_t zl_attention_workspace_floats(int batch, int seq_len, int num_heads, int head_dim);
+/* ===================================================================== */
+/* __nv_bfloat16 instances of the reference's kernel templates            */
+/* (the reference instantiates them for float only: linear.cu:173,183,     */
+/* mha.cu:332,340, layernorm.cu, softmax.cu, add.cu, relu.cu, adamw.cu).   */
+/* Storage is bf16, arithmetic fp32; sizes are checked as in the f32 forms. */
+/* ===================================================================== */
+/* linear.cuh:21-30 in bf16: Y[M,N] = X[M,K] W[N,K]^T (+ b) on the tcgen05 GEMM (no split-K
+ * workspace).  K and N multiples of 8, rows 16-byte aligned (ZL_EUNSUPPORTED otherwise). */
+zl_status zl_linear_forward_bf16(const zl_bf16 *input, const zl_bf16 *weight, const zl_bf16 *bias,
+                                 zl_bf16 *output, int64_t M, int64_t K, int64_t N, int use_bias,
+                                 zl_stream stream);
+/* linear.cuh:48-59 in bf16: dX = dY W and dW = dY^T X overwrite (tcgen05 GEMM), dB += column sums
+ * of dY (fp32 sums, one rounding to bf16).  M, K and N multiples of 8. */
+zl_status zl_linear_backward_bf16(const zl_bf16 *d_output, const zl_bf16 *input, const zl_bf16 *weight,
+                                  zl_bf16 *d_input, zl_bf16 *d_weight, zl_bf16 *d_bias, int64_t M, int64_t K,
+                                  int64_t N, int use_bias, zl_stream stream);
+/* mha.cuh:18-24 in bf16, on the tcgen05 flash-attention kernels: Q, K, V, attn_output [B*S, H*Dh]
+ * (separate tensors, 16-byte aligned).  Causal, no mask, head_dim 64 or 128, seq_len a multiple of
+ * 128 (ZL_EUNSUPPORTED otherwise).  The probability matrix is never formed: `state` (the reference
+ * API's attention_scores buffer, state_bytes long, 256-byte aligned) receives what the backward needs
+ * instead -- the per-row log-sum-exp and a copy of attn_output -- and the backward uses the rest of
+ * it as scratch; zl_mha_state_bytes_bf16() bytes are needed (ZL_EINVAL with the count otherwise).
+ * B*H*S*S bf16 elements are enough when seq_len >= 3 * head_dim + 6. */
+zl_status zl_mha_forward_bf16(const zl_bf16 *Q, const zl_bf16 *K, const zl_bf16 *V, zl_bf16 *attn_output,
+                              void *state, size_t state_bytes, const uint8_t *mask, int64_t batch,
+                              int64_t seq_len, int64_t num_heads, int64_t head_dim, int is_causal,
+                              zl_stream stream);
+/* mha.cuh:38-48 in bf16: d_Q, d_K, d_V from d_attn_output and the forward's `state`.
+ * reference_semantics = 1 leaves out the 1/sqrt(head_dim) factor of dQ and dK as mha.cu:284-295
+ * does; 0 gives the true gradient. */
+zl_status zl_mha_backward_bf16(const zl_bf16 *d_attn_output, const zl_bf16 *Q, const zl_bf16 *K,
+                               const zl_bf16 *V, void *state, size_t state_bytes, const uint8_t *mask,
+                               zl_bf16 *d_Q, zl_bf16 *d_K, zl_bf16 *d_V, int64_t batch, int64_t seq_len,
+                               int64_t num_heads, int64_t head_dim, int is_causal, int reference_semantics,
+                               zl_stream stream);
+size_t zl_mha_state_bytes_bf16(int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim);
+/* layernorm.cuh:22-61 in bf16 (gamma, beta, mean, rstd bf16; d_gamma / d_beta accumulate) */
+zl_status zl_layernorm_forward_bf16(const zl_bf16 *input, const zl_bf16 *gamma, const zl_bf16 *beta,
+                                    zl_bf16 *output, zl_bf16 *mean, zl_bf16 *rstd, int64_t M, int64_t N,
+                                    float eps, zl_stream stream);
+zl_status zl_layernorm_backward_bf16(const zl_bf16 *input, const zl_bf16 *d_output, const zl_bf16 *gamma,
+                                     const zl_bf16 *mean, const zl_bf16 *rstd, zl_bf16 *d_input,
+                                     zl_bf16 *d_gamma, zl_bf16 *d_beta, int64_t M, int64_t N, zl_stream stream);
+/* softmax.cuh:17-18, add.cuh:17-31, relu.cuh:16-31, adamw.cuh:28-41 in bf16 */
+zl_status zl_softmax_bf16(const zl_bf16 *input, zl_bf16 *output, int M, int N, zl_stream stream);
+zl_status zl_add_bf16(const zl_bf16 *a, const zl_bf16 *b, zl_bf16 *output, int size, zl_stream stream);
+zl_status zl_add_inplace_bf16(zl_bf16 *a, const zl_bf16 *b, int size, zl_stream stream);
+zl_status zl_relu_forward_bf16(const zl_bf16 *input, zl_bf16 *output, int size, zl_stream stream);
+zl_status zl_relu_backward_bf16(const zl_bf16 *input, const zl_bf16 *grad_output, zl_bf16 *grad_input, int size,
+                                zl_stream stream);
+zl_status zl_adamw_step_bf16(zl_bf16 *params, const zl_bf16 *grads, zl_bf16 *m, zl_bf16 *v, int64_t size,
+                             float learning_rate, float weight_decay, float beta1, float beta2, float eps,
+                             float bias_correction1, float bias_correction2, zl_stream stream);
+
 /* Norms on bf16 rows with fp32 statistics.  kind: 0 LayerNorm (mean/rstd), 1 RMSNorm (rstd only).
  * x and y must be 16-byte aligned (ZL_EINVAL otherwise). */
 zl_status zl_norm_forward_bf16(int kind, const zl_bf16 *x, const float *gamma, const float *beta, zl_bf16 *y,

@@ -146,3 +146,62 @@ def embedding_backward(ids, dout, dtable_in, B, S, D, V):
     dt = _d(dtable_in)
     _call("ref_embedding_backward", _d(ids, torch.int32), _d(dout), dt, B, S, D, V)
     return dt.cpu().numpy()
+
+
+# ------------------------------------------------------------------ the reference's model code
+MODEL_PATH = os.path.join(_HERE, "_ref", "libzlrefmodel.so")
+_MLIB = None
+
+
+def model_available() -> bool:
+    return os.path.exists(MODEL_PATH)
+
+
+def _mlib():
+    global _MLIB
+    if _MLIB is None:
+        L = C.CDLL(MODEL_PATH)
+        L.zlrefm_create.argtypes = [C.c_int] * 6 + [C.POINTER(C.c_void_p)]
+        L.zlrefm_destroy.argtypes = [C.c_void_p]
+        L.zlrefm_destroy.restype = None
+        L.zlrefm_save.argtypes = [C.c_void_p, C.c_char_p]
+        L.zlrefm_load.argtypes = [C.c_void_p, C.c_char_p]
+        L.zlrefm_forward_loss.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                          C.POINTER(C.c_float)]
+        _MLIB = L
+    return _MLIB
+
+
+def _check(name, rc):
+    if rc != 0:
+        raise RuntimeError(f"{name} failed with code {rc}")
+
+
+class RefModel:
+    """The reference's ZeroLLM (src/model/zerollm.cpp) built forward-only, with its own
+    initialisation, save / load and CrossEntropyLoss."""
+
+    def __init__(self, vocab, dim, layers, heads, ffn, max_seq):
+        self.vocab = vocab
+        h = C.c_void_p()
+        _check("zlrefm_create", _mlib().zlrefm_create(vocab, dim, layers, heads, ffn, max_seq, C.byref(h)))
+        self.h = h
+
+    def save(self, path):
+        _check("zlrefm_save", _mlib().zlrefm_save(self.h, os.fsencode(path)))
+
+    def load(self, path):
+        _check("zlrefm_load", _mlib().zlrefm_load(self.h, os.fsencode(path)))
+
+    def forward_loss(self, ids, targets, B, S):
+        ids = np.ascontiguousarray(ids, np.int32)
+        targets = np.ascontiguousarray(targets, np.int32)
+        out = C.c_float(0)
+        _check("zlrefm_forward_loss", _mlib().zlrefm_forward_loss(self.h, ids.ctypes.data, targets.ctypes.data, B, S,
+                                                                   self.vocab, C.byref(out)))
+        return float(out.value)
+
+    def close(self):
+        if self.h:
+            _mlib().zlrefm_destroy(self.h)
+            self.h = None

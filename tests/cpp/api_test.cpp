@@ -3,9 +3,11 @@
 // through the reference function names, then the Layer/Loss/Optimizer/Model
 // classes.  Exits non-zero on the first failure (the reference's tests print
 // PASS/FAIL and always exit 0).
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -182,6 +184,151 @@ static void test_model_api() {
   cudaFree(di); cudaFree(dtg); cudaFree(logits); cudaFree(dl);
 }
 
+// ---------------------------------------------------------------- __nv_bfloat16 instances
+// Each bf16 instance against the float instance of the same template on the same inputs (values
+// representable in bf16), normwise max|bf16 - f32| / max|f32| < 2e-2.
+static std::vector<float> seeded(size_t n, unsigned seed, float scale) {
+  std::vector<float> v(n);
+  uint64_t s = 0x9E3779B97F4A7C15ull * (seed + 1);
+  for (size_t i = 0; i < n; ++i) {
+    s ^= s << 13; s ^= s >> 7; s ^= s << 17;
+    const float u = (float)((s >> 11) * (1.0 / 9007199254740992.0)) * 2.f - 1.f;
+    v[i] = __bfloat162float(__float2bfloat16(u * scale));
+  }
+  return v;
+}
+static std::vector<__nv_bfloat16> to_bf(const std::vector<float>& v) {
+  std::vector<__nv_bfloat16> o(v.size());
+  for (size_t i = 0; i < v.size(); ++i) o[i] = __float2bfloat16(v[i]);
+  return o;
+}
+static float rel_err(const std::vector<__nv_bfloat16>& got, const std::vector<float>& want) {
+  float num = 0.f, den = 1e-30f;
+  for (size_t i = 0; i < want.size(); ++i) {
+    num = std::fmax(num, std::fabs(__bfloat162float(got[i]) - want[i]));
+    den = std::fmax(den, std::fabs(want[i]));
+  }
+  return num / den;
+}
+template <typename F>
+static void both(const std::vector<float>& h, F&& f) {  // run f(float*, bf16*) on device copies
+  float* a = dev(h);
+  __nv_bfloat16* b = dev(to_bf(h));
+  f(a, b);
+  cudaFree(a);
+  cudaFree(b);
+}
+
+static void test_bf16_instances() {
+  const float tol = 2e-2f;
+  {  // linear_forward / linear_backward (tcgen05 GEMM vs the f32 kernels)
+    const int M = 256, K = 192, N = 320;
+    auto x = seeded((size_t)M * K, 1, 1.f), w = seeded((size_t)N * K, 2, 0.1f), bias = seeded(N, 3, 0.5f);
+    auto dy = seeded((size_t)M * N, 4, 1.f);
+    float *xf = dev(x), *wf = dev(w), *bf = dev(bias), *dyf = dev(dy), *yf = dev(std::vector<float>((size_t)M * N));
+    __nv_bfloat16 *xb = dev(to_bf(x)), *wb = dev(to_bf(w)), *bb = dev(to_bf(bias)), *dyb = dev(to_bf(dy));
+    __nv_bfloat16* yb = dev(std::vector<__nv_bfloat16>((size_t)M * N));
+    linear_forward<float>(xf, wf, bf, yf, M, K, N, true);
+    linear_forward<__nv_bfloat16>(xb, wb, bb, yb, M, K, N, true);
+    const float e = rel_err(host(yb, (size_t)M * N), host(yf, (size_t)M * N));
+    EXPECT(e < tol, "linear_forward<bf16> rel %g", e);
+    std::vector<float> db0 = seeded(N, 5, 1.f);
+    float *dxf = dev(std::vector<float>((size_t)M * K)), *dwf = dev(std::vector<float>((size_t)N * K)), *dbf = dev(db0);
+    __nv_bfloat16 *dxb = dev(std::vector<__nv_bfloat16>((size_t)M * K)),
+                  *dwb = dev(std::vector<__nv_bfloat16>((size_t)N * K)), *dbb = dev(to_bf(db0));
+    linear_backward<float>(dyf, xf, wf, dxf, dwf, dbf, M, K, N, true);
+    linear_backward<__nv_bfloat16>(dyb, xb, wb, dxb, dwb, dbb, M, K, N, true);
+    float e1 = rel_err(host(dxb, (size_t)M * K), host(dxf, (size_t)M * K));
+    float e2 = rel_err(host(dwb, (size_t)N * K), host(dwf, (size_t)N * K));
+    float e3 = rel_err(host(dbb, N), host(dbf, N));
+    EXPECT(e1 < tol && e2 < tol && e3 < tol, "linear_backward<bf16> rel dX %g dW %g dB %g", e1, e2, e3);
+    for (void* p : {(void*)xf, (void*)wf, (void*)bf, (void*)dyf, (void*)yf, (void*)xb, (void*)wb, (void*)bb,
+                    (void*)dyb, (void*)yb, (void*)dxf, (void*)dwf, (void*)dbf, (void*)dxb, (void*)dwb, (void*)dbb})
+      cudaFree(p);
+  }
+  {  // mha_forward / mha_backward (tcgen05 flash attention vs the f32 kernels), causal
+    const int B = 1, S = 256, H = 2, Dh = 64, E = H * Dh;
+    const size_t n = (size_t)B * S * E, np = (size_t)B * H * S * S;
+    auto q = seeded(n, 6, 1.f), k = seeded(n, 7, 1.f), v = seeded(n, 8, 1.f), go = seeded(n, 9, 1.f);
+    float *qf = dev(q), *kf = dev(k), *vf = dev(v), *gf = dev(go), *of = dev(std::vector<float>(n)),
+          *pf = dev(std::vector<float>(np));
+    __nv_bfloat16 *qb = dev(to_bf(q)), *kb = dev(to_bf(k)), *vb = dev(to_bf(v)), *gb = dev(to_bf(go)),
+                  *ob = dev(std::vector<__nv_bfloat16>(n)), *pb = dev(std::vector<__nv_bfloat16>(np));
+    mha_forward<float>(qf, kf, vf, of, pf, nullptr, B, S, H, Dh, true);
+    mha_forward<__nv_bfloat16>(qb, kb, vb, ob, pb, nullptr, B, S, H, Dh, true);
+    const float e = rel_err(host(ob, n), host(of, n));
+    EXPECT(e < tol, "mha_forward<bf16> rel %g", e);
+    float *dqf = dev(std::vector<float>(n)), *dkf = dev(std::vector<float>(n)), *dvf = dev(std::vector<float>(n));
+    __nv_bfloat16 *dqb = dev(std::vector<__nv_bfloat16>(n)), *dkb = dev(std::vector<__nv_bfloat16>(n)),
+                  *dvb = dev(std::vector<__nv_bfloat16>(n));
+    for (int scaled = 0; scaled < 2; ++scaled) {
+      if (scaled) {
+        mha_backward_scaled<float>(gf, qf, kf, vf, pf, nullptr, dqf, dkf, dvf, B, S, H, Dh, true);
+        mha_backward_scaled<__nv_bfloat16>(gb, qb, kb, vb, pb, nullptr, dqb, dkb, dvb, B, S, H, Dh, true);
+      } else {  // the reference's own semantics (no 1/sqrt(head_dim) in dQ, dK)
+        mha_backward<float>(gf, qf, kf, vf, pf, nullptr, dqf, dkf, dvf, B, S, H, Dh, true);
+        mha_backward<__nv_bfloat16>(gb, qb, kb, vb, pb, nullptr, dqb, dkb, dvb, B, S, H, Dh, true);
+      }
+      const float a = rel_err(host(dqb, n), host(dqf, n)), b2 = rel_err(host(dkb, n), host(dkf, n)),
+                  c = rel_err(host(dvb, n), host(dvf, n));
+      EXPECT(a < tol && b2 < tol && c < tol, "mha_backward<bf16> (scaled %d) rel dQ %g dK %g dV %g", scaled, a, b2, c);
+    }
+    bool threw = false;
+    try { mha_forward<__nv_bfloat16>(qb, kb, vb, ob, pb, nullptr, B, S, H, Dh, false); } catch (const std::runtime_error&) { threw = true; }
+    EXPECT(threw, "mha_forward<bf16> without the causal mask must throw (flash path is causal only)");
+    for (void* p : {(void*)qf, (void*)kf, (void*)vf, (void*)gf, (void*)of, (void*)pf, (void*)qb, (void*)kb, (void*)vb,
+                    (void*)gb, (void*)ob, (void*)pb, (void*)dqf, (void*)dkf, (void*)dvf, (void*)dqb, (void*)dkb,
+                    (void*)dvb})
+      cudaFree(p);
+  }
+  {  // layernorm, softmax, add, relu, adamw
+    const int M = 64, N = 256;
+    const size_t n = (size_t)M * N;
+    auto x = seeded(n, 10, 2.f), g = seeded(N, 11, 0.5f), bta = seeded(N, 12, 0.5f), dy = seeded(n, 13, 1.f);
+    for (auto& t : g) t = __bfloat162float(__float2bfloat16(1.f + t));
+    float *xf = dev(x), *gf = dev(g), *bf = dev(bta), *dyf = dev(dy), *yf = dev(std::vector<float>(n)),
+          *mf = dev(std::vector<float>(M)), *rf = dev(std::vector<float>(M)), *dxf = dev(std::vector<float>(n)),
+          *dgf = dev(std::vector<float>(N)), *dbf = dev(std::vector<float>(N));
+    __nv_bfloat16 *xb = dev(to_bf(x)), *gb = dev(to_bf(g)), *bb = dev(to_bf(bta)), *dyb = dev(to_bf(dy)),
+                  *yb = dev(std::vector<__nv_bfloat16>(n)), *mb = dev(std::vector<__nv_bfloat16>(M)),
+                  *rb = dev(std::vector<__nv_bfloat16>(M)), *dxb = dev(std::vector<__nv_bfloat16>(n)),
+                  *dgb = dev(std::vector<__nv_bfloat16>(N)), *dbb = dev(std::vector<__nv_bfloat16>(N));
+    cuda_layernorm_forward<float>(xf, gf, bf, yf, mf, rf, M, N, 1e-5f);
+    cuda_layernorm_forward<__nv_bfloat16>(xb, gb, bb, yb, mb, rb, M, N, __float2bfloat16(1e-5f));
+    float e = rel_err(host(yb, n), host(yf, n));
+    EXPECT(e < tol, "cuda_layernorm_forward<bf16> rel %g", e);
+    cuda_layernorm_backward<float>(xf, dyf, gf, mf, rf, dxf, dgf, dbf, M, N);
+    cuda_layernorm_backward<__nv_bfloat16>(xb, dyb, gb, mb, rb, dxb, dgb, dbb, M, N);
+    const float e1 = rel_err(host(dxb, n), host(dxf, n)), e2 = rel_err(host(dgb, N), host(dgf, N)),
+                e3 = rel_err(host(dbb, N), host(dbf, N));
+    EXPECT(e1 < tol && e2 < tol && e3 < tol, "cuda_layernorm_backward<bf16> rel %g %g %g", e1, e2, e3);
+    softmax<float>(xf, yf, M, N);
+    softmax<__nv_bfloat16>(xb, yb, M, N);
+    e = rel_err(host(yb, n), host(yf, n));
+    EXPECT(e < tol, "softmax<bf16> rel %g", e);
+    add<float>(xf, dyf, yf, (int)n);
+    add<__nv_bfloat16>(xb, dyb, yb, (int)n);
+    e = rel_err(host(yb, n), host(yf, n));
+    EXPECT(e < tol, "add<bf16> rel %g", e);
+    relu_backward<float>(xf, dyf, yf, (int)n);
+    relu_backward<__nv_bfloat16>(xb, dyb, yb, (int)n);
+    e = rel_err(host(yb, n), host(yf, n));
+    EXPECT(e < tol, "relu_backward<bf16> rel %g", e);
+    auto m0 = seeded(n, 14, 1e-3f), v0 = seeded(n, 15, 1e-4f);
+    for (auto& t : v0) t = std::fabs(t);
+    float *mvf = dev(m0), *vvf = dev(v0);
+    __nv_bfloat16 *mvb = dev(to_bf(m0)), *vvb = dev(to_bf(v0));
+    adamw_step<float>(xf, dyf, mvf, vvf, (int)n, 1e-2f, 0.1f, 0.9f, 0.95f, 1e-8f, 0.1f, 0.05f);
+    adamw_step<__nv_bfloat16>(xb, dyb, mvb, vvb, (int)n, 1e-2f, 0.1f, 0.9f, 0.95f, 1e-8f, 0.1f, 0.05f);
+    e = rel_err(host(xb, n), host(xf, n));
+    EXPECT(e < tol, "adamw_step<bf16> rel %g", e);
+    for (void* p : {(void*)xf, (void*)gf, (void*)bf, (void*)dyf, (void*)yf, (void*)mf, (void*)rf, (void*)dxf,
+                    (void*)dgf, (void*)dbf, (void*)xb, (void*)gb, (void*)bb, (void*)dyb, (void*)yb, (void*)mb,
+                    (void*)rb, (void*)dxb, (void*)dgb, (void*)dbb, (void*)mvf, (void*)vvf, (void*)mvb, (void*)vvb})
+      cudaFree(p);
+  }
+}
+
 int main() {
   test_matmul_kat();
   test_relu_add_transpose();
@@ -189,6 +336,7 @@ int main() {
   test_mha_causal_kat();
   test_layers_and_loss();
   test_model_api();
+  test_bf16_instances();
   if (g_fail) {
     std::fprintf(stderr, "%d check(s) failed\n", g_fail);
     return 1;

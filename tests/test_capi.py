@@ -127,6 +127,26 @@ def test_bf16_entry_points_reject_misaligned_rows():
     assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
 
 
+def test_mha_bf16_rejects_unsupported_calls_before_device_work():
+    """The bf16 attention instance runs the causal flash-attention kernels: a non-causal call, a
+    mask, an unsupported head size or a state buffer below zl_mha_state_bytes_bf16() is refused on
+    the host (the pointers here are never dereferenced)."""
+    from zerollm_b200 import lib
+    L = lib.load()
+    a = 1 << 20
+    B, S, H, Dh = 2, 256, 2, 64
+    need = L.zl_mha_state_bytes_bf16(B, S, H, Dh)
+    assert need <= 2 * B * H * S * S  # the reference API's attention_scores buffer holds it at S >= 3 Dh + 6
+    ok = (a, a, a, a, a, need, None, B, S, H, Dh)
+    assert L.zl_mha_forward_bf16(*ok[:-4], B, S, H, Dh, 0, None) == lib.ZL_EUNSUPPORTED  # not causal
+    assert L.zl_mha_forward_bf16(a, a, a, a, a, need, a, B, S, H, Dh, 1, None) == lib.ZL_EUNSUPPORTED  # mask
+    assert L.zl_mha_forward_bf16(a, a, a, a, a, need, None, B, S, H, 96, 1, None) == lib.ZL_EUNSUPPORTED
+    assert L.zl_mha_forward_bf16(a, a, a, a, a, need, None, B, 200, H, Dh, 1, None) == lib.ZL_EUNSUPPORTED
+    st = L.zl_mha_backward_bf16(a, a, a, a, a, need - 1, None, a, a, a, B, S, H, Dh, 1, 1, None)
+    assert st == lib.ZL_EINVAL and b"needed" in L.zl_last_error()
+    assert L.zl_linear_forward_bf16(a, a, a, a, 4, 12, 16, 1, None) == lib.ZL_EUNSUPPORTED  # K % 8 != 0
+
+
 def test_cpp_api_program_builds():
     """The C++ drop-in headers compile against the C ABI (nvcc cross-compiles without a GPU)."""
     from zerollm_b200 import build

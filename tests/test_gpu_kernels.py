@@ -489,3 +489,65 @@ def test_colsum_bf16(L):
         L.call("zl_colsum_bf16", x.cuda().data_ptr(), db.data_ptr(), ws.data_ptr(), M, N, None)
         torch.cuda.synchronize()
         assert rel(db.cpu(), ref + 1) < 1e-5
+
+
+# ------------------------------------------------------------------ bf16 instances of the reference API
+def _bfr(x):
+    """The values of x rounded to bf16, as fp32 (both sides of a comparison see the same inputs)."""
+    return torch.from_numpy(np.asarray(x, np.float32)).bfloat16().float().numpy()
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 192, 320), (2048, 512, 1536)])
+def test_linear_bf16_api_vs_oracle(L, M, K, N):
+    """linear_forward / linear_backward in bf16 (tcgen05 GEMM, no split-K workspace) against the
+    oracle's fp32 restatement of linear.cu on the same bf16-rounded inputs."""
+    x, W, b = _bfr(O.normal(M * K, 1)), _bfr(O.normal(N * K, 2) * 0.1), _bfr(O.normal(N, 3) * 0.5)
+    dY, dB0 = _bfr(O.normal(M * N, 4)), _bfr(O.normal(N, 5))
+    # device copies are held in names: a pointer taken from a temporary could be reused by the next one
+    xd, Wd, bd, dYd = (torch.from_numpy(a).bfloat16().cuda() for a in (x, W, b, dY))
+    y = torch.empty(M * N, device="cuda", dtype=torch.bfloat16)
+    L.call("zl_linear_forward_bf16", xd.data_ptr(), Wd.data_ptr(), bd.data_ptr(), y.data_ptr(), M, K, N, 1, None)
+    torch.cuda.synchronize()
+    assert rel(y.float().cpu(), O.linear_forward(x, W, b, M, K, N)) < BF16_TOL
+    dx = torch.empty(M * K, device="cuda", dtype=torch.bfloat16)
+    dw = torch.empty(N * K, device="cuda", dtype=torch.bfloat16)
+    db = torch.from_numpy(dB0).bfloat16().cuda()
+    L.call("zl_linear_backward_bf16", dYd.data_ptr(), xd.data_ptr(), Wd.data_ptr(), dx.data_ptr(), dw.data_ptr(),
+           db.data_ptr(), M, K, N, 1, None)
+    torch.cuda.synchronize()
+    rdx, rdw, rdb = O.linear_backward(dY, x, W, dB0, M, K, N)
+    assert rel(dx.float().cpu(), rdx) < BF16_TOL
+    assert rel(dw.float().cpu(), rdw) < BF16_TOL
+    assert rel(db.float().cpu(), rdb) < BF16_TOL
+
+
+@pytest.mark.parametrize("B,S,H,Dh", [(2, 256, 2, 64), (1, 512, 2, 128), (2, 2048, 8, 64)])
+def test_mha_bf16_api_vs_oracle(L, B, S, H, Dh):
+    """mha_forward / mha_backward in bf16 with separate Q, K, V tensors (the reference API's layout) on
+    the tcgen05 kernels, against the oracle: the output and dQ / dK / dV of the true gradient
+    (reference_semantics = 0), and the reference's unscaled dQ / dK (reference_semantics = 1)."""
+    E, T = H * Dh, B * S
+    q, k, v = (_bfr(O.normal(T * E, s) * 0.5) for s in (21, 22, 23))
+    dO = _bfr(O.normal(T * E, 24))
+    o_ref, lse_ref = O.attention_forward(q, k, v, E, B, S, H, Dh)
+    qd, kd, vd, gd = (torch.from_numpy(a).bfloat16().cuda() for a in (q, k, v, dO))
+    nbytes = int(L.load().zl_mha_state_bytes_bf16(B, S, H, Dh))
+    state = torch.empty(nbytes, device="cuda", dtype=torch.uint8)
+    o = torch.empty(T * E, device="cuda", dtype=torch.bfloat16)
+    L.call("zl_mha_forward_bf16", qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), state.data_ptr(), nbytes,
+           None, B, S, H, Dh, 1, None)
+    torch.cuda.synchronize()
+    assert rel(o.float().cpu(), o_ref) < BF16_TOL
+    ob = o.float().cpu().numpy()
+    lse = state[:B * H * S * 4].view(torch.float32).cpu().numpy()
+    assert rel(lse, lse_ref) < 1e-3
+    dq_r, dk_r, dv_r = O.attention_backward(q, k, v, E, ob, dO, lse, B, S, H, Dh)
+    for ref_sem in (0, 1):
+        g = [torch.empty(T * E, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+        L.call("zl_mha_backward_bf16", gd.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), state.data_ptr(),
+               nbytes, None, g[0].data_ptr(), g[1].data_ptr(), g[2].data_ptr(), B, S, H, Dh, 1, ref_sem, None)
+        torch.cuda.synchronize()
+        f = float(np.sqrt(Dh)) if ref_sem else 1.0
+        assert rel(g[0].float().cpu(), dq_r * f) < BF16_TOL, ref_sem
+        assert rel(g[1].float().cpu(), dk_r * f) < BF16_TOL, ref_sem
+        assert rel(g[2].float().cpu(), dv_r) < BF16_TOL, ref_sem

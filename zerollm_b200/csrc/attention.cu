@@ -493,10 +493,11 @@ __global__ void __launch_bounds__(THREADS) fa_bwd_kernel(const __nv_bfloat16* __
   }
 }
 
-// dQ = scale * dq_acc, rotated back by RoPE, into the Q columns of d_qkv.  dq_acc is [T, E]
+// dQ = scale * dq_acc, rotated back by RoPE, into dq_out (`ld_out` elements per token: the Q columns
+// of the packed gradient, or a separate [T, E] tensor).  dq_acc is [T, E]
 // (token-major, the mma.sync kernel) or [B, H, S, Dh] (head-major, the tcgen05 kernel).  One thread
 // per 8 consecutive elements (two 16-byte loads, one 16-byte store).
-__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ d_qkv,
+__global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dq_out, int ld_out,
                                    const float* rope_cos, const float* rope_sin, int64_t T, int S, int H,
                                    int DH, float scale, int head_major) {
   // 32-bit index arithmetic (the host checks T * E < 2^31): 64-bit divisions by runtime values
@@ -528,7 +529,7 @@ __global__ void fa_bwd_post_kernel(const float* __restrict__ dq_acc, __nv_bfloat
   }
   uint4 u;
   u.x = pack_bf16(x[0], x[1]); u.y = pack_bf16(x[2], x[3]); u.z = pack_bf16(x[4], x[5]); u.w = pack_bf16(x[6], x[7]);
-  *reinterpret_cast<uint4*>(d_qkv + (size_t)t * 3 * E + c) = u;
+  *reinterpret_cast<uint4*>(dq_out + (size_t)t * (uint32_t)ld_out + c) = u;
 }
 
 }  // namespace fa
@@ -673,6 +674,14 @@ bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, c
 zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
                            float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
                            int S, int H, int Dh, cudaStream_t st);
+bool fa_fwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int ld,
+                       __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh, cudaStream_t st, zl_status* status);
+bool fa_bwd_tc_supported3(const void* q, const void* k, const void* v, int ld_in, const void* d_o, const void* dq_acc,
+                          const void* dk, const void* dv, int ld_out, int S, int Dh);
+zl_status fa_bwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int ld_in,
+                            const __nv_bfloat16* d_o, const float* nl, const float* Dsum, float* dq_acc,
+                            __nv_bfloat16* dk, __nv_bfloat16* dv, int ld_out, const float* rope_cos,
+                            const float* rope_sin, int B, int S, int H, int Dh, float dk_scale, cudaStream_t st);
 }
 using namespace zl;
 
@@ -787,8 +796,116 @@ zl_status zl::attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, cons
   }
   if (ev1) record_timing_event(ev1, st);
   fa::fa_bwd_post_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
-      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, T, seq_len, num_heads, head_dim, scale,
-      tc ? 1 : 0);
+      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), 3 * E, rope_cos, rope_sin, T, seq_len, num_heads, head_dim,
+      scale, tc ? 1 : 0);
+  return check_launch("fa_bwd_post_kernel");
+}
+
+// ------------------------------------------------------------ reference-style bf16 attention (mha.cuh:18-48)
+// State kept between the forward and the backward, laid out in the caller's `state` buffer (the
+// reference API's attention_scores, B*H*S*S elements): the per-row log-sum-exp, a copy of the output
+// (the backward's D = rowsum(dO * O) needs it and the reference backward is not given O), then the
+// backward's fp32 dQ accumulator and row vectors.  Each region starts on a 256-byte boundary.
+namespace {
+struct MhaState {
+  size_t lse, o, dq, dsum, nl, fwd_end, total;
+};
+MhaState mha_state_layout(int64_t B, int64_t S, int64_t H, int64_t Dh) {
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t rows = (size_t)B * H * S, te = (size_t)B * S * H * Dh;
+  MhaState m;
+  m.lse = 0;
+  m.o = up(m.lse + rows * 4);
+  m.fwd_end = up(m.o + te * 2);
+  m.dq = m.fwd_end;
+  m.dsum = up(m.dq + te * 4);
+  m.nl = up(m.dsum + rows * 4);
+  m.total = up(m.nl + rows * 4);
+  return m;
+}
+zl_status mha_bf16_check(const void* q, const void* k, const void* v, const void* state, int64_t B, int64_t S,
+                         int64_t H, int64_t Dh, int causal, const uint8_t* mask, size_t state_bytes, bool bwd) {
+  if (B <= 0 || S <= 0 || H <= 0 || Dh <= 0) return set_error(ZL_EINVAL, "mha bf16: invalid sizes");
+  if (!q || !k || !v || !state) return set_error(ZL_EINVAL, "mha bf16: null pointer");
+  if (!causal || mask)
+    return set_error(ZL_EUNSUPPORTED, "mha bf16: the flash-attention path is causal and takes no mask");
+  if ((Dh != 64 && Dh != 128) || S % 128 != 0)
+    return set_error(ZL_EUNSUPPORTED, "mha bf16: head_dim %lld (64 or 128) and seq_len %lld (a multiple of 128)",
+                     (long long)Dh, (long long)S);
+  if (B * S * H * Dh >= ((int64_t)1 << 31)) return set_error(ZL_EUNSUPPORTED, "mha bf16: batch*seq*embed >= 2^31");
+  const MhaState m = mha_state_layout(B, S, H, Dh);
+  const size_t need = bwd ? m.total : m.fwd_end;
+  if (state_bytes < need)
+    return set_error(ZL_EINVAL, "mha bf16: the state buffer holds %zu bytes, %zu needed", state_bytes, need);
+  if (reinterpret_cast<uintptr_t>(state) & 255) return set_error(ZL_EINVAL, "mha bf16: state must be 256-byte aligned");
+  return ZL_OK;
+}
+}  // namespace
+
+extern "C" size_t zl_mha_state_bytes_bf16(int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim) {
+  return mha_state_layout(batch, seq_len, num_heads, head_dim).total;
+}
+
+extern "C" zl_status zl_mha_forward_bf16(const zl_bf16* Q, const zl_bf16* K, const zl_bf16* V, zl_bf16* attn_output,
+                                         void* state, size_t state_bytes, const uint8_t* mask, int64_t batch,
+                                         int64_t seq_len, int64_t num_heads, int64_t head_dim, int is_causal,
+                                         zl_stream stream) {
+  zl_status st = mha_bf16_check(Q, K, V, state, batch, seq_len, num_heads, head_dim, is_causal, mask, state_bytes,
+                                false);
+  if (st != ZL_OK) return st;
+  if (!attn_output) return set_error(ZL_EINVAL, "mha bf16: null output");
+  const MhaState m = mha_state_layout(batch, seq_len, num_heads, head_dim);
+  uint8_t* base = static_cast<uint8_t*>(state);
+  const int E = (int)(num_heads * head_dim);
+  cudaStream_t cs = (cudaStream_t)stream;
+  zl_status ks = ZL_OK;
+  if (!fa_fwd_tc_launch3(reinterpret_cast<const __nv_bfloat16*>(Q), reinterpret_cast<const __nv_bfloat16*>(K),
+                         reinterpret_cast<const __nv_bfloat16*>(V), E, reinterpret_cast<__nv_bfloat16*>(attn_output),
+                         reinterpret_cast<float*>(base + m.lse), (int)batch, (int)seq_len, (int)num_heads,
+                         (int)head_dim, cs, &ks))
+    return set_error(ZL_EUNSUPPORTED, "mha bf16: Q, K, V must be 16-byte aligned");
+  if (ks != ZL_OK) return ks;
+  const cudaError_t e = cudaMemcpyAsync(base + m.o, attn_output, (size_t)batch * seq_len * E * 2,
+                                        cudaMemcpyDeviceToDevice, cs);
+  return e == cudaSuccess ? ZL_OK : set_error(ZL_ECUDA, "mha bf16: output copy: %s", cudaGetErrorString(e));
+}
+
+extern "C" zl_status zl_mha_backward_bf16(const zl_bf16* d_attn_output, const zl_bf16* Q, const zl_bf16* K,
+                                          const zl_bf16* V, void* state, size_t state_bytes, const uint8_t* mask,
+                                          zl_bf16* d_Q, zl_bf16* d_K, zl_bf16* d_V, int64_t batch, int64_t seq_len,
+                                          int64_t num_heads, int64_t head_dim, int is_causal, int reference_semantics,
+                                          zl_stream stream) {
+  zl_status st = mha_bf16_check(Q, K, V, state, batch, seq_len, num_heads, head_dim, is_causal, mask, state_bytes,
+                                true);
+  if (st != ZL_OK) return st;
+  if (!d_attn_output || !d_Q || !d_K || !d_V) return set_error(ZL_EINVAL, "mha bf16: null gradient pointer");
+  const MhaState m = mha_state_layout(batch, seq_len, num_heads, head_dim);
+  uint8_t* base = static_cast<uint8_t*>(state);
+  float* lse = reinterpret_cast<float*>(base + m.lse);
+  const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(base + m.o);
+  float* dq_acc = reinterpret_cast<float*>(base + m.dq);
+  float* Dsum = reinterpret_cast<float*>(base + m.dsum);
+  float* nl = reinterpret_cast<float*>(base + m.nl);
+  const int B = (int)batch, S = (int)seq_len, H = (int)num_heads, Dh = (int)head_dim, E = H * Dh;
+  if (!fa_bwd_tc_supported3(Q, K, V, E, d_attn_output, dq_acc, d_K, d_V, E, S, Dh) ||
+      (reinterpret_cast<uintptr_t>(d_Q) & 15))
+    return set_error(ZL_EUNSUPPORTED, "mha bf16: tensors must be 16-byte aligned");
+  cudaStream_t cs = (cudaStream_t)stream;
+  const int64_t T = (int64_t)B * S, chunks = T * (E / 8);
+  fa::fa_bwd_pre_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, cs>>>(
+      o, reinterpret_cast<const __nv_bfloat16*>(d_attn_output), lse, Dsum, nl, dq_acc, B, S, H, Dh);
+  st = check_launch("fa_bwd_pre_kernel");
+  if (st != ZL_OK) return st;
+  // the reference backward leaves out the softmax scale in dQ and dK (mha.cu:284-295)
+  const float g_scale = reference_semantics ? 1.0f : 1.0f / sqrtf((float)Dh);
+  st = fa_bwd_tc_launch3(reinterpret_cast<const __nv_bfloat16*>(Q), reinterpret_cast<const __nv_bfloat16*>(K),
+                         reinterpret_cast<const __nv_bfloat16*>(V), E,
+                         reinterpret_cast<const __nv_bfloat16*>(d_attn_output), nl, Dsum, dq_acc,
+                         reinterpret_cast<__nv_bfloat16*>(d_K), reinterpret_cast<__nv_bfloat16*>(d_V), E, nullptr,
+                         nullptr, B, S, H, Dh, g_scale, cs);
+  if (st != ZL_OK) return st;
+  fa::fa_bwd_post_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, cs>>>(
+      dq_acc, reinterpret_cast<__nv_bfloat16*>(d_Q), E, nullptr, nullptr, T, S, H, Dh, g_scale, 1);
   return check_launch("fa_bwd_post_kernel");
 }
 

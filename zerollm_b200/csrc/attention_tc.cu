@@ -17,13 +17,14 @@
 #include <cmath>
 #include <cstdlib>
 
+#include <initializer_list>
 #include <type_traits>
 
 #include "common.cuh"
 
 namespace zl {
 bool make_tma_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
-                  uint32_t box_rows, int swizzle_bytes = 128);
+                  uint32_t box_rows, int swizzle_bytes = 128, uint64_t row_stride = 0);
 int sm_count_current();
 
 namespace fatc {
@@ -59,7 +60,8 @@ __device__ __forceinline__ float fast_exp2(float x) {  // MUFU ex2 (inputs <= 0 
 
 template <int DH>
 __global__ void __launch_bounds__(THREADS, 1)
-    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out,
+    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ out,
                      float* __restrict__ lse, int S, int H, float scale_log2) {
   using C = Fwd<DH>;
   constexpr int KVST = C::KVST, SMEM_Q = C::SMEM_Q, SMEM_K = C::SMEM_K, SMEM_V = C::SMEM_V, SMEM_BAR = C::SMEM_BAR;
@@ -96,7 +98,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
-    tma_prefetch_desc(&tm);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, TMEM_COLS);
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive_expect_tx(q_full, T_BYTES);
 #pragma unroll
       for (int a = 0; a < C::ATOMS; ++a)
-        tma_load_2d(smem + SMEM_Q + a * TILE_BYTES, &tm, q_full, h * DH + a * 64, row0);
+        tma_load_2d(smem + SMEM_Q + a * TILE_BYTES, &tm_q, q_full, h * DH + a * 64, row0);
       int issued = 0;
       for (int j = 0; j < nkv; ++j) {
         const int st = j % KVST;
@@ -123,8 +127,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int krow = b * S + j * BKV;
 #pragma unroll
         for (int a = 0; a < C::ATOMS; ++a) {
-          tma_load_2d(smem + SMEM_K + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st], E + h * DH + a * 64, krow);
-          tma_load_2d(smem + SMEM_V + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st], 2 * E + h * DH + a * 64,
+          tma_load_2d(smem + SMEM_K + st * T_BYTES + a * TILE_BYTES, &tm_k, &kv_full[st], h * DH + a * 64, krow);
+          tma_load_2d(smem + SMEM_V + st * T_BYTES + a * TILE_BYTES, &tm_v, &kv_full[st], h * DH + a * 64,
                       krow);
         }
         issued = j + 1;
@@ -335,9 +339,26 @@ constexpr int THREADS_PP = 384;  // warp 0 TMA, warps 1-2 MMA of tiles 0-1, warp
 // unit in one round draws a light one in the next.
 __device__ __forceinline__ int pp_unit(int k, int cta, int G) { return k * G + ((k & 1) ? G - 1 - cta : cta); }
 
+// Backward unit u -> (key block, batch-head).  Heads are taken in groups of `hg` (all of them when
+// hg <= 0); inside a group the units run key-block-major, the ones with the most query blocks first.
+// A group of about one wave of units keeps the rows of the fp32 dQ accumulator that are being added
+// into within L2.
+__device__ __forceinline__ void bwd_unit_coords(int u, int nk, int nbh, int hg, int* kb, int* bh) {
+  if (hg <= 0 || hg >= nbh) {
+    *kb = u / nbh;
+    *bh = u % nbh;
+    return;
+  }
+  const int grp = u / (hg * nk), r = u - grp * hg * nk;
+  const int heads = min(hg, nbh - grp * hg);
+  *kb = r / heads;
+  *bh = grp * hg + r % heads;
+}
+
 template <int DH>
 __global__ void __launch_bounds__(THREADS_PP, 1)
-    fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out,
+    fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ out,
                      float* __restrict__ lse, int S, int H, int nunits, float scale_log2) {
   using C = FwdPP<DH>;
   constexpr int KVST = C::KVST, T_BYTES = C::T_BYTES;
@@ -379,7 +400,9 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
     }
     mbar_init(drain, 2);
     fence_mbar_init();
-    tma_prefetch_desc(&tm);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, TMEM_COLS);
@@ -405,7 +428,7 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
         for (int t = 0; t < 2; ++t)
 #pragma unroll
           for (int a = 0; a < C::ATOMS; ++a)
-            tma_load_2d(smem + C::SMEM_Q + t * T_BYTES + a * TILE_BYTES, &tm, q_full, h * DH + a * 64,
+            tma_load_2d(smem + C::SMEM_Q + t * T_BYTES + a * TILE_BYTES, &tm_q, q_full, h * DH + a * 64,
                         b * S + (2 * p + t) * BQ);
         ++nq_loads;
         const int nkv = 2 * p + 2;
@@ -416,10 +439,10 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
           const int krow = b * S + j * BKV;
 #pragma unroll
           for (int a = 0; a < C::ATOMS; ++a) {
-            tma_load_2d(smem + C::SMEM_K + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st], E + h * DH + a * 64,
+            tma_load_2d(smem + C::SMEM_K + st * T_BYTES + a * TILE_BYTES, &tm_k, &kv_full[st], h * DH + a * 64,
                         krow);
-            tma_load_2d(smem + C::SMEM_V + st * T_BYTES + a * TILE_BYTES, &tm, &kv_full[st],
-                        2 * E + h * DH + a * 64, krow);
+            tma_load_2d(smem + C::SMEM_V + st * T_BYTES + a * TILE_BYTES, &tm_v, &kv_full[st],
+                        h * DH + a * 64, krow);
           }
           ++g;
         }
@@ -705,12 +728,14 @@ template <int N> __device__ __forceinline__ void tmem_st_n(uint32_t taddr, const
 }
 
 __global__ void __launch_bounds__(THREADS_B, 1)
-    fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
+    fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
+                     const __grid_constant__ CUtensorMap tm_dv,
                      const float* __restrict__ nl_g,
                      const float* __restrict__ Dsum,
-                     __nv_bfloat16* __restrict__ d_qkv, const float* __restrict__ rope_cos,
-                     const float* __restrict__ rope_sin, int S, int H, int nunits, float scale, float scale_log2) {
+                     const float* __restrict__ rope_cos,
+                     const float* __restrict__ rope_sin, int S, int H, int nunits, int hgroup, float scale, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -744,7 +769,9 @@ __global__ void __launch_bounds__(THREADS_B, 1)
   auto unit_of = [&](int k) -> Unit {
     const int u = pp_unit(k, cta, G);
     if (u >= nunits) return Unit{0, 0, 0};
-    return Unit{u / nbh, u % nbh, nk - u / nbh};
+    int kb, bh;
+    bwd_unit_coords(u, nk, nbh, hgroup, &kb, &bh);
+    return Unit{kb, bh, nk - kb};
   };
 
   if (threadIdx.x == 0) {
@@ -760,10 +787,13 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     mbar_init(sd_used, 32 * NSOFT);
     mbar_init(dkv_free, 32 * NSOFT);
     fence_mbar_init();
-    tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_dq);
-    tma_prefetch_desc(&tm_dkv);
+    tma_prefetch_desc(&tm_dk);
+    tma_prefetch_desc(&tm_dv);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -791,7 +821,7 @@ __global__ void __launch_bounds__(THREADS_B, 1)
         const int kbuf = k & 1;
         if (!bounded_wait(&k_empty[kbuf], ((k >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
         mbar_arrive_expect_tx(&k_full[kbuf], TILE_BYTES);
-        tma_load_2d(smem + SM_K + kbuf * TILE_BYTES, &tm_qkv, &k_full[kbuf], E + h * D, krow);
+        tma_load_2d(smem + SM_K + kbuf * TILE_BYTES, &tm_k, &k_full[kbuf], h * D, krow);
         ++nkl;
         for (int i = 0; i < un.niter; ++i, ++n) {
           const uint32_t st = n % QST;
@@ -799,7 +829,7 @@ __global__ void __launch_bounds__(THREADS_B, 1)
           mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES + VEC_BYTES);
           const int qb = un.kb + i;
           const int qrow = b * S + qb * BQ;
-          tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_qkv, &q_full[st], h * D, qrow);
+          tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_q, &q_full[st], h * D, qrow);
           tma_load_2d(smem + SM_DO + st * TILE_BYTES, &tm_do, &q_full[st], h * D, qrow);
           float* vec = reinterpret_cast<float*>(smem + SM_VEC + st * VEC_BYTES);
           bulk_load(vec, nl_g + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
@@ -807,7 +837,7 @@ __global__ void __launch_bounds__(THREADS_B, 1)
           if (i == 0) {
             if (!bounded_wait(v_empty, (k & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; ++n; break; }
             mbar_arrive_expect_tx(v_full, TILE_BYTES);
-            tma_load_2d(smem + SM_V, &tm_qkv, v_full, 2 * E + h * D, krow);
+            tma_load_2d(smem + SM_V, &tm_v, v_full, h * D, krow);
             ++nvl;
           }
         }
@@ -990,8 +1020,8 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       __syncwarp();
       if (lane == 0) {
         const int y0 = b * S + pu.kb * BKV + quarter * 32;
-        tma_store_2d_bulk(&tm_dkv, stg, E + h * D + cs * DCOLS, y0);
-        tma_store_2d_bulk(&tm_dkv, stg + 2048, 2 * E + h * D + cs * DCOLS, y0);
+        tma_store_2d_bulk(&tm_dk, stg, h * D + cs * DCOLS, y0);
+        tma_store_2d_bulk(&tm_dv, stg + 2048, h * D + cs * DCOLS, y0);
         bulk_commit();
       }
     };
@@ -1157,11 +1187,12 @@ constexpr uint32_t IDESC_VK = make_idesc(1, 128, 128, 0, 1);  // dV / dK: A TMEM
 constexpr uint32_t IDESC_Q = make_idesc(1, 128, 64, 1, 1);    // dQ^T: A, B MN-major
 
 __global__ void __launch_bounds__(THREADS, 1)
-    fa_bwd_tc128_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
-                        const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_dq,
-                        const __grid_constant__ CUtensorMap tm_dkv, const float* __restrict__ nl_g,
+    fa_bwd_tc128_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                        const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
+                        const __grid_constant__ CUtensorMap tm_dv, const float* __restrict__ nl_g,
                         const float* __restrict__ Dsum, const float* __restrict__ rope_cos,
-                        const float* __restrict__ rope_sin, int S, int H, int nunits, float scale, float scale_log2) {
+                        const float* __restrict__ rope_sin, int S, int H, int nunits, int hgroup, float scale, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -1193,7 +1224,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto unit_of = [&](int k) -> Unit {
     const int u = pp_unit(k, cta, G);
     if (u >= nunits) return Unit{0, 0, 0};
-    return Unit{u / nbh, u % nbh, 2 * (nk - u / nbh)};
+    int kb, bh;
+    bwd_unit_coords(u, nk, nbh, hgroup, &kb, &bh);
+    return Unit{kb, bh, 2 * (nk - kb)};
   };
 
   if (threadIdx.x == 0) {
@@ -1209,11 +1242,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(sd_used, 32 * NSOFT);
     mbar_init(dkv_free, 32 * NSOFT);
     fence_mbar_init();
-    tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_dq);
-    tma_prefetch_desc(&tm_dkv);
+    tma_prefetch_desc(&tm_dk);
+    tma_prefetch_desc(&tm_dv);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -1239,7 +1274,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!bounded_wait(&k_empty[kbuf], ((k >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
         mbar_arrive_expect_tx(&k_full[kbuf], K_BYTES);
         for (int a = 0; a < 2; ++a)
-          tma_load_2d(smem + SM_K + kbuf * K_BYTES + a * KATOM, &tm_k, &k_full[kbuf], E + h * D + a * 64, krow);
+          tma_load_2d(smem + SM_K + kbuf * K_BYTES + a * KATOM, &tm_k, &k_full[kbuf], h * D + a * 64, krow);
         ++nkl;
         for (int i = 0; i < un.niter; ++i, ++n) {
           const uint32_t st = n % QST;
@@ -1258,7 +1293,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!bounded_wait(v_empty, (k & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; ++n; break; }
             mbar_arrive_expect_tx(v_full, K_BYTES);
             for (int a = 0; a < 2; ++a)
-              tma_load_2d(smem + SM_V + a * KATOM, &tm_k, v_full, 2 * E + h * D + a * 64, krow);
+              tma_load_2d(smem + SM_V + a * KATOM, &tm_v, v_full, h * D + a * 64, krow);
             ++nvl;
           }
         }
@@ -1421,7 +1456,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     };
     // a [32 keys][64 dims] bf16 box (128-byte rows, swizzled) by TMA store
-    auto store_box = [&](const uint32_t (&p)[32], int x, int y) {
+    auto store_box = [&](const CUtensorMap* map, const uint32_t (&p)[32], int x, int y) {
       stage_free();
 #pragma unroll
       for (int c = 0; c < 8; ++c)
@@ -1430,7 +1465,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d_bulk(&tm_dkv, stg, x, y);
+        tma_store_2d_bulk(map, stg, x, y);
         bulk_commit();
       }
     };
@@ -1457,8 +1492,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       dq_store(dq, y);
       const int b = pu.bh / H, h = pu.bh % H;
       const int y0 = b * S + pu.kb * BKV + quarter * 32;
-      store_box(pk, E + h * D + cs * DCOLS, y0);
-      store_box(pv, 2 * E + h * D + cs * DCOLS, y0);
+      store_box(&tm_dk, pk, h * D + cs * DCOLS, y0);
+      store_box(&tm_dv, pv, h * D + cs * DCOLS, y0);
     };
     uint32_t n = 0;
     int prev_y = 0;
@@ -1563,13 +1598,30 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace bwd128
 }  // namespace fatc
 
-// Returns true if the tcgen05 kernel handled the call (head dim 64 or 128, S a multiple of 128).
-bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh,
-                      cudaStream_t st, zl_status* status) {
-  if ((Dh != 64 && Dh != 128) || S % fatc::BQ != 0 || (reinterpret_cast<uintptr_t>(qkv) & 15)) return false;
-  CUtensorMap tm;
-  const int E = H * Dh;
-  if (!make_tma_map(&tm, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128)) {
+namespace {
+// Views of Q, K and V (or of dK and dV): `ld` elements between consecutive tokens.  The model's packed
+// [T, 3E] activation is three views of one buffer (ld = 3E); the reference-style API passes three
+// separate [T, E] tensors (ld = E).  Boxes are 64 head-dim columns by `box_rows` tokens.
+bool bf16_view_map(CUtensorMap* m, const __nv_bfloat16* p, int E, int T, int ld, int box_cols, int box_rows,
+                   int swizzle = 128) {
+  return make_tma_map(m, p, false, (uint64_t)E, (uint64_t)T, box_cols, box_rows, swizzle, (uint64_t)ld);
+}
+bool aligned16(std::initializer_list<const void*> ps) {
+  uintptr_t a = 0;
+  for (const void* p : ps) a |= reinterpret_cast<uintptr_t>(p);
+  return (a & 15) == 0;
+}
+}  // namespace
+
+// Returns true if a tcgen05 kernel handled the call (head dim 64 or 128, S a multiple of 128, 16-byte
+// aligned views with a row stride `ld` that is a multiple of 8).
+bool fa_fwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int ld,
+                       __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh, cudaStream_t st, zl_status* status) {
+  if ((Dh != 64 && Dh != 128) || S % fatc::BQ != 0 || ld % 8 != 0 || !aligned16({q, k, v})) return false;
+  CUtensorMap tq, tk, tv;
+  const int E = H * Dh, T = B * S;
+  if (!bf16_view_map(&tq, q, E, T, ld, 64, 128) || !bf16_view_map(&tk, k, E, T, ld, 64, 128) ||
+      !bf16_view_map(&tv, v, E, T, ld, 64, 128)) {
     *status = set_error(ZL_ECUDA, "attention: cuTensorMapEncodeTiled failed");
     return true;
   }
@@ -1584,7 +1636,7 @@ bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, 
     const int grid = nunits < sms ? nunits : sms;
     auto launch_pp = [&](auto kern, int smem) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      kern<<<grid, fatc::THREADS_PP, smem, st>>>(tm, out, lse, S, H, nunits, scale_log2);
+      kern<<<grid, fatc::THREADS_PP, smem, st>>>(tq, tk, tv, out, lse, S, H, nunits, scale_log2);
     };
     if (Dh == 64) launch_pp(fatc::fa_fwd_pp_kernel<64>, fatc::FwdPP<64>::SMEM_TOTAL);
     else launch_pp(fatc::fa_fwd_pp_kernel<128>, fatc::FwdPP<128>::SMEM_TOTAL);
@@ -1594,58 +1646,80 @@ bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, 
   const int grid = B * H * (S / fatc::BQ);
   auto launch = [&](auto kern, int smem) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    kern<<<grid, fatc::THREADS, smem, st>>>(tm, out, lse, S, H, scale_log2);
+    kern<<<grid, fatc::THREADS, smem, st>>>(tq, tk, tv, out, lse, S, H, scale_log2);
   };
   if (Dh == 64) launch(fatc::fa_fwd_tc_kernel<64>, fatc::Fwd<64>::SMEM_TOTAL);
   else launch(fatc::fa_fwd_tc_kernel<128>, fatc::Fwd<128>::SMEM_TOTAL);
   *status = check_launch("fa_fwd_tc_kernel");
   return true;
 }
+bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh,
+                      cudaStream_t st, zl_status* status) {
+  const int E = H * Dh;
+  return fa_fwd_tc_launch3(qkv, qkv + E, qkv + 2 * E, 3 * E, out, lse, B, S, H, Dh, st, status);
+}
 
 // Whether a tcgen05 backward takes this call: head_dim 64 or 128, S a multiple of 128, and 16-byte
-// aligned TMA sources, dQ accumulator and gradient rows.
+// aligned TMA sources, dQ accumulator and gradient views.
+bool fa_bwd_tc_supported3(const void* q, const void* k, const void* v, int ld_in, const void* d_o, const void* dq_acc,
+                          const void* dk, const void* dv, int ld_out, int S, int Dh) {
+  return (Dh == 64 || Dh == 128) && S % fatc::BQ == 0 && ld_in % 8 == 0 && ld_out % 8 == 0 &&
+         aligned16({q, k, v, d_o, dq_acc, dk, dv});
+}
 bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, const void* d_qkv, int S, int Dh) {
-  return (Dh == 64 || Dh == 128) && S % fatc::BQ == 0 &&
-         ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(d_o) | reinterpret_cast<uintptr_t>(dq_acc) |
-           reinterpret_cast<uintptr_t>(d_qkv)) & 15) == 0;
+  return fa_bwd_tc_supported3(qkv, qkv, qkv, 8, d_o, dq_acc, d_qkv, d_qkv, 8, S, Dh);
 }
 
 // Backward main pass.  Before it the caller's pre pass writes nl = -lse*log2(e) and D = rowsum(dO*O)
 // ([B, H, S]) and zeroes dq_acc; after it the post pass turns dq_acc ([B, H, S, Dh] fp32) into dQ.
-zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
-                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
-                           int S, int H, int Dh, cudaStream_t st) {
-  CUtensorMap tq, tdo, tdq, tdkv;
-  const int E = H * Dh;
+// dK is multiplied by `dk_scale` (the softmax scale; 1 for the reference's unscaled gradient).
+zl_status fa_bwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int ld_in,
+                            const __nv_bfloat16* d_o, const float* nl, const float* Dsum, float* dq_acc,
+                            __nv_bfloat16* dk, __nv_bfloat16* dv, int ld_out, const float* rope_cos,
+                            const float* rope_sin, int B, int S, int H, int Dh, float dk_scale, cudaStream_t st) {
+  CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
+  const int E = H * Dh, T = B * S;
   const float scale = 1.0f / sqrtf((float)Dh);
   const int nunits = B * H * (S / fatc::BKV);
   const int sms = sm_count_current();
   const int grid = nunits < sms ? nunits : sms;
+  // Units are taken one head at a time (heaviest key block first) when the fp32 dQ accumulator is
+  // too large to stay in L2 while every head's units run together: measured at batch 8 x 16 heads x
+  // 2048 x 128 (a 134 MB accumulator) 756 us against 948 us; at batch 16 x 8 heads x 2048 x 64 (67 MB)
+  // the key-block-major order over all heads is faster (311 us against 327 us).
+  const int hgroup = (double)B * H * S * Dh * 4.0 > 96e6 ? 1 : 0;
   if (Dh == 128) {
     namespace K = fatc::bwd128;
-    CUtensorMap tk;
     // K / V: 128-row boxes; Q / dO: 64-row boxes (64 head dims per box); dK / dV out: [32][64] boxes
-    if (!make_tma_map(&tk, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, K::BKV) ||
-        !make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, K::BQ) ||
-        !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, K::BQ) ||
+    if (!bf16_view_map(&tq, q, E, T, ld_in, 64, K::BQ) || !bf16_view_map(&tk, k, E, T, ld_in, 64, K::BKV) ||
+        !bf16_view_map(&tv, v, E, T, ld_in, 64, K::BKV) || !bf16_view_map(&tdo, d_o, E, T, E, 64, K::BQ) ||
         !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 32) ||
-        !make_tma_map(&tdkv, d_qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 32))
+        !bf16_view_map(&tdk, dk, E, T, ld_out, 64, 32) || !bf16_view_map(&tdv, dv, E, T, ld_out, 64, 32))
       return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
     cudaFuncSetAttribute(K::fa_bwd_tc128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM_TOTAL);
     K::fa_bwd_tc128_kernel<<<grid, K::THREADS, K::SMEM_TOTAL, st>>>(
-        tk, tq, tdo, tdq, tdkv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, scale, scale * 1.4426950408889634f);
+        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
+        scale * 1.4426950408889634f);
     return check_launch("fa_bwd_tc128_kernel");
   }
-  if (!make_tma_map(&tq, qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 64, 128) ||
-      !make_tma_map(&tdo, d_o, false, (uint64_t)E, (uint64_t)B * S, 64, 128) ||
+  if (!bf16_view_map(&tq, q, E, T, ld_in, 64, 128) || !bf16_view_map(&tk, k, E, T, ld_in, 64, 128) ||
+      !bf16_view_map(&tv, v, E, T, ld_in, 64, 128) || !bf16_view_map(&tdo, d_o, E, T, E, 64, 128) ||
       !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 32) ||
-      !make_tma_map(&tdkv, d_qkv, false, (uint64_t)3 * E, (uint64_t)B * S, 32, 32, 64))
+      !bf16_view_map(&tdk, dk, E, T, ld_out, 32, 32, 64) || !bf16_view_map(&tdv, dv, E, T, ld_out, 32, 32, 64))
     return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
   cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        fatc::bwd::SMEM_TOTAL);
   fatc::bwd::fa_bwd_tc_kernel<<<grid, fatc::bwd::THREADS_B, fatc::bwd::SMEM_TOTAL, st>>>(
-      tq, tdo, tdq, tdkv, nl, Dsum, d_qkv, rope_cos, rope_sin, S, H, nunits, scale, scale * 1.4426950408889634f);
+      tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
+      scale * 1.4426950408889634f);
   return check_launch("fa_bwd_tc_kernel");
+}
+zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
+                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
+                           int S, int H, int Dh, cudaStream_t st) {
+  const int E = H * Dh;
+  return fa_bwd_tc_launch3(qkv, qkv + E, qkv + 2 * E, 3 * E, d_o, nl, Dsum, dq_acc, d_qkv + E, d_qkv + 2 * E, 3 * E,
+                           rope_cos, rope_sin, B, S, H, Dh, 1.0f / sqrtf((float)Dh), st);
 }
 
 int attn_tc_dev_error_read_and_clear() {

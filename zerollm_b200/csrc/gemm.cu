@@ -1051,13 +1051,15 @@ int sm_count() {
 }
 
 // 2-D tiled map over a row-major [rows, inner] matrix with a box of [box_rows, box_inner].
+// A 2-D map over `rows` rows of `inner` elements; consecutive rows are `row_stride` elements apart
+// (0: packed rows), so a map can cover a column range of a wider matrix.
 bool make_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
-              uint32_t box_rows, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+              uint32_t box_rows, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B, uint64_t row_stride = 0) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
   const uint64_t esz = is_f32 ? 4 : 2;
   cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {inner * esz};
+  cuuint64_t strides[1] = {(row_stride ? row_stride : inner) * esz};
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, is_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
@@ -1230,9 +1232,9 @@ bool use_pair(int M, int K) {
 }  // namespace
 
 bool make_tma_map(CUtensorMap* map, const void* ptr, bool is_f32, uint64_t inner, uint64_t rows, uint32_t box_inner,
-                  uint32_t box_rows, int swizzle_bytes) {
+                  uint32_t box_rows, int swizzle_bytes, uint64_t row_stride) {
   return make_map(map, ptr, is_f32, inner, rows, box_inner, box_rows,
-                  swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+                  swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, row_stride);
 }
 int sm_count_current() { return sm_count(); }
 
@@ -1414,6 +1416,104 @@ __global__ void bias_grad_f32_kernel(float* __restrict__ dB, const float* __rest
   dB[n] += g;
 }
 }  // namespace zl
+
+namespace zl {
+// y[m, n] += bias[n] on bf16 rows, eight columns per thread (16-byte accesses); N % 8 == 0.
+__global__ void bias_add_bf16_kernel(__nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ bias, int64_t M,
+                                     int N) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int cpr = N / 8;
+  if (idx >= M * cpr) return;
+  const int n0 = (int)(idx % cpr) * 8;
+  uint4* yp = reinterpret_cast<uint4*>(y) + idx;
+  uint4 u = *yp;
+  const uint4 bb = __ldg(reinterpret_cast<const uint4*>(bias + n0));
+  uint32_t* uw = reinterpret_cast<uint32_t*>(&u);
+  const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bb);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 a = unpack_bf16(uw[k]), c = unpack_bf16(bw[k]);
+    uw[k] = pack_bf16(a.x + c.x, a.y + c.y);
+  }
+  *yp = u;
+}
+// db[n] += sum_m dy[m, n] (linear.cu:59-69 in bf16 storage, fp32 sums): one block per 64 columns,
+// 32 row lanes x 8 column groups of 8; N % 8 == 0.
+__global__ void __launch_bounds__(256) bias_grad_bf16_kernel(__nv_bfloat16* __restrict__ db,
+                                                             const __nv_bfloat16* __restrict__ dy, int64_t M, int N) {
+  __shared__ float red[32][65];
+  const int cg = threadIdx.x & 7, rl = threadIdx.x >> 3;
+  const int n0 = blockIdx.x * 64 + cg * 8;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (n0 < N) {
+    for (int64_t r = rl; r < M; r += 32) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(dy + r * N + n0));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16(w[k]);
+        acc[2 * k] += f.x;
+        acc[2 * k + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[rl][cg * 8 + j] = acc[j];
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    const int n = blockIdx.x * 64 + threadIdx.x;
+    if (n < N) {
+      float t = 0.f;
+      for (int i = 0; i < 32; ++i) t += red[i][threadIdx.x];
+      db[n] = __float2bfloat16_rn(__bfloat162float(db[n]) + t);
+    }
+  }
+}
+}  // namespace zl
+
+// linear.cuh:21-30 in bf16 (the reference instantiates float only): Y = X W^T on the tcgen05 GEMM
+// with no split-K workspace, then Y += b.  K and N multiples of 8, 16-byte aligned rows.
+extern "C" zl_status zl_linear_forward_bf16(const zl_bf16* input, const zl_bf16* weight, const zl_bf16* bias,
+                                            zl_bf16* output, int64_t M, int64_t K, int64_t N, int use_bias,
+                                            zl_stream s) {
+  if (M <= 0 || K <= 0 || N <= 0) return zl::set_error(ZL_EINVAL, "linear bf16: sizes must be positive");
+  if (K % 8 || N % 8 || M >= (int64_t)1 << 31)
+    return zl::set_error(ZL_EUNSUPPORTED, "linear bf16: K and N must be multiples of 8");
+  cudaStream_t st = static_cast<cudaStream_t>(s);
+  zl_status r = zl::gemm_tc<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(input),
+                                           reinterpret_cast<const __nv_bfloat16*>(weight), output, (int)M, (int)N,
+                                           (int)K, ZL_A_KMAJOR | ZL_B_KMAJOR, 0, nullptr, nullptr, st);
+  if (r == ZL_EUNSUPPORTED) return zl::set_error(ZL_EUNSUPPORTED, "linear bf16: operands must be 16-byte aligned");
+  if (r != ZL_OK || !use_bias || !bias) return r;
+  if (reinterpret_cast<uintptr_t>(bias) & 15) return zl::set_error(ZL_EINVAL, "linear bf16: bias must be 16-byte aligned");
+  const int64_t chunks = M * (N / 8);
+  zl::bias_add_bf16_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<__nv_bfloat16*>(output), reinterpret_cast<const __nv_bfloat16*>(bias), M, (int)N);
+  return zl::check_launch("add_bias_kernel");
+}
+// linear.cuh:48-59 in bf16: dX = dY W and dW = dY^T X overwrite, dB += column sums of dY.
+extern "C" zl_status zl_linear_backward_bf16(const zl_bf16* d_output, const zl_bf16* input, const zl_bf16* weight,
+                                             zl_bf16* d_input, zl_bf16* d_weight, zl_bf16* d_bias, int64_t M,
+                                             int64_t K, int64_t N, int use_bias, zl_stream s) {
+  if (M <= 0 || K <= 0 || N <= 0) return zl::set_error(ZL_EINVAL, "linear bf16: sizes must be positive");
+  if (K % 8 || N % 8 || M % 8 || M >= (int64_t)1 << 31)
+    return zl::set_error(ZL_EUNSUPPORTED, "linear bf16 backward: M, K and N must be multiples of 8");
+  cudaStream_t st = static_cast<cudaStream_t>(s);
+  const auto dY = reinterpret_cast<const __nv_bfloat16*>(d_output);
+  zl_status r = ZL_OK;
+  if (d_input)
+    r = zl::gemm_tc<__nv_bfloat16>(dY, reinterpret_cast<const __nv_bfloat16*>(weight), d_input, (int)M, (int)K, (int)N,
+                                   ZL_A_KMAJOR, 0, nullptr, nullptr, st);
+  if (r == ZL_OK && d_weight)
+    r = zl::gemm_tc<__nv_bfloat16>(dY, reinterpret_cast<const __nv_bfloat16*>(input), d_weight, (int)N, (int)K,
+                                   (int)M, 0, 0, nullptr, nullptr, st);
+  if (r == ZL_EUNSUPPORTED) return zl::set_error(ZL_EUNSUPPORTED, "linear bf16: operands must be 16-byte aligned");
+  if (r != ZL_OK || !use_bias || !d_bias) return r;
+  if (reinterpret_cast<uintptr_t>(d_output) & 15) return zl::set_error(ZL_EINVAL, "linear bf16: dY must be 16-byte aligned");
+  zl::bias_grad_bf16_kernel<<<(unsigned)((N + 63) / 64), 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(d_bias), dY,
+                                                                       M, (int)N);
+  return zl::check_launch("compute_bias_grad_kernel");
+}
 
 // matmul.cuh:20/:68  C[M,N] = A[M,K] B[K,N]
 extern "C" zl_status zl_matmul_f32(const float* A, const float* B, float* C, int M, int N, int K, zl_stream s) {

@@ -15,6 +15,7 @@
 #include <cstring>
 #include <initializer_list>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -567,15 +568,26 @@ __global__ void mean_kernel(const float* __restrict__ v, int64_t n, float* __res
   if (threadIdx.x == 0) *out = (float)(red[0] / denom);
 }
 
-// softmax.cu:12-65 (one CTA per row)
-__global__ void softmax_f32_kernel(const float* __restrict__ in, float* __restrict__ out, int N) {
+// The reference API's kernels are written once for fp32 and bf16 storage; arithmetic is fp32, and
+// the fp32 instances are plain loads and stores (the bf16 ones round each stored value to nearest).
+__device__ __forceinline__ float ldv(const float* p) { return *p; }
+__device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void stv(float* p, float v) { *p = v; }
+__device__ __forceinline__ void stv(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ void atomic_addv(float* p, float v) { atomicAdd(p, v); }
+__device__ __forceinline__ void atomic_addv(__nv_bfloat16* p, float v) { atomicAdd(p, __float2bfloat16_rn(v)); }
+
+// softmax.cu:12-65 (one CTA per row).  fp32 rows keep the reference's order (exponentials stored,
+// then divided); bf16 rows recompute the exponential in the last pass instead of storing it rounded.
+template <typename T = float>
+__global__ void softmax_f32_kernel(const T* __restrict__ in, T* __restrict__ out, int N) {
   __shared__ float red[32];
   const int64_t r = blockIdx.x;
-  const float* x = in + r * N;
-  float* y = out + r * N;
+  const T* x = in + r * N;
+  T* y = out + r * N;
   const int tid = threadIdx.x, nt = blockDim.x;
   float mx = -FLT_MAX;
-  for (int i = tid; i < N; i += nt) mx = fmaxf(mx, x[i]);
+  for (int i = tid; i < N; i += nt) mx = fmaxf(mx, ldv(x + i));
   mx = warp_max(mx);
   if ((tid & 31) == 0) red[tid >> 5] = mx;
   __syncthreads();
@@ -588,7 +600,11 @@ __global__ void softmax_f32_kernel(const float* __restrict__ in, float* __restri
   mx = red[0];
   __syncthreads();
   float s = 0.f;
-  for (int i = tid; i < N; i += nt) { const float e = expf(x[i] - mx); y[i] = e; s += e; }
+  for (int i = tid; i < N; i += nt) {
+    const float e = expf(ldv(x + i) - mx);
+    if constexpr (std::is_same<T, float>::value) y[i] = e;
+    s += e;
+  }
   s = warp_sum(s);
   if ((tid & 31) == 0) red[tid >> 5] = s;
   __syncthreads();
@@ -599,7 +615,11 @@ __global__ void softmax_f32_kernel(const float* __restrict__ in, float* __restri
   }
   __syncthreads();
   const float sum = red[0];
-  for (int i = tid; i < N; i += nt) y[i] = y[i] / sum;
+  if constexpr (std::is_same<T, float>::value) {
+    for (int i = tid; i < N; i += nt) y[i] = y[i] / sum;
+  } else {
+    for (int i = tid; i < N; i += nt) stv(y + i, expf(ldv(x + i) - mx) / sum);
+  }
 }
 // cross_entropy.cu:5-31
 __global__ void ce_bwd_f32_kernel(float* __restrict__ d, const float* __restrict__ p, const int32_t* __restrict__ t,
@@ -705,23 +725,45 @@ __global__ void sgd_kernel(float* __restrict__ p, const float* __restrict__ g, f
   p[i] = pv - lr * gv;
 }
 
-// ================================================================== element-wise (fp32 API)
-__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ o, int64_t n) {
+// ================================================================== element-wise (reference API)
+
+template <typename T>
+__global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ o, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) o[i] = a[i] + b[i];
+  if (i < n) stv(o + i, ldv(a + i) + ldv(b + i));
 }
-__global__ void add_inplace_kernel(float* __restrict__ a, const float* __restrict__ b, int64_t n) {
+template <typename T>
+__global__ void add_inplace_kernel(T* __restrict__ a, const T* __restrict__ b, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) a[i] += b[i];
+  if (i < n) stv(a + i, ldv(a + i) + ldv(b + i));
 }
-__global__ void relu_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+template <typename T>
+__global__ void relu_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = x[i] > 0 ? x[i] : 0.f;
+  if (i < n) {
+    const float v = ldv(x + i);
+    stv(y + i, v > 0 ? v : 0.f);
+  }
 }
-__global__ void relu_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gy, float* __restrict__ gx,
-                                int64_t n) {
+template <typename T>
+__global__ void relu_bwd_kernel(const T* __restrict__ x, const T* __restrict__ gy, T* __restrict__ gx, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) gx[i] = x[i] > 0 ? gy[i] : 0.f;
+  if (i < n) stv(gx + i, ldv(x + i) > 0 ? ldv(gy + i) : 0.f);
+}
+// adamw.cu:26-73 on bf16 parameters and moments: fp32 arithmetic, each stored value rounded.
+__global__ void adamw_bf16_kernel(__nv_bfloat16* __restrict__ p, const __nv_bfloat16* __restrict__ g,
+                                  __nv_bfloat16* __restrict__ m, __nv_bfloat16* __restrict__ v, int64_t n, float lr,
+                                  float wd, float b1, float b2, float eps, float bc1, float bc2) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gv = ldv(g + i), pv = ldv(p + i);
+  const float mv = b1 * ldv(m + i) + (1.0f - b1) * gv;
+  const float vv = b2 * ldv(v + i) + (1.0f - b2) * gv * gv;
+  const float step = lr * (mv / bc1) / (sqrtf(vv / bc2) + eps);
+  const float decay = wd != 0.f ? lr * wd * pv : 0.f;
+  stv(p + i, pv - (decay + step));
+  stv(m + i, mv);
+  stv(v + i, vv);
 }
 // 32x32 tiles through shared memory: coalesced reads and writes.
 __global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int cols) {
@@ -744,67 +786,67 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* _
 
 // LayerNorm / RMSNorm on fp32 rows (reference API): one warp per row, dgamma/dbeta
 // accumulated per block in shared memory and added with one atomic per column per block.
-template <int KIND>
-__global__ void norm_fwd_f32_kernel(const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
-                                    float* __restrict__ y, float* __restrict__ mean, float* __restrict__ rstd, int64_t M,
+template <int KIND, typename T = float>
+__global__ void norm_fwd_f32_kernel(const T* __restrict__ x, const T* __restrict__ g, const T* __restrict__ b,
+                                    T* __restrict__ y, T* __restrict__ mean, T* __restrict__ rstd, int64_t M,
                                     int N, float eps) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= M) return;
   const int lane = threadIdx.x & 31;
-  const float* xr = x + row * N;
+  const T* xr = x + row * N;
   float s = 0.f;
-  for (int i = lane; i < N; i += 32) s += KIND == 0 ? xr[i] : xr[i] * xr[i];
+  for (int i = lane; i < N; i += 32) s += KIND == 0 ? ldv(xr + i) : ldv(xr + i) * ldv(xr + i);
   s = warp_sum(s);
   float mu = 0.f, rs;
   if (KIND == 0) {
     mu = s / (float)N;
     float q = 0.f;
-    for (int i = lane; i < N; i += 32) { const float d = xr[i] - mu; q += d * d; }
+    for (int i = lane; i < N; i += 32) { const float d = ldv(xr + i) - mu; q += d * d; }
     q = warp_sum(q);
     rs = rsqrtf(q / (float)N + eps);
   } else {
     rs = rsqrtf(s / (float)N + eps);
   }
   if (lane == 0) {
-    if (mean) mean[row] = mu;
-    if (rstd) rstd[row] = rs;
+    if (mean) stv(mean + row, mu);
+    if (rstd) stv(rstd + row, rs);
   }
   for (int i = lane; i < N; i += 32)
-    y[row * N + i] = KIND == 0 ? (xr[i] - mu) * rs * g[i] + b[i] : xr[i] * rs * g[i];
+    stv(y + row * N + i, KIND == 0 ? (ldv(xr + i) - mu) * rs * ldv(g + i) + ldv(b + i) : ldv(xr + i) * rs * ldv(g + i));
 }
-template <int KIND>
-__global__ void norm_bwd_f32_kernel(const float* __restrict__ x, const float* __restrict__ dy, const float* __restrict__ g,
-                                    const float* __restrict__ mean, const float* __restrict__ rstd,
-                                    float* __restrict__ dx, float* __restrict__ dg, float* __restrict__ db, int64_t M,
+template <int KIND, typename T = float>
+__global__ void norm_bwd_f32_kernel(const T* __restrict__ x, const T* __restrict__ dy, const T* __restrict__ g,
+                                    const T* __restrict__ mean, const T* __restrict__ rstd,
+                                    T* __restrict__ dx, T* __restrict__ dg, T* __restrict__ db, int64_t M,
                                     int N) {
   extern __shared__ float sacc[];  // [2N]
   for (int i = threadIdx.x; i < 2 * N; i += blockDim.x) sacc[i] = 0.f;
   __syncthreads();
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   for (int64_t row = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += (int64_t)gridDim.x * warps) {
-    const float mu = KIND == 0 ? mean[row] : 0.f, rs = rstd[row];
-    const float* xr = x + row * N;
-    const float* dr = dy + row * N;
+    const float mu = KIND == 0 ? ldv(mean + row) : 0.f, rs = ldv(rstd + row);
+    const T* xr = x + row * N;
+    const T* dr = dy + row * N;
     float s1 = 0.f, s2 = 0.f;
     for (int i = lane; i < N; i += 32) {
-      const float xh = (xr[i] - mu) * rs, a = dr[i] * g[i];
+      const float xh = (ldv(xr + i) - mu) * rs, a = ldv(dr + i) * ldv(g + i);
       s1 += a;
       s2 += a * xh;
-      atomicAdd(&sacc[i], dr[i] * xh);
-      if (KIND == 0) atomicAdd(&sacc[N + i], dr[i]);
+      atomicAdd(&sacc[i], ldv(dr + i) * xh);
+      if (KIND == 0) atomicAdd(&sacc[N + i], ldv(dr + i));
     }
     s1 = warp_sum(s1);
     s2 = warp_sum(s2);
     const float invN = 1.f / (float)N;
     for (int i = lane; i < N; i += 32) {
-      const float xh = (xr[i] - mu) * rs, a = dr[i] * g[i];
-      dx[row * N + i] = KIND == 0 ? rs * (a - s1 * invN - xh * s2 * invN) : rs * (a - xh * s2 * invN);
+      const float xh = (ldv(xr + i) - mu) * rs, a = ldv(dr + i) * ldv(g + i);
+      stv(dx + row * N + i, KIND == 0 ? rs * (a - s1 * invN - xh * s2 * invN) : rs * (a - xh * s2 * invN));
     }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
-    atomicAdd(&dg[i], sacc[i]);
-    if (KIND == 0) atomicAdd(&db[i], sacc[N + i]);
+    atomic_addv(dg + i, sacc[i]);
+    if (KIND == 0) atomic_addv(db + i, sacc[N + i]);
   }
 }
 
@@ -1094,7 +1136,7 @@ extern "C" zl_status zl_f32_to_bf16(const float* x, zl_bf16* y, int64_t n, zl_st
 extern "C" zl_status zl_layernorm_forward_f32(const float* input, const float* gamma, const float* beta, float* output,
                                               float* mean, float* rstd, int64_t M, int64_t N, float eps, zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;  // layernorm.cu:178
-  norm_fwd_f32_kernel<0><<<nblk(M, 8), 256, 0, ST(s)>>>(input, gamma, beta, output, mean, rstd, M, (int)N, eps);
+  norm_fwd_f32_kernel<0, float><<<nblk(M, 8), 256, 0, ST(s)>>>(input, gamma, beta, output, mean, rstd, M, (int)N, eps);
   return check_launch("layernorm_forward_kernel");
 }
 extern "C" zl_status zl_layernorm_backward_f32(const float* input, const float* d_output, const float* gamma,
@@ -1102,14 +1144,14 @@ extern "C" zl_status zl_layernorm_backward_f32(const float* input, const float* 
                                                float* d_beta, int64_t M, int64_t N, zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;  // layernorm.cu:200
   const int nb = norm_bwd_blocks(M);
-  norm_bwd_f32_kernel<0><<<nb, 256, 2 * N * sizeof(float), ST(s)>>>(input, d_output, gamma, mean, rstd, d_input,
+  norm_bwd_f32_kernel<0, float><<<nb, 256, 2 * N * sizeof(float), ST(s)>>>(input, d_output, gamma, mean, rstd, d_input,
                                                                     d_gamma, d_beta, M, (int)N);
   return check_launch("layernorm_backward_kernel");
 }
 extern "C" zl_status zl_rmsnorm_forward_f32(const float* input, const float* gamma, float* output, float* rstd, int64_t M,
                                             int64_t N, float eps, zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;
-  norm_fwd_f32_kernel<1><<<nblk(M, 8), 256, 0, ST(s)>>>(input, gamma, nullptr, output, nullptr, rstd, M, (int)N, eps);
+  norm_fwd_f32_kernel<1, float><<<nblk(M, 8), 256, 0, ST(s)>>>(input, gamma, nullptr, output, nullptr, rstd, M, (int)N, eps);
   return check_launch("rmsnorm_forward_kernel");
 }
 extern "C" zl_status zl_rmsnorm_backward_f32(const float* input, const float* d_output, const float* gamma,
@@ -1117,7 +1159,7 @@ extern "C" zl_status zl_rmsnorm_backward_f32(const float* input, const float* d_
                                              zl_stream s) {
   if (M <= 0 || N <= 0) return ZL_OK;
   const int nb = norm_bwd_blocks(M);
-  norm_bwd_f32_kernel<1><<<nb, 256, 2 * N * sizeof(float), ST(s)>>>(input, d_output, gamma, nullptr, rstd, d_input,
+  norm_bwd_f32_kernel<1, float><<<nb, 256, 2 * N * sizeof(float), ST(s)>>>(input, d_output, gamma, nullptr, rstd, d_input,
                                                                     d_gamma, nullptr, M, (int)N);
   return check_launch("rmsnorm_backward_kernel");
 }
@@ -1200,4 +1242,63 @@ extern "C" zl_status zl_sgd_step_f32(float* params, const float* grads, float* v
   if (size <= 0) return set_error(ZL_EINVAL, "sgd_step: size must be > 0");
   sgd_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(params, grads, velocity, size, lr, momentum, weight_decay);
   return check_launch("sgd_kernel");
+}
+
+// ---------------------------------------------------------------- bf16 instances of the reference API
+// The reference instantiates these templates for float only; these are the __nv_bfloat16 instances
+// (bf16 storage, fp32 arithmetic) with the same size checks and silent returns.
+namespace {
+inline const __nv_bfloat16* B16(const zl_bf16* p) { return reinterpret_cast<const __nv_bfloat16*>(p); }
+inline __nv_bfloat16* B16(zl_bf16* p) { return reinterpret_cast<__nv_bfloat16*>(p); }
+}  // namespace
+extern "C" zl_status zl_layernorm_forward_bf16(const zl_bf16* input, const zl_bf16* gamma, const zl_bf16* beta,
+                                               zl_bf16* output, zl_bf16* mean, zl_bf16* rstd, int64_t M, int64_t N,
+                                               float eps, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;  // layernorm.cu:178
+  norm_fwd_f32_kernel<0, __nv_bfloat16><<<nblk(M, 8), 256, 0, ST(s)>>>(B16(input), B16(gamma), B16(beta), B16(output),
+                                                                       B16(mean), B16(rstd), M, (int)N, eps);
+  return check_launch("layernorm_forward_kernel");
+}
+extern "C" zl_status zl_layernorm_backward_bf16(const zl_bf16* input, const zl_bf16* d_output, const zl_bf16* gamma,
+                                                const zl_bf16* mean, const zl_bf16* rstd, zl_bf16* d_input,
+                                                zl_bf16* d_gamma, zl_bf16* d_beta, int64_t M, int64_t N, zl_stream s) {
+  if (M <= 0 || N <= 0) return ZL_OK;  // layernorm.cu:200
+  const int nb = norm_bwd_blocks(M);
+  norm_bwd_f32_kernel<0, __nv_bfloat16><<<nb, 256, 2 * N * sizeof(float), ST(s)>>>(
+      B16(input), B16(d_output), B16(gamma), B16(mean), B16(rstd), B16(d_input), B16(d_gamma), B16(d_beta), M, (int)N);
+  return check_launch("layernorm_backward_kernel");
+}
+extern "C" zl_status zl_softmax_bf16(const zl_bf16* input, zl_bf16* output, int M, int N, zl_stream s) {
+  if (M <= 0 || N <= 0) return set_error(ZL_EINVAL, "softmax: M and N must be > 0");  // softmax.cu:70-71
+  softmax_f32_kernel<__nv_bfloat16><<<M, 256, 0, ST(s)>>>(B16(input), B16(output), N);
+  return check_launch("softmax_kernel");
+}
+extern "C" zl_status zl_add_bf16(const zl_bf16* a, const zl_bf16* b, zl_bf16* output, int size, zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "add: size must be > 0");  // add.cu:36-38
+  add_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(B16(a), B16(b), B16(output), size);
+  return check_launch("add_kernel");
+}
+extern "C" zl_status zl_add_inplace_bf16(zl_bf16* a, const zl_bf16* b, int size, zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "add_inplace: size must be > 0");
+  add_inplace_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(B16(a), B16(b), size);
+  return check_launch("add_inplace_kernel");
+}
+extern "C" zl_status zl_relu_forward_bf16(const zl_bf16* input, zl_bf16* output, int size, zl_stream s) {
+  if (size <= 0) return ZL_OK;  // relu.cu:23
+  relu_fwd_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(B16(input), B16(output), size);
+  return check_launch("relu_forward");
+}
+extern "C" zl_status zl_relu_backward_bf16(const zl_bf16* input, const zl_bf16* grad_output, zl_bf16* grad_input,
+                                           int size, zl_stream s) {
+  if (size <= 0) return ZL_OK;  // relu.cu:35
+  relu_bwd_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(B16(input), B16(grad_output), B16(grad_input), size);
+  return check_launch("relu_backward");
+}
+extern "C" zl_status zl_adamw_step_bf16(zl_bf16* params, const zl_bf16* grads, zl_bf16* m, zl_bf16* v, int64_t size,
+                                        float lr, float wd, float b1, float b2, float eps, float bc1, float bc2,
+                                        zl_stream s) {
+  if (size <= 0) return set_error(ZL_EINVAL, "adamw_step: size must be > 0");  // adamw.cu:92-94
+  adamw_bf16_kernel<<<nblk(size, 256), 256, 0, ST(s)>>>(B16(params), B16(grads), B16(m), B16(v), size, lr, wd, b1, b2,
+                                                        eps, bc1, bc2);
+  return check_launch("adamw_kernel");
 }

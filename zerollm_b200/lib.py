@@ -82,6 +82,20 @@ SIGNATURES = {
     "zl_embedding_backward_bf16": (i32, [vp, vp, vp, i64, i32, i32, vp]),
     "zl_cross_entropy_fused_bf16": (i32, [vp, vp, i32, i32, f32, f32, vp, vp, vp]),
     "zl_colsum_bf16": (i32, [vp, vp, vp, i64, i32, vp]),
+    "zl_linear_forward_bf16": (i32, [vp, vp, vp, vp, i64, i64, i64, i32, vp]),
+    "zl_linear_backward_bf16": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, i32, vp]),
+    "zl_mha_forward_bf16": (i32, [vp, vp, vp, vp, vp, C.c_size_t, vp, i64, i64, i64, i64, i32, vp]),
+    "zl_mha_backward_bf16": (i32, [vp, vp, vp, vp, vp, C.c_size_t, vp, vp, vp, vp, i64, i64, i64, i64, i32, i32,
+                                   vp]),
+    "zl_mha_state_bytes_bf16": (C.c_size_t, [i64, i64, i64, i64]),
+    "zl_layernorm_forward_bf16": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, f32, vp]),
+    "zl_layernorm_backward_bf16": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, vp]),
+    "zl_softmax_bf16": (i32, [vp, vp, i32, i32, vp]),
+    "zl_add_bf16": (i32, [vp, vp, vp, i32, vp]),
+    "zl_add_inplace_bf16": (i32, [vp, vp, i32, vp]),
+    "zl_relu_forward_bf16": (i32, [vp, vp, i32, vp]),
+    "zl_relu_backward_bf16": (i32, [vp, vp, vp, i32, vp]),
+    "zl_adamw_step_bf16": (i32, [vp, vp, vp, vp, i64] + [f32] * 7 + [vp]),
     "zl_colsum_workspace_floats": (i64, [i64, i32]),
     "zl_colsum_bf16_noalloc": (i32, [vp, vp, i64, i32, vp]),
     "zl_colsum_noalloc_max_floats": (i64, []),
