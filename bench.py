@@ -474,10 +474,20 @@ def main():
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--no-breakdown", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="time each kernel of the step alone at the model's shapes (batch --batch) and exit; "
+                         "the small driver for per-kernel ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.batch is None:
         args.batch = 8 if args.model == "scaled" else 16
+    if args.kernels_only:
+        import torch
+        torch.cuda.set_device(0)
+        bd = kernel_breakdown(args.batch, args.seq, reps=2)
+        print(json.dumps({"kernels_only": True, "batch": args.batch, "seq_len": args.seq,
+                          "kernels_ms": {k: round(v["ms"], 4) for k, v in bd.items()}}), flush=True)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
