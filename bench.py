@@ -400,16 +400,22 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     wall = time.perf_counter() - t0
     ms_e2e = max_over_ranks(max(e0.elapsed_time(e1) / args.steps, 1e3 * wall / args.steps))
-    # In-step kernel durations for the roofline (N = 1): the same steps again, with timing-event nodes
-    # around each layer's attention kernels in the step graph.  The timed regions above run without
-    # them, since the nodes lengthen the step by ~2 %.
-    in_step = None
-    if world == 1:
-        model.set_kernel_timing(True)
-        for _ in range(3):
-            model.train_step(d_inp, d_tgt, B, S, lr)
-        in_step = model.kernel_times()
-        model.set_kernel_timing(False)
+    # In-step kernel durations for the roofline, and the step's phases: the same steps again, with
+    # timing-event nodes around each layer's attention kernels and at the step's start, after its last
+    # backward kernel and after the gradient exchange has rejoined (every rank takes these steps).
+    # The timed regions above run without them, since the nodes lengthen the step by ~2 %.
+    model.set_kernel_timing(True)
+    for _ in range(3):
+        model.train_step(d_inp, d_tgt, B, S, lr)
+    in_step = model.kernel_times()
+    step_ms_t, exposed_ms = model.step_times()
+    model.set_kernel_timing(False)
+    in_step = (max_over_ranks(in_step[0]), max_over_ranks(in_step[1]))
+    phases = {"step_ms": round(max_over_ranks(step_ms_t), 3),
+              "exposed_exchange_ms": round(max_over_ranks(exposed_ms), 3),
+              "timing": "event nodes in three extra steps after the timed regions, max over ranks; "
+                        "exposed_exchange_ms = end of the last backward kernel to the rejoin of the "
+                        "all-reduce side stream (AdamW not included in step_ms)"}
     csum = model.checksum()
     consistent = True
     if world > 1:
@@ -455,6 +461,7 @@ def run_ours(args, rank, world, local_rank):
     }
     if in_step:
         line["attention_ms_in_step"] = {"fwd": round(in_step[0], 4), "bwd": round(in_step[1], 4)}
+        line["step_phases"] = phases
     if roof:
         line["roofline"] = roof
         line["kernels_ms"] = {k: round(v["ms"], 4) for k, v in bd.items()}

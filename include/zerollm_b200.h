@@ -351,6 +351,11 @@ zl_status zl_model_set_graph(zl_model *m, int enabled);
  * recent step (it waits for that step's events); ZL_ESTATE when timing is off or no step ran. */
 zl_status zl_model_set_kernel_timing(zl_model *m, int enabled);
 zl_status zl_model_kernel_times(zl_model *m, float *attn_fwd_ms, float *attn_bwd_ms);
+/* With kernel timing on: the latest step's duration (zero_grad to the end of the step, AdamW not
+ * included) and the part of it after the last backward kernel, i.e. the time the step waited for the
+ * gradient all-reduces still running on the side stream (0 without a communicator).  No reference
+ * counterpart (a measurement aid). */
+zl_status zl_model_step_times(zl_model *model, float *step_ms, float *exposed_exchange_ms);
 /* Reference-API pieces: forward to fp32 logits [batch*seq, V] (zerollm.cpp:101-195) ... */
 zl_status zl_model_forward(zl_model *m, const int32_t *ids, int batch, int seq_len, float *logits,
                            zl_stream stream);

@@ -195,7 +195,8 @@ struct zl_model {
   int g_B = 0, g_S = 0, g_seen = 0, g_launches = 0;
   // In-step kernel timing: per layer, events just before and after the attention forward kernel
   // and the attention backward's main kernel (graph event nodes in the captured step).
-  std::vector<cudaEvent_t> kt_ev;  // [layer][fwd start, fwd end, bwd start, bwd end]
+  std::vector<cudaEvent_t> kt_ev;  // [layer][fwd start, fwd end, bwd start, bwd end], then step start,
+                                   // end of the last backward kernel, step end (side stream rejoined)
   bool kt_valid = false;           // a step has recorded them
 };
 
@@ -601,6 +602,8 @@ zl_status step_body(zl_model* M, const int32_t* ids, const int32_t* targets, int
                     cudaStream_t st) {
   M->launches = 0;
   M->dist.next_bucket = 0;
+  const size_t kt_step = 4 * (size_t)M->cfg.num_layers;  // step-phase events follow the per-layer ones
+  if (!M->kt_ev.empty()) zl::record_timing_event(M->kt_ev[kt_step], st);
   TRY(zl_model_zero_grad(M, st));
   M->launches++;
   TRY(forward(M, ids, B, S, nullptr, st));
@@ -608,7 +611,9 @@ zl_status step_body(zl_model* M, const int32_t* ids, const int32_t* targets, int
   TRY(zl_cross_entropy_fused_bf16(reinterpret_cast<zl_bf16*>(M->logits), targets, (int)T, M->cfg.vocab_size, 1e-8f,
                                   1.0f / (float)T, M->loss_rows, loss_out, st));
   M->launches += loss_out ? 2 : 1;
-  return backward(M, ids, B, S, st);
+  TRY(backward(M, ids, B, S, st));
+  if (!M->kt_ev.empty()) zl::record_timing_event(M->kt_ev[kt_step + 1], st);
+  return ZL_OK;
 }
 
 // Replays (or captures, the second time a binding is seen) the step body as one CUDA graph.
@@ -683,7 +688,7 @@ extern "C" zl_status zl_model_set_kernel_timing(zl_model* M, int enabled) {
   M->kt_ev.clear();
   M->kt_valid = false;
   if (enabled) {
-    M->kt_ev.resize(4 * (size_t)M->cfg.num_layers);
+    M->kt_ev.resize(4 * (size_t)M->cfg.num_layers + 3);
     for (auto& ev : M->kt_ev) {
       cudaError_t e = cudaEventCreate(&ev);
       if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "kernel timing: cudaEventCreate: %s", cudaGetErrorString(e));
@@ -718,6 +723,21 @@ extern "C" zl_status zl_model_kernel_times(zl_model* M, float* attn_fwd_ms, floa
   return ZL_OK;
 }
 
+extern "C" zl_status zl_model_step_times(zl_model* M, float* step_ms, float* exposed_exchange_ms) {
+  if (!M || !step_ms || !exposed_exchange_ms) return zl::set_error(ZL_EINVAL, "null argument");
+  if (M->kt_ev.empty()) return zl::set_error(ZL_ESTATE, "kernel timing is off");
+  if (!M->kt_valid) return zl::set_error(ZL_ESTATE, "kernel timing: no step has run since timing was enabled");
+  const size_t k = 4 * (size_t)M->cfg.num_layers;
+  cudaError_t e = cudaEventSynchronize(M->kt_ev[k + 2]);
+  float a = 0, b = 0;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&a, M->kt_ev[k], M->kt_ev[k + 2]);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&b, M->kt_ev[k + 1], M->kt_ev[k + 2]);
+  if (e != cudaSuccess) return zl::set_error(ZL_ECUDA, "step timing: %s", cudaGetErrorString(e));
+  *step_ms = a;
+  *exposed_exchange_ms = b;
+  return ZL_OK;
+}
+
 extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const int32_t* targets, int B, int S, float lr,
                                          int update, float* loss_out, zl_stream stream) {
   if (!M || !ids || !targets) return zl::set_error(ZL_EINVAL, "null argument");
@@ -726,7 +746,16 @@ extern "C" zl_status zl_model_train_step(zl_model* M, const int32_t* ids, const 
   M->dist.joined = false;
   if (M->use_graph) TRY(step_graph(M, ids, targets, B, S, loss_out, st));
   else TRY(step_body(M, ids, targets, B, S, loss_out, st));
-  if (!M->kt_ev.empty()) M->kt_valid = true;
+  if (!M->kt_ev.empty()) {
+    // step end: once the gradient exchange on the side stream has rejoined this stream
+    if (M->dist.comm && !M->dist.joined) {
+      cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);
+      cudaStreamWaitEvent(st, M->dist.done_ev, 0);
+      M->dist.joined = true;
+    }
+    zl::record_timing_event(M->kt_ev[4 * (size_t)M->cfg.num_layers + 2], st);
+    M->kt_valid = true;
+  }
   if (update) TRY(adamw(M, lr, st));
   else if (M->dist.comm && !M->dist.joined) {
     cudaEventRecord(M->dist.done_ev, M->dist.comm_stream);

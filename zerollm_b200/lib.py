@@ -117,6 +117,7 @@ SIGNATURES = {
     "zl_model_set_graph": (i32, [vp, i32]),
     "zl_model_set_kernel_timing": (i32, [vp, i32]),
     "zl_model_kernel_times": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
+    "zl_model_step_times": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
     "zl_nccl_unique_id": (i32, [vp, C.c_size_t]),
     "zl_model_attach_nccl": (i32, [vp, vp, i32, i32, i64]),
     "zl_bucket_plan": (i32, [vp, vp, i32, i64, vp, vp, i32, C.POINTER(i32)]),

@@ -164,6 +164,13 @@ class ZeroLLM:
         L.call("zl_model_kernel_times", self.h, C.byref(f), C.byref(b))
         return float(f.value), float(b.value)
 
+    def step_times(self) -> tuple:
+        """With kernel timing on: (step ms, ms the step waited for the gradient exchange after its last
+        backward kernel) of the latest step."""
+        a, b = C.c_float(0), C.c_float(0)
+        L.call("zl_model_step_times", self.h, C.byref(a), C.byref(b))
+        return a.value, b.value
+
     def last_launches(self) -> int:
         n = C.c_int(0)
         L.call("zl_model_last_launches", self.h, C.byref(n))
