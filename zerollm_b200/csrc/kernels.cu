@@ -157,7 +157,9 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
                                                           const __nv_bfloat16* __restrict__ dy,
                                                           const float* __restrict__ g, const float* __restrict__ mean,
                                                           const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-                                                          float* __restrict__ part, int64_t M, int N) {
+                                                          float* __restrict__ part, int64_t M, int N,
+                                                          float* __restrict__ sum0, float* __restrict__ sum1,
+                                                          float* __restrict__ sum2) {
   constexpr int NK = 1 + (KIND == 0 ? 1 : 0) + (COL ? 1 : 0);  // partial sets
   extern __shared__ __align__(16) uint8_t nb_smem[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, warps = blockDim.x >> 5;
@@ -300,18 +302,32 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
         }
     }
   };
+  // The block's sums go to `part` (row blockIdx.x, reduced by a second launch in a fixed order), or,
+  // when sum0 is given, are added straight into sum0 | sum1 | sum2 (columns [0,N) | [N,2N) | [2N,3N)
+  // of the partial set) with 16-byte atomics: no second launch, additions in any order.
+  auto emit4 = [&](int i, float4 t) {
+    if (sum0) {
+      float* o = i < N ? sum0 + i : (i < 2 * N ? sum1 + (i - N) : sum2 + (i - 2 * N));
+      atomicAdd(reinterpret_cast<float4*>(o), t);
+    } else {
+      *reinterpret_cast<float4*>(part + (int64_t)blockIdx.x * NP + i) = t;
+    }
+  };
   if (tree) {
     put(sacc + w * NP, false);
     __syncthreads();
-    for (int i = threadIdx.x; i < NP; i += blockDim.x) {
-      float t = 0.f;
-      for (int k = 0; k < warps; ++k) t += sacc[k * NP + i];
-      part[(int64_t)blockIdx.x * NP + i] = t;
+    for (int i = threadIdx.x * 4; i < NP; i += blockDim.x * 4) {
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < warps; ++k) {
+        const float4 v = *reinterpret_cast<const float4*>(sacc + k * NP + i);
+        t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+      }
+      emit4(i, t);
     }
   } else {
     put(sacc, true);
     __syncthreads();
-    for (int i = threadIdx.x; i < NP; i += blockDim.x) part[(int64_t)blockIdx.x * NP + i] = sacc[i];
+    for (int i = threadIdx.x * 4; i < NP; i += blockDim.x * 4) emit4(i, *reinterpret_cast<const float4*>(sacc + i));
   }
 }
 
@@ -857,7 +873,7 @@ __global__ void norm_bwd_f32_kernel(const T* __restrict__ x, const T* __restrict
 // blockIdx.y selects a slice of up to 2048 columns (rows longer than 2048 use several slices).
 __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* __restrict__ dy,
                                                           float* __restrict__ part, int64_t M, int N,
-                                                          int64_t rows_per_block) {
+                                                          int64_t rows_per_block, float* __restrict__ sum) {
   const int col0 = blockIdx.y * 2048;
   const int W = min(2048, N - col0);  // this slice's columns
   const int groups = W / 8;
@@ -891,6 +907,18 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
     for (int j = 0; j < 8; ++j) sc[rl * W + grp * 8 + j] = acc[j];
   }
   __syncthreads();
+  // the block's column sums: a partial row, or (sum given, 16-byte aligned) added straight into sum
+  if (sum) {
+    for (int c = threadIdx.x * 4; c < W; c += blockDim.x * 4) {
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < rpar; ++k) {
+        const float4 v = *reinterpret_cast<const float4*>(sc + k * W + c);
+        t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+      }
+      atomicAdd(reinterpret_cast<float4*>(sum + col0 + c), t);
+    }
+    return;
+  }
   for (int c = threadIdx.x; c < W; c += blockDim.x) {
     float s = 0.f;
     for (int k = 0; k < rpar; ++k) s += sc[k * W + c];
@@ -951,10 +979,14 @@ namespace zl {
 // `workspace` holds nb * N * (1 + LayerNorm + (dcol != null)) floats.
 zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma, const float* mean,
                              const float* rstd, zl_bf16* dx, float* dgamma, float* dbeta, float* dcol,
-                             float* workspace, int64_t M, int N, cudaStream_t s) {
+                             float* workspace, int64_t M, int N, cudaStream_t s, bool fused) {
   if (M <= 0 || N <= 0) return ZL_OK;
   if (N % 8 || N > 256 * kMaxRowChunks) return set_error(ZL_EUNSUPPORTED, "norm: N=%d must be a multiple of 8, <= 2048", N);
-  if (!workspace || !dgamma || (kind == 0 && (!dbeta || !mean))) return set_error(ZL_EINVAL, "norm bwd: null pointer");
+  // fused: every block adds its sums into dgamma / dbeta / dcol (16-byte atomics); otherwise block
+  // partials go to the workspace and one fixed-order reduction follows
+  fused = fused && !misaligned16({dgamma, dbeta, dcol});
+  if ((!fused && !workspace) || !dgamma || (kind == 0 && (!dbeta || !mean)))
+    return set_error(ZL_EINVAL, "norm bwd: null pointer");
   int nb = norm_bwd_blocks(M);
   const auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   const auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
@@ -969,11 +1001,19 @@ zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, cons
   // them, each warp with its rows in flight, beats more blocks
   if (stages > 0) nb = std::min(nb, sm_count_current() * (ch == 8 ? 1 : 2));
   const size_t sm = (size_t)8 * stages * 4 * N + (size_t)8 * stages * 8 + acc;
+  // the partial sets dgamma | dbeta (LayerNorm) | column sums, in the kernel's order
+  float* outs[3] = {dgamma, nullptr, nullptr};
+  {
+    int no = 1;
+    if (kind == 0) outs[no++] = dbeta;
+    if (dcol) outs[no++] = dcol;
+  }
 #define NB(K, C, COL, ST)                                                                                        \
   {                                                                                                              \
     auto kern = norm_bwd_bf16_kernel<K, C, COL, ST>;                                                             \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                            \
-    kern<<<nb, 256, sm, s>>>(X, DY, gamma, K == 0 ? mean : nullptr, rstd, DX, workspace, M, N);                  \
+    kern<<<nb, 256, sm, s>>>(X, DY, gamma, K == 0 ? mean : nullptr, rstd, DX, fused ? nullptr : workspace, M, N, \
+                             fused ? outs[0] : nullptr, outs[1], outs[2]);                                         \
   }
 #define NBS(K, C, COL) { if (stages == 3) NB(K, C, COL, 3) else if (stages == 2) NB(K, C, COL, 2) else NB(K, C, COL, 0) }
 #define NBC(K, COL) { if (ch == 1) NBS(K, 1, COL) else if (ch == 2) NBS(K, 2, COL) else if (ch == 4) NBS(K, 4, COL) else NBS(K, 8, COL) }
@@ -983,12 +1023,8 @@ zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, cons
 #undef NBS
 #undef NB
   zl_status st = check_launch("norm_bwd_bf16");
-  if (st != ZL_OK) return st;
+  if (st != ZL_OK || fused) return st;
   // one reduction over the partial sets dgamma | dbeta (LayerNorm) | column sums
-  float* outs[3] = {dgamma, nullptr, nullptr};
-  int no = 1;
-  if (kind == 0) outs[no++] = dbeta;
-  if (dcol) outs[no++] = dcol;
   launch_reduce_partials(workspace, nb, N, NK * N, outs[0], outs[1], s, outs[2]);
   return check_launch("norm_bwd_reduce");
 }
@@ -996,7 +1032,8 @@ zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, cons
 extern "C" zl_status zl_norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma,
                                            const float* mean, const float* rstd, zl_bf16* dx, float* dgamma,
                                            float* dbeta, float* workspace, int64_t M, int N, zl_stream s) {
-  return zl::norm_backward_bf16(kind, x, dy, gamma, mean, rstd, dx, dgamma, dbeta, nullptr, workspace, M, N, ST(s));
+  return zl::norm_backward_bf16(kind, x, dy, gamma, mean, rstd, dx, dgamma, dbeta, nullptr, workspace, M, N, ST(s),
+                                false);
 }
 
 extern "C" zl_status zl_embedding_forward_bf16(const int32_t* ids, const float* table, const float* pos, zl_bf16* out,
@@ -1062,12 +1099,32 @@ extern "C" zl_status zl_colsum_bf16(const zl_bf16* dy, float* db, float* workspa
   const int smem_rows = 256 / ((N - (slices - 1) * 2048) / 8);
   const size_t smem = (size_t)std::max(rpar * W, smem_rows * (N - (slices - 1) * 2048)) * sizeof(float);
   colsum_bf16_kernel<<<dim3(nb, slices), 256, smem, ST(s)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(dy), workspace, M, N, rpb);
+      reinterpret_cast<const __nv_bfloat16*>(dy), workspace, M, N, rpb, nullptr);
   zl_status st = check_launch("colsum_bf16");
   if (st != ZL_OK) return st;
   launch_reduce_partials(workspace, nb, N, N, db, nullptr, ST(s));
   return check_launch("colsum_reduce");
 }
+
+namespace zl {
+// The model's bias-gradient column sums: each block adds its sums straight into db (16-byte fp32
+// atomics, additions in any order), so there is no partial buffer and no second launch.
+zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return ZL_OK;
+  if (N % 8) return set_error(ZL_EUNSUPPORTED, "colsum: N=%d must be a multiple of 8", N);
+  if (misaligned16({dy, db})) return set_error(ZL_EINVAL, "colsum: dy and db must be 16-byte aligned");
+  const int64_t rpb = colsum_rows_per_block(M);
+  const int nb = (int)((M + rpb - 1) / rpb);
+  const int slices = (N + 2047) / 2048;
+  const int W = N < 2048 ? N : 2048;
+  const int rpar = 256 / (W / 8);
+  const int smem_rows = 256 / ((N - (slices - 1) * 2048) / 8);
+  const size_t smem = (size_t)std::max(rpar * W, smem_rows * (N - (slices - 1) * 2048)) * sizeof(float);
+  colsum_bf16_kernel<<<dim3(nb, slices), 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(dy), nullptr, M, N,
+                                                           rpb, db);
+  return check_launch("colsum_bf16");
+}
+}  // namespace zl
 
 // ---------------------------------------------------------------- colsum without a caller workspace
 // The partial sums of zl_colsum_bf16 live in this fixed device array instead of a caller buffer.

@@ -35,7 +35,9 @@ namespace zl {
 // kernels.cu: norm backward that also accumulates column sums of its output (a bias gradient)
 zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, const float* gamma, const float* mean,
                              const float* rstd, zl_bf16* dx, float* dgamma, float* dbeta, float* dcol,
-                             float* workspace, int64_t M, int N, cudaStream_t s);
+                             float* workspace, int64_t M, int N, cudaStream_t s, bool fused);
+// kernels.cu: column sums added straight into db (one launch)
+zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaStream_t s);
 // attention.cu: the attention backward with events recorded around its main kernel
 zl_status attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o, const float* lse,
                                   zl_bf16* d_qkv, float* workspace, int batch, int seq_len, int num_heads,
@@ -358,10 +360,11 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
   TRY(gemm(M, M->logits, M->hf, G(M, head_off), V, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
   if (!c.tied) TRY(grads_ready(M, end_of(M, M->L.head), st));
   TRY(gemm(M, M->logits, W(M, head_off), M->dtmp, Ti, d, V, ZL_A_KMAJOR, 0, nullptr, st));
-  TRY(zl_norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->x[c.num_layers]),
-                            reinterpret_cast<zl_bf16*>(M->dtmp), P(M, M->L.nog), M->meanf, M->rstdf,
-                            reinterpret_cast<zl_bf16*>(M->dx), G(M, M->L.nog), G(M, M->L.nob), M->ws, T, d, st));
-  M->launches += 2;
+  TRY(zl::norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->x[c.num_layers]),
+                             reinterpret_cast<zl_bf16*>(M->dtmp), P(M, M->L.nog), M->meanf, M->rstdf,
+                             reinterpret_cast<zl_bf16*>(M->dx), G(M, M->L.nog), c.norm == 0 ? G(M, M->L.nob) : nullptr,
+                             nullptr, M->ws, T, d, st, true));
+  M->launches += 1;
   TRY(grads_ready(M, end_of_any(M, {M->L.nog, M->L.nob}), st));
   for (int l = c.num_layers - 1; l >= 0; --l) {
     const auto& t = M->L.lay[l];
@@ -369,8 +372,9 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     // also the FF2 bias gradient: column sums of this norm's output dr
     TRY(zl::norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r2[l]), reinterpret_cast<zl_bf16*>(M->dx),
                                P(M, t[L_N2G]), M->mean2[l], M->rstd2[l], reinterpret_cast<zl_bf16*>(M->dr),
-                               G(M, t[L_N2G]), G(M, t[L_N2B]), c.bias ? G(M, t[L_B2]) : nullptr, M->ws, T, d, st));
-    M->launches += c.bias ? 3 : 2;
+                               G(M, t[L_N2G]), G(M, t[L_N2B]), c.bias ? G(M, t[L_B2]) : nullptr, M->ws, T, d, st,
+                               true));
+    M->launches += 1;
     TRY(grads_ready(M, end_of_any(M, {t[L_N2G], t[L_N2B]}), st));
     // r2 = h1 + f W2^T + b2
     TRY(gemm(M, M->dr, M->f[l], G(M, t[L_W2]), d, F, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
@@ -379,7 +383,7 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     e.aux = reinterpret_cast<zl_bf16*>(M->f[l]);
     TRY(gemm(M, M->dr, W(M, t[L_W2]), M->dF, Ti, F, d, ZL_A_KMAJOR, ZL_EPI_RELU_MASK, &e, st));
     TRY(gemm(M, M->dF, M->h1[l], G(M, t[L_W1]), F, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
-    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dF), G(M, t[L_B1]), M->ws, T, F, st)); M->launches += 2; }
+    if (c.bias) { TRY(zl::colsum_bf16_add(reinterpret_cast<zl_bf16*>(M->dF), G(M, t[L_B1]), T, F, st)); M->launches += 1; }
     TRY(grads_ready(M, end_of_any(M, {t[L_W1], t[L_B1]}), st));
     e = zl_epilogue{};
     e.residual = reinterpret_cast<zl_bf16*>(M->dr);
@@ -388,8 +392,9 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     // also the output-projection bias gradient: column sums of this norm's output dr
     TRY(zl::norm_backward_bf16(c.norm, reinterpret_cast<zl_bf16*>(M->r1[l]), reinterpret_cast<zl_bf16*>(M->dtmp),
                                P(M, t[L_N1G]), M->mean1[l], M->rstd1[l], reinterpret_cast<zl_bf16*>(M->dr),
-                               G(M, t[L_N1G]), G(M, t[L_N1B]), c.bias ? G(M, t[L_BO]) : nullptr, M->ws, T, d, st));
-    M->launches += c.bias ? 3 : 2;
+                               G(M, t[L_N1G]), G(M, t[L_N1B]), c.bias ? G(M, t[L_BO]) : nullptr, M->ws, T, d, st,
+                               true));
+    M->launches += 1;
     TRY(grads_ready(M, end_of_any(M, {t[L_N1G], t[L_N1B]}), st));
     // r1 = x + attn Wo^T + bo
     TRY(gemm(M, M->dr, M->attn[l], G(M, t[L_WO]), d, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
@@ -403,7 +408,7 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
                                     M->kt_ev.empty() ? nullptr : M->kt_ev[4 * l + 3]));
     M->launches += 3;
     TRY(gemm(M, M->dqkv, M->x[l], G(M, t[L_WQKV]), 3 * d, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
-    if (c.bias) { TRY(zl_colsum_bf16(reinterpret_cast<zl_bf16*>(M->dqkv), G(M, t[L_BQKV]), M->ws, T, 3 * d, st)); M->launches += 2; }
+    if (c.bias) { TRY(zl::colsum_bf16_add(reinterpret_cast<zl_bf16*>(M->dqkv), G(M, t[L_BQKV]), T, 3 * d, st)); M->launches += 1; }
     TRY(grads_ready(M, end_of_any(M, {t[L_WQKV], t[L_BQKV]}), st));
     e = zl_epilogue{};
     e.residual = reinterpret_cast<zl_bf16*>(M->dr);
