@@ -144,16 +144,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     auto issue_s = [&](int j) {  // S_j = Q K_j^T into TMEM buffer j & 1 (K from stage j % KVST)
       const int sb = j & 1;
       const uint32_t sk = smem_u32(smem + SMEM_K + (j % KVST) * T_BYTES);
-      if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < DH / 16; ++k) {  // 16 head dims per MMA: atom k / 4, 32 bytes per step inside it
-          const uint32_t off = (uint32_t)((k >> 2) * TILE_BYTES + (k & 3) * 32);
-          umma_f16(tmem + (uint32_t)(sb * BKV), smem_desc_sw128(sq + off, 16, 1024),
-                   smem_desc_sw128(sk + off, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[sb]);
+      for (int k = 0; k < DH / 16; ++k) {  // 16 head dims per MMA: atom k / 4, 32 bytes per step inside it
+        const uint32_t off = (uint32_t)((k >> 2) * TILE_BYTES + (k & 3) * 32);
+        umma_f16_w(tmem + (uint32_t)(sb * BKV), smem_desc_sw128(sq + off, 16, 1024),
+                 smem_desc_sw128(sk + off, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
       }
-      __syncwarp();
+      umma_commit_w(&s_full[sb]);
     };
     bool ok = bounded_wait_warp(q_full, 0, DEV_TIMEOUT_ATTN) && bounded_wait_warp(&kv_full[0], 0, DEV_TIMEOUT_ATTN);
     if (ok) {
@@ -172,19 +169,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!bounded_wait_warp(p_full, j & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
       tc_fence_after();
       const uint32_t sv = smem_u32(smem + SMEM_V + st * T_BYTES);
-      if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA: P columns k*8.., V rows k*16.. (atoms TILE_BYTES apart)
-          umma_f16_ts(tmem + O_COL, tmem + (uint32_t)(sb * BKV + k * 8),
-                      smem_desc_sw128(sv + k * 16 * 128, TILE_BYTES, 1024), C::IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(o_full);
-        umma_commit(&kv_empty[st]);
-      }
-      __syncwarp();
+      for (int k = 0; k < BKV / 16; ++k)  // 16 keys per MMA: P columns k*8.., V rows k*16.. (atoms TILE_BYTES apart)
+        umma_f16_ts_w(tmem + O_COL, tmem + (uint32_t)(sb * BKV + k * 8),
+                    smem_desc_sw128(sv + k * 16 * 128, TILE_BYTES, 1024), C::IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
+      umma_commit_w(o_full);
+      umma_commit_w(&kv_empty[st]);
     }
     // TMEM is freed below only after every MMA issued here has retired
-    if (lane == 0) umma_commit(drain);
-    __syncwarp();
+    umma_commit_w(drain);
     bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
   } else {
     // ------------------------------------------------------------ softmax + epilogue (one row per thread)
@@ -475,17 +468,14 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
           return false;
         tc_fence_after();
         const uint32_t sk = smem_u32(smem + C::SMEM_K + st * T_BYTES);
-        if (lane == 0) {
 #pragma unroll
-          for (int kk = 0; kk < DH / 16; ++kk) {
-            const uint32_t off = (uint32_t)((kk >> 2) * TILE_BYTES + (kk & 3) * 32);
-            umma_f16(t_s, smem_desc_sw128(sq + off, 16, 1024), smem_desc_sw128(sk + off, 16, 1024), IDESC_S,
-                     kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[t]);
-          if (j == n - 1) umma_commit(q_empty);  // the tile's Q is no longer read once this retires
+        for (int kk = 0; kk < DH / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * TILE_BYTES + (kk & 3) * 32);
+          umma_f16_w(t_s, smem_desc_sw128(sq + off, 16, 1024), smem_desc_sw128(sk + off, 16, 1024), IDESC_S,
+                   kk > 0 ? 1u : 0u);
         }
-        __syncwarp();
+        umma_commit_w(&s_full[t]);
+        if (j == n - 1) umma_commit_w(q_empty);  // the tile's Q is no longer read once this retires
         return true;
       };
       ok = issue_s(0);
@@ -495,15 +485,12 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
         tc_fence_after();
         const uint32_t st = (g + (uint32_t)j) % KVST;
         const uint32_t sv = smem_u32(smem + C::SMEM_V + st * T_BYTES);
-        if (lane == 0) {
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
-            umma_f16_ts(t_o, t_p + (uint32_t)(kk * 8), smem_desc_sw128(sv + kk * 16 * 128, TILE_BYTES, 1024),
-                        C::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&pv_done[t]);
-          umma_commit(&kv_empty[st]);
-        }
-        __syncwarp();
+        for (int kk = 0; kk < BKV / 16; ++kk)  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
+          umma_f16_ts_w(t_o, t_p + (uint32_t)(kk * 8), smem_desc_sw128(sv + kk * 16 * 128, TILE_BYTES, 1024),
+                      C::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_w(&pv_done[t]);
+        umma_commit_w(&kv_empty[st]);
         if (!C::SEP_P && j + 1 < n && !issue_s(j + 1)) { ok = false; break; }
       }
       if (!ok) break;
@@ -517,8 +504,7 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
       g += (uint32_t)nkv;
     }
     // TMEM is freed below only after every MMA issued here has retired
-    if (lane == 0) umma_commit(drain);
-    __syncwarp();
+    umma_commit_w(drain);
     bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue of tile t
@@ -880,18 +866,15 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       const uint32_t sk = smem_u32(smem + SM_K + (c.k & 1) * TILE_BYTES);
       const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES);
       const uint32_t sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
-      if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          umma_f16(tmem + C_S, smem_desc_sw128(sk + k * 32, 16, 1024), smem_desc_sw128(sq + k * 32, 16, 1024),
+      for (int k = 0; k < D / 16; ++k) {
+        umma_f16_w(tmem + C_S, smem_desc_sw128(sk + k * 32, 16, 1024), smem_desc_sw128(sq + k * 32, 16, 1024),
                    IDESC_SD, k > 0 ? 1u : 0u);
-          umma_f16(tmem + C_DP, smem_desc_sw128(sv + k * 32, 16, 1024), smem_desc_sw128(sdo + k * 32, 16, 1024),
+        umma_f16_w(tmem + C_DP, smem_desc_sw128(sv + k * 32, 16, 1024), smem_desc_sw128(sdo + k * 32, 16, 1024),
                    IDESC_SD, k > 0 ? 1u : 0u);
-        }
-        umma_commit(sd_full);
-        if (c.i == c.un.niter - 1) umma_commit(v_empty);
       }
-      __syncwarp();
+      umma_commit_w(sd_full);
+      if (c.i == c.un.niter - 1) umma_commit_w(v_empty);
       return true;
     };
     Cur cur{0, unit_of(0), 0, 0};
@@ -917,28 +900,24 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       const uint32_t st = cur.n % QST;
       const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
       const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * TILE_BYTES);
-      if (lane == 0) {
-        // dV, dK and dQ are three independent accumulation chains, issued interleaved
+      // dV, dK and dQ are three independent accumulation chains, issued interleaved
 #pragma unroll
-        for (int k = 0; k < BQ / 16; ++k) {  // 16 queries (dV, dK) / 16 keys (dQ) per MMA
-          const uint32_t acc = (cur.i > 0 || k > 0) ? 1u : 0u;
-          umma_f16_ts(tmem + C_DV, tmem + C_P + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
+      for (int k = 0; k < BQ / 16; ++k) {  // 16 queries (dV, dK) / 16 keys (dQ) per MMA
+        const uint32_t acc = (cur.i > 0 || k > 0) ? 1u : 0u;
+        umma_f16_ts_w(tmem + C_DV, tmem + C_P + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
                       IDESC_VK, acc);
-          umma_f16(tmem + C_DK, smem_desc_sw128(sds + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
+        umma_f16_w(tmem + C_DK, smem_desc_sw128(sds + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
                    smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024), IDESC_VK, acc);
-          umma_f16(tmem + C_DQ, smem_desc_sw128(sds + k * 2048, TILE_BYTES, 1024),
+        umma_f16_w(tmem + C_DQ, smem_desc_sw128(sds + k * 2048, TILE_BYTES, 1024),
                    smem_desc_sw128(sk + k * 2048, TILE_BYTES, 1024), IDESC_Q, k > 0 ? 1u : 0u);
-        }
-        umma_commit(mm_done);
-        umma_commit(&q_empty[st]);
-        if (cur.i == cur.un.niter - 1) umma_commit(&k_empty[cur.k & 1]);
       }
-      __syncwarp();
+      umma_commit_w(mm_done);
+      umma_commit_w(&q_empty[st]);
+      if (cur.i == cur.un.niter - 1) umma_commit_w(&k_empty[cur.k & 1]);
       cur = nxt;
     }
     // TMEM is freed below only after every MMA issued here has retired
-    if (lane == 0) umma_commit(drain);
-    __syncwarp();
+    umma_commit_w(drain);
     bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
   } else if (warp >= 4) {
     const int quarter = warp & 3;
@@ -1334,20 +1313,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t sk = smem_u32(smem + SM_K + (c.k & 1) * K_BYTES);
       const uint32_t sq = smem_u32(smem + SM_Q + st * Q_BYTES);
       const uint32_t sdo = smem_u32(smem + SM_DO + st * Q_BYTES);
-      if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {  // 16 head dims per MMA; atoms of 64 dims
-          const uint32_t ka = (uint32_t)((k >> 2) * KATOM + (k & 3) * 32);
-          const uint32_t qa = (uint32_t)((k >> 2) * QATOM + (k & 3) * 32);
-          umma_f16(tmem + C_S, smem_desc_sw128(sk + ka, 16, 1024), smem_desc_sw128(sq + qa, 16, 1024), IDESC_SD,
-                   k > 0 ? 1u : 0u);
-          umma_f16(tmem + C_DP, smem_desc_sw128(sv + ka, 16, 1024), smem_desc_sw128(sdo + qa, 16, 1024), IDESC_SD,
-                   k > 0 ? 1u : 0u);
-        }
-        umma_commit(sd_full);
-        if (c.i == c.un.niter - 1) umma_commit(v_empty);
+      for (int k = 0; k < D / 16; ++k) {  // 16 head dims per MMA; atoms of 64 dims
+        const uint32_t ka = (uint32_t)((k >> 2) * KATOM + (k & 3) * 32);
+        const uint32_t qa = (uint32_t)((k >> 2) * QATOM + (k & 3) * 32);
+        umma_f16_w(tmem + C_S, smem_desc_sw128(sk + ka, 16, 1024), smem_desc_sw128(sq + qa, 16, 1024), IDESC_SD,
+                 k > 0 ? 1u : 0u);
+        umma_f16_w(tmem + C_DP, smem_desc_sw128(sv + ka, 16, 1024), smem_desc_sw128(sdo + qa, 16, 1024), IDESC_SD,
+                 k > 0 ? 1u : 0u);
       }
-      __syncwarp();
+      umma_commit_w(sd_full);
+      if (c.i == c.un.niter - 1) umma_commit_w(v_empty);
       return true;
     };
     Cur cur{0, unit_of(0), 0, 0};
@@ -1368,29 +1344,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t st = cur.n % QST;
       const uint32_t sq = smem_u32(smem + SM_Q + st * Q_BYTES), sdo = smem_u32(smem + SM_DO + st * Q_BYTES);
       const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * K_BYTES);
-      if (lane == 0) {
-        // dQ^T (16 keys per MMA) interleaved with dV and dK (16 queries per MMA)
+      // dQ^T (16 keys per MMA) interleaved with dV and dK (16 queries per MMA)
 #pragma unroll
-        for (int j = 0; j < BKV / 16; ++j) {
-          umma_f16(tmem + C_DQ, smem_desc_sw128(sk + j * 2048, KATOM, 1024), smem_desc_sw128(sds + j * 2048, KATOM, 1024),
-                   IDESC_Q, j > 0 ? 1u : 0u);
-          if (j < BQ / 16) {
-            const uint32_t acc = (cur.i > 0 || j > 0) ? 1u : 0u;
-            umma_f16_ts(tmem + C_DV, tmem + C_P + (uint32_t)(j * 8), smem_desc_sw128(sdo + j * 2048, QATOM, 1024),
-                        IDESC_VK, acc);
-            umma_f16(tmem + C_DK, smem_desc_sw128(sds + j * 32, 16, 1024), smem_desc_sw128(sq + j * 2048, QATOM, 1024),
-                     IDESC_VK, acc);
-          }
+      for (int j = 0; j < BKV / 16; ++j) {
+        umma_f16_w(tmem + C_DQ, smem_desc_sw128(sk + j * 2048, KATOM, 1024), smem_desc_sw128(sds + j * 2048, KATOM, 1024),
+                 IDESC_Q, j > 0 ? 1u : 0u);
+        if (j < BQ / 16) {
+          const uint32_t acc = (cur.i > 0 || j > 0) ? 1u : 0u;
+          umma_f16_ts_w(tmem + C_DV, tmem + C_P + (uint32_t)(j * 8), smem_desc_sw128(sdo + j * 2048, QATOM, 1024),
+                      IDESC_VK, acc);
+          umma_f16_w(tmem + C_DK, smem_desc_sw128(sds + j * 32, 16, 1024), smem_desc_sw128(sq + j * 2048, QATOM, 1024),
+                   IDESC_VK, acc);
         }
-        umma_commit(mm_done);
-        umma_commit(&q_empty[st]);
-        if (cur.i == cur.un.niter - 1) umma_commit(&k_empty[cur.k & 1]);
       }
-      __syncwarp();
+      umma_commit_w(mm_done);
+      umma_commit_w(&q_empty[st]);
+      if (cur.i == cur.un.niter - 1) umma_commit_w(&k_empty[cur.k & 1]);
       cur = nxt;
     }
-    if (lane == 0) umma_commit(drain);
-    __syncwarp();
+    umma_commit_w(drain);
     bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
   } else if (warp >= 4) {
     const int quarter = warp & 3;
