@@ -47,8 +47,9 @@ const char *zl_version(void);
 
 /* ===================================================================== */
 /* Kernel API (fp32), one entry point per reference host launcher.        */
-/* GEMMs with 16-byte aligned rows run on tcgen05 kind::tf32; other       */
-/* shapes use a SIMT fp32 kernel.                                          */
+/* GEMMs whose reduction length is a multiple of 4 run on tcgen05         */
+/* kind::tf32 (MN-major operands through a K-major copy in stream-ordered  */
+/* scratch memory); other shapes use a SIMT fp32 kernel.                   */
 /* ===================================================================== */
 /* src/kernel/cuda/matmul.cuh:20 matmul and :68 matmul_tiled: C[M,N] = A[M,K] B[K,N] */
 zl_status zl_matmul_f32(const float *A, const float *B, float *C, int M, int N, int K, zl_stream stream);

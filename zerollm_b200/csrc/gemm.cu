@@ -1361,16 +1361,47 @@ zl_status gemm_simt_f32(const float* A, const float* B, float* D, int M, int N, 
   return check_launch("gemm_simt_f32");
 }
 
-// fp32 API GEMM: tcgen05 kind::tf32 when both operands are K-major and TMA-compatible,
-// else the SIMT kernel.  (MN-major 32-bit operands need the 32-byte-atom swizzle
-// variant of the shared-memory layout, which this kernel does not implement; with the
-// plain 128-byte swizzle the tensor core returns zeros for them.)
+// fp32 API GEMM on tcgen05 kind::tf32.  The kernel takes K-major operands (the reduction dimension
+// contiguous).  An MN-major operand (B of A·B, both operands of Aᵀ·B) is first transposed into
+// stream-ordered scratch memory (32 x 32 tiles through shared memory) and the K-major product runs
+// on that copy.  (MN-major 32-bit operands would need the 32-byte-atom swizzle variant of the
+// shared-memory layout, which the kernel does not implement; with the plain 128-byte swizzle the
+// tensor core returns zeros for them.)  Without a caller workspace, the split-K partials of products
+// with few output tiles go to the same scratch allocation.  Shapes the tensor-map rules exclude (K
+// not a multiple of 4, so rows are not 16-byte multiples, or unaligned bases) run on the SIMT kernel.
 zl_status gemm_f32(const float* A, const float* B, float* D, int M, int N, int K, int layout, int flags,
                    const zl_epilogue* epi, float* ws, cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error(ZL_EINVAL, "gemm: sizes must be positive");
-  if ((layout & ZL_A_KMAJOR) && (layout & ZL_B_KMAJOR)) {
-    zl_status s = gemm_tc<float>(A, B, D, M, N, K, layout, flags | ZL_EPI_OUT_F32, epi, ws, st);
-    if (s != ZL_EUNSUPPORTED) return s;
+  const bool a_mn = !(layout & ZL_A_KMAJOR), b_mn = !(layout & ZL_B_KMAJOR);
+  if (K % 4 == 0) {
+    const size_t na = a_mn ? (size_t)M * K : 0, nb = b_mn ? (size_t)N * K : 0;
+    // split-K partials for products with few output tiles and a long reduction, when the caller
+    // passes no workspace (the reference-style entry points have none)
+    const size_t nw = ws ? 0 : (size_t)gemm_workspace_floats(M, N, K, ZL_A_KMAJOR | ZL_B_KMAJOR, flags, true);
+    const size_t total = na + nb + nw;
+    float* scratch = nullptr;
+    if (total > 0 && cudaMallocAsync(reinterpret_cast<void**>(&scratch), total * sizeof(float), st) != cudaSuccess) {
+      cudaGetLastError();  // no scratch memory: the SIMT kernel needs none
+      scratch = nullptr;
+    }
+    if (nw > 0 && scratch) ws = scratch + na + nb;
+    if (total == 0 || scratch) {
+      const float* ak = A;
+      const float* bk = B;
+      zl_status s = ZL_OK;
+      if (a_mn) {  // A is stored [K][M]: its K-major copy is [M][K]
+        s = zl_transpose_f32(A, scratch, K, M, st);
+        ak = scratch;
+      }
+      if (s == ZL_OK && b_mn) {  // B is stored [K][N]: its K-major copy is [N][K]
+        s = zl_transpose_f32(B, scratch + na, K, N, st);
+        bk = scratch + na;
+      }
+      if (s == ZL_OK)
+        s = gemm_tc<float>(ak, bk, D, M, N, K, ZL_A_KMAJOR | ZL_B_KMAJOR, flags | ZL_EPI_OUT_F32, epi, ws, st);
+      if (scratch) cudaFreeAsync(scratch, st);
+      if (s != ZL_EUNSUPPORTED) return s;
+    }
   }
   return gemm_simt_f32(A, B, D, M, N, K, layout, flags, epi, st);
 }
