@@ -224,8 +224,11 @@ def test_scaled_config_step_properties():
 
 
 def test_graph_replay_matches_eager():
-    """Steps replayed from the captured CUDA graph equal eagerly launched steps (up to the
-    summation-order freedom of the fp32 atomics in the embedding and dQ accumulation)."""
+    """Steps replayed from the captured CUDA graph equal eagerly launched steps, up to the
+    summation-order freedom of the fp32 atomics (embedding gradient, dQ accumulation, the norm
+    backward's and column sums' block sums into the gradient arena).  That freedom compounds through
+    the AdamW steps: the first losses agree bit for bit, the fourth has been seen 1.2e-5 apart, so the
+    bar is 1e-4; a missing or misordered graph node moves the losses by orders of magnitude more."""
     from zerollm_b200 import ZeroLLM
     c = _cfgs(True)[0]
     B, S = 4, 128
@@ -240,13 +243,15 @@ def test_graph_replay_matches_eager():
         out.append((losses, m.params()))
         m.close()
     (l0, p0), (l1, p1) = out
-    assert np.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
-    assert rel(p1, p0) < 1e-5
+    assert l0[0] == l1[0], (l0, l1)  # the first step sees identical weights
+    assert np.allclose(l0, l1, rtol=1e-4, atol=0), (l0, l1)
+    assert rel(p1, p0) < 1e-4
 
 
 def test_in_step_kernel_timing():
     """With kernel timing on, the captured step carries event nodes around the attention kernels:
-    the step's results are unchanged, and the per-launch times are positive and below the step's."""
+    the step's results are unchanged (up to the atomics' summation order, as in the graph-replay
+    test), and the per-launch times are positive and below the step's."""
     from zerollm_b200 import ZeroLLM, ZLError
     c = _cfgs(True)[0]
     B, S = 4, 128
@@ -272,5 +277,6 @@ def test_in_step_kernel_timing():
         out.append((losses, m.params()))
         m.close()
     (l0, p0), (l1, p1) = out
-    assert np.allclose(l0, l1, rtol=1e-5, atol=0), (l0, l1)
-    assert rel(p1, p0) < 1e-5
+    assert l0[0] == l1[0], (l0, l1)  # the first step sees identical weights
+    assert np.allclose(l0, l1, rtol=1e-4, atol=0), (l0, l1)
+    assert rel(p1, p0) < 1e-4

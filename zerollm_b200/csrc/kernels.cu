@@ -182,6 +182,18 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
   int64_t row = (int64_t)blockIdx.x * warps + w;
   // register path: rows of up to 512 columns prefetch the next row; wider rows would run out of registers
   constexpr bool PREFETCH = STAGES == 0 && kMaxChunks <= 2;
+  // rows of up to 512 columns keep gamma in registers for the whole launch and x-hat, dy * gamma of
+  // the row between the two passes (reloading gamma twice per row cost more L1 traffic than the
+  // row itself); wider rows reload and recompute them
+  constexpr bool KEEP = kMaxChunks <= 2;
+  float gl[KEEP ? kMaxChunks : 1][8];
+  if constexpr (KEEP) {
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < N) load8f(g + col, gl[c]);
+    }
+  }
   uint4 nx[kMaxChunks], nd[kMaxChunks];
   auto fetch = [&](int64_t r) {
 #pragma unroll
@@ -212,10 +224,23 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
     __syncwarp();
   }
   if (PREFETCH && row < M) fetch(row);
+  // the row statistics of this warp's next 32 rows, one per lane (a load per row would put a memory
+  // round trip in front of every row's arithmetic)
+  float mu_l = 0.f, rs_l = 0.f;
+  auto stats = [&](int64_t k0) {
+    const int64_t rr = row + (k0 + lane) * nwarps;
+    if (rr < M) {
+      rs_l = rstd[rr];
+      if (KIND == 0) mu_l = mean[rr];
+    }
+  };
+  stats(0);
   int64_t k = 0;
   for (; row + k * nwarps < M; ++k) {
     const int64_t r = row + k * nwarps;
-    const float mu = KIND == 0 ? mean[r] : 0.f, rs = rstd[r];
+    if (k > 0 && (k & 31) == 0) stats(k);
+    const float mu = KIND == 0 ? __shfl_sync(0xffffffffu, mu_l, (int)(k & 31)) : 0.f;
+    const float rs = __shfl_sync(0xffffffffu, rs_l, (int)(k & 31));
     // keep only the packed row; both passes unpack it again (registers, not arithmetic, limit
     // the resident warps here)
     uint4 cx[kMaxChunks], cd[kMaxChunks];
@@ -240,12 +265,18 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
       if (PREFETCH && r + nwarps < M) fetch(r + nwarps);
     }
     float s1 = 0.f, s2 = 0.f;
+    float xhk[KEEP ? kMaxChunks : 1][8], ak[KEEP ? kMaxChunks : 1][8];
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < N) {
         float gv[8], xv[8], dv[8];
-        load8f(g + col, gv);
+        if constexpr (KEEP) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) gv[j] = gl[c][j];
+        } else {
+          load8f(g + col, gv);
+        }
         unpack8(cx[c], xv);
         unpack8(cd[c], dv);
 #pragma unroll
@@ -256,27 +287,40 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
           s2 += a * xh;
           pg[c][j] += dv[j] * xh;
           if (KIND == 0) pb[c][j] += dv[j];
+          if constexpr (KEEP) {
+            xhk[c][j] = xh;
+            ak[c][j] = a;
+          }
         }
       }
     }
     s1 = warp_sum(s1);
     s2 = warp_sum(s2);
     const float invN = 1.f / (float)N;
+    // dx = rs * (dy*g - s1/N - x-hat * s2/N)  (LayerNorm; RMSNorm has no s1 term)
+    const float c1 = KIND == 0 ? rs * s1 * invN : 0.f, c2 = rs * s2 * invN;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < N) {
-        float gv[8], xv[8], dv[8], o[8];
-        load8f(g + col, gv);
-        unpack8(cx[c], xv);
-        unpack8(cd[c], dv);
+        float o[8];
+        if constexpr (KEEP) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float xh = (xv[j] - mu) * rs;
-          const float a = dv[j] * gv[j];
-          o[j] = KIND == 0 ? rs * (a - s1 * invN - xh * s2 * invN) : rs * (a - xh * s2 * invN);
-          if (COL) pc[c][j] += o[j];
+          for (int j = 0; j < 8; ++j) o[j] = fmaf(-xhk[c][j], c2, fmaf(rs, ak[c][j], -c1));
+        } else {
+          float gv[8], xv[8], dv[8];
+          load8f(g + col, gv);
+          unpack8(cx[c], xv);
+          unpack8(cd[c], dv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float xh = (xv[j] - mu) * rs;
+            o[j] = fmaf(-xh, c2, fmaf(rs, dv[j] * gv[j], -c1));
+          }
         }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (COL) pc[c][j] += o[j];
         store8(dx + r * N + col, o);
       }
     }
