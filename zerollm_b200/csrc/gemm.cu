@@ -820,26 +820,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!bounded_wait_warp(&full[stage], phase, DEV_TIMEOUT_FULL)) { ok = false; break; }
           tc_fence_after();
-          if (lane == 0) {
-            const uint32_t a_base = smem_u32(smem + stage * L::STAGE_BYTES);
-            const uint32_t b_base = a_base + L::A_BYTES;
+          const uint32_t a_base = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t b_base = a_base + L::A_BYTES;
 #pragma unroll
-            for (int k = 0; k < BK / UMMA_K; ++k) {
-              uint64_t ad, bd;
-              if (!A_MN) ad = smem_desc_sw128(a_base + k * UMMA_K * 2, 16, 1024);
-              else       ad = smem_desc_sw128(a_base + k * UMMA_K * 128, BK * 128, 1024);
-              if (!B_MN) bd = smem_desc_sw128(b_base + k * UMMA_K * 2, 16, 1024);
-              else       bd = smem_desc_sw128(b_base + k * UMMA_K * 128, BK * 128, 1024);
-              umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
-            }
-            umma_commit_pair(&empty[stage], 0x3);
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            uint64_t ad, bd;
+            if (!A_MN) ad = smem_desc_sw128(a_base + k * UMMA_K * 2, 16, 1024);
+            else       ad = smem_desc_sw128(a_base + k * UMMA_K * 128, BK * 128, 1024);
+            if (!B_MN) bd = smem_desc_sw128(b_base + k * UMMA_K * 2, 16, 1024);
+            else       bd = smem_desc_sw128(b_base + k * UMMA_K * 128, BK * 128, 1024);
+            umma_f16_pair_w(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          __syncwarp();
+          umma_commit_pair_w(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        if (lane == 0) umma_commit_pair(&acc_full[acc], 0x3);
-        __syncwarp();
+        umma_commit_pair_w(&acc_full[acc], 0x3);
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
     }
