@@ -196,18 +196,21 @@ def test_linear_api(K):
 
 
 # ------------------------------------------------------------------ attention
-@pytest.mark.parametrize("kernel", ["tc", "tc_pp", "mma"])
+@pytest.mark.parametrize("kernel", ["tc", "tc_pp", "tc_r0", "mma"])
 @pytest.mark.parametrize("B,S,H,Dh", [(2, 128, 2, 64), (1, 200, 3, 64), (2, 512, 4, 64), (1, 1024, 2, 64),
                                       (2, 384, 2, 64), (2, 256, 2, 128), (1, 1024, 2, 128), (1, 200, 1, 128)])
 def test_attention_bf16_vs_oracle(L, B, S, H, Dh, kernel, monkeypatch):
     """Flash attention fwd+bwd against the oracle.  "tc" runs the one-tile tcgen05
     forward where the shape allows (S % 128 == 0) and mma.sync otherwise; "tc_pp" the
-    persistent two-tile forward where S % 256 == 0; "mma" forces the mma.sync kernels."""
+    persistent two-tile forward where S % 256 == 0; "tc_r0" the head-dim-64 tcgen05 backward
+    with the softmax warps doing the TMEM readout (ZL_ATTN_BWD_READOUT=0) instead of the
+    dedicated warpgroup; "mma" forces the mma.sync kernels."""
     if kernel == "mma":
         monkeypatch.setenv("ZL_ATTENTION_KERNEL", "mma")
     else:
         monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
         monkeypatch.setenv("ZL_ATTN_FWD_PP", "1" if kernel == "tc_pp" else "0")
+        monkeypatch.setenv("ZL_ATTN_BWD_READOUT", "0" if kernel == "tc_r0" else "1")
     _attention_vs_oracle(L, B, S, H, Dh)
 
 
@@ -310,6 +313,40 @@ def test_attention_bwd_rope_tcgen05_vs_mma(L, B, S, H, Dh, monkeypatch):
     for part in range(3):
         sl = slice(part * E, (part + 1) * E)
         assert rel(g_tc[:, sl], g_mma[:, sl]) < BF16_TOL, part
+
+
+@pytest.mark.parametrize("B,S,H", [(16, 2048, 8), (3, 1536, 5), (2, 256, 4)])
+@pytest.mark.parametrize("rope", [False, True])
+def test_attention_bwd_readout_forms_agree(L, B, S, H, rope, monkeypatch):
+    """The head-dim-64 tcgen05 backward in its two forms: TMEM readout by a dedicated warpgroup
+    (the default) and by the softmax warps (ZL_ATTN_BWD_READOUT=0).  Both issue the same products
+    in the same order, so dK and dV agree bit for bit; dQ's blocks are added into the fp32
+    accumulator from several CTAs in no fixed order, so dQ agrees to the rounding of that order."""
+    monkeypatch.delenv("ZL_ATTENTION_KERNEL", raising=False)
+    Dh = 64
+    E, T = H * Dh, B * S
+    gen = torch.Generator(device="cuda").manual_seed(B * 1000 + S)
+    qkv_d = (torch.randn(T * 3 * E, device="cuda", generator=gen) * 0.5).bfloat16()
+    dO_d = torch.randn(T * E, device="cuda", generator=gen).bfloat16()
+    if rope:
+        c, s_ = O.rope_table(S, Dh)
+        cos_d, sin_d = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+    o = torch.empty(T * E, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * H * S, device="cuda")
+    L.call("zl_attention_forward_bf16", qkv_d.data_ptr(), o.data_ptr(), lse.data_ptr(), B, S, H, Dh, None)
+    out = []
+    for form in ("1", "0"):
+        monkeypatch.setenv("ZL_ATTN_BWD_READOUT", form)
+        dqkv = torch.full((T * 3 * E,), float("nan"), device="cuda", dtype=torch.bfloat16)
+        ws = torch.empty(L.load().zl_attention_workspace_floats(B, S, H, Dh), device="cuda")
+        L.call("zl_attention_backward_bf16", qkv_d.data_ptr(), o.data_ptr(), dO_d.data_ptr(), lse.data_ptr(),
+               dqkv.data_ptr(), ws.data_ptr(), B, S, H, Dh, cos_d.data_ptr() if rope else None,
+               sin_d.data_ptr() if rope else None, None)
+        torch.cuda.synchronize()
+        out.append(dqkv.view(T, 3 * E))
+    assert torch.isfinite(out[0].float()).all()
+    assert torch.equal(out[0][:, E:], out[1][:, E:])  # dK, dV
+    assert rel(out[0][:, :E].float().cpu(), out[1][:, :E].float().cpu()) < 1e-2  # dQ
 
 
 @pytest.mark.parametrize("ref_sem", [True, False])

@@ -226,12 +226,19 @@ def test_scaled_config_step_properties():
 def test_graph_replay_matches_eager():
     """Steps replayed from the captured CUDA graph equal eagerly launched steps, up to the
     summation-order freedom of the fp32 atomics (embedding gradient, dQ accumulation, the norm
-    backward's and column sums' block sums into the gradient arena).  That freedom compounds through
-    the AdamW steps: the first losses agree bit for bit, the fourth has been seen 1.2e-5 apart, so the
-    bar is 1e-4; a missing or misordered graph node moves the losses by orders of magnitude more."""
+    backward's and column sums' block sums into the gradient arena).
+    - The gradients of the first step are compared directly (normwise 1e-4; the atomics' order
+      moves them by ~1e-6).
+    - The losses of four AdamW steps: the first agree bit for bit, the fourth has been seen 1.2e-5
+      apart, so the bar is 1e-4.
+    - The weights after four steps: AdamW normalises each update to about lr, so a weight whose
+      gradient sums to nearly zero can take a different update in the two runs from rounding alone
+      (measured up to 0.07 lr).  The bar is 0.25 lr per weight; a missing or misordered graph node
+      moves the losses, the first step's gradients and many weights by orders of magnitude more."""
     from zerollm_b200 import ZeroLLM
     c = _cfgs(True)[0]
     B, S = 4, 128
+    lr = 1e-3
     inp, tgt = _batch(B, S, c.vocab_size, 7)
     ids, tg = torch.from_numpy(inp).cuda(), torch.from_numpy(tgt).cuda()
     out = []
@@ -239,13 +246,16 @@ def test_graph_replay_matches_eager():
         m = ZeroLLM(c, B * S, seed=0)
         m.set_optimizer()
         m.set_graph(graph)
-        losses = [m.train_step(ids, tg, B, S, lr=1e-3).item() for _ in range(4)]
-        out.append((losses, m.params()))
+        m.train_step(ids, tg, B, S, lr=lr, update=False)
+        g = m.grads().copy()
+        losses = [m.train_step(ids, tg, B, S, lr=lr).item() for _ in range(4)]
+        out.append((g, losses, m.params()))
         m.close()
-    (l0, p0), (l1, p1) = out
+    (g0, l0, p0), (g1, l1, p1) = out
+    assert rel(g1, g0) < 1e-4
     assert l0[0] == l1[0], (l0, l1)  # the first step sees identical weights
     assert np.allclose(l0, l1, rtol=1e-4, atol=0), (l0, l1)
-    assert rel(p1, p0) < 1e-4
+    assert np.max(np.abs(p1.astype(np.float64) - p0)) < 0.25 * lr
 
 
 def test_in_step_kernel_timing():
@@ -279,4 +289,4 @@ def test_in_step_kernel_timing():
     (l0, p0), (l1, p1) = out
     assert l0[0] == l1[0], (l0, l1)  # the first step sees identical weights
     assert np.allclose(l0, l1, rtol=1e-4, atol=0), (l0, l1)
-    assert rel(p1, p0) < 1e-4
+    assert np.max(np.abs(p1.astype(np.float64) - p0)) < 0.25 * 1e-3  # a quarter of AdamW's step, lr = 1e-3

@@ -672,6 +672,16 @@ constexpr int NSOFT = 8;
 // per warpgroup, so the two idle warps cost none; moving registers from warpgroup 0 to the softmax
 // warps with setmaxnreg measured slower.)
 constexpr int THREADS_B = 128 + 32 * NSOFT;
+// With a dedicated readout warpgroup (the kernel's DQW form), warps 12-15 take every TMEM readout
+// off the softmax warps: each block's dQ (staged and added into the fp32 accumulator) and a finished
+// unit's dK / dV (stored as bf16), one TMEM lane quadrant per warp.  The softmax warps then only
+// compute and write P^T / dS^T.  The 512 threads launch at 128 registers each (65,536 per block);
+// warpgroup 0 and the readout warpgroup give registers up with setmaxnreg and the two softmax
+// warpgroups take them, and the four shares add up to the launch total.
+constexpr int THREADS_BQ = 512;
+constexpr int REG_WG0 = 96, REG_SOFT = 160, REG_OUT = 96;
+// (registers per warpgroup share x 128 threads) summed == 128 registers per thread x 512 threads
+static_assert((REG_WG0 + 2 * REG_SOFT + REG_OUT) * 128 == 128 * THREADS_BQ, "register shares = launch total");
 constexpr int WPQ = NSOFT / 4;              // softmax warps per TMEM lane quadrant
 constexpr int QCOLS = BQ / WPQ;             // query columns (of S^T / dP^T) per softmax warp
 constexpr int DCOLS = D / WPQ;              // head-dim columns (of dQ / dK / dV) per softmax warp
@@ -713,7 +723,8 @@ template <int N> __device__ __forceinline__ void tmem_st_n(uint32_t taddr, const
   else tmem_st16(taddr, r);
 }
 
-__global__ void __launch_bounds__(THREADS_B, 1)
+template <bool DQW>
+__global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
@@ -768,10 +779,10 @@ __global__ void __launch_bounds__(THREADS_B, 1)
     mbar_init(sd_full, 1);
     mbar_init(ds_ready, 32 * NSOFT);
     mbar_init(mm_done, 1);
-    mbar_init(dq_free, 32 * NSOFT);
+    mbar_init(dq_free, DQW ? 128 : 32 * NSOFT);
     mbar_init(drain, 1);
     mbar_init(sd_used, 32 * NSOFT);
-    mbar_init(dkv_free, 32 * NSOFT);
+    mbar_init(dkv_free, DQW ? 128 : 32 * NSOFT);
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
@@ -790,136 +801,143 @@ __global__ void __launch_bounds__(THREADS_B, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    // Per unit: K into buffer k & 1 (once the unit two back has finished with it), then the unit's
-    // first Q / dO / row-vector stage, then V (once the previous unit's last dP^T has read the single
-    // V buffer), then the remaining stages.  This is the order in which the slots drain.
-    if (lane == 0) {
-      uint32_t n = 0, nkl = 0, nvl = 0;  // Q stages, K and V tiles issued
-      bool ok = true;
-      for (int k = 0; ok; ++k) {
-        const Unit un = unit_of(k);
-        if (un.niter == 0) break;
-        const int b = un.bh / H, h = un.bh % H;
-        const int krow = b * S + un.kb * BKV;
-        const size_t row_base = (size_t)un.bh * S;
-        const int kbuf = k & 1;
-        if (!bounded_wait(&k_empty[kbuf], ((k >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
-        mbar_arrive_expect_tx(&k_full[kbuf], TILE_BYTES);
-        tma_load_2d(smem + SM_K + kbuf * TILE_BYTES, &tm_k, &k_full[kbuf], h * D, krow);
-        ++nkl;
-        for (int i = 0; i < un.niter; ++i, ++n) {
-          const uint32_t st = n % QST;
-          if (!bounded_wait(&q_empty[st], ((n / QST) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-          mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES + VEC_BYTES);
-          const int qb = un.kb + i;
-          const int qrow = b * S + qb * BQ;
-          tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_q, &q_full[st], h * D, qrow);
-          tma_load_2d(smem + SM_DO + st * TILE_BYTES, &tm_do, &q_full[st], h * D, qrow);
-          float* vec = reinterpret_cast<float*>(smem + SM_VEC + st * VEC_BYTES);
-          bulk_load(vec, nl_g + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
-          bulk_load(vec + BQ, Dsum + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
-          if (i == 0) {
-            if (!bounded_wait(v_empty, (k & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; ++n; break; }
-            mbar_arrive_expect_tx(v_full, TILE_BYTES);
-            tma_load_2d(smem + SM_V, &tm_v, v_full, h * D, krow);
-            ++nvl;
+  // Roles by warpgroup; in the DQW form each warpgroup first takes its register share (one
+  // setmaxnreg per warpgroup, inside its own branch, so no other role's values are live across it).
+  if (warp < 4) {
+    if constexpr (DQW) setmaxnreg_dec<REG_WG0>();
+    if (warp == 0) {
+      // ------------------------------------------------------------ TMA producer
+      // Per unit: K into buffer k & 1 (once the unit two back has finished with it), then the unit's
+      // first Q / dO / row-vector stage, then V (once the previous unit's last dP^T has read the single
+      // V buffer), then the remaining stages.  This is the order in which the slots drain.
+      if (lane == 0) {
+        uint32_t n = 0, nkl = 0, nvl = 0;  // Q stages, K and V tiles issued
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+          const Unit un = unit_of(k);
+          if (un.niter == 0) break;
+          const int b = un.bh / H, h = un.bh % H;
+          const int krow = b * S + un.kb * BKV;
+          const size_t row_base = (size_t)un.bh * S;
+          const int kbuf = k & 1;
+          if (!bounded_wait(&k_empty[kbuf], ((k >> 1) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) break;
+          mbar_arrive_expect_tx(&k_full[kbuf], TILE_BYTES);
+          tma_load_2d(smem + SM_K + kbuf * TILE_BYTES, &tm_k, &k_full[kbuf], h * D, krow);
+          ++nkl;
+          for (int i = 0; i < un.niter; ++i, ++n) {
+            const uint32_t st = n % QST;
+            if (!bounded_wait(&q_empty[st], ((n / QST) & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+            mbar_arrive_expect_tx(&q_full[st], 2 * TILE_BYTES + VEC_BYTES);
+            const int qb = un.kb + i;
+            const int qrow = b * S + qb * BQ;
+            tma_load_2d(smem + SM_Q + st * TILE_BYTES, &tm_q, &q_full[st], h * D, qrow);
+            tma_load_2d(smem + SM_DO + st * TILE_BYTES, &tm_do, &q_full[st], h * D, qrow);
+            float* vec = reinterpret_cast<float*>(smem + SM_VEC + st * VEC_BYTES);
+            bulk_load(vec, nl_g + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
+            bulk_load(vec + BQ, Dsum + row_base + (size_t)qb * BQ, BQ * 4, &q_full[st]);
+            if (i == 0) {
+              if (!bounded_wait(v_empty, (k & 1) ^ 1u, DEV_TIMEOUT_ATTN)) { ok = false; ++n; break; }
+              mbar_arrive_expect_tx(v_full, TILE_BYTES);
+              tma_load_2d(smem + SM_V, &tm_v, v_full, h * D, krow);
+              ++nvl;
+            }
           }
         }
+        // no copy may still be landing in shared memory when the CTA exits: the last load of every
+        // slot has completed (the consumers waited for all of them on the normal path)
+        for (uint32_t k = nkl > 2u ? nkl - 2 : 0; k < nkl; ++k)
+          bounded_wait(&k_full[k & 1], (k >> 1) & 1, DEV_TIMEOUT_ATTN);
+        if (nvl > 0) bounded_wait(v_full, (nvl - 1) & 1, DEV_TIMEOUT_ATTN);
+        for (uint32_t j = n > (uint32_t)QST ? n - QST : 0; j < n; ++j)
+          bounded_wait(&q_full[j % QST], (j / QST) & 1, DEV_TIMEOUT_ATTN);
       }
-      // no copy may still be landing in shared memory when the CTA exits: the last load of every
-      // slot has completed (the consumers waited for all of them on the normal path)
-      for (uint32_t k = nkl > 2u ? nkl - 2 : 0; k < nkl; ++k)
-        bounded_wait(&k_full[k & 1], (k >> 1) & 1, DEV_TIMEOUT_ATTN);
-      if (nvl > 0) bounded_wait(v_full, (nvl - 1) & 1, DEV_TIMEOUT_ATTN);
-      for (uint32_t j = n > (uint32_t)QST ? n - QST : 0; j < n; ++j)
-        bounded_wait(&q_full[j % QST], (j / QST) & 1, DEV_TIMEOUT_ATTN);
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
+      struct Cur {
+        int k;      // unit of this CTA
+        Unit un;
+        int i;      // query block inside the unit (query block kb + i)
+        uint32_t n; // block of the CTA's flat sequence
+      };
+      auto advance = [&](Cur c) -> Cur {
+        if (++c.i == c.un.niter) {
+          ++c.k;
+          c.un = unit_of(c.k);
+          c.i = 0;
+        }
+        ++c.n;
+        return c;
+      };
+      // S^T / dP^T of block c -> sd_full; the unit's last one also releases V
+      auto issue_sd = [&](const Cur& c) -> bool {
+        const uint32_t st = c.n % QST;
+        if (!bounded_wait_warp(&q_full[st], (c.n / QST) & 1, DEV_TIMEOUT_ATTN)) return false;
+        if (c.i == 0) {
+          if (!bounded_wait_warp(&k_full[c.k & 1], (c.k >> 1) & 1, DEV_TIMEOUT_ATTN)) return false;
+          if (!bounded_wait_warp(v_full, c.k & 1, DEV_TIMEOUT_ATTN)) return false;
+        }
+        tc_fence_after();
+        const uint32_t sk = smem_u32(smem + SM_K + (c.k & 1) * TILE_BYTES);
+        const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES);
+        const uint32_t sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
+  #pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          umma_f16_w(tmem + C_S, smem_desc_sw128(sk + k * 32, 16, 1024), smem_desc_sw128(sq + k * 32, 16, 1024),
+                     IDESC_SD, k > 0 ? 1u : 0u);
+          umma_f16_w(tmem + C_DP, smem_desc_sw128(sv + k * 32, 16, 1024), smem_desc_sw128(sdo + k * 32, 16, 1024),
+                     IDESC_SD, k > 0 ? 1u : 0u);
+        }
+        umma_commit_w(sd_full);
+        if (c.i == c.un.niter - 1) umma_commit_w(v_empty);
+        return true;
+      };
+      Cur cur{0, unit_of(0), 0, 0};
+      bool ok = cur.un.niter > 0 && issue_sd(cur);
+      while (ok && cur.un.niter > 0) {
+        const Cur nxt = advance(cur);
+        if (nxt.un.niter > 0) {
+          // the softmax warps hold S^T / dP^T of this block in registers: the next block (of this
+          // unit or the next) can overwrite them
+          if (!bounded_wait_warp(sd_used, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+          if (!issue_sd(nxt)) { ok = false; break; }
+        }
+        // softmax of this block is done: P^T (TMEM) and dS^T (smem) are ready
+        if (!bounded_wait_warp(ds_ready, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        // a unit's first dV / dK products overwrite the accumulators: the previous unit's must be read
+        if (cur.i == 0 && cur.k > 0 && !bounded_wait_warp(dkv_free, (cur.k - 1) & 1, DEV_TIMEOUT_ATTN)) {
+          ok = false;
+          break;
+        }
+        // dQ of the previous block has been read out of TMEM
+        if (cur.n > 0 && !bounded_wait_warp(dq_free, (cur.n - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = cur.n % QST;
+        const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
+        const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * TILE_BYTES);
+        // dV, dK and dQ are three independent accumulation chains, issued interleaved
+  #pragma unroll
+        for (int k = 0; k < BQ / 16; ++k) {  // 16 queries (dV, dK) / 16 keys (dQ) per MMA
+          const uint32_t acc = (cur.i > 0 || k > 0) ? 1u : 0u;
+          umma_f16_ts_w(tmem + C_DV, tmem + C_P + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
+                        IDESC_VK, acc);
+          umma_f16_w(tmem + C_DK, smem_desc_sw128(sds + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
+                     smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024), IDESC_VK, acc);
+          umma_f16_w(tmem + C_DQ, smem_desc_sw128(sds + k * 2048, TILE_BYTES, 1024),
+                     smem_desc_sw128(sk + k * 2048, TILE_BYTES, 1024), IDESC_Q, k > 0 ? 1u : 0u);
+        }
+        umma_commit_w(mm_done);
+        umma_commit_w(&q_empty[st]);
+        if (cur.i == cur.un.niter - 1) umma_commit_w(&k_empty[cur.k & 1]);
+        cur = nxt;
+      }
+      // TMEM is freed below only after every MMA issued here has retired
+      umma_commit_w(drain);
+      bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    const uint32_t sv = smem_u32(smem + SM_V), sds = smem_u32(smem + SM_DS);
-    struct Cur {
-      int k;      // unit of this CTA
-      Unit un;
-      int i;      // query block inside the unit (query block kb + i)
-      uint32_t n; // block of the CTA's flat sequence
-    };
-    auto advance = [&](Cur c) -> Cur {
-      if (++c.i == c.un.niter) {
-        ++c.k;
-        c.un = unit_of(c.k);
-        c.i = 0;
-      }
-      ++c.n;
-      return c;
-    };
-    // S^T / dP^T of block c -> sd_full; the unit's last one also releases V
-    auto issue_sd = [&](const Cur& c) -> bool {
-      const uint32_t st = c.n % QST;
-      if (!bounded_wait_warp(&q_full[st], (c.n / QST) & 1, DEV_TIMEOUT_ATTN)) return false;
-      if (c.i == 0) {
-        if (!bounded_wait_warp(&k_full[c.k & 1], (c.k >> 1) & 1, DEV_TIMEOUT_ATTN)) return false;
-        if (!bounded_wait_warp(v_full, c.k & 1, DEV_TIMEOUT_ATTN)) return false;
-      }
-      tc_fence_after();
-      const uint32_t sk = smem_u32(smem + SM_K + (c.k & 1) * TILE_BYTES);
-      const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES);
-      const uint32_t sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
-#pragma unroll
-      for (int k = 0; k < D / 16; ++k) {
-        umma_f16_w(tmem + C_S, smem_desc_sw128(sk + k * 32, 16, 1024), smem_desc_sw128(sq + k * 32, 16, 1024),
-                   IDESC_SD, k > 0 ? 1u : 0u);
-        umma_f16_w(tmem + C_DP, smem_desc_sw128(sv + k * 32, 16, 1024), smem_desc_sw128(sdo + k * 32, 16, 1024),
-                   IDESC_SD, k > 0 ? 1u : 0u);
-      }
-      umma_commit_w(sd_full);
-      if (c.i == c.un.niter - 1) umma_commit_w(v_empty);
-      return true;
-    };
-    Cur cur{0, unit_of(0), 0, 0};
-    bool ok = cur.un.niter > 0 && issue_sd(cur);
-    while (ok && cur.un.niter > 0) {
-      const Cur nxt = advance(cur);
-      if (nxt.un.niter > 0) {
-        // the softmax warps hold S^T / dP^T of this block in registers: the next block (of this
-        // unit or the next) can overwrite them
-        if (!bounded_wait_warp(sd_used, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-        if (!issue_sd(nxt)) { ok = false; break; }
-      }
-      // softmax of this block is done: P^T (TMEM) and dS^T (smem) are ready
-      if (!bounded_wait_warp(ds_ready, cur.n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-      // a unit's first dV / dK products overwrite the accumulators: the previous unit's must be read
-      if (cur.i == 0 && cur.k > 0 && !bounded_wait_warp(dkv_free, (cur.k - 1) & 1, DEV_TIMEOUT_ATTN)) {
-        ok = false;
-        break;
-      }
-      // dQ of the previous block has been read out of TMEM
-      if (cur.n > 0 && !bounded_wait_warp(dq_free, (cur.n - 1) & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t st = cur.n % QST;
-      const uint32_t sq = smem_u32(smem + SM_Q + st * TILE_BYTES), sdo = smem_u32(smem + SM_DO + st * TILE_BYTES);
-      const uint32_t sk = smem_u32(smem + SM_K + (cur.k & 1) * TILE_BYTES);
-      // dV, dK and dQ are three independent accumulation chains, issued interleaved
-#pragma unroll
-      for (int k = 0; k < BQ / 16; ++k) {  // 16 queries (dV, dK) / 16 keys (dQ) per MMA
-        const uint32_t acc = (cur.i > 0 || k > 0) ? 1u : 0u;
-        umma_f16_ts_w(tmem + C_DV, tmem + C_P + (uint32_t)(k * 8), smem_desc_sw128(sdo + k * 2048, TILE_BYTES, 1024),
-                      IDESC_VK, acc);
-        umma_f16_w(tmem + C_DK, smem_desc_sw128(sds + (k >> 2) * TILE_BYTES + (k & 3) * 32, 16, 1024),
-                   smem_desc_sw128(sq + k * 2048, TILE_BYTES, 1024), IDESC_VK, acc);
-        umma_f16_w(tmem + C_DQ, smem_desc_sw128(sds + k * 2048, TILE_BYTES, 1024),
-                   smem_desc_sw128(sk + k * 2048, TILE_BYTES, 1024), IDESC_Q, k > 0 ? 1u : 0u);
-      }
-      umma_commit_w(mm_done);
-      umma_commit_w(&q_empty[st]);
-      if (cur.i == cur.un.niter - 1) umma_commit_w(&k_empty[cur.k & 1]);
-      cur = nxt;
-    }
-    // TMEM is freed below only after every MMA issued here has retired
-    umma_commit_w(drain);
-    bounded_wait_warp(drain, 0, DEV_TIMEOUT_ATTN);
-  } else if (warp >= 4) {
+  } else if (warp < 12) {
+    // ------------------------------------------------------------ softmax (P^T, dS^T)
+    if constexpr (DQW) setmaxnreg_inc<REG_SOFT>();
     const int quarter = warp & 3;
     const int cs = (warp - 4) >> 2;               // column slice: queries [QCOLS*cs, +QCOLS), head dims [DCOLS*cs, +DCOLS)
     const int r_local = quarter * 32 + lane;      // key row (S^T / dP^T / dV / dK) and query row (dQ)
@@ -1096,7 +1114,7 @@ __global__ void __launch_bounds__(THREADS_B, 1)
             mbar_arrive(ds_ready);
           }
         }
-        if (ok && n > 0) {
+        if (!DQW && ok && n > 0) {
           // the previous block's dQ; at a unit's first block, also the previous unit's dK / dV (the
           // MMA warp waits for both before this block's products)
           if (i > 0) {
@@ -1112,7 +1130,118 @@ __global__ void __launch_bounds__(THREADS_B, 1)
       pu = un;
       if (!ok) break;
     }
-    if (n > 0 && ok && bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN)) unit_out(pu, prev_y);
+    if constexpr (!DQW) {
+      if (n > 0 && ok && bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN)) unit_out(pu, prev_y);
+      if (lane == 0) bulk_wait0();  // every dQ reduction and dK / dV store of this warp has landed
+    }
+  } else if constexpr (DQW) {
+    // ------------------------------------------------------------ TMEM readout (DQW form)
+    setmaxnreg_dec<REG_OUT>();
+    // Warp 12 + q reads TMEM lanes [32 q, 32 q + 32): after each block's products, the block's dQ rows
+    // (all 64 head dims) go through two [32][32] fp32 boxes (128-byte swizzle) into the accumulator by
+    // TMA reduce-add; after a unit's last block, its dK (times the softmax scale, rotated back by RoPE
+    // when tables are given) and dV rows leave as four [32][32] bf16 boxes (64-byte swizzle) by TMA
+    // store.  dq_free / dkv_free are arrived as soon as the TMEM columns have been read.
+    const int quarter = warp & 3;
+    const int r_local = quarter * 32 + lane;  // query row of dQ, key row of dK / dV
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t stg = smem_u32(smem + SM_DQ) + (uint32_t)(quarter * 8192);  // this warp's 8 KB
+    auto stage_free = [&]() {  // the warp's last bulk copy has read the staging area
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
+    };
+    bool ok = true;
+    uint32_t n = 0;
+    for (int ku = 0; ok; ++ku) {
+      const Unit un = unit_of(ku);
+      if (un.niter == 0) break;
+      const int b = un.bh / H, hd = un.bh % H;
+      for (int i = 0; i < un.niter; ++i, ++n) {
+        if (!bounded_wait_warp(mm_done, n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int part = 0; part < 4; ++part) {  // head dims [16 part, 16 part + 16)
+          uint32_t dq[16];
+          tmem_ld16(t_lane + C_DQ + (uint32_t)(part * 16), dq);
+          tmem_ld_wait();
+          if (part == 3) {
+            tc_fence_before();
+            mbar_arrive(dq_free);
+          }
+          if (part == 0) stage_free();
+          // box part / 2 ([32 rows][32 dims] fp32, 128-byte swizzle), 16-byte chunks 4 (part & 1) ..
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int k = (part & 1) * 4 + j;
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};"
+                         ::"r"(stg + (uint32_t)((part >> 1) * 4096 + lane * 128 + ((k ^ (lane & 7)) << 4))),
+                         "r"(dq[j * 4]), "r"(dq[j * 4 + 1]), "r"(dq[j * 4 + 2]), "r"(dq[j * 4 + 3]));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int y = (int)((size_t)un.bh * S + (size_t)(un.kb + i) * BQ) + quarter * 32;
+          tma_reduce_add_2d_bulk(&tm_dq, stg, 0, y);
+          tma_reduce_add_2d_bulk(&tm_dq, stg + 4096, 32, y);
+          bulk_commit();
+        }
+        if (i == un.niter - 1) {
+          const int key = un.kb * BKV + r_local;  // position of this thread's key
+#pragma unroll
+          for (int part = 0; part < 8; ++part) {  // 16 dims at a time: dK dims [0,64), then dV
+            const bool is_k = part < 4;
+            const int c0 = (part & 3) * 16;
+            uint32_t x[16];
+            tmem_ld16(t_lane + (is_k ? C_DK : C_DV) + (uint32_t)c0, x);
+            tmem_ld_wait();
+            if (part == 7) {
+              tc_fence_before();
+              mbar_arrive(dkv_free);
+            }
+            if (part == 0) stage_free();  // the dQ reduce-adds above have read the staging area
+            // [32 rows][32 dims] boxes: dK [0,32) at +0, dK [32,64) at +2048, dV likewise at +4096
+            const uint32_t box = stg + (uint32_t)((part >> 1) * 2048);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {  // 8 dims per 16-byte chunk
+              const int q = (part & 1) * 2 + h2;  // chunk inside the 32-dim box
+              float v[8];
+#pragma unroll
+              for (int t = 0; t < 8; ++t) v[t] = __uint_as_float(x[h2 * 8 + t]);
+              if (is_k) {
+#pragma unroll
+                for (int t = 0; t < 8; ++t) v[t] *= scale;
+                if (rope_cos) {  // the 4 rotation pairs of these 8 dims: one 16-byte load each
+                  const size_t pr = (size_t)key * (D / 2) + ((c0 + h2 * 8) >> 1);
+                  const float4 c4 = __ldg(reinterpret_cast<const float4*>(rope_cos + pr));
+                  const float4 s4 = __ldg(reinterpret_cast<const float4*>(rope_sin + pr));
+                  const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                  for (int t = 0; t < 4; ++t) {
+                    const float a0 = v[2 * t], a1 = v[2 * t + 1];
+                    v[2 * t] = a0 * cc[t] + a1 * ss[t];
+                    v[2 * t + 1] = -a0 * ss[t] + a1 * cc[t];
+                  }
+                }
+              }
+              const uint32_t off = (uint32_t)(lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
+              asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(box + off), "r"(pack_bf16(v[0], v[1])),
+                           "r"(pack_bf16(v[2], v[3])), "r"(pack_bf16(v[4], v[5])), "r"(pack_bf16(v[6], v[7])));
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int y0 = b * S + un.kb * BKV + quarter * 32;
+            tma_store_2d_bulk(&tm_dk, stg, hd * D, y0);
+            tma_store_2d_bulk(&tm_dk, stg + 2048, hd * D + 32, y0);
+            tma_store_2d_bulk(&tm_dv, stg + 4096, hd * D, y0);
+            tma_store_2d_bulk(&tm_dv, stg + 6144, hd * D + 32, y0);
+            bulk_commit();
+          }
+        }
+      }
+    }
     if (lane == 0) bulk_wait0();  // every dQ reduction and dK / dV store of this warp has landed
   }
 
@@ -1642,6 +1771,13 @@ bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, c
   return fa_bwd_tc_supported3(qkv, qkv, qkv, 8, d_o, dq_acc, d_qkv, d_qkv, 8, S, Dh);
 }
 
+// Head-dim-64 backward form: a dedicated TMEM-readout warpgroup (512 threads) unless
+// ZL_ATTN_BWD_READOUT=0 selects the form whose softmax warps read dQ / dK / dV out themselves.
+static bool attn_bwd_readout_warps() {
+  const char* f = getenv("ZL_ATTN_BWD_READOUT");
+  return f ? f[0] != '0' : true;
+}
+
 // Backward main pass.  Before it the caller's pre pass writes nl = -lse*log2(e) and D = rowsum(dO*O)
 // ([B, H, S]) and zeroes dq_acc; after it the post pass turns dq_acc ([B, H, S, Dh] fp32) into dQ.
 // dK is multiplied by `dk_scale` (the softmax scale; 1 for the reference's unscaled gradient).
@@ -1679,11 +1815,19 @@ zl_status fa_bwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, cons
       !make_tma_map(&tdq, dq_acc, true, (uint64_t)Dh, (uint64_t)B * H * S, 32, 32) ||
       !bf16_view_map(&tdk, dk, E, T, ld_out, 32, 32, 64) || !bf16_view_map(&tdv, dv, E, T, ld_out, 32, 32, 64))
     return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
-  cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       fatc::bwd::SMEM_TOTAL);
-  fatc::bwd::fa_bwd_tc_kernel<<<grid, fatc::bwd::THREADS_B, fatc::bwd::SMEM_TOTAL, st>>>(
-      tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
-      scale * 1.4426950408889634f);
+  if (attn_bwd_readout_warps()) {
+    cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         fatc::bwd::SMEM_TOTAL);
+    fatc::bwd::fa_bwd_tc_kernel<true><<<grid, fatc::bwd::THREADS_BQ, fatc::bwd::SMEM_TOTAL, st>>>(
+        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
+        scale * 1.4426950408889634f);
+  } else {
+    cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         fatc::bwd::SMEM_TOTAL);
+    fatc::bwd::fa_bwd_tc_kernel<false><<<grid, fatc::bwd::THREADS_B, fatc::bwd::SMEM_TOTAL, st>>>(
+        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
+        scale * 1.4426950408889634f);
+  }
   return check_launch("fa_bwd_tc_kernel");
 }
 zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,

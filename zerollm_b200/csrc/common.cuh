@@ -362,6 +362,16 @@ __device__ __forceinline__ void umma_commit_w(uint64_t* bar) {
       : "memory");
 }
 
+// Per-warpgroup register reallocation.  Every warp of a warpgroup executes the same call; the
+// increments draw on the registers the decrements released, out of the block's launch total
+// (threads x registers per thread at launch), so the shares of all warpgroups must add up to it.
+template <uint32_t R> __device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
+}
+template <uint32_t R> __device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100 version bit.
 //   start: byte address in shared memory
 //   lbo / sbo: leading / stride byte offsets (bytes; encoded >> 4)
