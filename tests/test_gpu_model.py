@@ -223,6 +223,17 @@ def test_scaled_config_step_properties():
     m.close()
 
 
+def _updates_agree(p_init, p0, p1, tol=1e-2):
+    """Two runs of the same AdamW steps agree when their weights differ by a small fraction of how far
+    the steps moved them, measured normwise.  Per weight no such bound holds: AdamW's first update
+    is lr * g / (|g| + eps), so a weight whose gradient sums to nearly zero (|g| ~ eps, which a few of
+    the ~4e5 weights always have) takes an update anywhere in (-lr, lr) depending on the atomics'
+    rounding (measured up to 0.56 lr).  A missing or misordered graph node changes whole tensors'
+    updates, which is orders of magnitude above the bar."""
+    p_init, p0, p1 = (np.asarray(x, np.float64) for x in (p_init, p0, p1))
+    return np.linalg.norm(p1 - p0) <= tol * np.linalg.norm(p0 - p_init)
+
+
 def test_graph_replay_matches_eager():
     """Steps replayed from the captured CUDA graph equal eagerly launched steps, up to the
     summation-order freedom of the fp32 atomics (embedding gradient, dQ accumulation, the norm
@@ -231,10 +242,7 @@ def test_graph_replay_matches_eager():
       moves them by ~1e-6).
     - The losses of four AdamW steps: the first agree bit for bit, the fourth has been seen 1.2e-5
       apart, so the bar is 1e-4.
-    - The weights after four steps: AdamW normalises each update to about lr, so a weight whose
-      gradient sums to nearly zero can take a different update in the two runs from rounding alone
-      (measured up to 0.07 lr).  The bar is 0.25 lr per weight; a missing or misordered graph node
-      moves the losses, the first step's gradients and many weights by orders of magnitude more."""
+    - The weights after four steps, normwise against the distance the steps moved them."""
     from zerollm_b200 import ZeroLLM
     c = _cfgs(True)[0]
     B, S = 4, 128
@@ -246,16 +254,18 @@ def test_graph_replay_matches_eager():
         m = ZeroLLM(c, B * S, seed=0)
         m.set_optimizer()
         m.set_graph(graph)
+        p_init = m.params()
         m.train_step(ids, tg, B, S, lr=lr, update=False)
         g = m.grads().copy()
         losses = [m.train_step(ids, tg, B, S, lr=lr).item() for _ in range(4)]
-        out.append((g, losses, m.params()))
+        out.append((g, losses, m.params(), p_init))
         m.close()
-    (g0, l0, p0), (g1, l1, p1) = out
+    (g0, l0, p0, pi0), (g1, l1, p1, pi1) = out
+    assert np.array_equal(pi0, pi1)
     assert rel(g1, g0) < 1e-4
     assert l0[0] == l1[0], (l0, l1)  # the first step sees identical weights
     assert np.allclose(l0, l1, rtol=1e-4, atol=0), (l0, l1)
-    assert np.max(np.abs(p1.astype(np.float64) - p0)) < 0.25 * lr
+    assert _updates_agree(pi0, p0, p1)
 
 
 def test_in_step_kernel_timing():
@@ -272,6 +282,7 @@ def test_in_step_kernel_timing():
         m = ZeroLLM(c, B * S, seed=0)
         m.set_optimizer()
         m.set_kernel_timing(timing)
+        p_init = m.params()
         if timing:
             with pytest.raises(ZLError):
                 m.kernel_times()  # no step recorded yet
@@ -284,9 +295,9 @@ def test_in_step_kernel_timing():
         if timing:
             f, b = m.kernel_times()
             assert 0 < f < e0.elapsed_time(e1) and 0 < b < e0.elapsed_time(e1), (f, b, e0.elapsed_time(e1))
-        out.append((losses, m.params()))
+        out.append((losses, m.params(), p_init))
         m.close()
-    (l0, p0), (l1, p1) = out
+    (l0, p0, pi), (l1, p1, _) = out
     assert l0[0] == l1[0], (l0, l1)  # the first step sees identical weights
     assert np.allclose(l0, l1, rtol=1e-4, atol=0), (l0, l1)
-    assert np.max(np.abs(p1.astype(np.float64) - p0)) < 0.25 * 1e-3  # a quarter of AdamW's step, lr = 1e-3
+    assert _updates_agree(pi, p0, p1)

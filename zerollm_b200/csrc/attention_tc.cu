@@ -57,6 +57,31 @@ __device__ __forceinline__ float fast_exp2(float x) {  // MUFU ex2 (inputs <= 0 
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed pairs of fp32 values (one 64-bit register pair) and the sm_100 paired fp32 arithmetic:
+// each lane of fma / sub / mul.rn.f32x2 rounds exactly like the scalar instruction.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 
 template <int DH>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -1047,6 +1072,7 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
             uint32_t rs[NB][16], rd[NB][16];
             uint32_t pp[QCOLS / 2], dd[QCOLS / 2];
             const uint32_t c0 = (uint32_t)(cs * QCOLS);
+            const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
             if constexpr (PREFETCH) {
               tmem_ld16(t_lane + C_S + c0, rs[0]);
               tmem_ld16(t_lane + C_DP + c0, rd[0]);
@@ -1074,10 +1100,18 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
                 const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
                 float p[4], d[4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                  p[t] = fast_exp2(fmaf(__uint_as_float(rs[bb][j + t]), scale_log2, nlv[t]));
+                for (int t = 0; t < 4; t += 2) {  // two queries per paired fp32 instruction
+                  float x0, x1;
+                  f2_unpack(fma2(f2_pack(__uint_as_float(rs[bb][j + t]), __uint_as_float(rs[bb][j + t + 1])), sc2,
+                                 f2_pack(nlv[t], nlv[t + 1])), x0, x1);
+                  p[t] = fast_exp2(x0);
+                  p[t + 1] = fast_exp2(x1);
                   if (DIAG && r_local > q0 + j + t) p[t] = 0.f;
-                  d[t] = p[t] * (__uint_as_float(rd[bb][j + t]) - dv[t]);
+                  if (DIAG && r_local > q0 + j + t + 1) p[t + 1] = 0.f;
+                  f2_unpack(mul2(f2_pack(p[t], p[t + 1]),
+                                 sub2(f2_pack(__uint_as_float(rd[bb][j + t]), __uint_as_float(rd[bb][j + t + 1])),
+                                      f2_pack(dv[t], dv[t + 1]))),
+                            d[t], d[t + 1]);
                 }
                 pp[g * 8 + (j >> 1)] = pack_bf16(p[0], p[1]);
                 pp[g * 8 + (j >> 1) + 1] = pack_bf16(p[2], p[3]);
@@ -1086,10 +1120,16 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
               }
               if constexpr (PREFETCH) {
                 if (g + 1 < NG) tmem_ld_wait();
+                if (g == NG - 2) {  // the last sub-chunk has landed: S^T / dP^T may be overwritten
+                  tc_fence_before();
+                  mbar_arrive(sd_used);
+                }
               }
             }
-            tc_fence_before();
-            mbar_arrive(sd_used);
+            if constexpr (!PREFETCH) {
+              tc_fence_before();
+              mbar_arrive(sd_used);
+            }
             if (n > 0) {
               // the previous block's dV / dK / dQ MMAs have finished reading P^T and dS^T
               ok = bounded_wait_warp(mm_done, (n - 1) & 1, DEV_TIMEOUT_ATTN);
@@ -1157,7 +1197,9 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
       if (un.niter == 0) break;
       const int b = un.bh / H, hd = un.bh % H;
       for (int i = 0; i < un.niter; ++i, ++n) {
-        if (!bounded_wait_warp(mm_done, n & 1, DEV_TIMEOUT_ATTN)) { ok = false; break; }
+        // off the critical path: the MMA warp needs this block's dq_free only after the next
+        // block's softmax, so the wait sleeps between polls
+        if (!bounded_wait_warp_sleep(mm_done, n & 1, DEV_TIMEOUT_ATTN, 100)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int part = 0; part < 4; ++part) {  // head dims [16 part, 16 part + 16)
@@ -1615,6 +1657,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t rs[2][16], rd[2][16];
             uint32_t pp[QCOLS / 2], dd[QCOLS / 2];
             const uint32_t c0 = (uint32_t)(cs * QCOLS);
+            const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
             tmem_ld16(t_lane + C_S + c0, rs[0]);
             tmem_ld16(t_lane + C_DP + c0, rd[0]);
             tmem_ld_wait();
@@ -1634,10 +1677,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
                 float p[4], d[4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                  p[t] = fast_exp2(fmaf(__uint_as_float(rs[bb][j + t]), scale_log2, nlv[t]));
+                for (int t = 0; t < 4; t += 2) {  // two queries per paired fp32 instruction
+                  float x0, x1;
+                  f2_unpack(fma2(f2_pack(__uint_as_float(rs[bb][j + t]), __uint_as_float(rs[bb][j + t + 1])), sc2,
+                                 f2_pack(nlv[t], nlv[t + 1])), x0, x1);
+                  p[t] = fast_exp2(x0);
+                  p[t + 1] = fast_exp2(x1);
                   if (DIAG && r_local > moff + q0 + j + t) p[t] = 0.f;
-                  d[t] = p[t] * (__uint_as_float(rd[bb][j + t]) - dv[t]);
+                  if (DIAG && r_local > moff + q0 + j + t + 1) p[t + 1] = 0.f;
+                  f2_unpack(mul2(f2_pack(p[t], p[t + 1]),
+                                 sub2(f2_pack(__uint_as_float(rd[bb][j + t]), __uint_as_float(rd[bb][j + t + 1])),
+                                      f2_pack(dv[t], dv[t + 1]))),
+                            d[t], d[t + 1]);
                 }
                 pp[g * 8 + (j >> 1)] = pack_bf16(p[0], p[1]);
                 pp[g * 8 + (j >> 1) + 1] = pack_bf16(p[2], p[3]);

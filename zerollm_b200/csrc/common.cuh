@@ -90,6 +90,23 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t phase, int 
 __device__ __forceinline__ bool bounded_wait_warp(uint64_t* bar, uint32_t phase, int err) {
   return __all_sync(0xffffffffu, bounded_wait(bar, phase, err)) != 0;
 }
+// bounded_wait_warp for a warp off the critical path: between polls it sleeps ~ns nanoseconds, so
+// that its polling does not take issue slots from the warps that share its sub-partition.
+__device__ __forceinline__ bool bounded_wait_warp_sleep(uint64_t* bar, uint32_t phase, int err, uint32_t ns) {
+  bool ok = mbar_try_wait(bar, phase);
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      __nanosleep(ns);
+      if (mbar_try_wait(bar, phase)) { ok = true; break; }
+      if ((it & 15u) == 0u && globaltimer_ns() - t0 > 2000000000ull) {
+        atomicCAS(&zl_dev_error, 0, err);
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok) != 0;
+}
 
 // ------------------------------------------------------------------ CTA pairs (cta_group::2)
 // A cluster of two CTAs on two SMs shares one MMA: the even CTA issues it, each CTA holds half of

@@ -1216,14 +1216,16 @@ cudaError_t dispatch_pair(bool a_mn, bool b_mn, int kind, const CUtensorMap& ma,
 
 // Which bf16 GEMMs run on the CTA-pair kernel.  Measured on B200: the pair wins once the reduction
 // is long (K >= 1536: +3 to +10 %, long-K dW products and the scaled model's GEMMs reach 94-97 % of
-// the measured peak) and loses a little at K = 512, where the per-tile work is short.
+// the measured peak) and loses a little at K = 512 with N <= 2048 (QKV, FF1 forward 53 / 65 us
+// against 57 / 72 us), where the per-tile work is short; at K = 512 with a wide output (the output
+// head, N = 6400) it wins again (170 against 190 us).
 // ZL_GEMM_PAIR=0 / =1 forces the one-SM / pair kernel (read on every call).
-bool use_pair(int M, int K) {
+bool use_pair(int M, int N, int K) {
   if (M < 2 * BM) return false;
   const char* e = getenv("ZL_GEMM_PAIR");
   if (e && e[0] == '0') return false;
   if (e && e[0] == '1') return true;
-  return K >= 1024;
+  return K >= 1024 || N >= 4096;
 }
 }  // namespace
 
@@ -1273,7 +1275,7 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   a.D = D; a.flags = flags;
   if (epi) a.epi = *epi; else memset(&a.epi, 0, sizeof(a.epi));
   // bf16 products of at least one 256-row tile go to the CTA-pair kernel
-  const bool pair = !is_f32 && sm_count() >= 2 && use_pair(M, K);
+  const bool pair = !is_f32 && sm_count() >= 2 && use_pair(M, N, K);
   Plan p = pair ? make_plan_pair(M, N, K) : make_plan(M, N, K, E::BK, true);
   const bool direct_ok = (is_f32 || (flags & ZL_EPI_OUT_F32)) && flags == (ZL_EPI_OUT_F32 | ZL_EPI_ACCUM) &&
                          N % 32 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
