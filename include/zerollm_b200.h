@@ -159,6 +159,16 @@ typedef struct {
 zl_status zl_gemm_bf16(const zl_bf16 *A, const zl_bf16 *B, void *D, int M, int N, int K, int layout,
                        int epi_flags, const zl_epilogue *epi, float *workspace, zl_stream stream);
 int64_t zl_gemm_workspace_floats(int M, int N, int K, int layout, int epi_flags);
+/* zl_gemm_bf16 for a bf16 output D that also adds D's column sums into colsum (fp32 [N], accumulated
+ * with atomics, so the order of the additions is not fixed): a bias gradient computed by the product
+ * that produces its input, as the model's FF1 bias gradient from the ReLU-masked dF product.  The
+ * reference computes bias gradients with a separate kernel (linear.cu:59-69); this entry has no
+ * counterpart there.  The sums are of the bf16-rounded stored values.  When the product does not
+ * take the pipelined bf16 epilogue (N not a multiple of 32, A MN-major, split-K), a column-sum pass
+ * over D runs after it.  ZL_EINVAL for fp32 outputs. */
+zl_status zl_gemm_bf16_colsum(const zl_bf16 *A, const zl_bf16 *B, void *D, int M, int N, int K, int layout,
+                              int epi_flags, const zl_epilogue *epi, float *workspace, float *colsum,
+                              zl_stream stream);
 /* Causal flash attention over a packed qkv buffer [B*S, 3*H*Dh] (q | k | v), output o [B*S, H*Dh],
  * lse [B, H, S] (natural log of the row sums of exp(scale * q.k)). */
 zl_status zl_attention_forward_bf16(const zl_bf16 *qkv, zl_bf16 *o, float *lse, int batch, int seq_len,

@@ -149,6 +149,39 @@ def test_gemm_bf16_epilogues(L, gemm_kind, b_k, M):
     assert torch.equal(o2, o)
 
 
+@pytest.mark.parametrize("M,N,K_,flags", [
+    (2048, 2048, 512, "mask"),    # the FF1 bias gradient's product shape: dF = (dR W2) masked by f > 0
+    (700, 1536, 512, "bias"),     # a partial last row tile (rows past M must not count)
+    (512, 520, 256, "plain"),     # N not a multiple of 32: no pipelined epilogue, column-sum pass after
+])
+def test_gemm_bf16_colsum(L, M, N, K_, flags, gemm_kind):
+    """zl_gemm_bf16_colsum: the output equals zl_gemm_bf16's bit for bit, and the column sums added
+    into colsum equal the fp32 column sums of the stored bf16 output (normwise 1e-5: the atomic
+    additions land in any order)."""
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    A = torch.randn(M, K_, device="cuda", generator=g).bfloat16()
+    B = (torch.randn(N, K_, device="cuda", generator=g) * 0.05).bfloat16()
+    aux = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    e = L.Epilogue()
+    e.aux, e.bias = aux.data_ptr(), bias.data_ptr()
+    fl = {"mask": L.EPI_RELU_MASK, "bias": L.EPI_BIAS, "plain": 0}[flags]
+    lay = L.A_KMAJOR | L.B_KMAJOR
+    want = _gemm(L, A.reshape(-1), B.reshape(-1), M, N, K_, lay, fl, e)
+    import ctypes as C
+    n = L.load().zl_gemm_workspace_floats(M, N, K_, lay, fl)
+    ws = torch.empty(max(int(n), 1), device="cuda")
+    out = torch.empty(M * N, device="cuda", dtype=torch.bfloat16)
+    cs0 = torch.randn(N, device="cuda", generator=g)
+    cs = cs0.clone()
+    L.call("zl_gemm_bf16_colsum", A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K_, lay, fl, C.byref(e),
+           ws.data_ptr(), cs.data_ptr(), None)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    ref = cs0.double() + out.view(M, N).double().sum(0)
+    assert rel(cs.cpu(), ref.cpu()) < 1e-5
+
+
 def test_gemm_bf16_kernel_bench_shape(L, gemm_kind):
     """The kernel-microbenchmark GEMM (M = 16384, K = 512, N = 2048, inputs N(0,1)) in its three
     forms -- forward Y = X W^T, input gradient dX = dY W, weight gradient dW = dY^T X -- against a

@@ -77,6 +77,11 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ float fmax3(float a, float b, float c) {  // sm_100 three-input maximum
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -573,10 +578,17 @@ __global__ void __launch_bounds__(THREADS_PP, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) mxp[i] = val(0, i);
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
+          for (int t = 0; t < 8; ++t) {  // three-input maxima: the row's 128 scores in 8 running maxima
+            mxp[t] = fmax3(mxp[t], val(0, 8 + t), val(0, 16 + t));
+            mxp[t] = fmaxf(mxp[t], val(0, 24 + t));
+          }
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (cc > 0 || i >= 8) mxp[i & 7] = fmaxf(mxp[i & 7], val(cc, i));
+          for (int cc = 1; cc < 4; ++cc)
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              mxp[t] = fmax3(mxp[t], val(cc, t), val(cc, 8 + t));
+              mxp[t] = fmax3(mxp[t], val(cc, 16 + t), val(cc, 24 + t));
+            }
           const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                                  fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
           // lazy rescaling, as in the one-tile kernel: m only rises by more than 8 (log2 units)

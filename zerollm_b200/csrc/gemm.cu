@@ -53,6 +53,7 @@ struct GemmArgs {
   int flags;
   zl_epilogue epi;
   float* ws;  // split-K partials [splits][M][N] (fp32) when splits > 1
+  float* colsum;  // when set (bf16 epilogue kinds only): column sums of the stored output added here
 };
 
 template <int BN, int STAGES, int ELEM_BYTES>
@@ -438,6 +439,23 @@ __device__ __forceinline__ void epi_prefetch_l2(const GemmArgs& a, int r, int c0
   }
 }
 
+// Column sums of a warp's 32 x 32 output chunk added into dst[0, 32): lane l holds row l's values x[j]
+// of columns j.  Five exchange steps (31 shuffles) halve the columns a lane keeps and sum them with the
+// partner lane's, leaving lane j with the sum over all 32 rows of column j; one atomic add per lane.
+__device__ __forceinline__ void chunk_colsum_add(float (&x)[32], int lane, float* dst) {
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool hi = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = hi ? x[i] : x[w + i];
+      const float keep = hi ? x[w + i] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  atomicAdd(dst + lane, x[0]);
+}
+
 template <int BN, int KIND>
 __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensorMap* tmD, uint32_t t_row,
                                                uint32_t stg, int lane, int r0, int n0, int cbase) {
@@ -487,6 +505,9 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
     }
+    uint32_t pk[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
     // stage [32][32] bf16 (64-byte swizzle) in box k & 1, whose store from chunk k-2 has read it
     const uint32_t box = stg + (uint32_t)((k & 1) * 2048);
     if (lane == 0) bulk_wait_read1();
@@ -494,15 +515,23 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t dst = box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4);
-      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(pack_bf16(v[q * 8 + 0], v[q * 8 + 1])),
-                   "r"(pack_bf16(v[q * 8 + 2], v[q * 8 + 3])), "r"(pack_bf16(v[q * 8 + 4], v[q * 8 + 5])),
-                   "r"(pack_bf16(v[q * 8 + 6], v[q * 8 + 7])));
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(pk[q * 4]), "r"(pk[q * 4 + 1]),
+                   "r"(pk[q * 4 + 2]), "r"(pk[q * 4 + 3]));
     }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
       tma_store_2d_bulk(tmD, box, c0, r0);
       bulk_commit();
+    }
+    if (a.colsum) {  // column sums of the stored (bf16-rounded) values; rows past M count as zero
+      const bool in = r < a.M;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[2 * j] = in ? __uint_as_float(pk[j] << 16) : 0.f;
+        v[2 * j + 1] = in ? __uint_as_float(pk[j] & 0xffff0000u) : 0.f;
+      }
+      chunk_colsum_add(v, lane, a.colsum + c0);
     }
     cur = nxt;
   }
@@ -1250,12 +1279,18 @@ int64_t gemm_workspace_floats(int M, int N, int K, int layout, int flags, bool f
 }
 
 // Generic tcgen05 GEMM launcher (T = __nv_bfloat16 or float/tf32).
+zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaStream_t s);
+
+// colsum (bf16 outputs only; may be null): the column sums of the stored output are added into it,
+// by the pipelined epilogue when it takes the product, else by a separate column-sum pass.
 template <typename T>
 zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layout, int flags,
-                  const zl_epilogue* epi, float* ws, cudaStream_t st) {
+                  const zl_epilogue* epi, float* ws, cudaStream_t st, float* colsum = nullptr) {
   using E = Elem<T>;
   if (M <= 0 || N <= 0 || K <= 0) return set_error(ZL_EINVAL, "gemm: sizes must be positive (M=%d N=%d K=%d)", M, N, K);
   if (!A || !B || !D) return set_error(ZL_EINVAL, "gemm: null operand");
+  if (colsum && (sizeof(T) == 4 || (flags & ZL_EPI_OUT_F32)))
+    return set_error(ZL_EINVAL, "gemm: column sums are for bf16 outputs");
   const bool a_mn = !(layout & ZL_A_KMAJOR), b_mn = !(layout & ZL_B_KMAJOR);
   const bool is_f32 = sizeof(T) == 4;
   if ((flags & ZL_EPI_BIAS) && (!epi || !epi->bias)) return set_error(ZL_EINVAL, "gemm: bias flag without bias");
@@ -1271,6 +1306,7 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
       (reinterpret_cast<uintptr_t>(B) & 15))
     return ZL_EUNSUPPORTED;
   GemmArgs a;
+  a.colsum = nullptr;
   a.M = M; a.N = N; a.K = K;
   a.D = D; a.flags = flags;
   if (epi) a.epi = *epi; else memset(&a.epi, 0, sizeof(a.epi));
@@ -1319,6 +1355,7 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
                              ((reinterpret_cast<uintptr_t>(a.epi.rope_cos) | reinterpret_cast<uintptr_t>(a.epi.rope_sin)) & 15))))
       kind = -1;
   }
+  if (colsum && kind >= 0) a.colsum = colsum;
   cudaError_t e;
   if (pair) {
     const int pairs = std::min(p.units, sm_count() / 2);
@@ -1333,16 +1370,21 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   if (p.splits > 1 && !a.split_direct) {
     const bool plain_f32 = (flags & ~(ZL_EPI_OUT_F32 | ZL_EPI_ACCUM)) == 0 && (flags & ZL_EPI_OUT_F32) && N % 4 == 0 &&
                            ((reinterpret_cast<uintptr_t>(D) | reinterpret_cast<uintptr_t>(ws)) & 15) == 0;
+    zl_status r;
     if (plain_f32) {
       const int64_t n4 = (int64_t)M * N / 4;
       splitk_reduce_f32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(ws, static_cast<float*>(D), M, N, p.splits,
                                                                             (flags & ZL_EPI_ACCUM) ? 1 : 0);
-      return check_launch("splitk_reduce_f32");
+      r = check_launch("splitk_reduce_f32");
+    } else {
+      const int64_t work = (int64_t)M * ((N + 31) / 32);
+      splitk_reduce_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(a);
+      r = check_launch("splitk_reduce");
     }
-    const int64_t work = (int64_t)M * ((N + 31) / 32);
-    splitk_reduce_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(a);
-    return check_launch("splitk_reduce");
+    if (r != ZL_OK) return r;
   }
+  // column sums the epilogue did not take (a shape outside the pipelined bf16 epilogue)
+  if (colsum && !a.colsum) return colsum_bf16_add(reinterpret_cast<const zl_bf16*>(D), colsum, M, N, st);
   return ZL_OK;
 }
 
@@ -1415,7 +1457,19 @@ int gemm_dev_error_read_and_clear() {
 }
 
 template zl_status gemm_tc<__nv_bfloat16>(const __nv_bfloat16*, const __nv_bfloat16*, void*, int, int, int, int, int,
-                                          const zl_epilogue*, float*, cudaStream_t);
+                                          const zl_epilogue*, float*, cudaStream_t, float*);
+
+// zl_gemm_bf16 that also adds the column sums of its bf16 output into colsum (a bias gradient):
+// in the epilogue when the product takes the pipelined bf16 epilogue, else by a column-sum pass.
+zl_status gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout, int flags,
+                           const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st) {
+  zl_status s = gemm_tc<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(A),
+                                       reinterpret_cast<const __nv_bfloat16*>(B), D, M, N, K, layout, flags, epi, ws,
+                                       st, colsum);
+  if (s == ZL_EUNSUPPORTED)
+    return set_error(ZL_EUNSUPPORTED, "gemm: operands must be 16-byte aligned with rows a multiple of 8");
+  return s;
+}
 
 }  // namespace zl
 
@@ -1428,6 +1482,14 @@ extern "C" zl_status zl_gemm_bf16(const zl_bf16* A, const zl_bf16* B, void* D, i
   if (s == ZL_EUNSUPPORTED)
     return zl::set_error(ZL_EUNSUPPORTED, "zl_gemm_bf16: operands must be 16-byte aligned with rows a multiple of 8");
   return s;
+}
+
+extern "C" zl_status zl_gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout,
+                                         int epi_flags, const zl_epilogue* epi, float* workspace, float* colsum,
+                                         zl_stream stream) {
+  if (!colsum) return zl::set_error(ZL_EINVAL, "zl_gemm_bf16_colsum: null colsum");
+  return zl::gemm_bf16_colsum(A, B, D, M, N, K, layout, epi_flags, epi, workspace, colsum,
+                              static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int64_t zl_gemm_workspace_floats(int M, int N, int K, int layout, int epi_flags) {

@@ -38,6 +38,9 @@ zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, cons
                              float* workspace, int64_t M, int N, cudaStream_t s, bool fused);
 // kernels.cu: column sums added straight into db (one launch)
 zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaStream_t s);
+// gemm.cu: a bf16 GEMM whose epilogue also adds the column sums of its output into colsum
+zl_status gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout, int flags,
+                           const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st);
 // attention.cu: the attention backward with events recorded around its main kernel
 zl_status attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o, const float* lse,
                                   zl_bf16* d_qkv, float* workspace, int batch, int seq_len, int num_heads,
@@ -245,6 +248,14 @@ zl_status gemm(zl_model* M, const bf16* A, const bf16* B, void* D, int m, int n,
                       flags, e, M->ws, st);
 }
 
+// the same, also adding the column sums of the bf16 output D into colsum (a bias gradient)
+zl_status gemm_colsum(zl_model* M, const bf16* A, const bf16* B, void* D, int m, int n, int k, int layout, int flags,
+                      const zl_epilogue* e, float* colsum, cudaStream_t st) {
+  M->launches += 1;
+  return zl::gemm_bf16_colsum(reinterpret_cast<const zl_bf16*>(A), reinterpret_cast<const zl_bf16*>(B), D, m, n, k,
+                              layout, flags, e, M->ws, colsum, st);
+}
+
 const bf16* W(zl_model* M, int64_t off) { return M->pbf + off; }
 const float* P(zl_model* M, int64_t off) { return off >= 0 ? M->params + off : nullptr; }
 float* G(zl_model* M, int64_t off) { return off >= 0 ? M->grads + off : nullptr; }
@@ -381,9 +392,10 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     TRY(grads_ready(M, end_of_any(M, {t[L_W2], t[L_B2]}), st));
     zl_epilogue e{};
     e.aux = reinterpret_cast<zl_bf16*>(M->f[l]);
-    TRY(gemm(M, M->dr, W(M, t[L_W2]), M->dF, Ti, F, d, ZL_A_KMAJOR, ZL_EPI_RELU_MASK, &e, st));
+    // dF, and with it the FF1 bias gradient: its column sums, added by the GEMM's epilogue
+    TRY(gemm_colsum(M, M->dr, W(M, t[L_W2]), M->dF, Ti, F, d, ZL_A_KMAJOR, ZL_EPI_RELU_MASK, &e,
+                    c.bias ? G(M, t[L_B1]) : nullptr, st));
     TRY(gemm(M, M->dF, M->h1[l], G(M, t[L_W1]), F, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
-    if (c.bias) { TRY(zl::colsum_bf16_add(reinterpret_cast<zl_bf16*>(M->dF), G(M, t[L_B1]), T, F, st)); M->launches += 1; }
     TRY(grads_ready(M, end_of_any(M, {t[L_W1], t[L_B1]}), st));
     e = zl_epilogue{};
     e.residual = reinterpret_cast<zl_bf16*>(M->dr);
