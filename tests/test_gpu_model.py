@@ -268,6 +268,30 @@ def test_graph_replay_matches_eager():
     assert _updates_agree(pi0, p0, p1)
 
 
+def test_attention_backward_forms_give_the_same_step(monkeypatch):
+    """The whole step with the head-dim-64 tcgen05 attention backward in its two forms (TMEM readout
+    by a dedicated warpgroup, the default, or by the softmax warps, ZL_ATTN_BWD_READOUT=0): one step's
+    gradients agree tensor by tensor up to the order of the fp32 additions (dQ accumulation, the
+    atomics of the bias gradients)."""
+    from zerollm_b200 import ZeroLLM
+    c = _cfgs(True)[0]
+    B, S = 2, 256
+    inp, tgt = _batch(B, S, c.vocab_size, 3)
+    ids, tg = torch.from_numpy(inp).cuda(), torch.from_numpy(tgt).cuda()
+    grads = []
+    for form in ("1", "0"):
+        monkeypatch.setenv("ZL_ATTN_BWD_READOUT", form)
+        m = ZeroLLM(c, B * S, seed=0)
+        m.set_optimizer()
+        m.train_step(ids, tg, B, S, lr=1e-3, update=False)
+        grads.append(m.grads().copy())
+        m.close()
+    om = _oracle_model(c)
+    offs, sizes, _, _ = O.param_layout(om)
+    for o, s in zip(offs, sizes):
+        assert rel(grads[0][o:o + s], grads[1][o:o + s]) < 1e-4, (o, s)
+
+
 def test_in_step_kernel_timing():
     """With kernel timing on, the captured step carries event nodes around the attention kernels:
     the step's results are unchanged (up to the atomics' summation order, as in the graph-replay
