@@ -387,7 +387,11 @@ zl_status zl_nccl_unique_id(void *id_out, size_t id_bytes);
  * buckets on a side stream as soon as their last producer finishes and folds 1/world into AdamW. */
 zl_status zl_model_attach_nccl(zl_model *m, const void *id, int rank, int world, int64_t bucket_bytes);
 /* Bucket plan (host-side, no GPU needed): splits [0,total) floats at tensor boundaries into buckets
- * of at most bucket_floats (a tensor larger than a bucket is split); returns bucket starts. */
+ * of at most bucket_floats (a tensor larger than a bucket is split); returns bucket starts.  The
+ * buckets are formed from the end of the arena, where backward finishes, and taper there: the last
+ * holds at most bucket_floats / 8, the one before it twice that, and so on up to bucket_floats (a
+ * single tensor larger than its share gets a bucket of its own), so that little is left to
+ * all-reduce after the step's last gradient is written. */
 zl_status zl_bucket_plan(const int64_t *tensor_offsets, const int64_t *tensor_sizes, int n_tensors,
                          int64_t bucket_floats, int64_t *starts, int64_t *lens, int max_buckets,
                          int *n_buckets);

@@ -112,3 +112,27 @@ def test_lost_rank_is_detected_by_timeout():
                 p.kill()
                 pytest.fail("a rank hung instead of timing out")
         assert open(os.path.join(d, "outcome")).read() != "completed"
+
+
+def test_bucket_plan_tapers_toward_the_end_of_backward():
+    """Buckets are formed from the end of the arena (the gradients backward finishes last): the last
+    bucket may hold cap/8, the one before it cap/4, and so on up to cap, each closed at a tensor
+    boundary, so that little is left to all-reduce when backward ends.  For the 26M model the last
+    bucket is the token embedding alone and the one before it layer 0's last-written tensors."""
+    from oracle import oracle as O
+    from zerollm_b200.model import bucket_plan
+    om = O.Model(vocab=6400, dim=512, layers=6, heads=8, ffn=2048, max_seq=2048, norm=1, pos=1, tied=0)
+    offs, sizes, _, total = O.param_layout(om)
+    cap = BUCKET_BYTES // 4
+    st, ln = bucket_plan(offs, sizes, cap)
+    assert st[0] == 0 and st[-1] + ln[-1] == total
+    assert all(a + la == b for a, b, la in zip(st, st[1:], ln))
+    assert st[-1] == offs[-1] and ln[-1] == sizes[-1]  # the token embedding's gradient alone
+    assert ln[-2] * 4 < 5e6                            # then layer 0's output projection, norm and QKV
+    tensors = set(zip(offs.tolist(), sizes.tolist()))
+    for j, (s, n) in enumerate(zip(st[::-1], ln[::-1])):
+        share = min(cap, (cap >> 3) << j)
+        assert n <= share or (s, n) in tensors, (j, n, share)
+    # a tensor larger than the cap is split into cap-sized pieces from its end
+    st, ln = bucket_plan([0, 10, 20, 30, 40], [10, 10, 10, 10, 100], 80)
+    assert list(st) == [0, 40, 60] and list(ln) == [40, 20, 80]

@@ -823,37 +823,43 @@ extern "C" zl_status zl_bucket_plan(const int64_t* tensor_offsets, const int64_t
                                     int* n_buckets) {
   if (!tensor_offsets || !tensor_sizes || n_tensors <= 0 || bucket_floats <= 0 || !n_buckets)
     return zl::set_error(ZL_EINVAL, "bucket_plan: invalid arguments");
-  // Greedy: close a bucket at a tensor boundary once adding the next tensor would exceed the
-  // budget; a tensor larger than the budget is split into budget-sized pieces.
-  int nb = 0;
-  int64_t cur_start = tensor_offsets[0], cur_len = 0;
-  auto emit = [&](int64_t s, int64_t l) {
-    if (l <= 0) return;
-    if (nb < max_buckets) {
-      if (starts) starts[nb] = s;
-      if (lens) lens[nb] = l;
-    }
-    ++nb;
-  };
-  for (int i = 0; i < n_tensors; ++i) {
-    int64_t off = tensor_offsets[i], sz = tensor_sizes[i];
-    if (i > 0 && off != tensor_offsets[i - 1] + tensor_sizes[i - 1])
+  for (int i = 1; i < n_tensors; ++i)
+    if (tensor_offsets[i] != tensor_offsets[i - 1] + tensor_sizes[i - 1])
       return zl::set_error(ZL_EINVAL, "bucket_plan: tensors must be contiguous and ordered");
-    if (cur_len > 0 && cur_len + sz > bucket_floats) {
-      emit(cur_start, cur_len);
-      cur_start = off;
-      cur_len = 0;
-    }
-    while (sz > bucket_floats) {
-      if (cur_len > 0) { emit(cur_start, cur_len); cur_start = off; cur_len = 0; }
-      emit(off, bucket_floats);
-      off += bucket_floats;
+  // Buckets are formed from the end of the arena, where backward finishes: the last bucket may hold
+  // bucket_floats / 8, the one before it twice that, and so on up to bucket_floats, each closed at a
+  // tensor boundary (a tensor larger than its bucket's share gets a bucket of its own; one larger
+  // than bucket_floats is split into bucket_floats pieces).  What is still to be all-reduced when
+  // backward ends is then the last tensors alone, not a whole bucket_floats of them.
+  std::vector<std::pair<int64_t, int64_t>> rev;  // buckets, last first: (start, length)
+  auto cap = [&](size_t j) {
+    int64_t c = std::max<int64_t>(bucket_floats >> 3, 1);
+    for (size_t k = 0; k < j && c < bucket_floats; ++k) c *= 2;
+    return std::min(c, bucket_floats);
+  };
+  int64_t cur_end = tensor_offsets[n_tensors - 1] + tensor_sizes[n_tensors - 1], cur_len = 0;
+  auto close = [&]() {
+    if (cur_len > 0) rev.emplace_back(cur_end - cur_len, cur_len);
+    cur_end -= cur_len;
+    cur_len = 0;
+  };
+  for (int i = n_tensors - 1; i >= 0; --i) {
+    int64_t sz = tensor_sizes[i];
+    if (cur_len > 0 && cur_len + sz > cap(rev.size())) close();
+    while (sz > bucket_floats) {  // pieces of bucket_floats from the tensor's end
+      close();
+      rev.emplace_back(cur_end - bucket_floats, bucket_floats);
+      cur_end -= bucket_floats;
       sz -= bucket_floats;
-      cur_start = off;
     }
     cur_len += sz;
   }
-  emit(cur_start, cur_len);
+  close();
+  const int nb = (int)rev.size();
+  for (int b = 0; b < nb && b < max_buckets; ++b) {
+    if (starts) starts[b] = rev[nb - 1 - b].first;
+    if (lens) lens[b] = rev[nb - 1 - b].second;
+  }
   *n_buckets = nb;
   if (nb > max_buckets) return zl::set_error(ZL_EINVAL, "bucket_plan: more than %d buckets", max_buckets);
   return ZL_OK;
