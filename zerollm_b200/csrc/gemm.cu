@@ -1170,12 +1170,19 @@ Plan make_plan_pair(int M, int N, int K) {
   const int pairs = sm_count() / 2;
   int best = 1;
   if (p.tiles < pairs && p.k_blocks >= 8) {
+    // Cost in k-block times of one pair tile (~0.3 us): each round of units costs its k-blocks plus
+    // a fixed ~16 (pipeline fill, accumulator drain), and each split adds its fp32 partial of the
+    // whole output to D (M*N*4 bytes through L2, ~1.5 MB per k-block time).  Measured on the weight
+    // gradients of the 26M model (K = 32768) this picks the fastest split count of a sweep of
+    // 1..16 for every shape (output head 152.6 us at 4 splits against 170.0 us at the 16 the
+    // earlier waves-only model chose; FF2 59.4 against 68.6 us).
     double best_t = 1e30;
     const int smax = std::min(16, p.k_blocks / 4);
+    const double red = (double)M * N * 4.0 / 1.5e6;
     for (int s = 1; s <= smax; ++s) {
       const int units = p.tiles * s;
-      const int waves = (units + pairs - 1) / pairs;
-      const double t = (double)waves * ((p.k_blocks + s - 1) / s) + 0.5 * s;
+      const int rounds = (units + pairs - 1) / pairs;
+      const double t = (double)rounds * ((p.k_blocks + s - 1) / s + 16) + red * s;
       if (t < best_t) { best_t = t; best = s; }
     }
   }
