@@ -169,6 +169,15 @@ int64_t zl_gemm_workspace_floats(int M, int N, int K, int layout, int epi_flags)
 zl_status zl_gemm_bf16_colsum(const zl_bf16 *A, const zl_bf16 *B, void *D, int M, int N, int K, int layout,
                               int epi_flags, const zl_epilogue *epi, float *workspace, float *colsum,
                               zl_stream stream);
+/* zl_gemm_bf16 with the ReLU mask kept as bits ([M][N/32] uint32 words, bit j of word w of a row =
+ * column 32 w + j; N a multiple of 32, bf16 output, A K-major): bits_out (may be NULL) receives
+ * (stored output > 0) of every element, as the FF1 product's ReLU output f; bits_in (may be NULL) masks
+ * a ZL_EPI_RELU_MASK product in place of epi->aux, so that the ReLU backward reads N/8 bytes per row
+ * instead of the 2 N bytes of f.  No counterpart in the reference (relu.cu:14-43 reads the saved
+ * input).  ZL_EINVAL for other outputs or shapes; the product runs unsplit. */
+zl_status zl_gemm_bf16_relu_bits(const zl_bf16 *A, const zl_bf16 *B, void *D, int M, int N, int K, int layout,
+                                 int epi_flags, const zl_epilogue *epi, float *workspace, uint32_t *bits_out,
+                                 const uint32_t *bits_in, zl_stream stream);
 /* Causal flash attention over a packed qkv buffer [B*S, 3*H*Dh] (q | k | v), output o [B*S, H*Dh],
  * lse [B, H, S] (natural log of the row sums of exp(scale * q.k)). */
 zl_status zl_attention_forward_bf16(const zl_bf16 *qkv, zl_bf16 *o, float *lse, int batch, int seq_len,

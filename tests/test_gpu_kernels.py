@@ -182,6 +182,47 @@ def test_gemm_bf16_colsum(L, M, N, K_, flags, gemm_kind):
     assert rel(cs.cpu(), ref.cpu()) < 1e-5
 
 
+@pytest.mark.parametrize("M", [2048, 2600])
+def test_gemm_bf16_relu_bits(L, M, gemm_kind):
+    """zl_gemm_bf16_relu_bits: the FF1-shaped product (bias + ReLU) writes f > 0 as bits next to an
+    output identical to zl_gemm_bf16's, and the ReLU-backward product masked by those bits equals the
+    one masked by f itself (ZL_EPI_RELU_MASK with aux = f), bit for bit.  2600 rows leave a partial
+    tile; both sizes have enough tiles that zl_gemm_bf16 does not split K either (a mask-bits product
+    always runs unsplit, and split partials round differently)."""
+    import ctypes as C
+    K_, N, K2 = 512, 2048, 512
+    g = torch.Generator(device="cuda").manual_seed(M)
+    X = torch.randn(M, K_, device="cuda", generator=g).bfloat16()
+    W1 = (torch.randn(N, K_, device="cuda", generator=g) * 0.05).bfloat16()
+    b1 = torch.randn(N, device="cuda", generator=g) * 0.1
+    dR = torch.randn(M, K2, device="cuda", generator=g).bfloat16()
+    W2 = (torch.randn(K2, N, device="cuda", generator=g) * 0.05).bfloat16()  # [K2, N]: B MN-major
+    e = L.Epilogue()
+    e.bias = b1.data_ptr()
+    fl = L.EPI_BIAS | L.EPI_RELU
+    lay = L.A_KMAJOR | L.B_KMAJOR
+    f_ref = _gemm(L, X.reshape(-1), W1.reshape(-1), M, N, K_, lay, fl, e)
+    f = torch.empty(M * N, device="cuda", dtype=torch.bfloat16)
+    bits = torch.full((M * N // 32,), -1, device="cuda", dtype=torch.int32)
+    ws = torch.empty(max(int(L.load().zl_gemm_workspace_floats(M, N, K_, lay, fl)), 1), device="cuda")
+    L.call("zl_gemm_bf16_relu_bits", X.data_ptr(), W1.data_ptr(), f.data_ptr(), M, N, K_, lay, fl, C.byref(e),
+           ws.data_ptr(), bits.data_ptr(), None, None)
+    torch.cuda.synchronize()
+    assert torch.equal(f, f_ref)
+    pos = (f.view(M, N).float() > 0).cpu().numpy().reshape(M, N // 32, 32)
+    want = (pos.astype(np.uint64) << np.arange(32, dtype=np.uint64)).sum(-1).astype(np.uint32)
+    assert np.array_equal(bits.cpu().numpy().view(np.uint32).reshape(M, N // 32), want)
+    # the ReLU backward: dF = (dR W2) masked by f > 0
+    e2 = L.Epilogue()
+    e2.aux = f.data_ptr()
+    dF_ref = _gemm(L, dR.reshape(-1), W2.reshape(-1), M, N, K2, L.A_KMAJOR, L.EPI_RELU_MASK, e2)
+    dF = torch.empty(M * N, device="cuda", dtype=torch.bfloat16)
+    L.call("zl_gemm_bf16_relu_bits", dR.data_ptr(), W2.data_ptr(), dF.data_ptr(), M, N, K2, L.A_KMAJOR,
+           L.EPI_RELU_MASK, C.byref(L.Epilogue()), ws.data_ptr(), None, bits.data_ptr(), None)
+    torch.cuda.synchronize()
+    assert torch.equal(dF, dF_ref)
+
+
 def test_gemm_bf16_kernel_bench_shape(L, gemm_kind):
     """The kernel-microbenchmark GEMM (M = 16384, K = 512, N = 2048, inputs N(0,1)) in its three
     forms -- forward Y = X W^T, input gradient dX = dY W, weight gradient dW = dY^T X -- against a

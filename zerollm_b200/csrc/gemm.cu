@@ -54,6 +54,10 @@ struct GemmArgs {
   zl_epilogue epi;
   float* ws;  // split-K partials [splits][M][N] (fp32) when splits > 1
   float* colsum;  // when set (bf16 epilogue kinds only): column sums of the stored output added here
+  // ReLU masks as bits ([M][N/32] words, bit j of word w = column 32 w + j): bits_out (when set, bf16
+  // epilogue kinds) receives (stored value > 0) of every output; bits_in is the EK_MASKBITS kind's mask
+  uint32_t* bits_out;
+  const uint32_t* bits_in;
 };
 
 template <int BN, int STAGES, int ELEM_BYTES>
@@ -379,12 +383,13 @@ __device__ __forceinline__ void partial_chunk(const GemmArgs& a, uint32_t stg, i
 // while chunk k is finished, and two 2 KB staging boxes alternate, so a chunk never waits for the
 // previous chunk's store to read its box.  KIND fixes which row-wise input the chunk reads, so
 // that only its prefetch registers exist; bias and ReLU are runtime flags.
-enum EpiKind : int { EK_PLAIN = 0, EK_RESIDUAL = 1, EK_MASK = 2, EK_ROPE = 3 };
+enum EpiKind : int { EK_PLAIN = 0, EK_RESIDUAL = 1, EK_MASK = 2, EK_ROPE = 3, EK_MASKBITS = 4 };
 
 template <int KIND>
 struct EpiPrefetch {
   float bias = 0.f;  // lane j: bias of column c0 + j
-  uint4 row[KIND == EK_PLAIN ? 1 : 4];      // residual / mask row segment (64 bytes)
+  uint4 row[(KIND == EK_RESIDUAL || KIND == EK_MASK) ? 4 : 1];  // residual / mask row segment (64 bytes)
+  uint32_t mword = 0;                       // EK_MASKBITS: this row's mask bits of the chunk's 32 columns
   float rc[KIND == EK_ROPE ? 16 : 1], rs[KIND == EK_ROPE ? 16 : 1];  // cos / sin of 16 pairs
 };
 
@@ -401,6 +406,7 @@ __device__ __forceinline__ void epi_fetch(const GemmArgs& a, int r, int lane, in
       for (int q = 0; q < 4; ++q) p.row[q] = __ldg(s + q);
     }
   }
+  if constexpr (KIND == EK_MASKBITS) p.mword = r < a.M ? __ldg(a.bits_in + (size_t)r * (a.N >> 5) + (c0 >> 5)) : 0u;
   if constexpr (KIND == EK_ROPE) {
     if (c0 < a.epi.rope_cols) {
       const int half = a.epi.head_dim >> 1, i0 = (c0 % a.epi.head_dim) >> 1, pos = r % a.epi.rope_seq;
@@ -489,6 +495,10 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
         }
       }
     }
+    if constexpr (KIND == EK_MASKBITS) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = ((cur.mword >> j) & 1u) ? v[j] : 0.f;
+    }
     if constexpr (KIND == EK_RESIDUAL || KIND == EK_MASK) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -508,6 +518,15 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
     uint32_t pk[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+    if (a.bits_out && r < a.M) {  // bit j: the stored bf16 value of column c0 + j is > 0
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        word |= ((int16_t)(pk[j] & 0xffffu) > 0 ? 1u : 0u) << (2 * j);
+        word |= ((int16_t)(pk[j] >> 16) > 0 ? 1u : 0u) << (2 * j + 1);
+      }
+      a.bits_out[(size_t)r * (a.N >> 5) + (c0 >> 5)] = word;
+    }
     // stage [32][32] bf16 (64-byte swizzle) in box k & 1, whose store from chunk k-2 has read it
     const uint32_t box = stg + (uint32_t)((k & 1) * 2048);
     if (lane == 0) bulk_wait_read1();
@@ -1145,6 +1164,7 @@ cudaError_t launch_kind(int kind, const CUtensorMap& ma, const CUtensorMap& mb, 
       case EK_RESIDUAL: return launch_tc<T, BN, STAGES, false, B_MN, EK_RESIDUAL>(ma, mb, md, mw, a, grid, st);
       case EK_MASK: return launch_tc<T, BN, STAGES, false, B_MN, EK_MASK>(ma, mb, md, mw, a, grid, st);
       case EK_ROPE: return launch_tc<T, BN, STAGES, false, B_MN, EK_ROPE>(ma, mb, md, mw, a, grid, st);
+      case EK_MASKBITS: return launch_tc<T, BN, STAGES, false, B_MN, EK_MASKBITS>(ma, mb, md, mw, a, grid, st);
       default: break;
     }
   }
@@ -1237,6 +1257,7 @@ cudaError_t launch_kind2(int kind, const CUtensorMap& ma, const CUtensorMap& mb,
     case EK_RESIDUAL: return launch_tc2<BN, STAGES, false, B_MN, EK_RESIDUAL>(ma, mb, md, mw, a, pairs, st);
     case EK_MASK: return launch_tc2<BN, STAGES, false, B_MN, EK_MASK>(ma, mb, md, mw, a, pairs, st);
     case EK_ROPE: return launch_tc2<BN, STAGES, false, B_MN, EK_ROPE>(ma, mb, md, mw, a, pairs, st);
+    case EK_MASKBITS: return launch_tc2<BN, STAGES, false, B_MN, EK_MASKBITS>(ma, mb, md, mw, a, pairs, st);
     default: return launch_tc2<BN, STAGES, false, B_MN, -1>(ma, mb, md, mw, a, pairs, st);
   }
 }
@@ -1290,9 +1311,12 @@ zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaSt
 
 // colsum (bf16 outputs only; may be null): the column sums of the stored output are added into it,
 // by the pipelined epilogue when it takes the product, else by a separate column-sum pass.
+// bits_out / bits_in (bf16 outputs only, N a multiple of 32; may be null): ReLU masks as bits, written by
+// this product's epilogue / read in place of epi->aux by a ZL_EPI_RELU_MASK product.
 template <typename T>
 zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layout, int flags,
-                  const zl_epilogue* epi, float* ws, cudaStream_t st, float* colsum = nullptr) {
+                  const zl_epilogue* epi, float* ws, cudaStream_t st, float* colsum = nullptr,
+                  uint32_t* bits_out = nullptr, const uint32_t* bits_in = nullptr) {
   using E = Elem<T>;
   if (M <= 0 || N <= 0 || K <= 0) return set_error(ZL_EINVAL, "gemm: sizes must be positive (M=%d N=%d K=%d)", M, N, K);
   if (!A || !B || !D) return set_error(ZL_EINVAL, "gemm: null operand");
@@ -1302,7 +1326,11 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   const bool is_f32 = sizeof(T) == 4;
   if ((flags & ZL_EPI_BIAS) && (!epi || !epi->bias)) return set_error(ZL_EINVAL, "gemm: bias flag without bias");
   if ((flags & ZL_EPI_RESIDUAL) && (!epi || !epi->residual)) return set_error(ZL_EINVAL, "gemm: residual flag without residual");
-  if ((flags & ZL_EPI_RELU_MASK) && (!epi || !epi->aux)) return set_error(ZL_EINVAL, "gemm: relu-mask flag without aux");
+  if ((flags & ZL_EPI_RELU_MASK) && (!epi || !epi->aux) && !bits_in)
+    return set_error(ZL_EINVAL, "gemm: relu-mask flag without aux");
+  if ((bits_out || bits_in) && (sizeof(T) == 4 || (flags & ZL_EPI_OUT_F32) || N % 32 != 0))
+    return set_error(ZL_EINVAL, "gemm: ReLU mask bits are for bf16 outputs with N a multiple of 32");
+  if (bits_in && !(flags & ZL_EPI_RELU_MASK)) return set_error(ZL_EINVAL, "gemm: mask bits without the relu-mask flag");
   if ((flags & ZL_EPI_ROPE) && (!epi || !epi->rope_cos || !epi->rope_sin || epi->head_dim <= 0 || epi->rope_seq <= 0 ||
                                 (epi->head_dim & 1)))
     return set_error(ZL_EINVAL, "gemm: rope flag without tables");
@@ -1314,6 +1342,8 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
     return ZL_EUNSUPPORTED;
   GemmArgs a;
   a.colsum = nullptr;
+  a.bits_out = nullptr;
+  a.bits_in = bits_in;
   a.M = M; a.N = N; a.K = K;
   a.D = D; a.flags = flags;
   if (epi) a.epi = *epi; else memset(&a.epi, 0, sizeof(a.epi));
@@ -1322,8 +1352,9 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   Plan p = pair ? make_plan_pair(M, N, K) : make_plan(M, N, K, E::BK, true);
   const bool direct_ok = (is_f32 || (flags & ZL_EPI_OUT_F32)) && flags == (ZL_EPI_OUT_F32 | ZL_EPI_ACCUM) &&
                          N % 32 == 0 && (reinterpret_cast<uintptr_t>(D) & 15) == 0;
-  if (p.splits > 1 && !ws && !direct_ok) {
-    // no workspace supplied: fall back to a single split
+  if (p.splits > 1 && ((!ws && !direct_ok) || bits_out || bits_in)) {
+    // no workspace supplied, or ReLU mask bits (which only the unsplit pipelined epilogue handles):
+    // a single split
     p.splits = 1; p.kb_per_split = p.k_blocks; p.units = p.tiles;
   }
   a.n_tiles_n = p.n_tiles_n; a.tiles = p.tiles; a.k_blocks = p.k_blocks; a.splits = p.splits;
@@ -1363,6 +1394,16 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
       kind = -1;
   }
   if (colsum && kind >= 0) a.colsum = colsum;
+  if (bits_in || bits_out) {
+    // the mask bits exist only in the pipelined bf16 epilogue
+    if (kind < 0) return set_error(ZL_EUNSUPPORTED, "gemm: ReLU mask bits need the pipelined bf16 epilogue "
+                                                    "(A K-major, 16-byte aligned output, no split-K)");
+    if (bits_in) {
+      if (kind != EK_MASK) return set_error(ZL_EUNSUPPORTED, "gemm: mask bits with another row-wise input");
+      kind = EK_MASKBITS;
+    }
+    a.bits_out = bits_out;
+  }
   cudaError_t e;
   if (pair) {
     const int pairs = std::min(p.units, sm_count() / 2);
@@ -1464,15 +1505,17 @@ int gemm_dev_error_read_and_clear() {
 }
 
 template zl_status gemm_tc<__nv_bfloat16>(const __nv_bfloat16*, const __nv_bfloat16*, void*, int, int, int, int, int,
-                                          const zl_epilogue*, float*, cudaStream_t, float*);
+                                          const zl_epilogue*, float*, cudaStream_t, float*, uint32_t*,
+                                          const uint32_t*);
 
 // zl_gemm_bf16 that also adds the column sums of its bf16 output into colsum (a bias gradient):
 // in the epilogue when the product takes the pipelined bf16 epilogue, else by a column-sum pass.
 zl_status gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout, int flags,
-                           const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st) {
+                           const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st, uint32_t* bits_out,
+                           const uint32_t* bits_in) {
   zl_status s = gemm_tc<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(A),
                                        reinterpret_cast<const __nv_bfloat16*>(B), D, M, N, K, layout, flags, epi, ws,
-                                       st, colsum);
+                                       st, colsum, bits_out, bits_in);
   if (s == ZL_EUNSUPPORTED)
     return set_error(ZL_EUNSUPPORTED, "gemm: operands must be 16-byte aligned with rows a multiple of 8");
   return s;
@@ -1496,7 +1539,15 @@ extern "C" zl_status zl_gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, voi
                                          zl_stream stream) {
   if (!colsum) return zl::set_error(ZL_EINVAL, "zl_gemm_bf16_colsum: null colsum");
   return zl::gemm_bf16_colsum(A, B, D, M, N, K, layout, epi_flags, epi, workspace, colsum,
-                              static_cast<cudaStream_t>(stream));
+                              static_cast<cudaStream_t>(stream), nullptr, nullptr);
+}
+
+extern "C" zl_status zl_gemm_bf16_relu_bits(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K,
+                                            int layout, int epi_flags, const zl_epilogue* epi, float* workspace,
+                                            uint32_t* bits_out, const uint32_t* bits_in, zl_stream stream) {
+  if (!bits_out && !bits_in) return zl::set_error(ZL_EINVAL, "zl_gemm_bf16_relu_bits: no mask bits given");
+  return zl::gemm_bf16_colsum(A, B, D, M, N, K, layout, epi_flags, epi, workspace, nullptr,
+                              static_cast<cudaStream_t>(stream), bits_out, bits_in);
 }
 
 extern "C" int64_t zl_gemm_workspace_floats(int M, int N, int K, int layout, int epi_flags) {

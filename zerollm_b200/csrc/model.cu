@@ -38,9 +38,11 @@ zl_status norm_backward_bf16(int kind, const zl_bf16* x, const zl_bf16* dy, cons
                              float* workspace, int64_t M, int N, cudaStream_t s, bool fused);
 // kernels.cu: column sums added straight into db (one launch)
 zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaStream_t s);
-// gemm.cu: a bf16 GEMM whose epilogue also adds the column sums of its output into colsum
+// gemm.cu: a bf16 GEMM whose epilogue also adds the column sums of its output into colsum (may be
+// null), writes its ReLU mask as bits (bits_out) or masks with bits written earlier (bits_in)
 zl_status gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout, int flags,
-                           const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st);
+                           const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st, uint32_t* bits_out,
+                           const uint32_t* bits_in);
 // attention.cu: the attention backward with events recorded around its main kernel
 zl_status attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o, const float* lse,
                                   zl_bf16* d_qkv, float* workspace, int batch, int seq_len, int num_heads,
@@ -173,6 +175,9 @@ struct zl_model {
   float *rope_cos_pm = nullptr, *rope_sin_pm = nullptr;  // the same tables pair-major ([Dh/2, S]) for the QKV epilogue
   // activations
   std::vector<bf16*> x, qkv, attn, r1, h1, f, r2;
+  // per layer, f > 0 as bits ([T][F/32] words), written by the FF1 product and read by the ReLU
+  // backward in place of f itself (empty when F is not a multiple of 32)
+  std::vector<uint32_t*> fbits;
   std::vector<float*> lse, mean1, rstd1, mean2, rstd2;
   bf16* hf = nullptr;
   float *meanf = nullptr, *rstdf = nullptr;
@@ -248,12 +253,13 @@ zl_status gemm(zl_model* M, const bf16* A, const bf16* B, void* D, int m, int n,
                       flags, e, M->ws, st);
 }
 
-// the same, also adding the column sums of the bf16 output D into colsum (a bias gradient)
-zl_status gemm_colsum(zl_model* M, const bf16* A, const bf16* B, void* D, int m, int n, int k, int layout, int flags,
-                      const zl_epilogue* e, float* colsum, cudaStream_t st) {
+// the same, also adding the column sums of the bf16 output D into colsum (a bias gradient) and writing
+// (bits_out) or reading (bits_in) the ReLU mask as bits
+zl_status gemm_ext(zl_model* M, const bf16* A, const bf16* B, void* D, int m, int n, int k, int layout, int flags,
+                   const zl_epilogue* e, float* colsum, uint32_t* bits_out, const uint32_t* bits_in, cudaStream_t st) {
   M->launches += 1;
   return zl::gemm_bf16_colsum(reinterpret_cast<const zl_bf16*>(A), reinterpret_cast<const zl_bf16*>(B), D, m, n, k,
-                              layout, flags, e, M->ws, colsum, st);
+                              layout, flags, e, M->ws, colsum, st, bits_out, bits_in);
 }
 
 const bf16* W(zl_model* M, int64_t off) { return M->pbf + off; }
@@ -333,8 +339,9 @@ zl_status forward(zl_model* M, const int32_t* ids, int B, int S, float* logits_f
     M->launches++;
     e = zl_epilogue{};
     e.bias = P(M, t[L_B1]);
-    TRY(gemm(M, M->h1[l], W(M, t[L_W1]), M->f[l], (int)T, F, d, KK, (c.bias ? ZL_EPI_BIAS : 0) | ZL_EPI_RELU, &e,
-             st));
+    // f = relu(h1 W1^T + b1), and f > 0 as bits for the ReLU backward
+    TRY(gemm_ext(M, M->h1[l], W(M, t[L_W1]), M->f[l], (int)T, F, d, KK, (c.bias ? ZL_EPI_BIAS : 0) | ZL_EPI_RELU, &e,
+                 nullptr, M->fbits.empty() ? nullptr : M->fbits[l], nullptr, st));
     e = zl_epilogue{};
     e.bias = P(M, t[L_B2]);
     e.residual = reinterpret_cast<zl_bf16*>(M->h1[l]);
@@ -391,10 +398,11 @@ zl_status backward(zl_model* M, const int32_t* ids, int B, int S, cudaStream_t s
     TRY(gemm(M, M->dr, M->f[l], G(M, t[L_W2]), d, F, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     TRY(grads_ready(M, end_of_any(M, {t[L_W2], t[L_B2]}), st));
     zl_epilogue e{};
-    e.aux = reinterpret_cast<zl_bf16*>(M->f[l]);
-    // dF, and with it the FF1 bias gradient: its column sums, added by the GEMM's epilogue
-    TRY(gemm_colsum(M, M->dr, W(M, t[L_W2]), M->dF, Ti, F, d, ZL_A_KMAJOR, ZL_EPI_RELU_MASK, &e,
-                    c.bias ? G(M, t[L_B1]) : nullptr, st));
+    if (M->fbits.empty()) e.aux = reinterpret_cast<zl_bf16*>(M->f[l]);
+    // dF = (dr W2) masked by f > 0 (the forward's mask bits), and with it the FF1 bias gradient: its
+    // column sums, added by the GEMM's epilogue
+    TRY(gemm_ext(M, M->dr, W(M, t[L_W2]), M->dF, Ti, F, d, ZL_A_KMAJOR, ZL_EPI_RELU_MASK, &e,
+                 c.bias ? G(M, t[L_B1]) : nullptr, nullptr, M->fbits.empty() ? nullptr : M->fbits[l], st));
     TRY(gemm(M, M->dF, M->h1[l], G(M, t[L_W1]), F, d, Ti, 0, ZL_EPI_OUT_F32 | ZL_EPI_ACCUM, nullptr, st));
     TRY(grads_ready(M, end_of_any(M, {t[L_W1], t[L_B1]}), st));
     e = zl_epilogue{};
@@ -501,6 +509,10 @@ extern "C" zl_status zl_model_create(const zl_model_config* cfg, int64_t max_tok
     A(M->qkv[l], T * 3 * d); A(M->attn[l], T * d); A(M->r1[l], T * d); A(M->h1[l], T * d); A(M->f[l], T * F);
     A(M->r2[l], T * d); A(M->lse[l], T * c.num_heads); A(M->mean1[l], T); A(M->rstd1[l], T); A(M->mean2[l], T);
     A(M->rstd2[l], T);
+  }
+  if (F % 32 == 0) {
+    M->fbits.resize(L);
+    for (int l = 0; l < L; ++l) A(M->fbits[l], T * (F / 32));
   }
   A(M->hf, T * d); A(M->meanf, T); A(M->rstdf, T); A(M->logits, T * V); A(M->loss_rows, T);
   A(M->dx, T * d); A(M->dr, T * d); A(M->dtmp, T * d); A(M->dF, T * F); A(M->dqkv, T * 3 * d); A(M->dattn, T * d);
