@@ -470,6 +470,9 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
   const int r = r0 + lane;
   EpiPrefetch<KIND> cur, nxt;
   epi_fetch<KIND>(a, r, lane, n0 + cbase, cur);
+  uint32_t words[NCH];  // mask bits of this row's chunks (bits_out)
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) words[k] = 0;
 #pragma unroll 1
   for (int k = 0; k < NCH; ++k) {
     const int c = cbase + k * 32, c0 = n0 + c;
@@ -518,14 +521,18 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
     uint32_t pk[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
-    if (a.bits_out && r < a.M) {  // bit j: the stored bf16 value of column c0 + j is > 0
+    if (a.bits_out) {  // bit j: the stored bf16 value of column c0 + j is > 0
       uint32_t word = 0;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         word |= ((int16_t)(pk[j] & 0xffffu) > 0 ? 1u : 0u) << (2 * j);
         word |= ((int16_t)(pk[j] >> 16) > 0 ? 1u : 0u) << (2 * j + 1);
       }
-      a.bits_out[(size_t)r * (a.N >> 5) + (c0 >> 5)] = word;
+#pragma unroll
+      for (int kk = 0; kk < NCH; ++kk)
+        if (kk == k) words[kk] = word;  // register-resident: the index is a compile-time constant
+      if (n0 + cbase + NCH * 32 > a.N && r < a.M)  // a partial warp slice: one word at a time
+        a.bits_out[(size_t)r * (a.N >> 5) + (c0 >> 5)] = word;
     }
     // stage [32][32] bf16 (64-byte swizzle) in box k & 1, whose store from chunk k-2 has read it
     const uint32_t box = stg + (uint32_t)((k & 1) * 2048);
@@ -553,6 +560,20 @@ __device__ __forceinline__ void drain_bf16_tma(const GemmArgs& a, const CUtensor
       chunk_colsum_add(v, lane, a.colsum + c0);
     }
     cur = nxt;
+  }
+  // the warp's whole slice of the row's mask words in 16-byte stores (the other column half's warp
+  // writes the neighbouring 16 bytes of the same row)
+  if (a.bits_out && r < a.M && n0 + cbase + NCH * 32 <= a.N) {
+    uint32_t* dst = a.bits_out + (size_t)r * (a.N >> 5) + ((n0 + cbase) >> 5);
+    static_assert(NCH % 2 == 0, "mask words go out in pairs or quadruples");
+    if constexpr (NCH % 4 == 0) {
+#pragma unroll
+      for (int k = 0; k < NCH; k += 4)
+        *reinterpret_cast<uint4*>(dst + k) = make_uint4(words[k], words[k + 1], words[k + 2], words[k + 3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < NCH; k += 2) *reinterpret_cast<uint2*>(dst + k) = make_uint2(words[k], words[k + 1]);
+    }
   }
 }
 
@@ -1330,6 +1351,9 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
     return set_error(ZL_EINVAL, "gemm: relu-mask flag without aux");
   if ((bits_out || bits_in) && (sizeof(T) == 4 || (flags & ZL_EPI_OUT_F32) || N % 32 != 0))
     return set_error(ZL_EINVAL, "gemm: ReLU mask bits are for bf16 outputs with N a multiple of 32");
+  // the epilogue writes a warp's four mask words of a row as one 16-byte store
+  if (bits_out && (N % 128 != 0 || (reinterpret_cast<uintptr_t>(bits_out) & 15)))
+    return set_error(ZL_EINVAL, "gemm: mask bits out need N a multiple of 128 and a 16-byte aligned buffer");
   if (bits_in && !(flags & ZL_EPI_RELU_MASK)) return set_error(ZL_EINVAL, "gemm: mask bits without the relu-mask flag");
   if ((flags & ZL_EPI_ROPE) && (!epi || !epi->rope_cos || !epi->rope_sin || epi->head_dim <= 0 || epi->rope_seq <= 0 ||
                                 (epi->head_dim & 1)))
