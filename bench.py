@@ -157,9 +157,21 @@ def kernel_breakdown(B, S, reps=5):
     e.residual = x.data_ptr()
     e_res_elems = x.numel()
 
-    def gemm(Mm, Nn, Kk, layout, flags, o):
-        L.call("zl_gemm_bf16", x.data_ptr(), w.data_ptr(), o.data_ptr(), Mm, Nn, Kk, layout, flags, C.byref(e),
-               ws.data_ptr(), sp)
+    # the model's FF1 product writes its ReLU mask as bits and the masked dF product reads them
+    # (zl_gemm_bf16_relu_bits; in the step the dF product also adds the FF1 bias gradient's column sums)
+    fbits = torch.empty(T * F // 32, device="cuda", dtype=torch.int32)
+    bsum = torch.zeros(F, device="cuda")
+
+    def gemm(Mm, Nn, Kk, layout, flags, o, bits_out=None, bits_in=None):
+        if bits_out is not None:
+            L.call("zl_gemm_bf16_relu_bits", x.data_ptr(), w.data_ptr(), o.data_ptr(), Mm, Nn, Kk, layout, flags,
+                   C.byref(e), ws.data_ptr(), bits_out.data_ptr(), None, sp)
+        elif bits_in is not None:
+            L.call("zl_gemm_bf16_relu_bits", x.data_ptr(), w.data_ptr(), o.data_ptr(), Mm, Nn, Kk, layout,
+                   flags | L.EPI_RELU_MASK, C.byref(L.Epilogue()), ws.data_ptr(), None, bits_in.data_ptr(), sp)
+        else:
+            L.call("zl_gemm_bf16", x.data_ptr(), w.data_ptr(), o.data_ptr(), Mm, Nn, Kk, layout, flags, C.byref(e),
+                   ws.data_ptr(), sp)
 
     shapes = [
         ("gemm_fwd_qkv", T, 3 * d, d, KK, L.EPI_BIAS, out),
@@ -182,8 +194,10 @@ def kernel_breakdown(B, S, reps=5):
         a_elems, b_elems, d_elems = Mm * Kk, Nn * Kk, Mm * Nn
         assert a_elems <= x.numel() and b_elems <= w.numel() and d_elems <= o.numel() and d_elems <= e_res_elems
         n_per_step = 1 if "head" in name else LAYERS
-        timeit(name, lambda Mm=Mm, Nn=Nn, Kk=Kk, lay=lay, fl=fl, o=o: gemm(Mm, Nn, Kk, lay, fl, o), n_per_step,
-               2.0 * Mm * Nn * Kk, "tensor")
+        bo = fbits if name == "gemm_fwd_ff1" else None
+        bi = fbits if name == "gemm_dx_ff2" else None
+        timeit(name, lambda Mm=Mm, Nn=Nn, Kk=Kk, lay=lay, fl=fl, o=o, bo=bo, bi=bi: gemm(Mm, Nn, Kk, lay, fl, o, bo, bi),
+               n_per_step, 2.0 * Mm * Nn * Kk, "tensor")
     qkv = rnd(T * 3 * d, scale=0.5)
     ob, dob = rnd(T * d), rnd(T * d)
     lse = torch.empty(B * H * S, device="cuda")
