@@ -173,6 +173,15 @@ def test_step_matches_oracle_head_dim_128():
     _compare_step(c, 2, 192)
 
 
+def test_step_matches_oracle_ffn_mask_from_activation():
+    """An FFN width that is a multiple of 64 (the model's granularity) but not of 128 (192): the FF1
+    product writes no ReLU mask bits and the ReLU backward masks with the stored activation f instead;
+    the step still meets the bars."""
+    from zerollm_b200 import Config
+    c = Config(vocab_size=512, embed_dim=128, num_layers=2, num_heads=2, ff_hidden_dim=192, max_seq_len=256)
+    _compare_step(c, 2, 128)
+
+
 def test_full_context_step_properties():
     """26M model at batch 16 x seq 2048 (the timed configuration): the oracle is too slow here, so the
     step is checked through size-independent properties: initial loss ~ ln(V) for N(0,0.02)

@@ -176,7 +176,7 @@ struct zl_model {
   // activations
   std::vector<bf16*> x, qkv, attn, r1, h1, f, r2;
   // per layer, f > 0 as bits ([T][F/32] words), written by the FF1 product and read by the ReLU
-  // backward in place of f itself (empty when F is not a multiple of 32)
+  // backward in place of f itself (empty when F is not a multiple of 128: the backward then reads f)
   std::vector<uint32_t*> fbits;
   std::vector<float*> lse, mean1, rstd1, mean2, rstd2;
   bf16* hf = nullptr;
@@ -510,7 +510,7 @@ extern "C" zl_status zl_model_create(const zl_model_config* cfg, int64_t max_tok
     A(M->r2[l], T * d); A(M->lse[l], T * c.num_heads); A(M->mean1[l], T); A(M->rstd1[l], T); A(M->mean2[l], T);
     A(M->rstd2[l], T);
   }
-  if (F % 32 == 0) {
+  if (F % 128 == 0) {  // the FF1 epilogue writes a row's mask words 16 bytes at a time
     M->fbits.resize(L);
     for (int l = 0; l < L; ++l) A(M->fbits[l], T * (F / 32));
   }
