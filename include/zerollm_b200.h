@@ -183,8 +183,9 @@ zl_status zl_gemm_bf16_relu_bits(const zl_bf16 *A, const zl_bf16 *B, void *D, in
 zl_status zl_attention_forward_bf16(const zl_bf16 *qkv, zl_bf16 *o, float *lse, int batch, int seq_len,
                                     int num_heads, int head_dim, zl_stream stream);
 /* Backward: d_qkv [B*S, 3*H*Dh] receives dq | dk | dv.  `workspace` fp32 of
- * zl_attention_workspace_floats() elements (dq accumulation and row dot products); o, d_o and
- * workspace 16-byte aligned.
+ * zl_attention_workspace_floats() elements (dq accumulation, row dot products and the counter from
+ * which the kernel's CTAs draw work units at run time, so one workspace serves one call in flight at
+ * a time); o, d_o and workspace 16-byte aligned.
  * rope_cos/rope_sin ([seq, head_dim/2], may be NULL, 16-byte aligned): dq and dk are rotated
  * back by the inverse of the interleaved-pair RoPE applied to q and k in the forward. */
 zl_status zl_attention_backward_bf16(const zl_bf16 *qkv, const zl_bf16 *o, const zl_bf16 *d_o,

@@ -255,12 +255,14 @@ __global__ void __launch_bounds__(THREADS) fa_fwd_kernel(const __nv_bfloat16* __
 // row (16-byte loads of O and dO, at element offset 8 * thread index); the Dh/8 threads of a head
 // reduce with shuffles.  Index arithmetic is 32-bit (the host checks B * S * H * Dh < 2^31).
 // The same threads zero the fp32 dQ accumulator (T * E floats, 8 per thread) that the main pass then
-// adds into, in place of a separate memset.
+// adds into, in place of a separate memset, and the first zeroes the main pass's unit counter.
 __global__ void fa_bwd_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
                                   const float* __restrict__ lse, float* __restrict__ Dsum, float* __restrict__ nl,
-                                  float* __restrict__ dq_zero, int B, int S, int H, int DH) {
+                                  float* __restrict__ dq_zero, int* __restrict__ unit_ctr, int B, int S, int H,
+                                  int DH) {
   const uint32_t cpt = (uint32_t)(H * DH) / 8u;  // chunks per token
   const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx == 0 && unit_ctr) *unit_ctr = 0;
   const bool live = idx < (uint32_t)B * (uint32_t)S * cpt;
   float s = 0.f;
   if (live) {
@@ -672,8 +674,8 @@ bool fa_fwd_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, float* lse, 
                       cudaStream_t st, zl_status* status);
 bool fa_bwd_tc_supported(const void* qkv, const void* d_o, const void* dq_acc, const void* d_qkv, int S, int Dh);
 zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
-                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
-                           int S, int H, int Dh, cudaStream_t st);
+                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin,
+                           int* unit_ctr, int B, int S, int H, int Dh, cudaStream_t st);
 bool fa_fwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int ld,
                        __nv_bfloat16* out, float* lse, int B, int S, int H, int Dh, cudaStream_t st, zl_status* status);
 bool fa_bwd_tc_supported3(const void* q, const void* k, const void* v, int ld_in, const void* d_o, const void* dq_acc,
@@ -681,7 +683,8 @@ bool fa_bwd_tc_supported3(const void* q, const void* k, const void* v, int ld_in
 zl_status fa_bwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int ld_in,
                             const __nv_bfloat16* d_o, const float* nl, const float* Dsum, float* dq_acc,
                             __nv_bfloat16* dk, __nv_bfloat16* dv, int ld_out, const float* rope_cos,
-                            const float* rope_sin, int B, int S, int H, int Dh, float dk_scale, cudaStream_t st);
+                            const float* rope_sin, int* unit_ctr, int B, int S, int H, int Dh, float dk_scale,
+                            cudaStream_t st);
 }
 using namespace zl;
 
@@ -720,8 +723,9 @@ extern "C" zl_status zl_attention_forward_bf16(const zl_bf16* qkv, zl_bf16* o, f
   return check_launch("fa_fwd_kernel");
 }
 
+// dq accumulator [B*S, H*Dh], D and nl [B, H, S], then 16 bytes holding the backward's unit counter
 extern "C" int64_t zl_attention_workspace_floats(int batch, int seq_len, int num_heads, int head_dim) {
-  return (int64_t)batch * seq_len * num_heads * head_dim + 2 * (int64_t)batch * num_heads * seq_len;
+  return (int64_t)batch * seq_len * num_heads * head_dim + 2 * (int64_t)batch * num_heads * seq_len + 4;
 }
 
 namespace zl {
@@ -764,20 +768,21 @@ zl_status zl::attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, cons
   float* dq_acc = workspace;
   float* Dsum = workspace + T * E;
   float* nl = Dsum + (int64_t)batch * num_heads * seq_len;
+  int* unit_ctr = reinterpret_cast<int*>(nl + (int64_t)batch * num_heads * seq_len);
   const bool tc = !force_mma_sync() && fa_bwd_tc_supported(qkv, d_o, dq_acc, d_qkv, seq_len, head_dim);
   // the dq accumulator starts at zero (both backward kernels add into it): the pre pass zeroes it
   const int64_t chunks = T * (E / 8);
   fa::fa_bwd_pre_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(d_o), lse, Dsum,
-      tc ? nl : nullptr, dq_acc, batch, seq_len, num_heads, head_dim);
+      tc ? nl : nullptr, dq_acc, unit_ctr, batch, seq_len, num_heads, head_dim);
   zl_status s = check_launch("fa_bwd_pre_kernel");
   if (s != ZL_OK) return s;
   const float scale = 1.0f / sqrtf((float)head_dim);
   if (ev0) record_timing_event(ev0, st);
   if (tc) {
     s = fa_bwd_tc_launch(reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(d_o), nl,
-                         Dsum, dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, batch, seq_len,
-                         num_heads, head_dim, st);
+                         Dsum, dq_acc, reinterpret_cast<__nv_bfloat16*>(d_qkv), rope_cos, rope_sin, unit_ctr, batch,
+                         seq_len, num_heads, head_dim, st);
     if (s != ZL_OK) return s;
   } else {
     const int nk = (seq_len + fa::TILE - 1) / fa::TILE;
@@ -808,7 +813,7 @@ zl_status zl::attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, cons
 // backward's fp32 dQ accumulator and row vectors.  Each region starts on a 256-byte boundary.
 namespace {
 struct MhaState {
-  size_t lse, o, dq, dsum, nl, fwd_end, total;
+  size_t lse, o, dq, dsum, nl, ctr, fwd_end, total;
 };
 MhaState mha_state_layout(int64_t B, int64_t S, int64_t H, int64_t Dh) {
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
@@ -820,7 +825,8 @@ MhaState mha_state_layout(int64_t B, int64_t S, int64_t H, int64_t Dh) {
   m.dq = m.fwd_end;
   m.dsum = up(m.dq + te * 4);
   m.nl = up(m.dsum + rows * 4);
-  m.total = up(m.nl + rows * 4);
+  m.ctr = up(m.nl + rows * 4);  // the backward's unit counter
+  m.total = up(m.ctr + 16);
   return m;
 }
 zl_status mha_bf16_check(const void* q, const void* k, const void* v, const void* state, int64_t B, int64_t S,
@@ -886,6 +892,7 @@ extern "C" zl_status zl_mha_backward_bf16(const zl_bf16* d_attn_output, const zl
   float* dq_acc = reinterpret_cast<float*>(base + m.dq);
   float* Dsum = reinterpret_cast<float*>(base + m.dsum);
   float* nl = reinterpret_cast<float*>(base + m.nl);
+  int* unit_ctr = reinterpret_cast<int*>(base + m.ctr);
   const int B = (int)batch, S = (int)seq_len, H = (int)num_heads, Dh = (int)head_dim, E = H * Dh;
   if (!fa_bwd_tc_supported3(Q, K, V, E, d_attn_output, dq_acc, d_K, d_V, E, S, Dh) ||
       (reinterpret_cast<uintptr_t>(d_Q) & 15))
@@ -893,7 +900,7 @@ extern "C" zl_status zl_mha_backward_bf16(const zl_bf16* d_attn_output, const zl
   cudaStream_t cs = (cudaStream_t)stream;
   const int64_t T = (int64_t)B * S, chunks = T * (E / 8);
   fa::fa_bwd_pre_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, cs>>>(
-      o, reinterpret_cast<const __nv_bfloat16*>(d_attn_output), lse, Dsum, nl, dq_acc, B, S, H, Dh);
+      o, reinterpret_cast<const __nv_bfloat16*>(d_attn_output), lse, Dsum, nl, dq_acc, unit_ctr, B, S, H, Dh);
   st = check_launch("fa_bwd_pre_kernel");
   if (st != ZL_OK) return st;
   // the reference backward leaves out the softmax scale in dQ and dK (mha.cu:284-295)
@@ -902,7 +909,7 @@ extern "C" zl_status zl_mha_backward_bf16(const zl_bf16* d_attn_output, const zl
                          reinterpret_cast<const __nv_bfloat16*>(V), E,
                          reinterpret_cast<const __nv_bfloat16*>(d_attn_output), nl, Dsum, dq_acc,
                          reinterpret_cast<__nv_bfloat16*>(d_K), reinterpret_cast<__nv_bfloat16*>(d_V), E, nullptr,
-                         nullptr, B, S, H, Dh, g_scale, cs);
+                         nullptr, unit_ctr, B, S, H, Dh, g_scale, cs);
   if (st != ZL_OK) return st;
   fa::fa_bwd_post_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, cs>>>(
       dq_acc, reinterpret_cast<__nv_bfloat16*>(d_Q), E, nullptr, nullptr, T, S, H, Dh, g_scale, 1);

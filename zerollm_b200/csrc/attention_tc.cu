@@ -378,6 +378,40 @@ __device__ __forceinline__ void bwd_unit_coords(int u, int nk, int nbh, int hg, 
   *bh = grp * hg + r % heads;
 }
 
+// Backward work units are handed out at run time.  A CTA's first unit is its own index; each later
+// one is the grid size plus the next value of a per-launch counter in global memory (zeroed by the
+// caller's pre pass), so units still start in index order (heaviest first) but a CTA that starts
+// late, because its SM is still busy with another kernel (an all-reduce on a side stream, say),
+// takes fewer of them instead of holding back the end of the launch.  One thread (the TMA issuer)
+// draws the units and publishes each in a ring of UNIT_RING shared-memory slots; every warp of the
+// other roles reads each slot once, in order, and releases it.
+constexpr int UNIT_RING = 4;
+struct UnitFeed {
+  uint64_t* full;   // [UNIT_RING] one arrival: the drawing thread has written the slot
+  uint64_t* empty;  // [UNIT_RING] one arrival per reader warp
+  volatile int* slot;
+  // the CTA's k-th unit index (>= the unit count when there are no more); one thread
+  __device__ __forceinline__ int draw(int k, int cta, int G, int* ctr) const {
+    return k == 0 ? cta : G + atomicAdd(ctr, 1);
+  }
+  __device__ __forceinline__ bool put(int k, int u) const {
+    const int r = k % UNIT_RING;
+    if (!bounded_wait(&empty[r], ((uint32_t)(k / UNIT_RING) & 1u) ^ 1u, DEV_TIMEOUT_ATTN)) return false;
+    slot[r] = u;
+    mbar_arrive(&full[r]);  // release: the slot's value is visible to the thread that sees the phase
+    return true;
+  }
+  // the CTA's k-th unit index, read by a whole warp; -1 when the wait timed out
+  __device__ __forceinline__ int get(int k) const {
+    const int r = k % UNIT_RING;
+    if (!bounded_wait_warp(&full[r], (uint32_t)(k / UNIT_RING) & 1u, DEV_TIMEOUT_ATTN)) return -1;
+    const int u = slot[r];
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[r]);
+    return u;
+  }
+};
+
 template <int DH>
 __global__ void __launch_bounds__(THREADS_PP, 1)
     fa_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -769,7 +803,8 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
                      const float* __restrict__ nl_g,
                      const float* __restrict__ Dsum,
                      const float* __restrict__ rope_cos,
-                     const float* __restrict__ rope_sin, int S, int H, int nunits, int hgroup, float scale, float scale_log2) {
+                     const float* __restrict__ rope_sin, int* __restrict__ unit_ctr, int S, int H, int nunits,
+                     int hgroup, float scale, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -788,6 +823,8 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
   uint64_t* sd_used = sd_full + 5;     // the softmax warps have loaded S^T / dP^T into registers
   uint64_t* dkv_free = sd_full + 6;    // the softmax warps have read dK / dV of the unit out of TMEM
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sd_full + 7);
+  const UnitFeed feed{sd_full + 8, sd_full + 8 + UNIT_RING, reinterpret_cast<volatile int*>(sd_full + 8 + 2 * UNIT_RING)};
+  static_assert((6 + 2 * QST + 8 + 2 * UNIT_RING) * 8 + UNIT_RING * 4 <= 256, "barrier area");
 
   const int E = H * D;
   const int nk = S / BKV;
@@ -795,18 +832,19 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
   const int G = (int)gridDim.x, cta = (int)blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Work unit u = (key block kb, batch-head bh), key-block-major so the units with the most query
-  // blocks come first; CTAs draw units in snake order.  The CTA's blocks form one flat sequence:
-  // unit k of this CTA contributes query blocks kb .. nk-1.
+  // blocks come first; the CTA's units come from the unit feed.  The CTA's blocks form one flat
+  // sequence: unit k of this CTA contributes query blocks kb .. nk-1.
   struct Unit {
     int kb, bh, niter;
   };
-  auto unit_of = [&](int k) -> Unit {
-    const int u = pp_unit(k, cta, G);
-    if (u >= nunits) return Unit{0, 0, 0};
+  auto decode = [&](int u) -> Unit {
+    if (u < 0 || u >= nunits) return Unit{0, 0, 0};
     int kb, bh;
     bwd_unit_coords(u, nk, nbh, hgroup, &kb, &bh);
     return Unit{kb, bh, nk - kb};
   };
+  // every reader warp calls this once for k = 0, 1, ... up to the first unit with niter == 0
+  auto unit_of = [&](int k) -> Unit { return decode(feed.get(k)); };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
@@ -820,6 +858,10 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
     mbar_init(drain, 1);
     mbar_init(sd_used, 32 * NSOFT);
     mbar_init(dkv_free, DQW ? 128 : 32 * NSOFT);
+    for (int i = 0; i < UNIT_RING; ++i) {
+      mbar_init(&feed.full[i], 1);
+      mbar_init(&feed.empty[i], 1 + NSOFT + (DQW ? 4 : 0));  // MMA warp, softmax warps, readout warps
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
@@ -851,7 +893,9 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
         uint32_t n = 0, nkl = 0, nvl = 0;  // Q stages, K and V tiles issued
         bool ok = true;
         for (int k = 0; ok; ++k) {
-          const Unit un = unit_of(k);
+          const int u = min(feed.draw(k, cta, G, unit_ctr), nunits);
+          if (!feed.put(k, u)) break;
+          const Unit un = decode(u);
           if (un.niter == 0) break;
           const int b = un.bh / H, h = un.bh % H;
           const int krow = b * S + un.kb * BKV;
@@ -1354,7 +1398,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
                         const __grid_constant__ CUtensorMap tm_dv, const float* __restrict__ nl_g,
                         const float* __restrict__ Dsum, const float* __restrict__ rope_cos,
-                        const float* __restrict__ rope_sin, int S, int H, int nunits, int hgroup, float scale, float scale_log2) {
+                        const float* __restrict__ rope_sin, int* __restrict__ unit_ctr, int S, int H, int nunits,
+                        int hgroup, float scale, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -1373,23 +1418,27 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* sd_used = sd_full + 5;     // the softmax warps hold S^T / dP^T of the block in registers
   uint64_t* dkv_free = sd_full + 6;    // the softmax warps have read dK / dV of the unit out of TMEM
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sd_full + 7);
+  const UnitFeed feed{sd_full + 8, sd_full + 8 + UNIT_RING, reinterpret_cast<volatile int*>(sd_full + 8 + 2 * UNIT_RING)};
+  static_assert((6 + 2 * QST + 8 + 2 * UNIT_RING) * 8 + UNIT_RING * 4 <= 256, "barrier area");
 
   const int E = H * D;
   const int nk = S / BKV;
   const int nbh = nunits / nk;
   const int G = (int)gridDim.x, cta = (int)blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // unit u = (key block kb, batch-head bh), key-block-major (most query blocks first), snake order
+  // unit u = (key block kb, batch-head bh), key-block-major (most query blocks first), from the
+  // unit feed
   struct Unit {
     int kb, bh, niter;
   };
-  auto unit_of = [&](int k) -> Unit {
-    const int u = pp_unit(k, cta, G);
-    if (u >= nunits) return Unit{0, 0, 0};
+  auto decode = [&](int u) -> Unit {
+    if (u < 0 || u >= nunits) return Unit{0, 0, 0};
     int kb, bh;
     bwd_unit_coords(u, nk, nbh, hgroup, &kb, &bh);
     return Unit{kb, bh, 2 * (nk - kb)};
   };
+  // every reader warp calls this once for k = 0, 1, ... up to the first unit with niter == 0
+  auto unit_of = [&](int k) -> Unit { return decode(feed.get(k)); };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
@@ -1403,6 +1452,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(sd_used, 32 * NSOFT);
     mbar_init(dkv_free, 32 * NSOFT);
+    for (int i = 0; i < UNIT_RING; ++i) {
+      mbar_init(&feed.full[i], 1);
+      mbar_init(&feed.empty[i], 1 + NSOFT);  // MMA warp, softmax warps
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
@@ -1427,7 +1480,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t n = 0, nkl = 0, nvl = 0;
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const Unit un = unit_of(k);
+        const int u = min(feed.draw(k, cta, G, unit_ctr), nunits);
+        if (!feed.put(k, u)) break;
+        const Unit un = decode(u);
         if (un.niter == 0) break;
         const int b = un.bh / H, h = un.bh % H;
         const int krow = b * S + un.kb * BKV;
@@ -1842,12 +1897,15 @@ static bool attn_bwd_readout_warps() {
 }
 
 // Backward main pass.  Before it the caller's pre pass writes nl = -lse*log2(e) and D = rowsum(dO*O)
-// ([B, H, S]) and zeroes dq_acc; after it the post pass turns dq_acc ([B, H, S, Dh] fp32) into dQ.
-// dK is multiplied by `dk_scale` (the softmax scale; 1 for the reference's unscaled gradient).
+// ([B, H, S]) and zeroes dq_acc and the unit counter; after it the post pass turns dq_acc
+// ([B, H, S, Dh] fp32) into dQ.  dK is multiplied by `dk_scale` (the softmax scale; 1 for the
+// reference's unscaled gradient).
 zl_status fa_bwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int ld_in,
                             const __nv_bfloat16* d_o, const float* nl, const float* Dsum, float* dq_acc,
                             __nv_bfloat16* dk, __nv_bfloat16* dv, int ld_out, const float* rope_cos,
-                            const float* rope_sin, int B, int S, int H, int Dh, float dk_scale, cudaStream_t st) {
+                            const float* rope_sin, int* unit_ctr, int B, int S, int H, int Dh, float dk_scale,
+                            cudaStream_t st) {
+  if (!unit_ctr) return set_error(ZL_EINVAL, "attention bwd: null unit counter");
   CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
   const int E = H * Dh, T = B * S;
   const float scale = 1.0f / sqrtf((float)Dh);
@@ -1869,7 +1927,7 @@ zl_status fa_bwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, cons
       return set_error(ZL_ECUDA, "attention bwd: cuTensorMapEncodeTiled failed");
     cudaFuncSetAttribute(K::fa_bwd_tc128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM_TOTAL);
     K::fa_bwd_tc128_kernel<<<grid, K::THREADS, K::SMEM_TOTAL, st>>>(
-        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
+        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, unit_ctr, S, H, nunits, hgroup, dk_scale,
         scale * 1.4426950408889634f);
     return check_launch("fa_bwd_tc128_kernel");
   }
@@ -1882,23 +1940,23 @@ zl_status fa_bwd_tc_launch3(const __nv_bfloat16* q, const __nv_bfloat16* k, cons
     cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          fatc::bwd::SMEM_TOTAL);
     fatc::bwd::fa_bwd_tc_kernel<true><<<grid, fatc::bwd::THREADS_BQ, fatc::bwd::SMEM_TOTAL, st>>>(
-        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
+        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, unit_ctr, S, H, nunits, hgroup, dk_scale,
         scale * 1.4426950408889634f);
   } else {
     cudaFuncSetAttribute(fatc::bwd::fa_bwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          fatc::bwd::SMEM_TOTAL);
     fatc::bwd::fa_bwd_tc_kernel<false><<<grid, fatc::bwd::THREADS_B, fatc::bwd::SMEM_TOTAL, st>>>(
-        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, S, H, nunits, hgroup, dk_scale,
+        tq, tk, tv, tdo, tdq, tdk, tdv, nl, Dsum, rope_cos, rope_sin, unit_ctr, S, H, nunits, hgroup, dk_scale,
         scale * 1.4426950408889634f);
   }
   return check_launch("fa_bwd_tc_kernel");
 }
 zl_status fa_bwd_tc_launch(const __nv_bfloat16* qkv, const __nv_bfloat16* d_o, const float* nl, const float* Dsum,
-                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin, int B,
-                           int S, int H, int Dh, cudaStream_t st) {
+                           float* dq_acc, __nv_bfloat16* d_qkv, const float* rope_cos, const float* rope_sin,
+                           int* unit_ctr, int B, int S, int H, int Dh, cudaStream_t st) {
   const int E = H * Dh;
   return fa_bwd_tc_launch3(qkv, qkv + E, qkv + 2 * E, 3 * E, d_o, nl, Dsum, dq_acc, d_qkv + E, d_qkv + 2 * E, 3 * E,
-                           rope_cos, rope_sin, B, S, H, Dh, 1.0f / sqrtf((float)Dh), st);
+                           rope_cos, rope_sin, unit_ctr, B, S, H, Dh, 1.0f / sqrtf((float)Dh), st);
 }
 
 int attn_tc_dev_error_read_and_clear() {
