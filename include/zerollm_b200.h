@@ -178,6 +178,17 @@ zl_status zl_gemm_bf16_colsum(const zl_bf16 *A, const zl_bf16 *B, void *D, int M
 zl_status zl_gemm_bf16_relu_bits(const zl_bf16 *A, const zl_bf16 *B, void *D, int M, int N, int K, int layout,
                                  int epi_flags, const zl_epilogue *epi, float *workspace, uint32_t *bits_out,
                                  const uint32_t *bits_in, zl_stream stream);
+/* zl_gemm_bf16 whose persistent CTAs draw their work units (output tiles x split-K slices) at run
+ * time from `unit_counters` (one int32 in device memory, 4-byte aligned, zero before the first call)
+ * instead of taking them round-robin: a CTA that starts late, because another kernel (an all-reduce
+ * on a side stream, say) still holds its SM, takes fewer units instead of holding back the end of
+ * the product.  The CTA that draws a launch's last value puts the counter back to zero, so
+ * consecutive calls in one stream can share it; calls that may run at the same time (other
+ * streams) must each have their own.  The result is the one zl_gemm_bf16 gives.  No counterpart in the reference, whose GEMMs
+ * launch one thread block per output tile (matmul.cu:227-230, 257-260). */
+zl_status zl_gemm_bf16_sched(const zl_bf16 *A, const zl_bf16 *B, void *D, int M, int N, int K, int layout,
+                             int epi_flags, const zl_epilogue *epi, float *workspace, int *unit_counters,
+                             zl_stream stream);
 /* Causal flash attention over a packed qkv buffer [B*S, 3*H*Dh] (q | k | v), output o [B*S, H*Dh],
  * lse [B, H, S] (natural log of the row sums of exp(scale * q.k)). */
 zl_status zl_attention_forward_bf16(const zl_bf16 *qkv, zl_bf16 *o, float *lse, int batch, int seq_len,

@@ -127,6 +127,21 @@ def test_bf16_entry_points_reject_misaligned_rows():
     assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
 
 
+def test_gemm_sched_rejects_bad_counters_before_device_work():
+    """zl_gemm_bf16_sched refuses null or misaligned unit counters on the host (the operand pointers
+    here are never dereferenced)."""
+    import ctypes as C
+    from zerollm_b200 import lib
+    L = lib.load()
+    a = 1 << 20
+    e = lib.Epilogue()
+    lay = lib.A_KMAJOR | lib.B_KMAJOR
+    st = L.zl_gemm_bf16_sched(a, a, a, 256, 256, 64, lay, 0, C.byref(e), None, None, None)
+    assert st == lib.ZL_EINVAL and b"unit counters" in L.zl_last_error()
+    st = L.zl_gemm_bf16_sched(a, a, a, 256, 256, 64, lay, 0, C.byref(e), None, a + 2, None)
+    assert st == lib.ZL_EINVAL and b"4-byte aligned" in L.zl_last_error()
+
+
 def test_mha_bf16_rejects_unsupported_calls_before_device_work():
     """The bf16 attention instance runs the causal flash-attention kernels: a non-causal call, a
     mask, an unsupported head size or a state buffer below zl_mha_state_bytes_bf16() is refused on

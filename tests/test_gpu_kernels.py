@@ -182,6 +182,36 @@ def test_gemm_bf16_colsum(L, M, N, K_, flags, gemm_kind):
     assert rel(cs.cpu(), ref.cpu()) < 1e-5
 
 
+@pytest.mark.parametrize("M,N,K_,a_mn,f32", [
+    (8192, 2048, 512, False, False),   # FF1-shaped: many units per CTA
+    (512, 2048, 8192, True, True),     # a weight-gradient shape: split-K slices as units, fp32 output
+    (256, 256, 64, False, False),      # fewer units than CTAs: every CTA's first draw is its last
+])
+def test_gemm_bf16_sched(L, M, N, K_, a_mn, f32, gemm_kind):
+    """zl_gemm_bf16_sched: CTAs that draw their units from the counters give zl_gemm_bf16's output
+    bit for bit, the CTA that draws the last value leaves the counter at zero, and repeated calls
+    sharing it agree."""
+    import ctypes as C
+    g = torch.Generator(device="cuda").manual_seed(M + N + K_)
+    A = (torch.randn(K_, M, device="cuda", generator=g) if a_mn else torch.randn(M, K_, device="cuda", generator=g))
+    A = A.bfloat16()
+    B = (torch.randn(N, K_, device="cuda", generator=g) * 0.05).bfloat16()
+    lay = (0 if a_mn else L.A_KMAJOR) | L.B_KMAJOR
+    fl = L.EPI_OUT_F32 if f32 else 0
+    want = _gemm(L, A.reshape(-1), B.reshape(-1), M, N, K_, lay, fl)
+    n = L.load().zl_gemm_workspace_floats(M, N, K_, lay, fl)
+    ws = torch.empty(max(int(n), 1), device="cuda")
+    counters = torch.zeros(2, device="cuda", dtype=torch.int32)  # the second int must stay untouched
+    e = L.Epilogue()
+    for _ in range(3):
+        out = torch.full_like(want, float("nan"))
+        L.call("zl_gemm_bf16_sched", A.data_ptr(), B.data_ptr(), out.data_ptr(), M, N, K_, lay, fl, C.byref(e),
+               ws.data_ptr(), counters.data_ptr(), None)
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+        assert counters.tolist() == [0, 0]
+
+
 @pytest.mark.parametrize("M", [2048, 2600])
 def test_gemm_bf16_relu_bits(L, M, gemm_kind):
     """zl_gemm_bf16_relu_bits: the FF1-shaped product (bias + ReLU) writes f > 0 as bits next to an

@@ -383,17 +383,16 @@ __device__ __forceinline__ void bwd_unit_coords(int u, int nk, int nbh, int hg, 
 // caller's pre pass), so units still start in index order (heaviest first) but a CTA that starts
 // late, because its SM is still busy with another kernel (an all-reduce on a side stream, say),
 // takes fewer of them instead of holding back the end of the launch.  One thread (the TMA issuer)
-// draws the units and publishes each in a ring of UNIT_RING shared-memory slots; every warp of the
-// other roles reads each slot once, in order, and releases it.
+// draws each unit one unit ahead, so the counter's round trip overlaps a unit's loads, and publishes
+// every unit in a ring of UNIT_RING shared-memory slots; every warp of the other roles reads each
+// slot once, in order, and releases it.
 constexpr int UNIT_RING = 4;
 struct UnitFeed {
   uint64_t* full;   // [UNIT_RING] one arrival: the drawing thread has written the slot
   uint64_t* empty;  // [UNIT_RING] one arrival per reader warp
   volatile int* slot;
-  // the CTA's k-th unit index (>= the unit count when there are no more); one thread
-  __device__ __forceinline__ int draw(int k, int cta, int G, int* ctr) const {
-    return k == 0 ? cta : G + atomicAdd(ctr, 1);
-  }
+  // the CTA's next unit index (>= the unit count when there are no more); one thread
+  __device__ __forceinline__ int draw(int G, int* ctr) const { return G + atomicAdd(ctr, 1); }
   __device__ __forceinline__ bool put(int k, int u) const {
     const int r = k % UNIT_RING;
     if (!bounded_wait(&empty[r], ((uint32_t)(k / UNIT_RING) & 1u) ^ 1u, DEV_TIMEOUT_ATTN)) return false;
@@ -892,11 +891,12 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
       if (lane == 0) {
         uint32_t n = 0, nkl = 0, nvl = 0;  // Q stages, K and V tiles issued
         bool ok = true;
+        int u = cta;
         for (int k = 0; ok; ++k) {
-          const int u = min(feed.draw(k, cta, G, unit_ctr), nunits);
           if (!feed.put(k, u)) break;
           const Unit un = decode(u);
           if (un.niter == 0) break;
+          const int u_next = min(feed.draw(G, unit_ctr), nunits);
           const int b = un.bh / H, h = un.bh % H;
           const int krow = b * S + un.kb * BKV;
           const size_t row_base = (size_t)un.bh * S;
@@ -923,6 +923,7 @@ __global__ void __launch_bounds__(DQW ? THREADS_BQ : THREADS_B, 1)
               ++nvl;
             }
           }
+          u = u_next;
         }
         // no copy may still be landing in shared memory when the CTA exits: the last load of every
         // slot has completed (the consumers waited for all of them on the normal path)
@@ -1479,11 +1480,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t n = 0, nkl = 0, nvl = 0;
       bool ok = true;
+      int u = cta;
       for (int k = 0; ok; ++k) {
-        const int u = min(feed.draw(k, cta, G, unit_ctr), nunits);
         if (!feed.put(k, u)) break;
         const Unit un = decode(u);
         if (un.niter == 0) break;
+        const int u_next = min(feed.draw(G, unit_ctr), nunits);
         const int b = un.bh / H, h = un.bh % H;
         const int krow = b * S + un.kb * BKV;
         const size_t row_base = (size_t)un.bh * S;
@@ -1514,6 +1516,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ++nvl;
           }
         }
+        u = u_next;
       }
       // no copy may still be landing in shared memory when the CTA exits
       for (uint32_t k = nkl > 2u ? nkl - 2 : 0; k < nkl; ++k)

@@ -24,6 +24,7 @@ enum DevErr : int {
   DEV_TIMEOUT_FULL = 1,     // consumer gave up waiting for a TMA stage
   DEV_TIMEOUT_EMPTY = 2,    // producer gave up waiting for a free stage
   DEV_TIMEOUT_ACC = 3,      // epilogue / MMA gave up on an accumulator buffer
+  DEV_TIMEOUT_UNIT = 4,     // a GEMM role gave up waiting for its next work unit
 };
 
 // ------------------------------------------------------------------ misc

@@ -58,6 +58,7 @@ struct GemmArgs {
   // epilogue kinds) receives (stored value > 0) of every output; bits_in is the EK_MASKBITS kind's mask
   uint32_t* bits_out;
   const uint32_t* bits_in;
+  int* sched;  // the run-time unit counter, or null for round-robin units
 };
 
 template <int BN, int STAGES, int ELEM_BYTES>
@@ -69,6 +70,71 @@ struct Smem {
   static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * kStgBytes;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers + alignment slack
 };
+
+// ------------------------------------------------------------------ work units
+// A persistent CTA (or CTA pair) walks output tiles (x split-K slices) as work units.  Its first
+// unit is its own index (the grid never exceeds the unit count), known to every role.  With
+// args.sched set, each later one is drawn at run time: the number of CTAs (pairs) plus the next
+// value of the counter *sched.  Units still start in index order, but a CTA that starts late,
+// because another kernel still holds its SM (an all-reduce on a side stream), takes fewer of them
+// instead of holding back the end of the launch.  Every drawing CTA draws until it gets a value at
+// or past the unit count (its end marker) and then stops, so a launch draws exactly `units` values;
+// the CTA that draws the last one puts the counter back to zero.  Consecutive launches in one stream
+// can therefore share it; launches that may run at the same time must not.  Without sched the units
+// go round-robin over the CTAs, and no role touches the ring (measured: the ring's hand-offs alone
+// cost the bf16-epilogue products 2-8 %).  The TMA thread (of the even CTA, in a pair) draws each
+// unit one unit ahead, so the counter's round trip overlaps a unit's loads, and publishes the CTA's
+// units after the first in a ring of UNIT_RING shared-memory slots, which every other role reads
+// once each, in order (ring position k - 1 holds the CTA's k-th unit).
+constexpr int UNIT_RING = 4;
+__device__ __forceinline__ int unit_draw(const GemmArgs& a, int ctas) { return ctas + atomicAdd(a.sched, 1); }
+// After the CTA's last draw (`drawn`, -1 if none): a CTA that stopped early, on a timed-out wait,
+// draws on to its end marker, and the CTA that drew the launch's last value resets the counter.
+__device__ __forceinline__ void unit_settle(const GemmArgs& a, int drawn, int ctas) {
+  if (!a.sched) return;
+  while (drawn < a.units) drawn = ctas + atomicAdd(a.sched, 1);
+  if (drawn == ctas + a.units - 1) atomicExch(a.sched, 0);
+}
+// one-SM kernel: the TMA thread publishes; readers are whole warps
+__device__ __forceinline__ bool unit_put(uint64_t* full, uint64_t* empty, volatile int* slot, int k, int u) {
+  const int r = k % UNIT_RING;
+  if (!bounded_wait(&empty[r], ((uint32_t)(k / UNIT_RING) & 1u) ^ 1u, DEV_TIMEOUT_UNIT)) return false;
+  slot[r] = u;
+  mbar_arrive(&full[r]);
+  return true;
+}
+__device__ __forceinline__ int unit_get_warp(uint64_t* full, uint64_t* empty, volatile int* slot, int k) {
+  const int r = k % UNIT_RING;
+  if (!bounded_wait_warp(&full[r], (uint32_t)(k / UNIT_RING) & 1u, DEV_TIMEOUT_UNIT)) return -1;
+  const int u = slot[r];
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[r]);
+  return u;
+}
+// CTA pair: the even CTA's TMA thread writes the slot in both CTAs and arrives on both `full`
+// barriers; the readers of both CTAs release the slot on the even CTA's `empty` barrier
+__device__ __forceinline__ bool unit_put_pair(uint64_t* full, uint64_t* empty, volatile int* slot, int k, int u) {
+  const int r = k % UNIT_RING;
+  if (!bounded_wait_cluster(&empty[r], ((uint32_t)(k / UNIT_RING) & 1u) ^ 1u, DEV_TIMEOUT_UNIT)) return false;
+  slot[r] = u;
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(mapa_shared(smem_u32((const void*)&slot[r]), 1)), "r"(u)
+               : "memory");
+  mbar_arrive(&full[r]);
+  mbar_arrive_cluster(mapa_shared(smem_u32(&full[r]), 1));  // release: the store above is seen first
+  return true;
+}
+// a whole warp (warp_wide) or a single thread reads the CTA's k-th unit; -1 when the wait timed out
+__device__ __forceinline__ int unit_get_pair(uint64_t* full, uint64_t* empty, volatile int* slot, int k,
+                                             bool warp_wide) {
+  const int r = k % UNIT_RING;
+  bool ok = bounded_wait_cluster(&full[r], (uint32_t)(k / UNIT_RING) & 1u, DEV_TIMEOUT_UNIT);
+  if (warp_wide) ok = __all_sync(0xffffffffu, ok);
+  if (!ok) return -1;
+  const int u = slot[r];
+  if (warp_wide) __syncwarp();
+  if (!warp_wide || (threadIdx.x & 31) == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&empty[r]), 0));
+  return u;
+}
 
 // ------------------------------------------------------------------ epilogue
 // Per-thread fused epilogue for 32 consecutive columns [c0, c0+32) of row r (used for
@@ -610,12 +676,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* u_full = acc_empty + 3;  // [UNIT_RING] the work-unit ring
+  uint64_t* u_empty = u_full + UNIT_RING;
+  volatile int* u_slot = reinterpret_cast<volatile int*>(u_empty + UNIT_RING);
+  static_assert((2 * STAGES + 5 + 2 * UNIT_RING) * 8 + UNIT_RING * 4 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps * 32); }
+    for (int i = 0; i < UNIT_RING; ++i) { mbar_init(&u_full[i], 1); mbar_init(&u_empty[i], 1 + kEpiWarps); }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -635,7 +706,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+      int u = (int)blockIdx.x, drawn = -1;
+      for (int ku = 0; ok; ++ku) {
+        if (args.sched && ku > 0 && !unit_put(u_full, u_empty, u_slot, ku - 1, u)) break;
+        if (u >= args.units) break;
+        const int u_next = args.sched ? unit_draw(args, (int)gridDim.x) : u + (int)gridDim.x;
+        drawn = u_next;
         const int tile = u / args.splits, split = u % args.splits;
         const int m0 = (tile / args.n_tiles_n) * BM, n0 = (tile % args.n_tiles_n) * BN;
         const int kb0 = split * args.kb_per_split;
@@ -660,7 +736,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
+        u = u_next;
       }
+      unit_settle(args, drawn, (int)gridDim.x);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
@@ -669,7 +747,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < args.units && ok; u += gridDim.x) {
+    for (int ku = 0; ok; ++ku) {
+      const int u = (ku == 0 || !args.sched) ? (int)blockIdx.x + ku * (int)gridDim.x
+                                             : unit_get_warp(u_full, u_empty, u_slot, ku - 1);
+      if (u < 0 || u >= args.units) break;
       const int split = u % args.splits;
       const int kb0 = split * args.kb_per_split;
       const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
@@ -714,7 +795,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool use_tma = fast_ok && args.tma_out;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < args.units; u += gridDim.x) {
+    for (int ku = 0;; ++ku) {
+      const int u = (ku == 0 || !args.sched) ? (int)blockIdx.x + ku * (int)gridDim.x
+                                             : unit_get_warp(u_full, u_empty, u_slot, ku - 1);
+      if (u < 0 || u >= args.units) break;
       const int tile = u / args.splits, split = u % args.splits;
       const int m0 = (tile / args.n_tiles_n) * BM, n0 = (tile % args.n_tiles_n) * BN;
       if constexpr (KIND >= 0) epi_prefetch_l2<BN, KIND>(args, m0 + quarter * 32 + lane, n0 + col_half * (BN / 2));
@@ -808,6 +892,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* u_full = acc_empty + 3;  // [UNIT_RING] the work-unit ring (the even CTA's `empty` counts)
+  uint64_t* u_empty = u_full + UNIT_RING;
+  volatile int* u_slot = reinterpret_cast<volatile int*>(u_empty + UNIT_RING);
+  static_assert((2 * STAGES + 5 + 2 * UNIT_RING) * 8 + UNIT_RING * 4 <= 256, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -817,6 +905,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 2 * kEpiWarps * 32); }
+    // readers of a unit slot: the even CTA's MMA warp and epilogue warps, the odd CTA's TMA thread and
+    // epilogue warps
+    for (int i = 0; i < UNIT_RING; ++i) { mbar_init(&u_full[i], 1); mbar_init(&u_empty[i], 2 + 2 * kEpiWarps); }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -837,7 +928,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = pair; u < args.units && ok; u += npairs) {
+      int u_next = pair, drawn = -1;
+      for (int ku = 0; ok; ++ku) {
+        int u = pair + ku * npairs;
+        if (args.sched) {
+          if (leader) {
+            u = u_next;
+            if (ku > 0 && !unit_put_pair(u_full, u_empty, u_slot, ku - 1, u)) break;
+            if (u < args.units) drawn = u_next = unit_draw(args, npairs);
+          } else if (ku > 0) {
+            u = unit_get_pair(u_full, u_empty, u_slot, ku - 1, false);
+            if (u < 0) break;
+          }
+        }
+        if (u >= args.units) break;
         const int tile = u / args.splits, split = u % args.splits;
         const int m0 = (tile / args.n_tiles_n) * (2 * BM) + (int)rank * BM;  // this CTA's rows
         const int n0 = (tile % args.n_tiles_n) * BN + (int)rank * (BN / 2);  // this CTA's half of B
@@ -866,6 +970,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
+      if (leader) unit_settle(args, drawn, npairs);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (even CTA only)
@@ -875,7 +980,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = pair; u < args.units && ok; u += npairs) {
+      for (int ku = 0; ok; ++ku) {
+        const int u = (ku == 0 || !args.sched) ? pair + ku * npairs
+                                               : unit_get_pair(u_full, u_empty, u_slot, ku - 1, true);
+        if (u < 0 || u >= args.units) break;
         const int split = u % args.splits;
         const int kb0 = split * args.kb_per_split;
         const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
@@ -921,7 +1029,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                           mapa_shared(smem_u32(&acc_empty[1]), 0)};
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = pair; u < args.units; u += npairs) {
+    for (int ku = 0;; ++ku) {
+      const int u = (ku == 0 || !args.sched) ? pair + ku * npairs
+                                             : unit_get_pair(u_full, u_empty, u_slot, ku - 1, true);
+      if (u < 0 || u >= args.units) break;
       const int tile = u / args.splits, split = u % args.splits;
       const int m0 = (tile / args.n_tiles_n) * (2 * BM) + (int)rank * BM;
       const int n0 = (tile % args.n_tiles_n) * BN;
@@ -1337,7 +1448,7 @@ zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaSt
 template <typename T>
 zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layout, int flags,
                   const zl_epilogue* epi, float* ws, cudaStream_t st, float* colsum = nullptr,
-                  uint32_t* bits_out = nullptr, const uint32_t* bits_in = nullptr) {
+                  uint32_t* bits_out = nullptr, const uint32_t* bits_in = nullptr, int* sched = nullptr) {
   using E = Elem<T>;
   if (M <= 0 || N <= 0 || K <= 0) return set_error(ZL_EINVAL, "gemm: sizes must be positive (M=%d N=%d K=%d)", M, N, K);
   if (!A || !B || !D) return set_error(ZL_EINVAL, "gemm: null operand");
@@ -1368,6 +1479,7 @@ zl_status gemm_tc(const T* A, const T* B, void* D, int M, int N, int K, int layo
   a.colsum = nullptr;
   a.bits_out = nullptr;
   a.bits_in = bits_in;
+  a.sched = sched;
   a.M = M; a.N = N; a.K = K;
   a.D = D; a.flags = flags;
   if (epi) a.epi = *epi; else memset(&a.epi, 0, sizeof(a.epi));
@@ -1530,16 +1642,19 @@ int gemm_dev_error_read_and_clear() {
 
 template zl_status gemm_tc<__nv_bfloat16>(const __nv_bfloat16*, const __nv_bfloat16*, void*, int, int, int, int, int,
                                           const zl_epilogue*, float*, cudaStream_t, float*, uint32_t*,
-                                          const uint32_t*);
+                                          const uint32_t*, int*);
 
 // zl_gemm_bf16 that also adds the column sums of its bf16 output into colsum (a bias gradient):
 // in the epilogue when the product takes the pipelined bf16 epilogue, else by a column-sum pass.
+// sched (an int, zero before the first launch, may be null) lets the CTAs draw their work units at
+// run time; every GEMM given the same counter must run in one stream.
 zl_status gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout, int flags,
                            const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st, uint32_t* bits_out,
-                           const uint32_t* bits_in) {
+                           const uint32_t* bits_in, int* sched) {
+  if (reinterpret_cast<uintptr_t>(sched) & 3) return set_error(ZL_EINVAL, "gemm: unit counters must be 4-byte aligned");
   zl_status s = gemm_tc<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(A),
                                        reinterpret_cast<const __nv_bfloat16*>(B), D, M, N, K, layout, flags, epi, ws,
-                                       st, colsum, bits_out, bits_in);
+                                       st, colsum, bits_out, bits_in, sched);
   if (s == ZL_EUNSUPPORTED)
     return set_error(ZL_EUNSUPPORTED, "gemm: operands must be 16-byte aligned with rows a multiple of 8");
   return s;
@@ -1563,7 +1678,7 @@ extern "C" zl_status zl_gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, voi
                                          zl_stream stream) {
   if (!colsum) return zl::set_error(ZL_EINVAL, "zl_gemm_bf16_colsum: null colsum");
   return zl::gemm_bf16_colsum(A, B, D, M, N, K, layout, epi_flags, epi, workspace, colsum,
-                              static_cast<cudaStream_t>(stream), nullptr, nullptr);
+                              static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr);
 }
 
 extern "C" zl_status zl_gemm_bf16_relu_bits(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K,
@@ -1571,7 +1686,15 @@ extern "C" zl_status zl_gemm_bf16_relu_bits(const zl_bf16* A, const zl_bf16* B, 
                                             uint32_t* bits_out, const uint32_t* bits_in, zl_stream stream) {
   if (!bits_out && !bits_in) return zl::set_error(ZL_EINVAL, "zl_gemm_bf16_relu_bits: no mask bits given");
   return zl::gemm_bf16_colsum(A, B, D, M, N, K, layout, epi_flags, epi, workspace, nullptr,
-                              static_cast<cudaStream_t>(stream), bits_out, bits_in);
+                              static_cast<cudaStream_t>(stream), bits_out, bits_in, nullptr);
+}
+
+extern "C" zl_status zl_gemm_bf16_sched(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout,
+                                        int epi_flags, const zl_epilogue* epi, float* workspace, int* unit_counters,
+                                        zl_stream stream) {
+  if (!unit_counters) return zl::set_error(ZL_EINVAL, "zl_gemm_bf16_sched: null unit counters");
+  return zl::gemm_bf16_colsum(A, B, D, M, N, K, layout, epi_flags, epi, workspace, nullptr,
+                              static_cast<cudaStream_t>(stream), nullptr, nullptr, unit_counters);
 }
 
 extern "C" int64_t zl_gemm_workspace_floats(int M, int N, int K, int layout, int epi_flags) {

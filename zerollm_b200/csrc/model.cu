@@ -42,7 +42,7 @@ zl_status colsum_bf16_add(const zl_bf16* dy, float* db, int64_t M, int N, cudaSt
 // null), writes its ReLU mask as bits (bits_out) or masks with bits written earlier (bits_in)
 zl_status gemm_bf16_colsum(const zl_bf16* A, const zl_bf16* B, void* D, int M, int N, int K, int layout, int flags,
                            const zl_epilogue* epi, float* ws, float* colsum, cudaStream_t st, uint32_t* bits_out,
-                           const uint32_t* bits_in);
+                           const uint32_t* bits_in, int* sched);
 // attention.cu: the attention backward with events recorded around its main kernel
 zl_status attention_backward_bf16(const zl_bf16* qkv, const zl_bf16* o, const zl_bf16* d_o, const float* lse,
                                   zl_bf16* d_qkv, float* workspace, int batch, int seq_len, int num_heads,
@@ -259,7 +259,7 @@ zl_status gemm_ext(zl_model* M, const bf16* A, const bf16* B, void* D, int m, in
                    const zl_epilogue* e, float* colsum, uint32_t* bits_out, const uint32_t* bits_in, cudaStream_t st) {
   M->launches += 1;
   return zl::gemm_bf16_colsum(reinterpret_cast<const zl_bf16*>(A), reinterpret_cast<const zl_bf16*>(B), D, m, n, k,
-                              layout, flags, e, M->ws, colsum, st, bits_out, bits_in);
+                              layout, flags, e, M->ws, colsum, st, bits_out, bits_in, nullptr);
 }
 
 const bf16* W(zl_model* M, int64_t off) { return M->pbf + off; }

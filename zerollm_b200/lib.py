@@ -73,6 +73,7 @@ SIGNATURES = {
     "zl_gemm_bf16": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, C.POINTER(Epilogue), vp, vp]),
     "zl_gemm_bf16_colsum": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, C.POINTER(Epilogue), vp, vp, vp]),
     "zl_gemm_bf16_relu_bits": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, C.POINTER(Epilogue), vp, vp, vp, vp]),
+    "zl_gemm_bf16_sched": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, C.POINTER(Epilogue), vp, vp, vp]),
     "zl_gemm_workspace_floats": (i64, [i32, i32, i32, i32, i32]),
     "zl_attention_forward_bf16": (i32, [vp, vp, vp, i32, i32, i32, i32, vp]),
     "zl_attention_backward_bf16": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, vp]),
