@@ -331,7 +331,7 @@ def run_reference(args, rank, world):
                              "sample": "1x2048 tokens per step, fp32 fwd+bwd+AdamW, oracle/liboracle.so",
                              "single_thread": one},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------- our arm
@@ -481,10 +481,27 @@ def run_ours(args, rank, world, local_rank):
         line["kernels_ms"] = {k: round(v["ms"], 4) for k, v in bd.items()}
     if cpu:
         line["cpu_baseline"] = cpu
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the process's original standard output."""
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 def main():
+    global _RESULT_OUT
+    # The result is one JSON line on standard output, but native libraries may write there too (NCCL
+    # prints a version banner when its debug level asks for one): for the rest of the run file
+    # descriptor 1 points at standard error, and the result line goes to a copy of the original.
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -506,8 +523,8 @@ def main():
         import torch
         torch.cuda.set_device(0)
         bd = kernel_breakdown(args.batch, args.seq, reps=2)
-        print(json.dumps({"kernels_only": True, "batch": args.batch, "seq_len": args.seq,
-                          "kernels_ms": {k: round(v["ms"], 4) for k, v in bd.items()}}), flush=True)
+        emit({"kernels_only": True, "batch": args.batch, "seq_len": args.seq,
+              "kernels_ms": {k: round(v["ms"], 4) for k, v in bd.items()}})
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
