@@ -494,14 +494,18 @@ def emit(line: dict) -> None:
     out.flush()
 
 
-def main():
+def claim_stdout() -> None:
+    """The result is one JSON line on standard output, but native libraries may write there too
+    (NCCL prints a version banner when its debug level asks for one): from here on file descriptor 1
+    points at standard error, and emit() writes to a copy of the original."""
     global _RESULT_OUT
-    # The result is one JSON line on standard output, but native libraries may write there too (NCCL
-    # prints a version banner when its debug level asks for one): for the rest of the run file
-    # descriptor 1 points at standard error, and the result line goes to a copy of the original.
     sys.stdout.flush()
     _RESULT_OUT = os.fdopen(os.dup(1), "w")
     os.dup2(2, 1)
+
+
+def main():
+    claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

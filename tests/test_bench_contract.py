@@ -54,3 +54,17 @@ def test_peaks_come_from_the_measured_file(bench):
         assert p["source"] == "measured" and p["bf16_tflops"] > 1000 and p["hbm_gbs"] > 5000
     else:
         assert p["source"] == "fallback"
+
+
+def test_result_line_is_alone_on_stdout():
+    """Output that a native library writes to file descriptor 1 after claim_stdout() lands on
+    standard error; standard output holds the result line only."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import os, bench; bench.claim_stdout(); os.write(1, b'NCCL version x\\n'); print('chatter'); "
+            "bench.emit({'metric': 'm', 'value': 1.0})")
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.splitlines() == ['{"metric": "m", "value": 1.0}']
+    assert "NCCL version x" in r.stderr and "chatter" in r.stderr
