@@ -127,6 +127,21 @@ def test_bf16_entry_points_reject_misaligned_rows():
     assert st == lib.ZL_EINVAL and b"16-byte aligned" in L.zl_last_error()
 
 
+def test_attention_workspace_holds_the_unit_counter():
+    """The attention backward's workspace is the dQ accumulator, D and nl, then 16 bytes for the
+    counter its CTAs draw work units from; the bf16 MHA state ends with the same counter."""
+    from zerollm_b200 import lib
+    L = lib.load()
+    B, S, H, Dh = 2, 256, 4, 64
+    assert L.zl_attention_workspace_floats(B, S, H, Dh) == B * S * H * Dh + 2 * B * H * S + 4
+    rows, te = B * H * S, B * S * H * Dh
+    up = lambda x: (x + 255) // 256 * 256
+    o = up(rows * 4)
+    dq = up(o + te * 2)
+    ctr = up(up(up(dq + te * 4) + rows * 4) + rows * 4)
+    assert L.zl_mha_state_bytes_bf16(B, S, H, Dh) == up(ctr + 16)
+
+
 def test_gemm_sched_rejects_bad_counters_before_device_work():
     """zl_gemm_bf16_sched refuses null or misaligned unit counters on the host (the operand pointers
     here are never dereferenced)."""
