@@ -187,11 +187,21 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
   // row itself); wider rows reload and recompute them
   constexpr bool KEEP = kMaxChunks <= 2;
   float gl[KEEP ? kMaxChunks : 1][8];
+  // KEEP rows run their per-element arithmetic on column pairs (paired fp32 instructions, each lane
+  // rounding like the scalar one): gamma, the dgamma / dbeta / column-sum accumulators and the
+  // row's x-hat, dy * gamma are held as pairs
+  uint64_t gl2[KEEP ? kMaxChunks : 1][4], pg2[KEEP ? kMaxChunks : 1][4], pb2[KEEP ? kMaxChunks : 1][4],
+      pc2[KEEP ? kMaxChunks : 1][4];
   if constexpr (KEEP) {
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < N) load8f(g + col, gl[c]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        gl2[c][i] = f2_pack(gl[c][2 * i], gl[c][2 * i + 1]);
+        pg2[c][i] = pb2[c][i] = pc2[c][i] = 0ull;  // +0.0f in both halves
+      }
     }
   }
   uint4 nx[kMaxChunks], nd[kMaxChunks];
@@ -265,31 +275,53 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
       if (PREFETCH && r + nwarps < M) fetch(r + nwarps);
     }
     float s1 = 0.f, s2 = 0.f;
-    float xhk[KEEP ? kMaxChunks : 1][8], ak[KEEP ? kMaxChunks : 1][8];
+    uint64_t xhk2[KEEP ? kMaxChunks : 1][4], ak2[KEEP ? kMaxChunks : 1][4];
+    if constexpr (KEEP) {
+      const uint64_t mu2 = f2_pack(mu, mu), rs2 = f2_pack(rs, rs);
+      uint64_t s12 = 0ull, s22 = 0ull;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      if (col < N) {
-        float gv[8], xv[8], dv[8];
-        if constexpr (KEEP) {
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < N) {
+          const uint32_t xw[4] = {cx[c].x, cx[c].y, cx[c].z, cx[c].w}, dw[4] = {cd[c].x, cd[c].y, cd[c].z, cd[c].w};
 #pragma unroll
-          for (int j = 0; j < 8; ++j) gv[j] = gl[c][j];
-        } else {
-          load8f(g + col, gv);
+          for (int i = 0; i < 4; ++i) {
+            // bf16 pair -> fp32 pair (element 2i in the low half of the word)
+            const uint64_t x2 = f2_pack(__uint_as_float(xw[i] << 16), __uint_as_float(xw[i] & 0xffff0000u));
+            const uint64_t d2 = f2_pack(__uint_as_float(dw[i] << 16), __uint_as_float(dw[i] & 0xffff0000u));
+            const uint64_t xh2 = KIND == 0 ? mul2(sub2(x2, mu2), rs2) : mul2(x2, rs2);
+            const uint64_t a2 = mul2(d2, gl2[c][i]);
+            s12 = add2(s12, a2);
+            s22 = fma2(a2, xh2, s22);
+            pg2[c][i] = fma2(d2, xh2, pg2[c][i]);
+            if (KIND == 0) pb2[c][i] = add2(pb2[c][i], d2);
+            xhk2[c][i] = xh2;
+            ak2[c][i] = a2;
+          }
         }
-        unpack8(cx[c], xv);
-        unpack8(cd[c], dv);
+      }
+      float e, o;
+      f2_unpack(s12, e, o);
+      s1 = e + o;
+      f2_unpack(s22, e, o);
+      s2 = e + o;
+    } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float xh = (xv[j] - mu) * rs;
-          const float a = dv[j] * gv[j];
-          s1 += a;
-          s2 += a * xh;
-          pg[c][j] += dv[j] * xh;
-          if (KIND == 0) pb[c][j] += dv[j];
-          if constexpr (KEEP) {
-            xhk[c][j] = xh;
-            ak[c][j] = a;
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int col = (c * 32 + lane) * 8;
+        if (col < N) {
+          float gv[8], xv[8], dv[8];
+          load8f(g + col, gv);
+          unpack8(cx[c], xv);
+          unpack8(cd[c], dv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float xh = (xv[j] - mu) * rs;
+            const float a = dv[j] * gv[j];
+            s1 += a;
+            s2 += a * xh;
+            pg[c][j] += dv[j] * xh;
+            if (KIND == 0) pb[c][j] += dv[j];
           }
         }
       }
@@ -305,8 +337,13 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
       if (col < N) {
         float o[8];
         if constexpr (KEEP) {
+          const uint64_t rs2 = f2_pack(rs, rs), nc1 = f2_pack(-c1, -c1), nc2 = f2_pack(-c2, -c2);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = fmaf(-xhk[c][j], c2, fmaf(rs, ak[c][j], -c1));
+          for (int i = 0; i < 4; ++i) {
+            const uint64_t o2 = fma2(xhk2[c][i], nc2, fma2(rs2, ak2[c][i], nc1));
+            if (COL) pc2[c][i] = add2(pc2[c][i], o2);
+            f2_unpack(o2, o[2 * i], o[2 * i + 1]);
+          }
         } else {
           float gv[8], xv[8], dv[8];
           load8f(g + col, gv);
@@ -318,9 +355,11 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
             o[j] = fmaf(-xh, c2, fmaf(rs, dv[j] * gv[j], -c1));
           }
         }
+        if constexpr (!KEEP) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (COL) pc[c][j] += o[j];
+          for (int j = 0; j < 8; ++j)
+            if (COL) pc[c][j] += o[j];
+        }
         store8(dx + r * N + col, o);
       }
     }
@@ -330,6 +369,16 @@ __global__ void __launch_bounds__(256) norm_bwd_bf16_kernel(const __nv_bfloat16*
       for (int64_t j = k; j < k + STAGES; ++j)
         if (row + j * nwarps < M) bounded_wait(&bars[j % STAGES], (uint32_t)((j / STAGES) & 1), DEV_TIMEOUT_FULL);
     __syncwarp();
+  }
+  if constexpr (KEEP) {
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f2_unpack(pg2[c][i], pg[c][2 * i], pg[c][2 * i + 1]);
+        f2_unpack(pb2[c][i], pb[c][2 * i], pb[c][2 * i + 1]);
+        f2_unpack(pc2[c][i], pc[c][2 * i], pc[c][2 * i + 1]);
+      }
   }
   // block partials: [dgamma | dbeta | column sums]
   auto put = [&](float* base, bool atomic) {
